@@ -1,0 +1,81 @@
+/* B200 extensions of the pinfer C API and the kernel-level C ABI of the verify path.
+ *
+ * Everything here is additive to include/pinfer.h (the reference grew its own API the same way,
+ * engine/include/pinfer.h:62-66,153-155). Device pointers are plain `void *` / typed pointers
+ * into CUDA device memory of the current device; `stream` is a cudaStream_t passed as void *
+ * (NULL = the legacy default stream). No function here allocates on the CPU side of the model
+ * path, and none has a CPU fallback: without a CUDA device they return PINFER_E_NOMEM. */
+#ifndef NB_B200_H
+#define NB_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "pinfer.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Message of the last failure on this thread ("" if none). */
+const char *pinfer_b200_last_error(void);
+
+/* Greedy speculative decoding with the benchmark's synthetic drafter (no reference
+ * counterpart: the reference drafts with its MTP head, engine/src/spec.c:301-321; this replaces
+ * step 1 of pf_spec_decode and keeps steps 2-3, verify / accept / commit, spec.c:323-351).
+ * Draft for output index j: with probability p the token greedy[j] (the target's own greedy
+ * output, n_max entries, from a plain run), else a uniform token; the drafter is the pure
+ * function of (seed, j) in oracle/ref_spec.c. The whole round runs on the device. Resets the
+ * context first, like pinfer_generate_greedy_ex. Returns tokens written (out[0..ret)) or a
+ * negative PINFER_E_*; *status as in pinfer_generate_greedy_ex; stats accumulated. */
+int pinfer_b200_generate_synthetic(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt,
+                                   int32_t *out, int n_max, int k, const int32_t *greedy,
+                                   uint64_t seed, float p, pinfer_spec_stats *stats, int *status);
+
+/* pinfer_b200_generate_synthetic with append (1: continue after the tokens already in context,
+ * like pinfer_generate_greedy_cont) and *decode_ms (may be NULL): device time of the
+ * verify / accept loop after the prompt, from CUDA events on the context's stream. */
+int pinfer_b200_generate_synthetic_ex(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt,
+                                      int32_t *out, int n_max, int k, const int32_t *greedy,
+                                      uint64_t seed, float p, int append,
+                                      pinfer_spec_stats *stats, int *status, float *decode_ms);
+
+/* Kernel launches in one verify round of draft depth k (the nodes of its CUDA graph). */
+int pinfer_b200_round_kernels(pinfer_ctx *ctx, int k);
+
+/* Feed n tokens and return the logits of EVERY row, [n][n_vocab] (the logits_all output of
+ * the reference's pf_forward, engine/src/forward.h:293-300). */
+int pinfer_b200_forward_all(pinfer_ctx *ctx, const int32_t *tokens, int n, float *logits_all);
+
+/* The CUDA stream every call on ctx runs on (for timing with events on the same stream). */
+void *pinfer_b200_stream(pinfer_ctx *ctx);
+
+/* ---- kernel-level ABI: the Q4K x A8 matmul on device buffers ----------------------------
+ * The pf_matmul contract for dtype Q4K_G32 (engine/src/ops.h:49-52: Y[n][rows] = W X, weights
+ * read once for all n) with the reference's arithmetic (kern_quant_act, kern_act.c:14-41;
+ * kern_q4k, kern_quant.c:296-304): bit-identical outputs. Weights are in the panel layout
+ * (nb_q4k_repack of the .pq bytes, then copied to the device). */
+size_t nb_q4k_panel_bytes(int rows, int cols);
+/* .pq Q4K tiles (host) -> panel layout (host), panel_bytes(rows, cols) bytes. 0 or -4. */
+int nb_q4k_repack(const uint8_t *pq, int rows, int cols, uint8_t *panels);
+
+typedef struct nb_mv nb_mv;
+/* Activation scratch (A8 of up to nmax vectors of `cols`) and a control block on the device.
+ * nmax <= 16. NULL on failure (no device, bad shape). */
+nb_mv *nb_mv_create(int rows, int cols, int nmax);
+void nb_mv_destroy(nb_mv *h);
+/* Set the vector count n (1..nmax) used by the next calls (one tiny kernel on `stream`). */
+int nb_mv_set_n(nb_mv *h, int n, void *stream);
+/* A8-quantise X [n][cols] (device fp32) into the scratch: kern_quant_act. */
+int nb_mv_quant(nb_mv *h, const float *X, void *stream);
+/* Y [n][rows] = W (device panel layout) x scratch activations. */
+int nb_mv_matmul(nb_mv *h, const void *W, float *Y, void *stream);
+/* nb_mv_quant + nb_mv_matmul. */
+int nb_mv_run(nb_mv *h, const void *W, const float *X, float *Y, void *stream);
+/* Copy the scratch activations out (device buffers: q [n][cols] int8, d / fsum [n][cols/32]). */
+int nb_mv_get_act(nb_mv *h, int8_t *q, float *d, float *fsum, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

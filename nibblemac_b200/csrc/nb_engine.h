@@ -1,0 +1,150 @@
+// Internal interface between the host engine (nb_engine.cu, C++) and the device kernels
+// (nb_kernels.cu). Not part of the public API.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "nb_math.cuh"
+
+namespace nb {
+
+// ---- Q4K weights in HBM: the panel layout -------------------------------------------------
+// The .pq file stores Q4K_G32 as 4-row tiles of 576-byte superblocks (engine/FORMAT.md,
+// "Quantized dtypes"). At upload every matrix is repacked, without touching a code or a
+// scale value, into panels of 32 rows: for panel p and superblock sb (256 columns) one
+// 4608-byte unit holds
+//   [32 rows x 16 B scale entry][block 0: 32 rows x 16 B codes] ... [block 7: 32 x 16 B]
+// so a warp with lane = row reads every part of the unit with one coalesced 512-byte load.
+// Scale entry of a row (two little-endian u64): A = s6[0..7] (6 bits each, bits 6k..6k+5) |
+// D fp16 bits << 48, B = m6[0..7] | M fp16 bits << 48. Codes: byte j holds column j (low
+// nibble) and column j + 16 (high nibble) of the 32-column block, as in the file.
+constexpr int kPanelRows = 32;
+constexpr int kUnitBytes = 4608;
+
+struct Mat {
+    const uint8_t *w = nullptr;  // panel layout
+    int rows = 0, cols = 0, npanels = 0, nsb = 0;
+};
+
+// int8 activations, vector-major: q [nmax][cols], d / fs [nmax][cols / 32]
+struct Act {
+    int8_t *q = nullptr;
+    float *d = nullptr, *fs = nullptr;
+    int cols = 0;
+};
+
+constexpr int kMaxRows = 16;      // rows (tokens) per forward pass on the small-batch path
+constexpr int kMaxLayers = 32;
+
+// Mutable per-pass control block in device memory. Kernels read the pass shape from it, so a
+// captured CUDA graph replays a whole verify round with no host round trip.
+struct Step {
+    int n;                 // rows in this pass (0 = nothing to do)
+    int pos0;              // position of row 0 (= tokens already in context)
+    int logged;            // 1: verify pass (rows >= 1 on state copies, logged for commit)
+    int wr;                // log half the next logged pass writes
+    int pend_keep;         // recurrent updates (log rows 1..pend_keep of half wr^1) to replay
+    int pend_conv;         // conv commit owed: keep = pend_conv tokens of the last logged pass
+    int tokens[kMaxRows];  // input tokens of the pass
+    int argmax[kMaxRows];  // head argmax of every row (first maximum)
+    // generation loop (nb_accept)
+    int count, n_max, done, status;
+    int k;                 // drafts per round
+    int eos;               // stop token (< 0: none)
+    int n_stop;
+    int stop_ids[8];
+    int cur;
+    int max_ctx;
+    int vocab;
+    unsigned p24;          // synthetic drafter acceptance threshold (p * 2^24)
+    unsigned long long seed;
+    long long rounds, drafted, accepted;
+};
+
+struct GenArgs {
+    int n_max, k, eos, n_stop, max_ctx, vocab;
+    int stop_ids[8];
+    unsigned p24;
+    unsigned long long seed;
+};
+
+// Per-layer parameters of a Gated DeltaNet layer on the device
+struct LinLayer {
+    float *conv_state;     // [K-1][C]
+    float *rec;            // [nv][dk][dv]
+    float *xin;            // [cap][C] raw conv inputs of rows 1.. of a logged pass
+    float *upd;            // [2][cap][nv][dk + dv + 1]
+    const float *conv_w;   // [C][K]
+    const float *A;        // [nv] = -expf(A_log) (computed on the host with glibc) or A
+    const float *dt_bias;  // [nv]
+    const float *norm_w;   // [dv]
+};
+
+struct LinDims {
+    int C, K, kd, vd, nk, nv, rep, dk, dv, cap, ldy;
+    float eps;
+};
+
+struct AttnLayer {
+    float *kc, *vc;        // [nkv][max_ctx][hd]
+    const float *q_norm, *k_norm;
+};
+
+struct AttnDims {
+    int nq, nkv, hd, rot, max_ctx, ldy;
+    float eps;
+    const float *rope_cos, *rope_sin;   // [max_ctx][rot / 2]
+};
+
+// ---- launchers (nb_kernels.cu); all asynchronous on `s` ---------------------------------
+void launch_embed(const Mat &E, const Step *st, float *x, int H, cudaStream_t s);
+void launch_norm_quant(const float *x, const float *w, int H, float eps, const Step *st,
+                       Act out, cudaStream_t s);
+// Y = W A8(x): mode 0 store y[v][ldy], mode 1 residual x[v][ldy] += y
+void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode, int nmax,
+                   cudaStream_t s);
+// gate / up with SwiGLU and A8 quantisation of the product
+void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Act out, int nmax,
+                          cudaStream_t s);
+// tied head: logits (may be null) [v][ld] and per-panel argmax partials
+void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int ld,
+                        unsigned long long *partial, int *nan0, int nmax, cudaStream_t s);
+void launch_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
+                         Step *st, cudaStream_t s);
+void launch_deltanet(const LinLayer &L, const LinDims &d, const LibmTables &T, const float *y,
+                     Step *st, Act out, cudaStream_t s);
+void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
+                      const Step *st, cudaStream_t s);
+void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
+                 const Step *st, Act out, cudaStream_t s);
+void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s);
+void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s);
+void launch_pass_end(Step *st, cudaStream_t s);
+size_t deltanet_smem(int rep);
+void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s);
+void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s);
+void kernels_init(int max_ctx, int hd, int rep);
+void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s);
+// small-n standalone entry points for the C-ABI kernel tests
+void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s);
+
+// ---- host-side helpers -----------------------------------------------------------------------
+size_t panel_bytes(int rows, int cols);
+// repack one Q4K matrix (.pq tile layout, rows % 4 == 0, cols % 256 == 0) into the panel
+// layout; `out` has panel_bytes(rows, cols) bytes; rows beyond `rows` are zero.
+void repack_q4k(const uint8_t *pq, int rows, int cols, uint8_t *out);
+
+// libm tables (nb_libm.cpp)
+struct HostLibm {
+    uint32_t *exp_bits = nullptr, *log1p_bits = nullptr;
+    size_t exp_words = 0, log1p_words = 0;
+    uint32_t *ovf_key = nullptr;   // pairs (fn, bits)
+    float *ovf_val = nullptr;
+    int n_ovf = 0;
+};
+int libm_tables_get(HostLibm *out, int threads, char *err, size_t errlen);
+void libm_tables_free(HostLibm *t);
+
+}  // namespace nb

@@ -1,0 +1,1031 @@
+// Device kernels of the B200 verify path (sm_100a).
+//
+// Every kernel reproduces the reference engine's arithmetic bit for bit (file:line cited per
+// kernel); nb_math.cuh holds the shared scalar primitives. Kernels read the pass shape (rows n,
+// first position pos0, logged or not) from the Step block in device memory, so one captured
+// CUDA graph serves every round of a generation.
+#include <cuda_fp16.h>
+
+#include <cstdio>
+
+#include "nb_engine.h"
+
+namespace nb {
+
+namespace {
+
+// ------------------------------------------------------------------ warp helpers
+__device__ __forceinline__ float warp_max_abs(float v) {
+    float m = fabsf(v);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return m;
+}
+__device__ __forceinline__ int warp_sum_int(int v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = w > v ? w : v;
+    }
+    return v;
+}
+
+// A8 quantisation of one 32-column block held one value per lane (kern_quant_act,
+// engine/src/kern_act.c:14-41): amax = max |x|, id = amax > 0 ? 127 / amax : 0,
+// q = round-half-even(x * id) (vcvtnq: NaN -> 0, saturating), d = amax / 127,
+// fsum = d * (float)sum(q). Writes q at qdst[lane] and d / fsum through lane 0.
+__device__ __forceinline__ void quant_block_warp(float x, int lane, int8_t *qdst, float *ddst,
+                                                 float *fdst) {
+    const float amax = warp_max_abs(x);
+    const float id = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    const int q = __float2int_rn(__fmul_rn(x, id));
+    const int sum = warp_sum_int(q);
+    qdst[lane] = (int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q));
+    if (lane == 0) {
+        const float d = __fdiv_rn(amax, 127.0f);
+        *ddst = d;
+        *fdst = __fmul_rn(d, (float)sum);
+    }
+}
+
+// Order-preserving key of a (logit, row) pair: larger logit wins, then the lower row, NaN
+// never wins (pf_argmax, engine/src/forward_ops.c:387-409: first maximum, NaN skipped).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+    uint32_t u = __float_as_uint(v);
+    if (v != v) u = 0u;
+    else if (v == 0.0f) u = 0x80000000u;                 // +0 and -0 compare equal
+    else u = (u >> 31) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (0xffffffffu - (uint32_t)row);
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t h) {
+    return __half2float(__ushort_as_half((unsigned short)h));
+}
+
+__device__ __forceinline__ int dot_block(const uint4 c, const int4 x0, const int4 x1) {
+    // 16 code bytes: byte j = column j (low nibble) | column j + 16 (high nibble)
+    int s = 0;
+    s = __dp4a((int)(c.x & 0x0f0f0f0fu), x0.x, s);
+    s = __dp4a((int)(c.y & 0x0f0f0f0fu), x0.y, s);
+    s = __dp4a((int)(c.z & 0x0f0f0f0fu), x0.z, s);
+    s = __dp4a((int)(c.w & 0x0f0f0f0fu), x0.w, s);
+    s = __dp4a((int)((c.x >> 4) & 0x0f0f0f0fu), x1.x, s);
+    s = __dp4a((int)((c.y >> 4) & 0x0f0f0f0fu), x1.y, s);
+    s = __dp4a((int)((c.z >> 4) & 0x0f0f0f0fu), x1.z, s);
+    s = __dp4a((int)((c.w >> 4) & 0x0f0f0f0fu), x1.w, s);
+    return s;
+}
+
+// ------------------------------------------------------------------ Q4K x A8 matvec
+// Per (row, vector) the reference computes, blocks in column order (kern_q4k / q4_tile /
+// q4_block, engine/src/kern_quant.c:148-245):
+//   isum = sum_j u[j] * q[j]                     (int32, exact)
+//   acc  = fmaf((float)isum, (D * s6) * d_act, acc)
+//   acc  = fmaf(-(M * m6), fsum_act, acc)
+// A CTA of 4 warps owns one 32-row panel (lane = row). The superblocks of the row are split
+// over the warps in chunks of 4: each warp computes the integer block dots of one superblock
+// (coalesced 512-byte loads, dp4a on CUDA cores), then the ordered FMA chain runs over the
+// chunk's 32 blocks from shared memory, one thread per (row, vector). The chain order, and so
+// every bit of the result, is independent of n and of the split.
+constexpr int kMvWarps = 4;
+constexpr int kMvThreads = kMvWarps * 32;
+
+template <int NMAX>
+struct MvSmem {
+    int32_t isum[kMvWarps * 8][NMAX][32];
+    float ds[kMvWarps * 8][32];
+    float os[kMvWarps * 8][32];
+    float da[NMAX][kMvWarps * 8];
+    float fa[NMAX][kMvWarps * 8];
+};
+
+template <int NMAX>
+__device__ __forceinline__ void mv_panel(const Mat &W, const Act &in, int n, int panel,
+                                         MvSmem<NMAX> &sm, float (&acc)[(NMAX + 3) / 4]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = W.cols >> 5;
+#pragma unroll
+    for (int i = 0; i < (NMAX + 3) / 4; i++) acc[i] = 0.0f;
+    for (int c0 = 0; c0 < W.nsb; c0 += kMvWarps) {
+        const int sb = c0 + warp;
+        if (sb < W.nsb) {
+            const uint8_t *u = W.w + ((size_t)panel * W.nsb + sb) * kUnitBytes + lane * 16;
+            const uint4 sc = __ldcs(reinterpret_cast<const uint4 *>(u));
+            uint4 cd[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) cd[k] = __ldcs(reinterpret_cast<const uint4 *>(u + 512 * (k + 1)));
+            const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
+            const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
+            const float D = half_bits_to_float((uint32_t)(A >> 48));
+            const float M = half_bits_to_float((uint32_t)(B >> 48));
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                sm.ds[warp * 8 + k][lane] = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
+                sm.os[warp * 8 + k][lane] = __fmul_rn(M, (float)(uint32_t)((B >> (6 * k)) & 63u));
+            }
+            for (int v = 0; v < n; v++) {
+                const int4 *xq = reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols + sb * 256);
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const int4 x0 = __ldg(xq + 2 * k), x1 = __ldg(xq + 2 * k + 1);
+                    sm.isum[warp * 8 + k][v][lane] = dot_block(cd[k], x0, x1);
+                }
+                if (lane < 8) {
+                    sm.da[v][warp * 8 + lane] = __ldg(in.d + (size_t)v * nb + sb * 8 + lane);
+                    sm.fa[v][warp * 8 + lane] = __ldg(in.fs + (size_t)v * nb + sb * 8 + lane);
+                }
+            }
+        }
+        __syncthreads();
+        const int left = W.nsb - c0;
+        const int nblk = (left < kMvWarps ? left : kMvWarps) * 8;
+#pragma unroll
+        for (int i = 0; i < (NMAX + 3) / 4; i++) {
+            const int v = warp + 4 * i;
+            if (v < n) {
+                float a = acc[i];
+                for (int b = 0; b < nblk; b++) {
+                    const float s = (float)sm.isum[b][v][lane];
+                    a = __fmaf_rn(s, __fmul_rn(sm.ds[b][lane], sm.da[v][b]), a);
+                    a = __fmaf_rn(-sm.os[b][lane], sm.fa[v][b], a);
+                }
+                acc[i] = a;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// mode 0: y[v][row] = acc; mode 1: y[v][row] += acc (residual, pf_add_rows
+// engine/src/forward.c:68-72: x = x + out)
+template <int NMAX, int MODE>
+__global__ void __launch_bounds__(kMvThreads) k_matvec(Mat W, Act in, const Step *st, float *y,
+                                                       int ldy) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    MvSmem<NMAX> &sm = *reinterpret_cast<MvSmem<NMAX> *>(smraw);
+    const int n = st->n;
+    if (n <= 0) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int panel = blockIdx.x; panel < W.npanels; panel += gridDim.x) {
+        float acc[(NMAX + 3) / 4];
+        mv_panel<NMAX>(W, in, n, panel, sm, acc);
+        const int row = panel * kPanelRows + lane;
+#pragma unroll
+        for (int i = 0; i < (NMAX + 3) / 4; i++) {
+            const int v = warp + 4 * i;
+            if (v < n && row < W.rows) {
+                float *p = y + (size_t)v * ldy + row;
+                *p = MODE == 0 ? acc[i] : __fadd_rn(*p, acc[i]);
+            }
+        }
+    }
+}
+
+// Tied LM head (engine/src/forward.c:142-145): logits of every row and, per panel, the
+// (max, first index) key of every vector for the on-device argmax.
+template <int NMAX>
+__global__ void __launch_bounds__(kMvThreads) k_matvec_head(Mat W, Act in, const Step *st,
+                                                            float *logits, int ld,
+                                                            unsigned long long *partial,
+                                                            int *nan0) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    MvSmem<NMAX> &sm = *reinterpret_cast<MvSmem<NMAX> *>(smraw);
+    const int n = st->n;
+    if (n <= 0) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int panel = blockIdx.x; panel < W.npanels; panel += gridDim.x) {
+        float acc[(NMAX + 3) / 4];
+        mv_panel<NMAX>(W, in, n, panel, sm, acc);
+        const int row = panel * kPanelRows + lane;
+#pragma unroll
+        for (int i = 0; i < (NMAX + 3) / 4; i++) {
+            const int v = warp + 4 * i;
+            if (v < n) {   // warp-uniform
+                if (logits && row < W.rows) logits[(size_t)v * ld + row] = acc[i];
+                const unsigned long long key = row < W.rows ? argmax_key(acc[i], row) : 0ull;
+                const unsigned long long best = warp_max_u64(key);
+                if (lane == 0) partial[(size_t)v * W.npanels + panel] = best;
+                if (panel == 0 && lane == 0) nan0[v] = acc[i] != acc[i];
+            }
+        }
+    }
+}
+
+// gate / up projections with SwiGLU (pf_mlp + pf_silu_mul, engine/src/forward.c:49-58,
+// forward_ops.c:98-101: h = silu(g) * u) and the A8 quantisation of h for the down projection
+// (one 32-row panel = one 32-column activation block).
+template <int NMAX>
+__global__ void __launch_bounds__(kMvThreads) k_matvec_swiglu(Mat G, Mat U, Act in,
+                                                              const Step *st, Act out) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    MvSmem<NMAX> &sm = *reinterpret_cast<MvSmem<NMAX> *>(smraw);
+    const int n = st->n;
+    if (n <= 0) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nbo = out.cols >> 5;
+    for (int panel = blockIdx.x; panel < G.npanels; panel += gridDim.x) {
+        float g[(NMAX + 3) / 4], u[(NMAX + 3) / 4];
+        mv_panel<NMAX>(G, in, n, panel, sm, g);
+        mv_panel<NMAX>(U, in, n, panel, sm, u);
+#pragma unroll
+        for (int i = 0; i < (NMAX + 3) / 4; i++) {
+            const int v = warp + 4 * i;
+            if (v < n) {
+                const float h = __fmul_rn(pf_silu(g[i]), u[i]);
+                quant_block_warp(h, lane, out.q + (size_t)v * out.cols + panel * 32,
+                                 out.d + (size_t)v * nbo + panel, out.fs + (size_t)v * nbo + panel);
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ argmax over the panels
+__global__ void k_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
+                               Step *st) {
+    const int v = blockIdx.x;
+    if (v >= st->n) return;
+    __shared__ unsigned long long red[32];
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < npanels; i += blockDim.x) {
+        const unsigned long long k = partial[(size_t)v * npanels + i];
+        best = k > best ? k : best;
+    }
+    best = warp_max_u64(best);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        unsigned long long b = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+        b = warp_max_u64(b);
+        if (threadIdx.x == 0)
+            st->argmax[v] = nan0[v] ? 0 : (int)(0xffffffffu - (uint32_t)(b & 0xffffffffu));
+    }
+}
+
+// ------------------------------------------------------------------ embedding rows
+// kern_get_row_q, Q4K branch (engine/src/kern_act.c:76-85): dd = D * s6, mm = M * m6,
+// x = dd * u - mm (two roundings), read from the panel layout.
+__global__ void k_embed(Mat E, const Step *st, float *x, int H) {
+    const int v = blockIdx.x;
+    if (v >= st->n) return;
+    int tok = st->tokens[v];
+    if (tok < 0 || tok >= E.rows) tok = 0;   // host and accept kernel validate ids
+    const int panel = tok >> 5, r = tok & 31;
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+        const int sb = c >> 8, k = (c >> 5) & 7, j = c & 31;
+        const uint8_t *u = E.w + ((size_t)panel * E.nsb + sb) * kUnitBytes + r * 16;
+        const uint4 sc = *reinterpret_cast<const uint4 *>(u);
+        const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
+        const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
+        const float dd = __fmul_rn(half_bits_to_float((uint32_t)(A >> 48)),
+                                   (float)(uint32_t)((A >> (6 * k)) & 63u));
+        const float mm = __fmul_rn(half_bits_to_float((uint32_t)(B >> 48)),
+                                   (float)(uint32_t)((B >> (6 * k)) & 63u));
+        const uint8_t byte = u[512 * (k + 1) + (j & 15)];
+        const float q = (float)(j < 16 ? (byte & 15) : (byte >> 4));
+        x[(size_t)v * H + c] = __fadd_rn(__fmul_rn(dd, q), -mm);
+    }
+}
+
+// ------------------------------------------------------------------ RMSNorm + A8
+// sumsq (engine/src/forward_ops.c:170-181): 4 interleaved partial sums over the first n/4*4
+// elements, sequential tail, result ((c0 + c1) + (c2 + c3)) + tail. Threads 0..3 of warp 0
+// run the four chains, thread 4 the tail.
+__device__ float sumsq_ref(const float *x, int n) {
+    const int lane = threadIdx.x & 31;
+    float c = 0.0f;
+    const int n4 = n & ~3;
+    if (lane < 4) {
+        for (int i = lane; i < n4; i += 4) c = madd(c, x[i], x[i]);
+    } else if (lane == 4) {
+        for (int i = n4; i < n; i++) c = madd(c, x[i], x[i]);
+    }
+    const float c1 = __shfl_sync(0xffffffffu, c, 1), c2 = __shfl_sync(0xffffffffu, c, 2);
+    const float c3 = __shfl_sync(0xffffffffu, c, 3), t = __shfl_sync(0xffffffffu, c, 4);
+    const float c0 = __shfl_sync(0xffffffffu, c, 0);
+    return __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), t);
+}
+
+// pf_softmax_exp's sum (forward_ops.c:320-353): 4 interleaved partial sums over the first
+// n/4*4 elements, sequential tail, ((c0 + c1) + (c2 + c3)) + tail. Called by warp 0.
+__device__ float sum4_ref(const float *a, int n) {
+    const int lane = threadIdx.x & 31;
+    float c = 0.0f;
+    const int n4 = n & ~3;
+    if (lane < 4) {
+        for (int i = lane; i < n4; i += 4) c = __fadd_rn(c, a[i]);
+    } else if (lane == 4) {
+        for (int i = n4; i < n; i++) c = __fadd_rn(c, a[i]);
+    }
+    const float c1 = __shfl_sync(0xffffffffu, c, 1), c2 = __shfl_sync(0xffffffffu, c, 2);
+    const float c3 = __shfl_sync(0xffffffffu, c, 3), t = __shfl_sync(0xffffffffu, c, 4);
+    const float c0 = __shfl_sync(0xffffffffu, c, 0);
+    return __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), t);
+}
+
+// pf_rmsnorm (forward_ops.c:191-200): r = 1 / sqrtf(sumsq / n + eps), y = (x * r) * w, then
+// A8 blocks of 32 (kern_quant_act). One CTA per row, H floats of shared memory.
+__global__ void k_norm_quant(const float *x, const float *w, int H, float eps, const Step *st,
+                             Act out) {
+    const int v = blockIdx.x;
+    if (v >= st->n) return;
+    extern __shared__ float xs[];
+    __shared__ float rr;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = x[(size_t)v * H + i];
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const float s = sumsq_ref(xs, H);
+        if (threadIdx.x == 0) rr = inv_sqrt_ref(__fadd_rn(__fdiv_rn(s, (float)H), eps));
+    }
+    __syncthreads();
+    const float r = rr;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int nb = H >> 5;
+    for (int b = warp; b < nb; b += nw) {
+        const int i = b * 32 + lane;
+        const float y = __fmul_rn(__fmul_rn(xs[i], r), w[i]);
+        quant_block_warp(y, lane, out.q + (size_t)v * out.cols + b * 32,
+                         out.d + (size_t)v * nb + b, out.fs + (size_t)v * nb + b);
+    }
+}
+
+// plain A8 quantisation of n rows (kernel-level C-ABI entry point)
+__global__ void k_quant_act(const float *x, int n, int cols, Act out) {
+    const int lane = threadIdx.x & 31;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nb = cols >> 5;
+    if (gw >= n * nb) return;
+    const int v = gw / nb, b = gw % nb;
+    quant_block_warp(x[(size_t)v * cols + b * 32 + lane], lane,
+                     out.q + (size_t)v * cols + b * 32, out.d + (size_t)v * nb + b,
+                     out.fs + (size_t)v * nb + b);
+}
+
+// ------------------------------------------------------------------ Gated DeltaNet layer
+// pf_linear_attn (engine/src/forward_lin.c:322-361) after its four projections, which the
+// W_in matvec already wrote to y[t][0..ldy): qkv | z | b | a.
+//  1. pending conv commit of the last verify pass (pf_lin_commit, :413-432), then causal
+//     depthwise conv + SiLU per channel and token (pre_task :264-286, pf_conv_silu
+//     forward_ops.c:237-260); a logged pass shifts the live state by token 0 only and records
+//     the raw inputs of rows 1..;
+//  2. L2 norm of q and k per head (pf_l2norm_scale, forward_ops.c:202-210), q scaled by
+//     1/sqrt(dk);
+//  3. gates: beta = 1 / (1 + expf(-b)), decay = expf(A * softplus(a + dt_bias)) with glibc's
+//     expf / log1pf values (:19, :288-293);
+//  4. the recurrence (delta_rule / pf_lin_rule / replay_first: matvec_ref.c:114-188,
+//     kern_lin.c:42-62): first the deferred updates of the last commit, then per token
+//     S *= decay; kv = S^T k; delta = (v - kv) beta; S += k delta^T; o = S^T q, no fused
+//     multiply-add, sums over the key index in order; token 0 in place, rows 1.. of a logged
+//     pass on the register copy with k | delta | decay logged;
+//  5. gated RMSNorm rmsnorm(o) * w * silu(z) (post_task :298-309);
+//  6. A8 quantisation of the result for out_proj.
+// One CTA per key head (rep value heads of 128 columns each); thread (r, j) keeps column j of
+// value head r's 128 x 128 state in registers.
+constexpr int kDK = 128, kDV = 128;
+
+struct DnSmem {   // carved from dynamic shared memory
+    float *cq, *ck, *cv, *so;  // [nmax][dk], [nmax][dk], [nmax][rep*dv], [nmax][rep*dv]
+    float *beta, *decay;       // [nmax][rep]
+    float *kp;                 // [rep][dk] replay staging
+    float *pdec;               // [rep]
+    float *rn;                 // [nmax][rep] gated-norm factors
+};
+
+__global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, LibmTables T,
+                                                  const float *y, Step *st, Act out) {
+    const int n = st->n;
+    if (n <= 0) return;
+    const int logged = st->logged, pend_keep = st->pend_keep, pend_conv = st->pend_conv;
+    const int wr = st->wr;
+    const int kh = blockIdx.x, rep = d.rep, tid = threadIdx.x, nthr = blockDim.x;
+    extern __shared__ __align__(16) float dsm[];
+    DnSmem s;
+    s.cq = dsm;
+    s.ck = s.cq + kMaxRows * kDK;
+    s.cv = s.ck + kMaxRows * kDK;
+    s.so = s.cv + kMaxRows * rep * kDV;
+    s.beta = s.so + kMaxRows * rep * kDV;
+    s.decay = s.beta + kMaxRows * rep;
+    s.kp = s.decay + kMaxRows * rep;
+    s.pdec = s.kp + kDK;
+    s.rn = s.pdec + 4;
+    const int C = d.C, K = d.K, S = K - 1;
+
+    // ---- 1. conv + SiLU
+    const int nch = 2 * kDK + rep * kDV;
+    for (int ch = tid; ch < nch; ch += nthr) {
+        int c;
+        float *dst;
+        int dstride;
+        if (ch < kDK) { c = kh * kDK + ch; dst = s.cq + ch; dstride = kDK; }
+        else if (ch < 2 * kDK) { c = d.kd + kh * kDK + (ch - kDK); dst = s.ck + (ch - kDK); dstride = kDK; }
+        else {
+            const int vv = ch - 2 * kDK;
+            c = 2 * d.kd + kh * rep * kDV + vv;
+            dst = s.cv + vv;
+            dstride = rep * kDV;
+        }
+        float stt[8], wc[8], live[8];
+        for (int j = 0; j < S; j++) stt[j] = L.conv_state[(size_t)j * C + c];
+        for (int j = 0; j < K; j++) wc[j] = L.conv_w[(size_t)c * K + j];
+        if (pend_conv > 1) {   // new state = last S rows of [state after token 0, inputs 1..e-1]
+            const int e1 = pend_conv - 1;
+            float ns[8];
+            for (int j = 0; j < S; j++) {
+                const int src = j + e1;
+                ns[j] = src < S ? stt[src] : L.xin[(size_t)(src - S + 1) * C + c];
+            }
+            for (int j = 0; j < S; j++) stt[j] = ns[j];
+        }
+        for (int t = 0; t < n; t++) {
+            const float xc = y[(size_t)t * d.ldy + c];
+            float acc = __fmul_rn(wc[0], S > 0 ? stt[0] : xc);
+            for (int j = 1; j < K; j++) acc = madd(acc, wc[j], j < S ? stt[j] : xc);
+            for (int j = 0; j + 1 < S; j++) stt[j] = stt[j + 1];
+            if (S > 0) stt[S - 1] = xc;
+            dst[t * dstride] = pf_silu(acc);
+            if (logged) {
+                if (t == 0) for (int j = 0; j < S; j++) live[j] = stt[j];
+                else L.xin[(size_t)t * C + c] = xc;
+            }
+        }
+        const float *fin = logged ? live : stt;
+        for (int j = 0; j < S; j++) L.conv_state[(size_t)j * C + c] = fin[j];
+    }
+    __syncthreads();
+
+    // ---- 2. L2 norm of q and k, 4 lanes per (token, vector)
+    {
+        const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
+        const float qscale = inv_sqrt_ref((float)kDK);
+        for (int u0 = warp * 8; u0 < 2 * n; u0 += nw * 8) {
+            const int u = u0 + (lane >> 2), l = lane & 3;
+            const bool act = u < 2 * n;
+            float *vec = act ? ((u & 1) ? s.ck : s.cq) + (u >> 1) * kDK : s.cq;
+            float c = 0.0f;
+            if (act)
+                for (int i = l; i < kDK; i += 4) c = madd(c, vec[i], vec[i]);
+            const int base = lane & ~3;
+            const float c0 = __shfl_sync(0xffffffffu, c, base), c1 = __shfl_sync(0xffffffffu, c, base + 1);
+            const float c2 = __shfl_sync(0xffffffffu, c, base + 2), c3 = __shfl_sync(0xffffffffu, c, base + 3);
+            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+            const float r = inv_sqrt_ref(__fadd_rn(ss, 1e-6f));
+            __syncwarp();
+            if (act) {
+                const float sc = (u & 1) ? 1.0f : qscale;
+                for (int i = l; i < kDK; i += 4) vec[i] = __fmul_rn(__fmul_rn(vec[i], r), sc);
+            }
+        }
+    }
+    // ---- 3. gates
+    for (int u = tid; u < n * rep; u += nthr) {
+        const int t = u / rep, r = u % rep, h = kh * rep + r;
+        const float b = y[(size_t)t * d.ldy + C + d.vd + h];
+        const float a = y[(size_t)t * d.ldy + C + d.vd + d.nv + h];
+        s.beta[t * rep + r] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(T, -b)));
+        const float xs = __fadd_rn(a, L.dt_bias[h]);
+        const float sp = xs > 20.0f ? xs : glibc_log1pf(T, glibc_expf(T, xs));
+        s.decay[t * rep + r] = glibc_expf(T, __fmul_rn(L.A[h], sp));
+    }
+    __syncthreads();
+
+    // ---- 4. recurrence, value heads of this key head one after another
+    const size_t logw = (size_t)kDK + kDV + 1;
+    const int j = tid;
+    for (int r = 0; r < rep; r++) {
+        const int h = kh * rep + r;
+        float Sc[kDK];
+        float *rec = L.rec + (size_t)h * kDK * kDV + j;
+#pragma unroll
+        for (int i = 0; i < kDK; i++) Sc[i] = rec[(size_t)i * kDV];
+        for (int tp = 1; tp <= pend_keep; tp++) {   // deferred commit: rows 1..keep of half wr^1
+            const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp) * d.nv + h) * logw;
+            __syncthreads();
+            s.kp[j] = u[j];
+            if (j == 0) s.pdec[0] = u[kDK + kDV];
+            __syncthreads();
+            const float dl = u[kDK + j], pd = s.pdec[0];
+#pragma unroll
+            for (int i = 0; i < kDK; i++)
+                Sc[i] = __fadd_rn(__fmul_rn(Sc[i], pd), __fmul_rn(s.kp[i], dl));
+        }
+        for (int t = 0; t < n; t++) {
+            const float *qt = s.cq + t * kDK, *kt = s.ck + t * kDK;
+            const float dec = s.decay[t * rep + r], beta = s.beta[t * rep + r];
+            float kv = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kDK; i++) {
+                Sc[i] = __fmul_rn(Sc[i], dec);
+                kv = madd(kv, Sc[i], kt[i]);
+            }
+            const float delta = __fmul_rn(__fadd_rn(s.cv[t * rep * kDV + r * kDV + j], -kv), beta);
+            float o = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kDK; i++) {
+                Sc[i] = __fadd_rn(Sc[i], __fmul_rn(kt[i], delta));
+                o = madd(o, Sc[i], qt[i]);
+            }
+            s.so[t * rep * kDV + r * kDV + j] = o;
+            if (logged) {
+                if (t == 0) {
+#pragma unroll
+                    for (int i = 0; i < kDK; i++) rec[(size_t)i * kDV] = Sc[i];
+                } else {
+                    float *u = L.upd + (((size_t)wr * d.cap + t) * d.nv + h) * logw;
+                    u[kDK + j] = delta;
+                    u[j] = kt[j];
+                    if (j == 0) u[kDK + kDV] = dec;
+                }
+            }
+        }
+        if (!logged) {
+#pragma unroll
+            for (int i = 0; i < kDK; i++) rec[(size_t)i * kDV] = Sc[i];
+        }
+    }
+    __syncthreads();
+
+    // ---- 5. gated RMSNorm: per (token, head) r = 1 / sqrtf(sumsq(o) / dv + eps), 4 chains
+    {
+        const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
+        for (int u0 = warp * 8; u0 < n * rep; u0 += nw * 8) {
+            const int u = u0 + (lane >> 2), l = lane & 3;
+            const bool act = u < n * rep;
+            const float *vec = act ? s.so + (size_t)(u / rep) * rep * kDV + (u % rep) * kDV : s.so;
+            float c = 0.0f;
+            if (act)
+                for (int i = l; i < kDV; i += 4) c = madd(c, vec[i], vec[i]);
+            const int base = lane & ~3;
+            const float c0 = __shfl_sync(0xffffffffu, c, base), c1 = __shfl_sync(0xffffffffu, c, base + 1);
+            const float c2 = __shfl_sync(0xffffffffu, c, base + 2), c3 = __shfl_sync(0xffffffffu, c, base + 3);
+            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+            if (act && l == 0) s.rn[u] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)kDV), d.eps));
+        }
+    }
+    __syncthreads();
+    // ---- 6. y = (o * r) * w * silu(z), A8 per 32 columns
+    {
+        const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
+        const int nblk = n * rep * (kDV / 32);
+        const int nbo = out.cols >> 5;
+        for (int b = warp; b < nblk; b += nw) {
+            const int t = b / (rep * (kDV / 32)), rem = b % (rep * (kDV / 32));
+            const int rr = rem / (kDV / 32), cb = rem % (kDV / 32);
+            const int jj = cb * 32 + lane, hh = kh * rep + rr;
+            const float rn = s.rn[t * rep + rr];
+            float v = __fmul_rn(__fmul_rn(s.so[t * rep * kDV + rr * kDV + jj], rn), L.norm_w[jj]);
+            const float z = y[(size_t)t * d.ldy + C + hh * kDV + jj];
+            v = __fmul_rn(v, pf_silu(z));
+            const int col = hh * kDV + jj;
+            quant_block_warp(v, lane, out.q + (size_t)t * out.cols + (col & ~31),
+                             out.d + (size_t)t * nbo + (col >> 5), out.fs + (size_t)t * nbo + (col >> 5));
+        }
+    }
+}
+
+// Apply every deferred commit now (pf_lin_flush, engine/src/forward_lin.c:435-444, and the
+// conv half of pf_lin_commit): grid (key heads, linear layers).
+struct FlushArgs {
+    LinLayer layers[kMaxLayers];
+};
+
+__global__ void k_flush(FlushArgs fa, LinDims d, const Step *st) {
+    const int keep = st->pend_keep, pend_conv = st->pend_conv, wr = st->wr;
+    const LinLayer &L = fa.layers[blockIdx.y];
+    const int kh = blockIdx.x, rep = d.rep, tid = threadIdx.x, nthr = blockDim.x;
+    const int C = d.C, S = d.K - 1;
+    if (pend_conv > 1) {
+        const int nch = 2 * kDK + rep * kDV, e1 = pend_conv - 1;
+        for (int ch = tid; ch < nch; ch += nthr) {
+            int c;
+            if (ch < kDK) c = kh * kDK + ch;
+            else if (ch < 2 * kDK) c = d.kd + kh * kDK + (ch - kDK);
+            else c = 2 * d.kd + kh * rep * kDV + (ch - 2 * kDK);
+            float stt[8], ns[8];
+            for (int j = 0; j < S; j++) stt[j] = L.conv_state[(size_t)j * C + c];
+            for (int j = 0; j < S; j++) {
+                const int src = j + e1;
+                ns[j] = src < S ? stt[src] : L.xin[(size_t)(src - S + 1) * C + c];
+            }
+            for (int j = 0; j < S; j++) L.conv_state[(size_t)j * C + c] = ns[j];
+        }
+    }
+    if (keep > 0) {
+        const int j = tid;
+        const size_t logw = (size_t)kDK + kDV + 1;
+        for (int r = 0; r < rep; r++) {
+            const int h = kh * rep + r;
+            float *rec = L.rec + (size_t)h * kDK * kDV + j;
+            for (int tp = 1; tp <= keep; tp++) {
+                const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp) * d.nv + h) * logw;
+                const float pd = u[kDK + kDV], dl = u[kDK + j];
+                for (int i = 0; i < kDK; i++)   // pf_lin_apply: row *= decay; row += k_i * delta_j
+                    rec[(size_t)i * kDV] = __fadd_rn(__fmul_rn(rec[(size_t)i * kDV], pd), __fmul_rn(u[i], dl));
+            }
+        }
+    }
+}
+
+// End of a pass: its deferred commit has been consumed by every layer.
+__global__ void k_pass_end(Step *st) {
+    if (st->n <= 0) return;   // no pass ran (generation finished): the commit is still owed
+    st->pend_keep = 0;
+    st->pend_conv = 0;
+}
+
+__global__ void k_clear_pending(Step *st) {
+    st->pend_keep = 0;
+    st->pend_conv = 0;
+}
+
+// Host-chosen pass (prefill chunks, plain eval): shape and tokens by value.
+struct PassArgs {
+    int n, pos0, logged;
+    int tokens[kMaxRows];
+};
+__global__ void k_set_pass(Step *st, PassArgs a) {
+    st->n = a.n;
+    st->pos0 = a.pos0;
+    st->logged = a.logged;
+    for (int i = 0; i < a.n && i < kMaxRows; i++) st->tokens[i] = a.tokens[i];
+}
+
+// Generation parameters before k_gen_start.
+__global__ void k_set_gen(Step *st, GenArgs g) {
+    st->n_max = g.n_max;
+    st->k = g.k;
+    st->eos = g.eos;
+    st->n_stop = g.n_stop;
+    for (int i = 0; i < 8; i++) st->stop_ids[i] = g.stop_ids[i];
+    st->max_ctx = g.max_ctx;
+    st->vocab = g.vocab;
+    st->p24 = g.p24;
+    st->seed = g.seed;
+    st->rounds = st->drafted = st->accepted = 0;
+    st->count = 0;
+    st->done = 0;
+    st->status = 0;
+}
+
+// ------------------------------------------------------------------ attention
+// pf_full_attn (engine/src/forward_attn.c:231-266), first part: per token, the K row of each
+// KV head (RMSNorm with k_norm, RoPE, stored at position pos0 + t), its V row, and every query
+// head (RMSNorm with q_norm, RoPE). RoPE tables come from the host, computed with glibc
+// exactly as pf_rope_tables does (forward.c:19-32). grid (rows, nq + nkv), hd threads.
+__global__ void k_attn_prep(AttnLayer L, AttnDims d, const float *y, float *qbuf,
+                            const Step *st) {
+    const int t = blockIdx.x;
+    if (t >= st->n) return;
+    const int idx = blockIdx.y, hd = d.hd, tid = threadIdx.x;
+    const int pos = st->pos0 + t;
+    if (pos >= d.max_ctx) return;
+    extern __shared__ float xa[];
+    __shared__ float rr;
+    const float *src;
+    const float *w;
+    if (idx < d.nq) { src = y + (size_t)t * d.ldy + (size_t)2 * hd * idx; w = L.q_norm; }
+    else { src = y + (size_t)t * d.ldy + (size_t)2 * hd * d.nq + (size_t)(idx - d.nq) * hd; w = L.k_norm; }
+    xa[tid] = src[tid];
+    __syncthreads();
+    if (tid < 32) {
+        const float sq = sumsq_ref(xa, hd);
+        if (tid == 0) rr = inv_sqrt_ref(__fadd_rn(__fdiv_rn(sq, (float)hd), d.eps));
+    }
+    __syncthreads();
+    float v = __fmul_rn(__fmul_rn(xa[tid], rr), w[tid]);
+    __syncthreads();
+    xa[tid] = v;
+    __syncthreads();
+    const int h2 = d.rot >> 1;
+    if (tid < h2) {   // pf_rope (forward_ops.c:149-165): pairs (i, i + rot/2)
+        const float c = d.rope_cos[(size_t)pos * h2 + tid], sn = d.rope_sin[(size_t)pos * h2 + tid];
+        const float a = xa[tid], b = xa[tid + h2];
+        v = __fadd_rn(__fmul_rn(a, c), -__fmul_rn(b, sn));
+    } else if (tid < 2 * h2) {
+        const int i = tid - h2;
+        const float c = d.rope_cos[(size_t)pos * h2 + i], sn = d.rope_sin[(size_t)pos * h2 + i];
+        const float a = xa[i], b = xa[tid];
+        v = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sn));
+    }
+    if (idx < d.nq) {
+        qbuf[((size_t)t * d.nq + idx) * hd + tid] = v;
+    } else {
+        const int g = idx - d.nq;
+        L.kc[((size_t)g * d.max_ctx + pos) * hd + tid] = v;
+        L.vc[((size_t)g * d.max_ctx + pos) * hd + tid] =
+            y[(size_t)t * d.ldy + (size_t)2 * hd * d.nq + (size_t)d.nkv * hd + (size_t)g * hd + tid];
+    }
+}
+
+// Second part (attend / score_task / softmax_task / pv_task, forward_attn.c:95-229): per
+// (token, query head): scores pf_dot(q, K row) * (1/sqrt(hd)) with pf_dot's 16-lane order
+// (forward_ops.c:265-287), softmax max, pf_expf(a - max) and the 4-lane sum
+// (forward_ops.c:320-353), p = a * (1 / sum), P.V accumulated in row order from zero,
+// o *= sigmoid(gate), then A8 blocks of 32 for o_proj. grid (rows, nq), hd threads,
+// dynamic shared memory: q [hd] + att [max_ctx].
+__global__ void k_attn(AttnLayer L, AttnDims d, const float *y, const float *qbuf,
+                       const Step *st, Act out) {
+    const int t = blockIdx.x;
+    if (t >= st->n) return;
+    const int h = blockIdx.y, hd = d.hd, tid = threadIdx.x;
+    const int g = h / (d.nq / d.nkv);
+    const int pos = st->pos0 + t;
+    if (pos >= d.max_ctx) return;
+    const int np = pos + 1;
+    extern __shared__ float sm[];
+    float *q = sm, *att = sm + hd;
+    __shared__ float red[32];
+    __shared__ float s_mx, s_inv;
+    q[tid] = qbuf[((size_t)t * d.nq + h) * hd + tid];
+    __syncthreads();
+    const float scale = inv_sqrt_ref((float)hd);
+    const int lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const float *K = L.kc + (size_t)g * d.max_ctx * hd;
+    for (int p0 = warp * 2; p0 < np; p0 += nw * 2) {
+        const int p = p0 + (lane >> 4), l = lane & 15;
+        float c = 0.0f;
+        if (p < np) {
+            const float *kr = K + (size_t)p * hd;
+            for (int i = l; i < hd; i += 16) c = madd(c, q[i], kr[i]);
+        }
+        c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 1));
+        c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 2));
+        c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 4));
+        c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 8));
+        if (l == 0 && p < np) att[p] = __fmul_rn(__fadd_rn(c, 0.0f), scale);
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (int p = tid; p < np; p += blockDim.x) m = fmaxf(m, att[p]);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid < 32) {
+        float mm = tid < nw ? red[tid] : -INFINITY;
+        for (int o = 16; o; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        if (tid == 0) s_mx = mm;
+    }
+    __syncthreads();
+    const float mx = s_mx;
+    for (int p = tid; p < np; p += blockDim.x) att[p] = pf_expf(__fadd_rn(att[p], -mx));
+    __syncthreads();
+    if (tid < 32) {
+        const float sum = sum4_ref(att, np);
+        if (tid == 0) s_inv = __fdiv_rn(1.0f, sum);
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    for (int p = tid; p < np; p += blockDim.x) att[p] = __fmul_rn(att[p], inv);
+    __syncthreads();
+    const float *V = L.vc + (size_t)g * d.max_ctx * hd + tid;
+    float o = 0.0f;
+    int jj = 0;
+    for (; jj + 8 <= np; jj += 8) {
+        float vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) vv[u] = V[(size_t)(jj + u) * hd];
+#pragma unroll
+        for (int u = 0; u < 8; u++) o = madd(o, att[jj + u], vv[u]);
+    }
+    for (; jj < np; jj++) o = madd(o, att[jj], V[(size_t)jj * hd]);
+    const float gate = y[(size_t)t * d.ldy + (size_t)2 * hd * h + hd + tid];
+    o = __fmul_rn(o, pf_sigmoid(gate));
+    const int col = h * hd + tid, nbo = out.cols >> 5;
+    quant_block_warp(o, lane, out.q + (size_t)t * out.cols + (col & ~31),
+                     out.d + (size_t)t * nbo + (col >> 5), out.fs + (size_t)t * nbo + (col >> 5));
+}
+
+
+// ------------------------------------------------------------------ generation control
+// splitmix64 output function and the synthetic drafter of the benchmark: the draft for output
+// index j is, with probability p24 / 2^24, the target's greedy token greedy[j], else a uniform
+// token (the same function as the CPU harness, oracle/ref_spec.c).
+__device__ __forceinline__ unsigned long long mix64(unsigned long long x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+__device__ __forceinline__ int synth_draft(unsigned long long seed, long long j, unsigned p24,
+                                           int vocab, int greedy_j) {
+    const unsigned long long h = mix64(seed ^ mix64((unsigned long long)j));
+    if ((unsigned)(h >> 40) < p24) return greedy_j;
+    return (int)(mix64(h) % (unsigned long long)vocab);
+}
+
+// One emitted token (spec.c emit, engine/src/spec.c:206-215): returns 1 when generation stops.
+__device__ __forceinline__ int emit_tok(Step *st, int *out, int tok) {
+    out[st->count++] = tok;
+    int stop = st->count >= st->n_max;
+    if (tok == st->eos) stop = 1;
+    for (int i = 0; i < st->n_stop && !stop; i++) stop = tok == st->stop_ids[i];
+    return stop;
+}
+
+// Shape of the next round (spec.c:285-293): never draft past n_max or the context.
+__device__ void prepare_round(Step *st, const int *greedy) {
+    int left = st->n_max - st->count - 1;
+    const int room = st->max_ctx - st->pos0 - 1;
+    if (left > room) left = room;
+    if (left < 0) {
+        st->status = -5;   // PINFER_E_CTX_FULL
+        st->done = 1;
+        st->n = 0;
+        return;
+    }
+    const int ke = st->k < left ? st->k : left;
+    st->tokens[0] = st->cur;
+    for (int s = 1; s <= ke; s++) {
+        const long long j = st->count - 1 + s;
+        st->tokens[s] = synth_draft(st->seed, j, st->p24, st->vocab, greedy ? greedy[j] : 0);
+    }
+    st->n = ke + 1;
+    st->logged = 1;
+}
+
+// After the prefill pass: the first token is the argmax of the prompt's last row.
+__global__ void k_gen_start(Step *st, const int *greedy, int *out) {
+    if (threadIdx.x != 0) return;
+    const int n = st->n;
+    st->cur = st->argmax[n - 1];
+    st->pos0 += n;
+    st->count = 0;
+    st->done = 0;
+    st->status = 0;
+    if (emit_tok(st, out, st->cur)) {
+        st->done = 1;
+        st->n = 0;
+        return;
+    }
+    prepare_round(st, greedy);
+}
+
+// Greedy acceptance and commit of one verify pass (spec.c:337-351): the longest draft prefix
+// that equals the model's argmax, plus the model's own next token; the e emitted tokens are
+// committed (recurrent updates deferred, conv shifted at the next pass) and n_past advances
+// by e (stale KV rows above it are overwritten later).
+__global__ void k_accept(Step *st, const int *greedy, int *out) {
+    if (threadIdx.x != 0) return;
+    const int n = st->n;
+    if (n <= 0) return;
+    const int ke = n - 1;
+    int vt[kMaxRows + 1];
+    for (int i = 0; i < n; i++) vt[i] = st->tokens[i];
+    int a = 0, g = st->argmax[0];
+    while (a < ke && vt[a + 1] == g) {
+        a++;
+        g = st->argmax[a];
+    }
+    vt[a + 1] = g;
+    int e = 0, done = 0;
+    while (e <= a && !done) done = emit_tok(st, out, vt[++e]);
+    st->pend_keep = e - 1;   // pf_lin_commit (forward_lin.c:413-432)
+    st->pend_conv = e;
+    st->wr ^= 1;
+    st->pos0 += e;
+    st->cur = vt[e];
+    st->rounds++;
+    st->drafted += ke;
+    st->accepted += a;
+    if (done) {
+        st->done = 1;
+        st->n = 0;
+        return;
+    }
+    prepare_round(st, greedy);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ launchers
+namespace {
+template <int NMAX>
+size_t mv_smem() { return sizeof(MvSmem<NMAX>); }
+
+int mv_grid(const Mat &W) {
+    return W.npanels;   // one panel per CTA
+}
+
+template <int NMAX>
+void matvec_t(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode, cudaStream_t s) {
+    const size_t sm = mv_smem<NMAX>();
+    if (mode == 0) {
+        k_matvec<NMAX, 0><<<mv_grid(W), kMvThreads, sm, s>>>(W, in, st, y, ldy);
+    } else {
+        k_matvec<NMAX, 1><<<mv_grid(W), kMvThreads, sm, s>>>(W, in, st, y, ldy);
+    }
+}
+template <int NMAX>
+void swiglu_t(const Mat &G, const Mat &U, Act in, const Step *st, Act out, cudaStream_t s) {
+    const size_t sm = mv_smem<NMAX>();
+    k_matvec_swiglu<NMAX><<<mv_grid(G), kMvThreads, sm, s>>>(G, U, in, st, out);
+}
+template <int NMAX>
+void head_t(const Mat &W, Act in, const Step *st, float *logits, int ld, unsigned long long *partial,
+            int *nan0, cudaStream_t s) {
+    const size_t sm = mv_smem<NMAX>();
+    k_matvec_head<NMAX><<<mv_grid(W), kMvThreads, sm, s>>>(W, in, st, logits, ld, partial, nan0);
+}
+}  // namespace
+
+void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode, int nmax,
+                   cudaStream_t s) {
+    if (nmax <= 1) matvec_t<1>(W, in, st, y, ldy, mode, s);
+    else if (nmax <= 4) matvec_t<4>(W, in, st, y, ldy, mode, s);
+    else if (nmax <= 8) matvec_t<8>(W, in, st, y, ldy, mode, s);
+    else matvec_t<16>(W, in, st, y, ldy, mode, s);
+}
+void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Act out, int nmax,
+                          cudaStream_t s) {
+    if (nmax <= 1) swiglu_t<1>(G, U, in, st, out, s);
+    else if (nmax <= 4) swiglu_t<4>(G, U, in, st, out, s);
+    else if (nmax <= 8) swiglu_t<8>(G, U, in, st, out, s);
+    else swiglu_t<16>(G, U, in, st, out, s);
+}
+void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int ld,
+                        unsigned long long *partial, int *nan0, int nmax, cudaStream_t s) {
+    if (nmax <= 1) head_t<1>(W, in, st, logits, ld, partial, nan0, s);
+    else if (nmax <= 4) head_t<4>(W, in, st, logits, ld, partial, nan0, s);
+    else if (nmax <= 8) head_t<8>(W, in, st, logits, ld, partial, nan0, s);
+    else head_t<16>(W, in, st, logits, ld, partial, nan0, s);
+}
+void launch_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
+                         Step *st, cudaStream_t s) {
+    k_argmax_final<<<kMaxRows, 256, 0, s>>>(partial, nan0, npanels, st);
+}
+void launch_embed(const Mat &E, const Step *st, float *x, int H, cudaStream_t s) {
+    k_embed<<<kMaxRows, 256, 0, s>>>(E, st, x, H);
+}
+void launch_norm_quant(const float *x, const float *w, int H, float eps, const Step *st, Act out,
+                       cudaStream_t s) {
+    k_norm_quant<<<kMaxRows, 256, (size_t)H * sizeof(float), s>>>(x, w, H, eps, st, out);
+}
+void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s) {
+    const int warps = n * (cols / 32);
+    k_quant_act<<<(warps * 32 + 255) / 256, 256, 0, s>>>(x, n, cols, out);
+}
+size_t deltanet_smem(int rep) {
+    return sizeof(float) * ((size_t)kMaxRows * kDK * 2 + (size_t)kMaxRows * rep * kDV * 2 +
+                            (size_t)kMaxRows * rep * 3 + (size_t)kDK + 8);
+}
+void launch_deltanet(const LinLayer &L, const LinDims &d, const LibmTables &T, const float *y,
+                     Step *st, Act out, cudaStream_t s) {
+    const size_t sm = deltanet_smem(d.rep);
+    k_deltanet<<<d.nk, kDV, sm, s>>>(L, d, T, y, st, out);
+}
+void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
+                      const Step *st, cudaStream_t s) {
+    k_attn_prep<<<dim3(kMaxRows, d.nq + d.nkv), d.hd, (size_t)d.hd * sizeof(float), s>>>(L, d, y, qbuf, st);
+}
+void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
+                 const Step *st, Act out, cudaStream_t s) {
+    const size_t sm = ((size_t)d.hd + d.max_ctx) * sizeof(float);
+    k_attn<<<dim3(kMaxRows, d.nq), d.hd, sm, s>>>(L, d, y, qbuf, st, out);
+}
+void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s) {
+    k_gen_start<<<1, 32, 0, s>>>(st, greedy, out);
+}
+void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s) {
+    k_accept<<<1, 32, 0, s>>>(st, greedy, out);
+}
+void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s) {
+    FlushArgs fa;
+    for (int i = 0; i < n_lin && i < kMaxLayers; i++) fa.layers[i] = layers[i];
+    if (n_lin > 0) k_flush<<<dim3(d.nk, n_lin), kDV, 0, s>>>(fa, d, st);
+    k_clear_pending<<<1, 1, 0, s>>>(st);
+}
+void launch_pass_end(Step *st, cudaStream_t s) { k_pass_end<<<1, 1, 0, s>>>(st); }
+void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s) {
+    PassArgs a;
+    a.n = n;
+    a.pos0 = pos0;
+    a.logged = logged;
+    for (int i = 0; i < kMaxRows; i++) a.tokens[i] = i < n ? tokens[i] : 0;
+    k_set_pass<<<1, 1, 0, s>>>(st, a);
+}
+void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s) { k_set_gen<<<1, 1, 0, s>>>(st, g); }
+void kernels_init(int max_ctx, int hd, int rep) {
+    // raise the dynamic shared memory limits once, outside any stream capture
+    cudaFuncSetAttribute(k_matvec<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<1>());
+    cudaFuncSetAttribute(k_matvec<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<1>());
+    cudaFuncSetAttribute(k_matvec<4, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
+    cudaFuncSetAttribute(k_matvec<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
+    cudaFuncSetAttribute(k_matvec<8, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
+    cudaFuncSetAttribute(k_matvec<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
+    cudaFuncSetAttribute(k_matvec<16, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
+    cudaFuncSetAttribute(k_matvec<16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
+    cudaFuncSetAttribute(k_matvec_swiglu<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<1>());
+    cudaFuncSetAttribute(k_matvec_swiglu<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
+    cudaFuncSetAttribute(k_matvec_swiglu<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
+    cudaFuncSetAttribute(k_matvec_swiglu<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
+    cudaFuncSetAttribute(k_matvec_head<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<1>());
+    cudaFuncSetAttribute(k_matvec_head<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
+    cudaFuncSetAttribute(k_matvec_head<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
+    cudaFuncSetAttribute(k_matvec_head<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
+    if (max_ctx <= 0) return;   // matvec kernels only (kernel-level ABI)
+    cudaFuncSetAttribute(k_deltanet, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)deltanet_smem(rep));
+    cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(((size_t)hd + max_ctx) * sizeof(float)));
+}
+
+}  // namespace nb

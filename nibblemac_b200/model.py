@@ -1,0 +1,155 @@
+"""Python view of a loaded model (the calls of the reference's pinfer.Model that touch the
+verify path, python/pinfer/model.py:33-120), over the ctypes table in _lib.py."""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from ._lib import (GenOpts, Lib, PINFER_OK, Params, SpecParams, SpecStats, load_library,
+                   _c_float_p, _c_int32_p)
+
+
+class PinferError(RuntimeError):
+    def __init__(self, code: int, what: str, detail: str = "") -> None:
+        super().__init__(f"{what} failed with {code}" + (f": {detail}" if detail else ""))
+        self.code = code
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+class Model:
+    """A context on the B200: ``Model(path).generate(prompt, 128)``."""
+
+    def __init__(self, path: str | os.PathLike, max_ctx: int = 4096, lib: Lib | None = None) -> None:
+        self.lib = lib or load_library()
+        p = self.lib.pinfer_default_params()
+        p.max_ctx = max_ctx
+        err = ctypes.c_int(0)
+        self.ctx = self.lib.pinfer_load(os.fspath(path).encode(), ctypes.byref(p), ctypes.byref(err))
+        if not self.ctx:
+            raise PinferError(err.value, "pinfer_load", self.lib.last_error())
+        self.n_vocab = self.lib.pinfer_n_vocab(self.ctx)
+        self.eos_id = self.lib.pinfer_eos_id(self.ctx)
+
+    def close(self) -> None:
+        if self.ctx:
+            self.lib.pinfer_free(self.ctx)
+            self.ctx = None
+
+    def __enter__(self) -> "Model":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def n_past(self) -> int:
+        return self.lib.pinfer_n_past(self.ctx)
+
+    def reset(self) -> None:
+        self.lib.pinfer_reset(self.ctx)
+
+    def eval(self, tokens, logits: bool = True) -> np.ndarray | None:
+        t = _i32(tokens)
+        out = np.empty(self.n_vocab, np.float32) if logits else None
+        rc = self.lib.pinfer_eval(self.ctx, t.ctypes.data_as(_c_int32_p), len(t),
+                                  out.ctypes.data_as(_c_float_p) if logits else None)
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_eval", self.lib.last_error())
+        return out
+
+    def forward_all(self, tokens) -> np.ndarray:
+        t = _i32(tokens)
+        out = np.empty((len(t), self.n_vocab), np.float32)
+        rc = self.lib.pinfer_b200_forward_all(self.ctx, t.ctypes.data_as(_c_int32_p), len(t),
+                                              out.ctypes.data_as(_c_float_p))
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_b200_forward_all", self.lib.last_error())
+        return out
+
+    def generate(self, prompt, n_max: int, k: int = 0, stop_ids=None, on_token=None,
+                 ) -> tuple[list[int], int]:
+        """pinfer_generate_greedy_ex: (tokens, status)."""
+        t = _i32(prompt)
+        out = np.zeros(n_max, np.int32)
+        sp = SpecParams(k, 0, 0, 0)
+        st = SpecStats()
+        status = ctypes.c_int(0)
+        opts = None
+        keep = []
+        if stop_ids is not None or on_token is not None:
+            ids = _i32(stop_ids or [])
+            keep.append(ids)
+            cb = ctypes.cast(None, type(GenOpts().on_token)) if on_token is None else \
+                type(GenOpts().on_token)(lambda tok, user: int(bool(on_token(int(tok)))))
+            keep.append(cb)
+            opts = GenOpts(ids.ctypes.data_as(_c_int32_p) if len(ids) else None, len(ids), cb, None)
+        n = self.lib.pinfer_generate_greedy_ex(self.ctx, t.ctypes.data_as(_c_int32_p), len(t),
+                                               out.ctypes.data_as(_c_int32_p), n_max,
+                                               ctypes.byref(sp), ctypes.byref(opts) if opts else None,
+                                               ctypes.byref(st), ctypes.byref(status))
+        if n < 0:
+            raise PinferError(n, "pinfer_generate_greedy_ex", self.lib.last_error())
+        return out[:n].tolist(), status.value
+
+    def generate_synthetic(self, prompt, n_max: int, k: int, greedy, seed: int, p: float
+                           ) -> tuple[list[int], SpecStats, int]:
+        """Speculative decoding with the synthetic drafter (pinfer_b200_generate_synthetic)."""
+        t = _i32(prompt)
+        g = _i32(greedy)
+        if len(g) < n_max:
+            raise ValueError("greedy stream shorter than n_max")
+        out = np.zeros(n_max, np.int32)
+        st = SpecStats()
+        status = ctypes.c_int(0)
+        n = self.lib.pinfer_b200_generate_synthetic(
+            self.ctx, t.ctypes.data_as(_c_int32_p), len(t), out.ctypes.data_as(_c_int32_p), n_max,
+            k, g.ctypes.data_as(_c_int32_p), seed, p, ctypes.byref(st), ctypes.byref(status))
+        if n < 0:
+            raise PinferError(n, "pinfer_b200_generate_synthetic", self.lib.last_error())
+        return out[:n].tolist(), st, status.value
+
+    def generate_synthetic_ex(self, prompt, n_max: int, k: int, greedy, seed: int, p: float,
+                              append: bool = False):
+        """(tokens, stats, status, decode_ms) with the device-timed decode loop."""
+        t = _i32(prompt)
+        g = _i32(greedy)
+        if len(g) < n_max:
+            raise ValueError("greedy stream shorter than n_max")
+        out = np.zeros(n_max, np.int32)
+        st = SpecStats()
+        status = ctypes.c_int(0)
+        ms = ctypes.c_float(0.0)
+        n = self.lib.pinfer_b200_generate_synthetic_ex(
+            self.ctx, t.ctypes.data_as(_c_int32_p), len(t), out.ctypes.data_as(_c_int32_p), n_max,
+            k, g.ctypes.data_as(_c_int32_p), seed, p, int(append), ctypes.byref(st),
+            ctypes.byref(status), ctypes.byref(ms))
+        if n < 0:
+            raise PinferError(n, "pinfer_b200_generate_synthetic_ex", self.lib.last_error())
+        return out[:n].tolist(), st, status.value, ms.value
+
+    def checkpoint(self) -> None:
+        rc = self.lib.pinfer_checkpoint(self.ctx)
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_checkpoint", self.lib.last_error())
+
+    def rewind(self) -> None:
+        rc = self.lib.pinfer_rewind(self.ctx)
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_rewind", self.lib.last_error())
+
+    def round_kernels(self, k: int) -> int:
+        return self.lib.pinfer_b200_round_kernels(self.ctx, k)
+
+    def stream(self) -> int:
+        return self.lib.pinfer_b200_stream(self.ctx) or 0

@@ -1,0 +1,111 @@
+"""Q4K x A8 matmul on the B200 through the kernel-level C ABI, bit-exact against the oracle.
+
+The oracle is pinned by the reference's recorded kbench hashes (test_oracle_golden.py), so a
+hash match here proves the device kernel bit-identical to the reference's NEON kernel on the
+same inputs: A8 quantisation, int32 block dots and the ordered fused block FMAs.
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GOLD = json.loads((Path(__file__).parent / "golden" / "kbench_yhash.json").read_text())
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch
+    assert torch.cuda.is_available()
+    return torch
+
+
+class Dev:
+    def __init__(self, lib, torch, rows, cols, nmax=16):
+        self.lib, self.t, self.rows, self.cols = lib, torch, rows, cols
+        self.h = lib.nb_mv_create(rows, cols, nmax)
+        assert self.h, lib.last_error()
+        self.stream = torch.cuda.current_stream().cuda_stream
+
+    def upload(self, w_pq: np.ndarray):
+        panels = np.zeros(self.lib.nb_q4k_panel_bytes(self.rows, self.cols), np.uint8)
+        assert self.lib.nb_q4k_repack(w_pq.ctypes.data, self.rows, self.cols, panels.ctypes.data) == 0
+        return self.t.from_numpy(panels).cuda()
+
+    def run(self, dW, x: np.ndarray) -> np.ndarray:
+        n = x.shape[0]
+        dX = self.t.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+        dY = self.t.zeros((n, self.rows), dtype=self.t.float32, device="cuda")
+        assert self.lib.nb_mv_set_n(self.h, n, self.stream) == 0
+        assert self.lib.nb_mv_run(self.h, dW.data_ptr(), dX.data_ptr(), dY.data_ptr(), self.stream) == 0
+        self.t.cuda.synchronize()
+        return dY.cpu().numpy()
+
+    def act(self, n):
+        q = self.t.zeros((n, self.cols), dtype=self.t.int8, device="cuda")
+        d = self.t.zeros((n, self.cols // 32), dtype=self.t.float32, device="cuda")
+        f = self.t.zeros((n, self.cols // 32), dtype=self.t.float32, device="cuda")
+        assert self.lib.nb_mv_get_act(self.h, q.data_ptr(), d.data_ptr(), f.data_ptr(), self.stream) == 0
+        self.t.cuda.synchronize()
+        return q.cpu().numpy(), d.cpu().numpy(), f.cpu().numpy()
+
+    def close(self):
+        self.lib.nb_mv_destroy(self.h)
+
+
+SHAPES = sorted({(c["shape"], c["rows"], c["cols"]) for c in GOLD["cases"]})
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: s[0])
+def test_kbench_yhash_on_device(lib, torch, q4k_oracle, shape):
+    name, rows, cols = shape
+    cases = [c for c in GOLD["cases"] if c["shape"] == name and c["n"] <= 16]
+    dev = Dev(lib, torch, rows, cols)
+    try:
+        dW = dev.upload(q4k_oracle.kb_matrix(rows, cols, GOLD["matrix_seed"]))
+        nmax = max(c["n"] for c in cases)
+        x = q4k_oracle.kb_vec(nmax * cols, GOLD["vec_seed"]).reshape(nmax, cols)
+        for c in cases:
+            y = dev.run(dW, x[: c["n"]])
+            assert f"{q4k_oracle.fnv1a(y):016x}" == c["yhash"], f"{name} n={c['n']}"
+    finally:
+        dev.close()
+
+
+@pytest.mark.parametrize("rows,cols,n", [(3584, 1024, 1), (3584, 1024, 2), (3584, 1024, 4),
+                                         (1024, 3584, 4), (8224, 1024, 3), (36, 256, 5),
+                                         (4, 2048, 16), (100, 768, 7)])
+def test_random_matrices_bit_exact(lib, torch, q4k_oracle, rows, cols, n):
+    from nibblemac_b200 import pq
+    rng = np.random.default_rng(rows * 7 + cols + n)
+    w = rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)
+    wq = np.frombuffer(pq.quantize_q4k(w), np.uint8)
+    x = rng.standard_normal((n, cols), dtype=np.float32)
+    x[0, :32] = 0.0                                 # an all-zero activation block
+    dev = Dev(lib, torch, rows, cols)
+    try:
+        y = dev.run(dev.upload(wq), x)
+        ref = q4k_oracle.matmul(wq, rows, cols, x)
+        assert np.array_equal(y.view(np.uint32), ref.view(np.uint32))
+        q, d, f = dev.act(n)
+        rq, rd, rf = q4k_oracle.quant_act(x, cols)
+        assert np.array_equal(q, rq) and np.array_equal(d.view(np.uint32), rd.view(np.uint32))
+        assert np.array_equal(f.view(np.uint32), rf.view(np.uint32))
+    finally:
+        dev.close()
+
+
+def test_rows_independent_of_batch(lib, torch, q4k_oracle):
+    """kbench.c:216-219 on the device: row v of an n-vector call == the 1-vector call."""
+    rows, cols = 3584, 1024
+    dev = Dev(lib, torch, rows, cols)
+    try:
+        dW = dev.upload(q4k_oracle.kb_matrix(rows, cols, 42))
+        x = q4k_oracle.kb_vec(9 * cols, 3).reshape(9, cols)
+        yb = dev.run(dW, x)
+        for v in range(9):
+            assert np.array_equal(yb[v].view(np.uint32), dev.run(dW, x[v:v + 1])[0].view(np.uint32))
+    finally:
+        dev.close()

@@ -1,0 +1,107 @@
+"""The whole verify path on the B200 against the reference engine (oracle/_ref, the reference's
+own C sources run on the host CPU): logits bit for bit, greedy tokens identical, and
+speculative decoding with the synthetic drafter identical to plain decoding with the same
+acceptance counts as the reference's own speculative loop."""
+import numpy as np
+import pytest
+
+from conftest import ref_available
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not ref_available(), reason="oracle/_ref not built")]
+
+
+@pytest.fixture(scope="module", params=["tiny", "small"])
+def pair(request, tiny_model, small_model):
+    from nibblemac_b200.model import Model
+    from oracle import RefEngine
+    path = tiny_model if request.param == "tiny" else small_model
+    dev = Model(path, max_ctx=512)
+    ref = RefEngine(path, max_ctx=512)
+    yield request.param, dev, ref
+    dev.close()
+    ref.close()
+
+
+def prompt(vocab, n, seed):
+    return np.random.default_rng(seed).integers(0, vocab, n).astype(np.int32)
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def test_logits_all_rows_bit_exact(pair):
+    name, dev, ref = pair
+    toks = prompt(dev.n_vocab, 40, 1)            # 40 rows: chunks of 16, 16, 8 on the device
+    dev.reset()
+    ref.reset()
+    got = dev.forward_all(toks)
+    want = ref.forward_all(toks)
+    bad = np.nonzero((bits(got) != bits(want)).any(axis=1))[0]
+    assert len(bad) == 0, f"{name}: rows {bad[:8]} differ; max |d| {np.abs(got - want).max()}"
+
+
+def test_eval_continues_exactly(pair):
+    """Two evals in a row (positions continue) and the last-token logits of each."""
+    name, dev, ref = pair
+    a, b = prompt(dev.n_vocab, 21, 2), prompt(dev.n_vocab, 5, 3)
+    dev.reset()
+    ref.reset()
+    assert np.array_equal(bits(dev.eval(a)), bits(ref.eval(a)))
+    assert np.array_equal(bits(dev.eval(b)), bits(ref.eval(b)))
+    assert dev.n_past == 26
+
+
+def test_plain_greedy_tokens_identical(pair):
+    name, dev, ref = pair
+    p = prompt(dev.n_vocab, 64, 4)
+    got, status = dev.generate(p, 48)
+    assert status == 0
+    assert got == ref.generate(p, 48)
+
+
+@pytest.mark.parametrize("p_acc", [0.0, 0.5, 0.8, 1.0])
+def test_synthetic_speculation_matches_plain_and_reference(pair, p_acc):
+    name, dev, ref = pair
+    p = prompt(dev.n_vocab, 64, 5)
+    n = 40
+    greedy, _ = dev.generate(p, n)
+    got, st, status = dev.generate_synthetic(p, n, 3, greedy, seed=11, p=p_acc)
+    assert status == 0 and got == greedy
+    ref_toks, ref_st = ref.spec_generate(p, n, 3, greedy, 11, p_acc)
+    assert ref_toks == greedy
+    assert [st.rounds, st.drafted, st.accepted] == ref_st
+    if p_acc == 1.0:
+        assert st.accepted == st.drafted
+
+
+def test_state_after_speculation_equals_plain(pair):
+    """After a speculative generation (deferred commits flushed) the next eval gives the same
+    logits as after a plain one: the rollback / replay left exact states."""
+    name, dev, ref = pair
+    p = prompt(dev.n_vocab, 30, 6)
+    greedy, _ = dev.generate(p, 20)
+    nxt = np.array([greedy[-1], 7, 9], np.int32)
+    plain_logits = dev.eval(nxt)
+    dev.generate_synthetic(p, 20, 3, greedy, seed=5, p=0.5)
+    assert np.array_equal(bits(dev.eval(nxt)), bits(plain_logits))
+
+
+def test_invalid_token_leaves_state(pair):
+    from nibblemac_b200.model import PinferError
+    name, dev, ref = pair
+    dev.reset()
+    dev.eval([1, 2, 3])
+    with pytest.raises(PinferError) as e:
+        dev.eval([1, dev.n_vocab])
+    assert e.value.code == -4 and dev.n_past == 3
+
+
+def test_context_full(pair):
+    from nibblemac_b200.model import PinferError
+    name, dev, ref = pair
+    dev.reset()
+    with pytest.raises(PinferError) as e:
+        dev.eval(np.zeros(513, np.int32))
+    assert e.value.code == -5 and dev.n_past == 0
