@@ -1,0 +1,371 @@
+"""Benchmark of the speculative verify path (BASELINE.json metric: greedy spec-decode tok/s/GPU
+at k = 3, and Q4K matvec HBM GB/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N ...
+
+Workload: the Qwen3.5-0.8B-shaped model, random init (std 0.02,
+norms 1), Q4K-quantised; a 512-token uniform-random context; 128 greedy tokens with draft
+depth k = 3 and the synthetic drafter at acceptance p = 0.8 (the sweep p in {0, 0.5, 0.8, 1}
+is reported beside it). A step is one generation of 128 tokens continuing the prefilled
+context (restored with pinfer_rewind before every step, outside the timed region).
+  value  tokens / device time of the verify / accept loop (CUDA events on the engine's stream;
+         weights, states and context already in HBM)
+  e2e    tokens / wall time of the public API call (pinfer_b200_generate_synthetic_ex: prompt
+         and greedy stream copied in, 1-token prefill, decode, tokens copied out)
+Multi-GPU: one independent replica per GPU (replicas only, no collective on the data path),
+weak scaling; value = all tokens / max over ranks of the device time.
+--impl reference: the reference engine's own CPU path (oracle/_ref, scalar C) on the host
+cores, same metric, a bounded sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+K_DRAFT = 3
+N_GEN = 128
+CTX = 512
+P_MAIN = 0.8
+P_SWEEP = (0.0, 0.5, 0.8, 1.0)
+SEED_MODEL = 0
+METRIC = "greedy spec-decode tok/s/GPU (k=3) and Q4K matvec HBM GB/s vs ~8 TB/s peak"
+UNIT = "tok/s"
+
+
+def peaks() -> tuple[float, str]:
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, gpu: int) -> None:
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            try:
+                sm.append(float(r[0]))
+                mx = max(mx, float(r[1]))
+                for n, v in zip(names, r[3:7]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def model_path(rank: int, dist) -> Path:
+    from nibblemac_b200 import pq
+    path = ROOT / "_models" / f"bench-0.8b-s{SEED_MODEL}.pq"
+    if rank == 0 and not path.exists():
+        pq.make_synthetic(path, pq.QWEN35_08B, SEED_MODEL, std=0.02)
+    if dist is not None:
+        dist.barrier()
+    while not path.exists():
+        time.sleep(0.5)
+    return path
+
+
+def context_tokens(rank: int, vocab: int) -> np.ndarray:
+    return np.random.default_rng(1234 + rank).integers(0, vocab, CTX).astype(np.int32)
+
+
+def matvec_roofline(torch, lib, peak_gbs: float) -> dict:
+    """The dominant kernel, the Q4K x A8 matvec, timed alone with CUDA events on the stream it
+    runs on: the LM-head shape (248320 x 1024, n = 4 verify rows, 143 MB of weights, the
+    largest matrix of a round) over two weight copies (286 MB > L2, so every launch streams
+    from HBM), and the config-1 shape (3584 x 1024, n = 1, 2, 4) over a rotating arena of
+    copies larger than 2x L2."""
+    from oracle import Q4KOracle
+    orc = Q4KOracle()
+    s = torch.cuda.current_stream()
+    out = {}
+
+    def run(rows, cols, n, copies, iters):
+        w = orc.kb_matrix(rows, cols, 42)
+        panels = np.zeros(lib.nb_q4k_panel_bytes(rows, cols), np.uint8)
+        lib.nb_q4k_repack(w.ctypes.data, rows, cols, panels.ctypes.data)
+        dw = torch.from_numpy(panels).cuda()
+        arena = [dw] + [dw.clone() for _ in range(copies - 1)]
+        x = torch.from_numpy(orc.kb_vec(n * cols, 7).reshape(n, cols)).cuda()
+        y = torch.empty((n, rows), dtype=torch.float32, device="cuda")
+        h = lib.nb_mv_create(rows, cols, max(4, n))
+        lib.nb_mv_set_n(h, n, s.cuda_stream)
+        lib.nb_mv_quant(h, x.data_ptr(), s.cuda_stream)
+        for i in range(3 * copies if copies < 8 else copies):
+            lib.nb_mv_matmul(h, arena[i % copies].data_ptr(), y.data_ptr(), s.cuda_stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(s)
+        for i in range(iters):
+            lib.nb_mv_matmul(h, arena[i % copies].data_ptr(), y.data_ptr(), s.cuda_stream)
+        e1.record(s)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / iters
+        ref = orc.matmul(w, rows, cols, x.cpu().numpy())
+        exact = bool(np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32)))
+        lib.nb_mv_destroy(h)
+        wbytes = rows // 4 * (cols // 256) * 576
+        alg = wbytes + n * cols * 4 + n * rows * 4     # W + X (fp32 in) + Y (fp32 out)
+        del arena, dw
+        torch.cuda.empty_cache()
+        return us, alg, exact
+
+    us, alg, exact = run(248320, 1024, 4, 2, 20)
+    achieved = alg / (us * 1e-6) / 1e9
+    out["head"] = {"rows": 248320, "cols": 1024, "n": 4, "us": round(us, 2),
+                   "bytes": alg, "gbs": round(achieved, 1), "bit_exact": exact}
+    cfg1 = {}
+    for n in (1, 2, 4):
+        us1, alg1, ex1 = run(3584, 1024, n, 128, 256)
+        cfg1[str(n)] = {"us": round(us1, 2), "gbs": round(alg1 / (us1 * 1e-6) / 1e9, 1), "bit_exact": ex1}
+    out["config1_3584x1024"] = cfg1
+    out["_achieved"] = achieved
+    out["_peak"] = peak_gbs
+    return out
+
+
+def traffic_from_profiles() -> float | None:
+    """dram bytes per launch of the head-shaped matvec from the committed ncu summary."""
+    p = ROOT / "profiles" / "q4k_matvec_head_n4.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_baseline_sample(path: Path) -> dict:
+    """The reference's CPU path (oracle/_ref: the reference engine's own scalar C, one thread)
+    on a bounded sample of the same workload: 32-token context, 16 tokens, k = 3, p = 0.8;
+    tokens / seconds of the decode loop."""
+    from oracle import RefEngine
+    ref = RefEngine(path, max_ctx=256)
+    ctx = context_tokens(0, ref.n_vocab)[:32]
+    greedy = ref.generate(ctx, 16)
+    toks, st = ref.spec_generate(ctx, 16, K_DRAFT, greedy, 11, P_MAIN)
+    assert toks == greedy
+    sec = ref.last_decode_s
+    ref.close()
+    return {"value": round(len(toks) / sec, 3), "unit": UNIT, "cores": 1, "kind": "reference",
+            "sample": "reference engine (scalar C, oracle/_ref) on the 0.8B model: 32-token "
+                      "context, 16 tokens at k=3 p=0.8, decode loop timed"}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    from oracle import RefEngine
+    path = model_path(0, None)
+    ref = RefEngine(path, max_ctx=256)
+    ctx = context_tokens(0, ref.n_vocab)[:32]
+    n_gen = 12
+    greedy = ref.generate(ctx, n_gen)
+    secs, toks = [], 0
+    for i in range(args.warmup + args.steps):
+        out, st = ref.spec_generate(ctx, n_gen, K_DRAFT, greedy, 11 + i, P_MAIN)
+        assert out == greedy
+        if i >= args.warmup:
+            secs.append(ref.last_decode_s)
+            toks += len(out)
+    ref.close()
+    total = sum(secs)
+    value = toks / total
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total * 1000 / args.steps, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4k x int8 -> fp32", "data": "synthetic",
+            "config": {"workload": "configs[2] sample: 0.8B-shaped Q4K model, k=3, p=0.8, "
+                                   f"32-token context, {n_gen} tokens per step (CPU-bounded)",
+                       "parallelism": "single process"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": 1, "kind": "reference",
+                             "sample": f"reference engine scalar C, {n_gen} tokens per step"},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="setup, then exactly one generation inside cudaProfilerStart/Stop (for "
+                         "ncu --profile-from-start off); prints nothing else")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        sys.path.insert(0, str(ROOT / "oracle"))
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from nibblemac_b200._lib import load_library
+    from nibblemac_b200.model import Model
+    lib = load_library()
+    path = model_path(rank, dist)
+    m = Model(path, max_ctx=CTX + N_GEN + 16)
+    ctx = context_tokens(rank, m.n_vocab)
+    m.reset()
+    m.eval(ctx[:-1], logits=False)
+    m.checkpoint()
+    greedy, _, st0, _ = m.generate_synthetic_ex(ctx[-1:], N_GEN, 0, np.zeros(N_GEN, np.int32), 0, 0.0,
+                                                append=True)
+    assert st0 == 0 and len(greedy) == N_GEN
+    kernels_per_round = m.round_kernels(K_DRAFT)
+
+    def step(p: float, seed: int):
+        m.rewind()
+        t0 = time.perf_counter()
+        toks, st, status, ms = m.generate_synthetic_ex(ctx[-1:], N_GEN, K_DRAFT, greedy, seed, p,
+                                                       append=True)
+        wall = time.perf_counter() - t0
+        assert status == 0 and toks == greedy, "speculative output differs from plain greedy"
+        return ms, wall, st
+
+    if args.profile:
+        step(P_MAIN, 99)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        ms, wall, st = step(P_MAIN, 100)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"profile_step_ms": ms, "rounds": st.rounds,
+                          "kernels_per_round": kernels_per_round}), flush=True)
+        m.close()
+        return
+    for i in range(args.warmup):
+        step(P_MAIN, 100 + i)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    dev_ms, walls, rounds = [], [], 0
+    with Clocks(local) as clk:
+        for i in range(args.steps):
+            ms, wall, st = step(P_MAIN, 1000 + i)
+            dev_ms.append(ms)
+            walls.append(wall)
+            rounds += st.rounds
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    t_dev = sum(dev_ms) / 1000.0
+    t_wall = sum(walls)
+    if dist is not None:
+        tt = torch.tensor([t_dev, t_wall], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_dev, t_wall = tt.tolist()
+    tokens = N_GEN * args.steps * world
+    value = tokens / t_dev
+    e2e = tokens / t_wall
+
+    sweep = {}
+    for p in P_SWEEP:
+        ms, _, st = step(p, 77)
+        sweep[str(p)] = {"tok_s": round(N_GEN / (ms / 1000.0), 1),
+                         "tokens_per_round": round(N_GEN / st.rounds, 3)}
+
+    roof = None
+    extra = {}
+    if rank == 0:
+        peak, kind = peaks()
+        mv = matvec_roofline(torch, lib, peak)
+        roof = {"bound": "hbm", "achieved": round(mv["_achieved"], 1), "peak": peak, "unit": "GB/s",
+                "frac": round(mv["_achieved"] / peak, 4), "traffic": traffic_from_profiles(),
+                "peak_kind": kind,
+                "kernel": "q4k x a8 matvec, LM-head shape 248320x1024, n=4 (verify rows)"}
+        extra["matvec"] = {k: v for k, v in mv.items() if not k.startswith("_")}
+    m.close()
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(t_dev * 1000.0 / args.steps, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "q4k x int8 -> fp32",
+                "data": "synthetic (random-init 0.8B-shaped weights, uniform-random context, "
+                        "synthetic drafter)",
+                "config": {"workload": "configs[2]: Qwen3.5-0.8B-shaped Q4K, k=3 speculation, "
+                                       f"p={P_MAIN}, {CTX}-token context, {N_GEN} generated",
+                           "k": K_DRAFT, "p": P_MAIN, "context": CTX, "generated": N_GEN,
+                           "parallelism": f"replicas x{world}" if world > 1 else "single replica",
+                           "l2": "inputs larger than L2 (425 MB of weights streamed per round)"},
+                "e2e": {"value": round(e2e, 2), "unit": UNIT,
+                        "h2d_bytes_per_step": 4 * (1 + N_GEN), "d2h_bytes_per_step": 4 * N_GEN},
+                "gpu_launches": int(rounds * kernels_per_round * world),
+                "kernels_per_round": kernels_per_round, "rounds": rounds,
+                "sweep": sweep, "roofline": roof, "clocks": clk.summary()}
+        line.update(extra)
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample(path)
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

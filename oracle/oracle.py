@@ -152,10 +152,11 @@ class RefEngine:
         t = np.ascontiguousarray(prompt, np.int32)
         g = np.ascontiguousarray(greedy, np.int32)
         out = np.zeros(n_max, np.int32)
-        st = np.zeros(3, np.int64)
+        st = np.zeros(4, np.int64)
         p24 = min(1 << 24, int(np.floor(p * (1 << 24) + 0.5)))
         n = self.lib.ref_spec_generate(self.ctx, _ptr(t), len(t), _ptr(out), n_max, k, _ptr(g),
                                        seed, p24, _ptr(st))
         if n < 0:
             raise RuntimeError(f"reference spec generate: {n}")
-        return out[:n].tolist(), st.tolist()
+        self.last_decode_s = st[3] * 1e-9
+        return out[:n].tolist(), st[:3].tolist()

@@ -10,9 +10,11 @@
  *   end:     pf_lin_flush (spec.c:376)
  * The drafter is the pure function nb_synth_draft below (the device engine implements the same
  * function), so both sides draft the same tokens. */
+#define _POSIX_C_SOURCE 200809L
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "forward.h"
 #include "pinfer.h"
@@ -33,7 +35,14 @@ int32_t nb_synth_draft(uint64_t seed, int64_t j, uint32_t p24, int32_t vocab, in
     return (int32_t)(mix64(h) % (uint64_t)vocab);
 }
 
-/* stats (may be NULL): [0] rounds, [1] drafted, [2] accepted. greedy: the plain greedy
+static int64_t now_ns(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (int64_t)ts.tv_sec * 1000000000 + ts.tv_nsec;
+}
+
+/* stats (may be NULL): [0] rounds, [1] drafted, [2] accepted, [3] ns spent after the prompt
+ * (the decode loop, for the benchmark's CPU baseline). greedy: the plain greedy
  * output of the same prompt, n_max entries. Returns tokens written or a negative code. */
 int ref_spec_generate(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt, int32_t *out,
                       int n_max, int k, const int32_t *greedy, uint64_t seed, uint32_t p24,
@@ -55,6 +64,7 @@ int ref_spec_generate(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt, int3
     int count = 0;
     out[count++] = cur;
     const int batch = ctx->batch;
+    const int64_t t0 = now_ns();
     while (count < n_max) {
         const int P = ctx->n_past;
         int left = n_max - count - 1;
@@ -94,6 +104,7 @@ int ref_spec_generate(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt, int3
         if (stats) { stats[1] += ke; stats[2] += a; }
     }
     pf_lin_flush(ctx);
+    if (stats) stats[3] += now_ns() - t0;
     free(logits);
     return rc == PINFER_OK || count > 0 ? count : rc;
 }
