@@ -129,24 +129,35 @@ def matvec_roofline(torch, lib, peak_gbs: float) -> dict:
     s = torch.cuda.current_stream()
     out = {}
 
-    def run(rows, cols, n, copies, iters):
+    def run(rows, cols, n, copies, iters, head=False):
         w = orc.kb_matrix(rows, cols, 42)
-        panels = np.zeros(lib.nb_q4k_panel_bytes(rows, cols), np.uint8)
+        nbytes = lib.nb_q4k_panel_bytes(rows, cols)
+        panels = np.zeros(nbytes, np.uint8)
         lib.nb_q4k_repack(w.ctypes.data, rows, cols, panels.ctypes.data)
-        dw = torch.from_numpy(panels).cuda()
-        arena = [dw] + [dw.clone() for _ in range(copies - 1)]
+        stride = (nbytes + 255) // 256 * 256
+        arena = torch.empty(stride * copies, dtype=torch.uint8, device="cuda")
+        one = torch.from_numpy(panels).cuda()
+        for c in range(copies):
+            arena[c * stride:c * stride + nbytes].copy_(one)
         x = torch.from_numpy(orc.kb_vec(n * cols, 7).reshape(n, cols)).cuda()
         y = torch.empty((n, rows), dtype=torch.float32, device="cuda")
+        part = torch.empty((n, (rows + 31) // 32), dtype=torch.int64, device="cuda")
+        nan0 = torch.empty(16, dtype=torch.int32, device="cuda")
         h = lib.nb_mv_create(rows, cols, max(4, n))
         lib.nb_mv_set_n(h, n, s.cuda_stream)
         lib.nb_mv_quant(h, x.data_ptr(), s.cuda_stream)
-        for i in range(3 * copies if copies < 8 else copies):
-            lib.nb_mv_matmul(h, arena[i % copies].data_ptr(), y.data_ptr(), s.cuda_stream)
+
+        def launch(k):
+            if head:
+                return lib.nb_mv_head_repeat(h, arena.data_ptr(), stride, copies, y.data_ptr(), k,
+                                             part.data_ptr(), nan0.data_ptr(), s.cuda_stream)
+            return lib.nb_mv_matmul_repeat(h, arena.data_ptr(), stride, copies, y.data_ptr(), k, s.cuda_stream)
+
+        assert launch(max(copies, 3)) == 0
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(s)
-        for i in range(iters):
-            lib.nb_mv_matmul(h, arena[i % copies].data_ptr(), y.data_ptr(), s.cuda_stream)
+        assert launch(iters) == 0
         e1.record(s)
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1000.0 / iters
@@ -155,11 +166,11 @@ def matvec_roofline(torch, lib, peak_gbs: float) -> dict:
         lib.nb_mv_destroy(h)
         wbytes = rows // 4 * (cols // 256) * 576
         alg = wbytes + n * cols * 4 + n * rows * 4     # W + X (fp32 in) + Y (fp32 out)
-        del arena, dw
+        del arena, one
         torch.cuda.empty_cache()
         return us, alg, exact
 
-    us, alg, exact = run(248320, 1024, 4, 2, 20)
+    us, alg, exact = run(248320, 1024, 4, 2, 20, head=True)
     achieved = alg / (us * 1e-6) / 1e9
     out["head"] = {"rows": 248320, "cols": 1024, "n": 4, "us": round(us, 2),
                    "bytes": alg, "gbs": round(achieved, 1), "bit_exact": exact}

@@ -70,6 +70,14 @@ int nb_mv_set_n(nb_mv *h, int n, void *stream);
 int nb_mv_quant(nb_mv *h, const float *X, void *stream);
 /* Y [n][rows] = W (device panel layout) x scratch activations. */
 int nb_mv_matmul(nb_mv *h, const void *W, float *Y, void *stream);
+/* `iters` back-to-back nb_mv_matmul launches, launch i reading weights at W + (i % copies) *
+ * stride (a rotating arena of copies, so timed launches stream from HBM). For timing. */
+int nb_mv_matmul_repeat(nb_mv *h, const void *W, size_t stride, int copies, float *Y, int iters,
+                        void *stream);
+/* The same with the LM-head kernel (logits into Y, may be NULL; argmax keys into partial
+ * [n][rows/32] uint64, NaN flags into nan0 [n]). */
+int nb_mv_head_repeat(nb_mv *h, const void *W, size_t stride, int copies, float *Y, int iters,
+                      void *partial, int *nan0, void *stream);
 /* nb_mv_quant + nb_mv_matmul. */
 int nb_mv_run(nb_mv *h, const void *W, const float *X, float *Y, void *stream);
 /* Copy the scratch activations out (device buffers: q [n][cols] int8, d / fsum [n][cols/32]). */

@@ -86,6 +86,37 @@ int nb_mv_matmul(nb_mv *h, const void *W, float *Y, void *stream) {
     return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
 }
 
+int nb_mv_matmul_repeat(nb_mv *h, const void *W, size_t stride, int copies, float *Y, int iters,
+                        void *stream) {
+    if (!h || !W || !Y || h->n < 1 || copies < 1 || iters < 1) return PINFER_E_ARG;
+    Mat m;
+    m.rows = h->rows;
+    m.cols = h->cols;
+    m.npanels = (h->rows + kPanelRows - 1) / kPanelRows;
+    m.nsb = h->cols / 256;
+    for (int i = 0; i < iters; i++) {
+        m.w = (const uint8_t *)W + (size_t)(i % copies) * stride;
+        launch_matvec(m, h->act, h->step, Y, h->rows, 0, h->nmax, (cudaStream_t)stream);
+    }
+    return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
+}
+
+int nb_mv_head_repeat(nb_mv *h, const void *W, size_t stride, int copies, float *Y, int iters,
+                      void *partial, int *nan0, void *stream) {
+    if (!h || !W || h->n < 1 || copies < 1 || iters < 1 || !partial || !nan0) return PINFER_E_ARG;
+    Mat m;
+    m.rows = h->rows;
+    m.cols = h->cols;
+    m.npanels = (h->rows + kPanelRows - 1) / kPanelRows;
+    m.nsb = h->cols / 256;
+    for (int i = 0; i < iters; i++) {
+        m.w = (const uint8_t *)W + (size_t)(i % copies) * stride;
+        launch_matvec_head(m, h->act, h->step, Y, h->rows, (unsigned long long *)partial, nan0,
+                           h->nmax, (cudaStream_t)stream);
+    }
+    return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
+}
+
 int nb_mv_run(nb_mv *h, const void *W, const float *X, float *Y, void *stream) {
     const int rc = nb_mv_quant(h, X, stream);
     return rc ? rc : nb_mv_matmul(h, W, Y, stream);

@@ -105,6 +105,8 @@ void launch_norm_quant(const float *x, const float *w, int H, float eps, const S
 // Y = W A8(x): mode 0 store y[v][ldy], mode 1 residual x[v][ldy] += y
 void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode, int nmax,
                    cudaStream_t s);
+void launch_matvec_chunked(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode,
+                           int nmax, cudaStream_t s);
 // gate / up with SwiGLU and A8 quantisation of the product
 void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Act out, int nmax,
                           cudaStream_t s);

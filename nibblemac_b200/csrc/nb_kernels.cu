@@ -6,6 +6,7 @@
 // CUDA graph serves every round of a generation.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cstdio>
 
 #include "nb_engine.h"
@@ -239,6 +240,283 @@ __global__ void __launch_bounds__(kMvThreads) k_matvec_swiglu(Mat G, Mat U, Act 
             }
         }
     }
+}
+
+// ------------------------------------------------------------------ TMA-fed matvec
+// The same per-(row, vector) arithmetic as mv_panel, restructured for HBM streaming on B200:
+// weight units (one 32-row panel x 256 columns, 4608 bytes) are fetched with cp.async.bulk
+// (TMA bulk copies, completion counted on an mbarrier) into a ring of shared-memory slots per
+// warp, so every SM keeps ~110 KB of weights in flight while its warps compute. A warp owns
+// whole panels (lane = row) and walks their superblocks in column order, so the ordered FMA
+// chain of every (row, vector) stays in registers and never crosses warps.
+constexpr int kTallWarps = 8;
+constexpr int kRing = 2;
+constexpr size_t kTallSmem = (size_t)kTallWarps * kRing * kUnitBytes + kTallWarps * kRing * 8;
+constexpr unsigned kSpinLimit = 1u << 22;   // bounded mbarrier waits
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// expect `bytes` and start the bulk copy global -> shared that completes them
+__device__ __forceinline__ void tma_load_1d(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+// wait for phase `parity` of the barrier; false after kSpinLimit polls (the caller reports
+// the timeout instead of hanging)
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    for (unsigned i = 0; i < kSpinLimit; i++) {
+        uint32_t ok;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) {
+    return *reinterpret_cast<const uint4 *>(p);
+}
+
+// One superblock of one row (this lane) for every vector: decode the 6-bit scales, integer
+// block dots against the A8 activations (staged in shared memory), and the ordered fused chain
+// into acc[v]. sq: [NMAX][cols] int8, sdf: [nb][NMAX] (d, fsum) block-major.
+template <int NMAX>
+__device__ __forceinline__ void sb_accumulate(const uint4 sc, const uint4 (&cd)[8], const int8_t *sq,
+                                              const float2 *sdf, int cols, int sb, int n,
+                                              float (&acc)[NMAX]) {
+    const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
+    const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
+    const float D = half_bits_to_float((uint32_t)(A >> 48));
+    const float M = half_bits_to_float((uint32_t)(B >> 48));
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const float ds = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
+        const float os = __fmul_rn(M, (float)(uint32_t)((B >> (6 * k)) & 63u));
+        const int b = sb * 8 + k;
+        const int lo0 = (int)(cd[k].x & 0x0f0f0f0fu), lo1 = (int)(cd[k].y & 0x0f0f0f0fu);
+        const int lo2 = (int)(cd[k].z & 0x0f0f0f0fu), lo3 = (int)(cd[k].w & 0x0f0f0f0fu);
+        const int hi0 = (int)((cd[k].x >> 4) & 0x0f0f0f0fu), hi1 = (int)((cd[k].y >> 4) & 0x0f0f0f0fu);
+        const int hi2 = (int)((cd[k].z >> 4) & 0x0f0f0f0fu), hi3 = (int)((cd[k].w >> 4) & 0x0f0f0f0fu);
+#pragma unroll
+        for (int v = 0; v < NMAX; v++) {
+            if (v < n) {
+                const int4 *xq = reinterpret_cast<const int4 *>(sq + (size_t)v * cols + b * 32);
+                const int4 x0 = xq[0], x1 = xq[1];
+                int sacc = __dp4a(lo0, x0.x, 0);
+                sacc = __dp4a(lo1, x0.y, sacc);
+                sacc = __dp4a(lo2, x0.z, sacc);
+                sacc = __dp4a(lo3, x0.w, sacc);
+                sacc = __dp4a(hi0, x1.x, sacc);
+                sacc = __dp4a(hi1, x1.y, sacc);
+                sacc = __dp4a(hi2, x1.z, sacc);
+                sacc = __dp4a(hi3, x1.w, sacc);
+                const float2 df = sdf[b * NMAX + v];
+                acc[v] = __fmaf_rn((float)sacc, __fmul_rn(ds, df.x), acc[v]);
+                acc[v] = __fmaf_rn(-os, df.y, acc[v]);
+            }
+        }
+    }
+}
+
+size_t tall_smem(int cols, int nmax) {
+    return kTallSmem + (size_t)nmax * cols + (size_t)(cols / 32) * nmax * 8 + 16;
+}
+
+// The tied LM head (248320 rows): persistent CTAs, a warp owns whole panels (lane = row) and
+// walks their superblocks in column order through its TMA ring, so each (row, vector) chain
+// stays in registers; logits (optional) and per-panel (max, first index) keys.
+template <int NMAX>
+__global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Step *st, float *y,
+                                                             int ldy, unsigned long long *partial,
+                                                             int *nan0) {
+    extern __shared__ __align__(128) uint8_t tsm[];
+    const int n = st->n;
+    if (n <= 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t *ring = tsm + (size_t)warp * kRing * kUnitBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(tsm + (size_t)kTallWarps * kRing * kUnitBytes) + warp * kRing;
+    const int cols = W0.cols, nb = cols >> 5, nsb = W0.nsb;
+    int8_t *sq = reinterpret_cast<int8_t *>(tsm + kTallSmem);
+    float2 *sdf = reinterpret_cast<float2 *>(tsm + kTallSmem + (size_t)NMAX * cols);
+    const int gw = warp * gridDim.x + blockIdx.x, tw = gridDim.x * kTallWarps;
+    const int npw = W0.npanels > gw ? (W0.npanels - 1 - gw) / tw + 1 : 0;
+    const int total = npw * nsb;
+    auto src = [&](int u) -> const uint8_t * {
+        const int panel = gw + (u / nsb) * tw;
+        return W0.w + ((size_t)panel * nsb + (u % nsb)) * kUnitBytes;
+    };
+    if (lane == 0) {
+        for (int i = 0; i < kRing; i++) mbar_init(bars + i, 1);
+        fence_mbar_init();
+        for (int u = 0; u < kRing && u < total; u++) tma_load_1d(ring + (size_t)u * kUnitBytes, src(u), kUnitBytes, bars + u);
+    }
+    // stage the activations while the first weight units are in flight
+    for (int i = threadIdx.x; i < n * cols / 16; i += blockDim.x) {
+        const int v = i / (cols / 16), j = i % (cols / 16);
+        reinterpret_cast<int4 *>(sq)[i] = __ldg(reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols) + j);
+    }
+    for (int i = threadIdx.x; i < n * nb; i += blockDim.x) {
+        const int v = i / nb, b = i % nb;
+        sdf[b * NMAX + v] = make_float2(__ldg(in.d + (size_t)v * nb + b), __ldg(in.fs + (size_t)v * nb + b));
+    }
+    __syncthreads();
+    float acc[NMAX];
+#pragma unroll
+    for (int v = 0; v < NMAX; v++) acc[v] = 0.0f;
+    for (int u = 0; u < total; u++) {
+        const int slot = u % kRing;
+        if (!mbar_wait(bars + slot, (uint32_t)(u / kRing) & 1u)) {
+            if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
+            return;
+        }
+        const uint8_t *sp = ring + (size_t)slot * kUnitBytes + lane * 16;
+        const uint4 sc = lds128(sp);
+        uint4 cd[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) cd[k] = lds128(sp + 512 * (k + 1));
+        __syncwarp();
+        if (lane == 0 && u + kRing < total) {
+            fence_proxy_async();
+            tma_load_1d(ring + (size_t)slot * kUnitBytes, src(u + kRing), kUnitBytes, bars + slot);
+        }
+        const int sb = u % nsb;
+        if (sb == 0) {
+#pragma unroll
+            for (int v = 0; v < NMAX; v++) acc[v] = 0.0f;
+        }
+        sb_accumulate<NMAX>(sc, cd, sq, sdf, cols, sb, n, acc);
+        if (sb != nsb - 1) continue;
+        const int panel = gw + (u / nsb) * tw, row = panel * kPanelRows + lane;
+#pragma unroll
+        for (int v = 0; v < NMAX; v++) {
+            if (v >= n) break;
+            if (y && row < W0.rows) y[(size_t)v * ldy + row] = acc[v];
+            const unsigned long long key = row < W0.rows ? argmax_key(acc[v], row) : 0ull;
+            const unsigned long long best = warp_max_u64(key);
+            if (lane == 0) partial[(size_t)v * W0.npanels + panel] = best;
+            if (panel == 0 && lane == 0) nan0[v] = acc[v] != acc[v];
+        }
+    }
+}
+
+// Every matrix except the LM head: one CTA per 32-row panel, one warp per superblock unit
+// (up to kPanelWarps), every unit of the panel requested at once with a TMA bulk copy. Warps
+// write their integer block dots and decoded scales to shared memory; after a CTA barrier the
+// ordered fused chains run with lane = row, vectors spread over warps, and the epilogue writes
+//   EPI 0: y[v][row] = acc        (projections feeding DeltaNet / attention)
+//   EPI 1: y[v][row] += acc       (out_proj / o_proj / down_proj into the residual stream)
+//   EPI 3: SwiGLU over (W0 = gate, W1 = up) and A8 of the product for down_proj.
+// nmax <= 4.
+constexpr int kPanelWarps = 16;
+
+template <int NMAX, int EPI>
+__global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, Act in, Step *st,
+                                                               float *y, int ldy, Act out) {
+    extern __shared__ __align__(128) uint8_t wsm[];
+    const int n = st->n;
+    if (n <= 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int nsb = W0.nsb, nb = W0.cols >> 5, panel = blockIdx.x;
+    const int nmat = EPI == 3 ? 2 : 1, nunit = nsb * nmat;
+    uint8_t *units = wsm;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(wsm + (size_t)nw * kUnitBytes);
+    int32_t *isum = reinterpret_cast<int32_t *>(bars + nw);                 // [nmat][nb][NMAX][32]
+    float *ds = reinterpret_cast<float *>(isum + (size_t)nmat * nb * NMAX * 32);   // [nmat][nb][32]
+    float *os = ds + (size_t)nmat * nb * 32;
+    if (lane == 0) {
+        mbar_init(bars + warp, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    for (int u = warp, it = 0; u < nunit; u += nw, it++) {
+        const int m = u / nsb, sb = u % nsb;
+        const Mat &W = m ? W1 : W0;
+        uint8_t *slot = units + (size_t)warp * kUnitBytes;
+        if (lane == 0) {
+            if (it > 0) fence_proxy_async();
+            tma_load_1d(slot, W.w + ((size_t)panel * nsb + sb) * kUnitBytes, kUnitBytes, bars + warp);
+        }
+        if (!mbar_wait(bars + warp, (uint32_t)it & 1u)) {
+            if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
+            return;
+        }
+        const uint8_t *sp = slot + lane * 16;
+        const uint4 sc = lds128(sp);
+        uint4 cd[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) cd[k] = lds128(sp + 512 * (k + 1));
+        __syncwarp();
+        const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
+        const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
+        const float D = half_bits_to_float((uint32_t)(A >> 48));
+        const float M = half_bits_to_float((uint32_t)(B >> 48));
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int b = sb * 8 + k;
+            ds[((size_t)m * nb + b) * 32 + lane] = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
+            os[((size_t)m * nb + b) * 32 + lane] = __fmul_rn(M, (float)(uint32_t)((B >> (6 * k)) & 63u));
+            const int lo0 = (int)(cd[k].x & 0x0f0f0f0fu), lo1 = (int)(cd[k].y & 0x0f0f0f0fu);
+            const int lo2 = (int)(cd[k].z & 0x0f0f0f0fu), lo3 = (int)(cd[k].w & 0x0f0f0f0fu);
+            const int hi0 = (int)((cd[k].x >> 4) & 0x0f0f0f0fu), hi1 = (int)((cd[k].y >> 4) & 0x0f0f0f0fu);
+            const int hi2 = (int)((cd[k].z >> 4) & 0x0f0f0f0fu), hi3 = (int)((cd[k].w >> 4) & 0x0f0f0f0fu);
+#pragma unroll
+            for (int v = 0; v < NMAX; v++) {
+                if (v < n) {
+                    const int4 *xq = reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols + b * 32);
+                    const int4 x0 = __ldg(xq), x1 = __ldg(xq + 1);
+                    int sacc = __dp4a(lo0, x0.x, 0);
+                    sacc = __dp4a(lo1, x0.y, sacc);
+                    sacc = __dp4a(lo2, x0.z, sacc);
+                    sacc = __dp4a(lo3, x0.w, sacc);
+                    sacc = __dp4a(hi0, x1.x, sacc);
+                    sacc = __dp4a(hi1, x1.y, sacc);
+                    sacc = __dp4a(hi2, x1.z, sacc);
+                    sacc = __dp4a(hi3, x1.w, sacc);
+                    isum[(((size_t)m * nb + b) * NMAX + v) * 32 + lane] = sacc;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int row = panel * kPanelRows + lane;
+    for (int v = warp; v < n; v += nw) {
+        float acc[2];
+        for (int m = 0; m < nmat; m++) {
+            float a = 0.0f;
+            for (int b = 0; b < nb; b++) {
+                const float s = (float)isum[(((size_t)m * nb + b) * NMAX + v) * 32 + lane];
+                a = __fmaf_rn(s, __fmul_rn(ds[((size_t)m * nb + b) * 32 + lane], __ldg(in.d + (size_t)v * nb + b)), a);
+                a = __fmaf_rn(-os[((size_t)m * nb + b) * 32 + lane], __ldg(in.fs + (size_t)v * nb + b), a);
+            }
+            acc[m] = a;
+        }
+        if (EPI == 3) {
+            const float h = __fmul_rn(pf_silu(acc[0]), acc[1]);
+            const int nbo = out.cols >> 5;
+            quant_block_warp(h, lane, out.q + (size_t)v * out.cols + panel * 32,
+                             out.d + (size_t)v * nbo + panel, out.fs + (size_t)v * nbo + panel);
+        } else if (row < W0.rows) {
+            float *p = y + (size_t)v * ldy + row;
+            *p = EPI == 0 ? acc[0] : __fadd_rn(*p, acc[0]);
+        }
+    }
+}
+
+size_t panel_smem(int nw, int nb, int nmat, int nmax) {
+    return (size_t)nw * kUnitBytes + (size_t)nw * 8 + (size_t)nmat * nb * nmax * 32 * 4 +
+           (size_t)nmat * nb * 32 * 8;
 }
 
 // ------------------------------------------------------------------ argmax over the panels
@@ -929,15 +1207,50 @@ void head_t(const Mat &W, Act in, const Step *st, float *logits, int ld, unsigne
 }
 }  // namespace
 
+int num_sms() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
+}
+
+template <int NMAX>
+void head_t2(const Mat &W, Act in, const Step *st, float *y, int ldy, unsigned long long *partial,
+             int *nan0, cudaStream_t s) {
+    const int grid = std::min(2 * num_sms(), (W.npanels + kTallWarps - 1) / kTallWarps);
+    k_mv_head<NMAX><<<std::max(grid, 1), kTallWarps * 32, tall_smem(W.cols, NMAX), s>>>(
+        W, in, const_cast<Step *>(st), y, ldy, partial, nan0);
+}
+
+template <int NMAX, int EPI>
+bool panel_t(const Mat &W0, const Mat &W1, Act in, const Step *st, float *y, int ldy, Act out,
+             cudaStream_t s) {
+    const int nmat = EPI == 3 ? 2 : 1;
+    const int nw = std::min(W0.nsb * nmat, kPanelWarps);
+    const size_t sm = panel_smem(nw, W0.cols / 32, nmat, NMAX);
+    if (sm > 227 * 1024) return false;
+    k_mv_panel<NMAX, EPI><<<W0.npanels, nw * 32, sm, s>>>(W0, W1, in, const_cast<Step *>(st), y, ldy, out);
+    return true;
+}
+
 void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode, int nmax,
                    cudaStream_t s) {
-    if (nmax <= 1) matvec_t<1>(W, in, st, y, ldy, mode, s);
-    else if (nmax <= 4) matvec_t<4>(W, in, st, y, ldy, mode, s);
-    else if (nmax <= 8) matvec_t<8>(W, in, st, y, ldy, mode, s);
-    else matvec_t<16>(W, in, st, y, ldy, mode, s);
+    Act none;
+    bool done = false;
+    if (nmax <= 1) done = mode ? panel_t<1, 1>(W, W, in, st, y, ldy, none, s) : panel_t<1, 0>(W, W, in, st, y, ldy, none, s);
+    else if (nmax <= 4) done = mode ? panel_t<4, 1>(W, W, in, st, y, ldy, none, s) : panel_t<4, 0>(W, W, in, st, y, ldy, none, s);
+    if (!done) launch_matvec_chunked(W, in, st, y, ldy, mode, nmax, s);
 }
 void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Act out, int nmax,
                           cudaStream_t s) {
+    bool done = false;
+    if (nmax <= 1) done = panel_t<1, 3>(G, U, in, st, nullptr, 0, out, s);
+    else if (nmax <= 4) done = panel_t<4, 3>(G, U, in, st, nullptr, 0, out, s);
+    if (done) return;
     if (nmax <= 1) swiglu_t<1>(G, U, in, st, out, s);
     else if (nmax <= 4) swiglu_t<4>(G, U, in, st, out, s);
     else if (nmax <= 8) swiglu_t<8>(G, U, in, st, out, s);
@@ -945,10 +1258,19 @@ void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Ac
 }
 void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int ld,
                         unsigned long long *partial, int *nan0, int nmax, cudaStream_t s) {
-    if (nmax <= 1) head_t<1>(W, in, st, logits, ld, partial, nan0, s);
-    else if (nmax <= 4) head_t<4>(W, in, st, logits, ld, partial, nan0, s);
-    else if (nmax <= 8) head_t<8>(W, in, st, logits, ld, partial, nan0, s);
-    else head_t<16>(W, in, st, logits, ld, partial, nan0, s);
+    if (nmax <= 1) head_t2<1>(W, in, st, logits, ld, partial, nan0, s);
+    else if (nmax <= 4) head_t2<4>(W, in, st, logits, ld, partial, nan0, s);
+    else if (nmax <= 8) head_t2<8>(W, in, st, logits, ld, partial, nan0, s);
+    else head_t2<16>(W, in, st, logits, ld, partial, nan0, s);
+}
+// The first-generation kernel (chunked shared-memory chains, any shape) stays available for
+// the kernel-level ABI's reference timing.
+void launch_matvec_chunked(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode,
+                           int nmax, cudaStream_t s) {
+    if (nmax <= 1) matvec_t<1>(W, in, st, y, ldy, mode, s);
+    else if (nmax <= 4) matvec_t<4>(W, in, st, y, ldy, mode, s);
+    else if (nmax <= 8) matvec_t<8>(W, in, st, y, ldy, mode, s);
+    else matvec_t<16>(W, in, st, y, ldy, mode, s);
 }
 void launch_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
                          Step *st, cudaStream_t s) {
@@ -1023,6 +1345,16 @@ void kernels_init(int max_ctx, int hd, int rep) {
     cudaFuncSetAttribute(k_matvec_head<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
     cudaFuncSetAttribute(k_matvec_head<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
     cudaFuncSetAttribute(k_matvec_head<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
+    cudaFuncSetAttribute(k_mv_head<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_head<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_head<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_head<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_panel<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_panel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_panel<1, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_panel<4, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_panel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_mv_panel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (max_ctx <= 0) return;   // matvec kernels only (kernel-level ABI)
     cudaFuncSetAttribute(k_deltanet, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)deltanet_smem(rep));
     cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(((size_t)hd + max_ctx) * sizeof(float)));
