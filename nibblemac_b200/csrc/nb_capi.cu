@@ -47,7 +47,10 @@ nb_mv *nb_mv_create(int rows, int cols, int nmax) {
         nb_mv_destroy(h);
         return nullptr;
     }
-    kernels_init(0, 0, 0);
+    if (kernels_init(0, 0, 0) != 0) {
+        nb_mv_destroy(h);
+        return nullptr;
+    }
     return h;
 }
 

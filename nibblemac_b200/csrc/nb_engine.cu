@@ -349,8 +349,7 @@ int alloc_and_upload(pinfer_ctx *c) {
     CUDA_OK(cudaMemcpy(ov, T.ovf_val, sizeof(float) * T.n_ovf, cudaMemcpyHostToDevice));
     c->tables = LibmTables{eb, lb, ok, ov, T.n_ovf};
     libm_tables_free(&c->host_tables);
-    kernels_init(c->max_ctx, c->hd, c->lind.rep);
-    CUDA_OK(cudaGetLastError());
+    if (kernels_init(c->max_ctx, c->hd, c->lind.rep) != 0) return PINFER_E_NOMEM;
     return PINFER_OK;
 }
 
@@ -367,28 +366,31 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head) {
     launch_embed(c->embed, c->step, c->x, c->H, s);
     for (int l = 0; l < c->n_layers; l++) {
         auto &D = c->layers[l];
-        launch_norm_quant(c->x, D.in_norm, c->H, c->eps, c->step, c->act_h, s);
         if (D.is_full) {
             const Act o = mid_act(c, c->nq * c->hd);
-            launch_matvec(D.win, c->act_h, c->step, c->y, c->attd.ldy, 0, nmax, s);
+            launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->attd.ldy, nmax, c->act_h, s);
             launch_attn_prep(c->att[l], c->attd, c->y, c->qbuf, c->step, s);
             launch_attn(c->att[l], c->attd, c->y, c->qbuf, c->step, o, s);
             launch_matvec(D.out, o, c->step, c->x, c->H, 1, nmax, s);
         } else {
             const Act o = mid_act(c, c->vd);
-            launch_matvec(D.win, c->act_h, c->step, c->y, c->lind.ldy, 0, nmax, s);
+            launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->lind.ldy, nmax, c->act_h, s);
             launch_deltanet(c->lin[D.lin], c->lind, c->tables, c->y, c->step, o, s);
             launch_matvec(D.out, o, c->step, c->x, c->H, 1, nmax, s);
         }
-        launch_norm_quant(c->x, D.post_norm, c->H, c->eps, c->step, c->act_h, s);
         const Act h = mid_act(c, c->ffn);
-        launch_matvec_swiglu(D.gate, D.up, c->act_h, c->step, h, nmax, s);
+        launch_matvec_swiglu_norm(D.gate, D.up, c->x, D.post_norm, c->eps, c->step, h, nmax, c->act_h, s);
         launch_matvec(D.down, h, c->step, c->x, c->H, 1, nmax, s);
     }
     if (head) {
-        launch_norm_quant(c->x, c->norm, c->H, c->eps, c->step, c->act_h, s);
-        launch_matvec_head(c->head, c->act_h, c->step, head == 1 ? c->logits : nullptr, c->vocab,
-                           c->partial, c->nan0, nmax, s);
+        if (nmax <= 4) {
+            launch_matvec_head_norm(c->head, c->x, c->norm, c->eps, c->step, head == 1 ? c->logits : nullptr,
+                                    c->vocab, c->partial, c->nan0, nmax, s);
+        } else {
+            launch_norm_quant(c->x, c->norm, c->H, c->eps, c->step, c->act_h, s);
+            launch_matvec_head(c->head, c->act_h, c->step, head == 1 ? c->logits : nullptr, c->vocab,
+                               c->partial, c->nan0, nmax, s);
+        }
         launch_argmax_final(c->partial, c->nan0, c->head.npanels, c->step, s);
     }
     launch_pass_end(c->step, s);

@@ -107,6 +107,15 @@ void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int 
                    cudaStream_t s);
 void launch_matvec_chunked(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode,
                            int nmax, cudaStream_t s);
+// The same with the RMSNorm + A8 of the residual rows x fused into the kernel (scratch: the A8
+// buffer a fallback path may use for large passes)
+void launch_matvec_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
+                        float *y, int ldy, int nmax, Act scratch, cudaStream_t s);
+void launch_matvec_swiglu_norm(const Mat &G, const Mat &U, const float *x, const float *w, float eps,
+                               const Step *st, Act out, int nmax, Act scratch, cudaStream_t s);
+void launch_matvec_head_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
+                             float *logits, int ld, unsigned long long *partial, int *nan0, int nmax,
+                             cudaStream_t s);
 // gate / up with SwiGLU and A8 quantisation of the product
 void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Act out, int nmax,
                           cudaStream_t s);
@@ -127,7 +136,7 @@ void launch_pass_end(Step *st, cudaStream_t s);
 size_t deltanet_smem(int rep);
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s);
 void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s);
-void kernels_init(int max_ctx, int hd, int rep);
+int kernels_init(int max_ctx, int hd, int rep);   // 0, or -1 if a CUDA call failed
 void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s);
 // small-n standalone entry points for the C-ABI kernel tests
 void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s);

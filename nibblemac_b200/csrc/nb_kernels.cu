@@ -285,17 +285,61 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     }
     return false;
 }
+__device__ __forceinline__ void cp_async4(float *dst, const float *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) {
     return *reinterpret_cast<const uint4 *>(p);
 }
 
+struct NormIn {          // RMSNorm input of a NORM panel kernel
+    const float *x;      // [n][cols] residual rows
+    const float *w;      // [cols] norm multiplier
+    float eps;
+};
+
+// RMSNorm + A8 of n rows into shared memory (pf_rmsnorm, forward_ops.c:191-200, then
+// kern_quant_act). sx: [n][cols] fp32 and sw: [cols] already staged. Threads of the CTA.
+__device__ __forceinline__ void norm_quant_smem(const float *sx, const float *sw, int n, int cols,
+                                                float eps, int8_t *sq, float2 *sdf, float *srr) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    if (warp == 0) {
+        // lanes 4v..4v+3: the four interleaved partial sums of row v (cols % 4 == 0)
+        const int v = lane >> 2, l = lane & 3;
+        float c = 0.0f;
+        if (v < n) {
+            const float *x = sx + (size_t)v * cols;
+#pragma unroll 8
+            for (int i = l; i < cols; i += 4) c = madd(c, x[i], x[i]);
+        }
+        const int base = lane & ~3;
+        const float c0 = __shfl_sync(0xffffffffu, c, base), c1 = __shfl_sync(0xffffffffu, c, base + 1);
+        const float c2 = __shfl_sync(0xffffffffu, c, base + 2), c3 = __shfl_sync(0xffffffffu, c, base + 3);
+        const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+        if (v < n && l == 0) srr[v] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)cols), eps));
+    }
+    __syncthreads();
+    const int nb = cols >> 5;
+    for (int u = warp; u < n * nb; u += nw) {
+        const int v = u / nb, b = u % nb, i = b * 32 + lane;
+        const float yv = __fmul_rn(__fmul_rn(sx[(size_t)v * cols + i], srr[v]), sw[i]);
+        float d, f;
+        quant_block_warp(yv, lane, sq + (size_t)v * cols + b * 32, &d, &f);
+        if (lane == 0) sdf[(size_t)v * nb + b] = make_float2(d, f);
+    }
+}
+
 // One superblock of one row (this lane) for every vector: decode the 6-bit scales, integer
 // block dots against the A8 activations (staged in shared memory), and the ordered fused chain
-// into acc[v]. sq: [NMAX][cols] int8, sdf: [nb][NMAX] (d, fsum) block-major.
+// into acc[v]. sq: [NMAX][cols] int8, sdf: [NMAX][nb] (d, fsum).
 template <int NMAX>
 __device__ __forceinline__ void sb_accumulate(const uint4 sc, const uint4 (&cd)[8], const int8_t *sq,
                                               const float2 *sdf, int cols, int sb, int n,
                                               float (&acc)[NMAX]) {
+    const int nb = cols >> 5;
     const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
     const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
     const float D = half_bits_to_float((uint32_t)(A >> 48));
@@ -322,7 +366,7 @@ __device__ __forceinline__ void sb_accumulate(const uint4 sc, const uint4 (&cd)[
                 sacc = __dp4a(hi1, x1.y, sacc);
                 sacc = __dp4a(hi2, x1.z, sacc);
                 sacc = __dp4a(hi3, x1.w, sacc);
-                const float2 df = sdf[b * NMAX + v];
+                const float2 df = sdf[(size_t)v * nb + b];
                 acc[v] = __fmaf_rn((float)sacc, __fmul_rn(ds, df.x), acc[v]);
                 acc[v] = __fmaf_rn(-os, df.y, acc[v]);
             }
@@ -330,17 +374,20 @@ __device__ __forceinline__ void sb_accumulate(const uint4 sc, const uint4 (&cd)[
     }
 }
 
-size_t tall_smem(int cols, int nmax) {
-    return kTallSmem + (size_t)nmax * cols + (size_t)(cols / 32) * nmax * 8 + 16;
+size_t tall_smem(int cols, int nmax, bool norm) {
+    size_t b = kTallSmem + (size_t)nmax * cols + (size_t)(cols / 32) * nmax * 8 + 16;
+    b = (b + 15) & ~(size_t)15;
+    if (norm) b += (size_t)nmax * cols * 4 + (size_t)cols * 4;
+    return b;
 }
 
 // The tied LM head (248320 rows): persistent CTAs, a warp owns whole panels (lane = row) and
 // walks their superblocks in column order through its TMA ring, so each (row, vector) chain
 // stays in registers; logits (optional) and per-panel (max, first index) keys.
-template <int NMAX>
-__global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Step *st, float *y,
-                                                             int ldy, unsigned long long *partial,
-                                                             int *nan0) {
+template <int NMAX, bool NORM>
+__global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, NormIn nin, Step *st,
+                                                             float *y, int ldy,
+                                                             unsigned long long *partial, int *nan0) {
     extern __shared__ __align__(128) uint8_t tsm[];
     const int n = st->n;
     if (n <= 0) return;
@@ -362,14 +409,27 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Ste
         fence_mbar_init();
         for (int u = 0; u < kRing && u < total; u++) tma_load_1d(ring + (size_t)u * kUnitBytes, src(u), kUnitBytes, bars + u);
     }
-    // stage the activations while the first weight units are in flight
-    for (int i = threadIdx.x; i < n * cols / 16; i += blockDim.x) {
-        const int v = i / (cols / 16), j = i % (cols / 16);
-        reinterpret_cast<int4 *>(sq)[i] = __ldg(reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols) + j);
-    }
-    for (int i = threadIdx.x; i < n * nb; i += blockDim.x) {
-        const int v = i / nb, b = i % nb;
-        sdf[b * NMAX + v] = make_float2(__ldg(in.d + (size_t)v * nb + b), __ldg(in.fs + (size_t)v * nb + b));
+    // stage the activations while the first weight units are in flight: the A8 input, or
+    // (NORM) the final RMSNorm of the residual rows computed here
+    __shared__ float srr[NMAX];
+    if (NORM) {
+        const size_t off = ((kTallSmem + (size_t)NMAX * cols + (size_t)nb * NMAX * 8 + 16) + 15) & ~(size_t)15;
+        float *sx = reinterpret_cast<float *>(tsm + off), *sw = sx + (size_t)NMAX * cols;
+        for (int i = threadIdx.x; i < n * cols / 4; i += blockDim.x)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sx + 4 * i)), "l"(nin.x + 4 * i) : "memory");
+        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sw + 4 * i)), "l"(nin.w + 4 * i) : "memory");
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sdf, srr);
+    } else {
+        for (int i = threadIdx.x; i < n * cols / 16; i += blockDim.x) {
+            const int v = i / (cols / 16), j = i % (cols / 16);
+            reinterpret_cast<int4 *>(sq)[i] = __ldg(reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols) + j);
+        }
+        for (int i = threadIdx.x; i < n * nb; i += blockDim.x)
+            sdf[i] = make_float2(__ldg(in.d + i), __ldg(in.fs + i));
     }
     __syncthreads();
     float acc[NMAX];
@@ -412,41 +472,71 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Ste
 }
 
 // Every matrix except the LM head: one CTA per 32-row panel, one warp per superblock unit
-// (up to kPanelWarps), every unit of the panel requested at once with a TMA bulk copy. Warps
-// write their integer block dots and decoded scales to shared memory; after a CTA barrier the
-// ordered fused chains run with lane = row, vectors spread over warps, and the epilogue writes
+// (up to kPanelWarps), every unit of the panel requested at once with a TMA bulk copy. While
+// the units are in flight the CTA stages its activations in shared memory: the A8 input of the
+// previous kernel, or (NORM) the RMSNorm of the residual rows x [n][cols] quantised right here
+// (pf_rmsnorm + kern_quant_act: every CTA computes the same bits). Warps write their integer
+// block dots and decoded scales to shared memory; after a barrier the ordered fused chains run
+// with lane = row, vectors spread over warps, and the epilogue writes
 //   EPI 0: y[v][row] = acc        (projections feeding DeltaNet / attention)
 //   EPI 1: y[v][row] += acc       (out_proj / o_proj / down_proj into the residual stream)
 //   EPI 3: SwiGLU over (W0 = gate, W1 = up) and A8 of the product for down_proj.
 // nmax <= 4.
 constexpr int kPanelWarps = 16;
 
-template <int NMAX, int EPI>
-__global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, Act in, Step *st,
-                                                               float *y, int ldy, Act out) {
+template <int NMAX, int EPI, bool NORM>
+__global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, Act in, NormIn nin,
+                                                               Step *st, float *y, int ldy, Act out) {
     extern __shared__ __align__(128) uint8_t wsm[];
     const int n = st->n;
     if (n <= 0) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int nsb = W0.nsb, nb = W0.cols >> 5, panel = blockIdx.x;
+    const int nsb = W0.nsb, cols = W0.cols, nb = cols >> 5, panel = blockIdx.x;
     const int nmat = EPI == 3 ? 2 : 1, nunit = nsb * nmat;
     uint8_t *units = wsm;
     uint64_t *bars = reinterpret_cast<uint64_t *>(wsm + (size_t)nw * kUnitBytes);
-    int32_t *isum = reinterpret_cast<int32_t *>(bars + nw);                 // [nmat][nb][NMAX][32]
+    int32_t *isum = reinterpret_cast<int32_t *>(wsm + (size_t)nw * kUnitBytes + (((size_t)nw * 8 + 15) & ~(size_t)15));
     float *ds = reinterpret_cast<float *>(isum + (size_t)nmat * nb * NMAX * 32);   // [nmat][nb][32]
     float *os = ds + (size_t)nmat * nb * 32;
+    float2 *sdf = reinterpret_cast<float2 *>(os + (size_t)nmat * nb * 32);   // [NMAX][nb]
+    int8_t *sq = reinterpret_cast<int8_t *>(sdf + (size_t)NMAX * nb);         // [NMAX][cols]
+    float *sx = reinterpret_cast<float *>(sq + (size_t)NMAX * cols);           // NORM: [NMAX][cols]
+    float *sw = sx + (size_t)NMAX * cols;                                       // NORM: [cols]
+    __shared__ float srr[NMAX];
     if (lane == 0) {
         mbar_init(bars + warp, 1);
         fence_mbar_init();
+        if (warp < nunit) {   // first unit of every warp, before anything else
+            const int m = warp / nsb, sb = warp % nsb;
+            tma_load_1d(units + (size_t)warp * kUnitBytes,
+                        (m ? W1 : W0).w + ((size_t)panel * nsb + sb) * kUnitBytes, kUnitBytes, bars + warp);
+        }
     }
-    __syncwarp();
+    // activations into shared memory while the weights are in flight
+    if (NORM) {
+        for (int i = threadIdx.x; i < n * cols / 4; i += blockDim.x)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sx + 4 * i)), "l"(nin.x + 4 * i) : "memory");
+        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sw + 4 * i)), "l"(nin.w + 4 * i) : "memory");
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+        norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sdf, srr);
+    } else {
+        for (int i = threadIdx.x; i < n * cols / 16; i += blockDim.x) {
+            const int v = i / (cols / 16), jj = i % (cols / 16);
+            reinterpret_cast<int4 *>(sq)[i] = __ldg(reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols) + jj);
+        }
+        for (int i = threadIdx.x; i < n * nb; i += blockDim.x)
+            sdf[i] = make_float2(__ldg(in.d + i), __ldg(in.fs + i));
+    }
+    __syncthreads();
     for (int u = warp, it = 0; u < nunit; u += nw, it++) {
         const int m = u / nsb, sb = u % nsb;
-        const Mat &W = m ? W1 : W0;
         uint8_t *slot = units + (size_t)warp * kUnitBytes;
-        if (lane == 0) {
-            if (it > 0) fence_proxy_async();
-            tma_load_1d(slot, W.w + ((size_t)panel * nsb + sb) * kUnitBytes, kUnitBytes, bars + warp);
+        if (it > 0 && lane == 0) {
+            fence_proxy_async();
+            tma_load_1d(slot, (m ? W1 : W0).w + ((size_t)panel * nsb + sb) * kUnitBytes, kUnitBytes, bars + warp);
         }
         if (!mbar_wait(bars + warp, (uint32_t)it & 1u)) {
             if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
@@ -474,8 +564,8 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
 #pragma unroll
             for (int v = 0; v < NMAX; v++) {
                 if (v < n) {
-                    const int4 *xq = reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols + b * 32);
-                    const int4 x0 = __ldg(xq), x1 = __ldg(xq + 1);
+                    const int4 *xq = reinterpret_cast<const int4 *>(sq + (size_t)v * cols + b * 32);
+                    const int4 x0 = xq[0], x1 = xq[1];
                     int sacc = __dp4a(lo0, x0.x, 0);
                     sacc = __dp4a(lo1, x0.y, sacc);
                     sacc = __dp4a(lo2, x0.z, sacc);
@@ -492,13 +582,20 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
     __syncthreads();
     const int row = panel * kPanelRows + lane;
     for (int v = warp; v < n; v += nw) {
-        float acc[2];
-        for (int m = 0; m < nmat; m++) {
+        float acc[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            if (m >= nmat) break;
             float a = 0.0f;
+            const int32_t *is = isum + ((size_t)m * nb * NMAX + v) * 32 + lane;
+            const float *dsp = ds + (size_t)m * nb * 32 + lane, *osp = os + (size_t)m * nb * 32 + lane;
+            const float2 *df = sdf + (size_t)v * nb;
+#pragma unroll 4
             for (int b = 0; b < nb; b++) {
-                const float s = (float)isum[(((size_t)m * nb + b) * NMAX + v) * 32 + lane];
-                a = __fmaf_rn(s, __fmul_rn(ds[((size_t)m * nb + b) * 32 + lane], __ldg(in.d + (size_t)v * nb + b)), a);
-                a = __fmaf_rn(-os[((size_t)m * nb + b) * 32 + lane], __ldg(in.fs + (size_t)v * nb + b), a);
+                const float s = (float)is[(size_t)b * NMAX * 32];
+                const float2 f = df[b];
+                a = __fmaf_rn(s, __fmul_rn(dsp[b * 32], f.x), a);
+                a = __fmaf_rn(-osp[b * 32], f.y, a);
             }
             acc[m] = a;
         }
@@ -514,9 +611,13 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
     }
 }
 
-size_t panel_smem(int nw, int nb, int nmat, int nmax) {
-    return (size_t)nw * kUnitBytes + (size_t)nw * 8 + (size_t)nmat * nb * nmax * 32 * 4 +
-           (size_t)nmat * nb * 32 * 8;
+size_t panel_smem(int nw, int cols, int nmat, int nmax, bool norm) {
+    const size_t nb = cols / 32;
+    size_t b = (size_t)nw * kUnitBytes + (((size_t)nw * 8 + 15) & ~(size_t)15) + (size_t)nmat * nb * nmax * 32 * 4 +
+               (size_t)nmat * nb * 32 * 8 + (size_t)nmax * nb * 8 + (size_t)nmax * cols;
+    b = (b + 15) & ~(size_t)15;
+    if (norm) b += (size_t)nmax * cols * 4 + (size_t)cols * 4;
+    return b;
 }
 
 // ------------------------------------------------------------------ argmax over the panels
@@ -575,6 +676,7 @@ __device__ float sumsq_ref(const float *x, int n) {
     float c = 0.0f;
     const int n4 = n & ~3;
     if (lane < 4) {
+#pragma unroll 8
         for (int i = lane; i < n4; i += 4) c = madd(c, x[i], x[i]);
     } else if (lane == 4) {
         for (int i = n4; i < n; i++) c = madd(c, x[i], x[i]);
@@ -592,6 +694,7 @@ __device__ float sum4_ref(const float *a, int n) {
     float c = 0.0f;
     const int n4 = n & ~3;
     if (lane < 4) {
+#pragma unroll 8
         for (int i = lane; i < n4; i += 4) c = __fadd_rn(c, a[i]);
     } else if (lane == 4) {
         for (int i = n4; i < n; i++) c = __fadd_rn(c, a[i]);
@@ -608,9 +711,13 @@ __global__ void k_norm_quant(const float *x, const float *w, int H, float eps, c
                              Act out) {
     const int v = blockIdx.x;
     if (v >= st->n) return;
-    extern __shared__ float xs[];
+    extern __shared__ float xs[];   // [H] x, then [H] w
     __shared__ float rr;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) xs[i] = x[(size_t)v * H + i];
+    float *ws = xs + H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        xs[i] = x[(size_t)v * H + i];
+        ws[i] = w[i];
+    }
     __syncthreads();
     if (threadIdx.x < 32) {
         const float s = sumsq_ref(xs, H);
@@ -622,7 +729,7 @@ __global__ void k_norm_quant(const float *x, const float *w, int H, float eps, c
     const int nb = H >> 5;
     for (int b = warp; b < nb; b += nw) {
         const int i = b * 32 + lane;
-        const float y = __fmul_rn(__fmul_rn(xs[i], r), w[i]);
+        const float y = __fmul_rn(__fmul_rn(xs[i], r), ws[i]);
         quant_block_warp(y, lane, out.q + (size_t)v * out.cols + b * 32,
                          out.d + (size_t)v * nb + b, out.fs + (size_t)v * nb + b);
     }
@@ -686,9 +793,30 @@ __global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, Libm
     s.beta = s.so + kMaxRows * rep * kDV;
     s.decay = s.beta + kMaxRows * rep;
     s.kp = s.decay + kMaxRows * rep;
-    s.pdec = s.kp + kDK;
-    s.rn = s.pdec + 4;
+    s.pdec = s.kp + kMaxRows * kDK;
+    s.rn = s.pdec + kMaxRows;
     const int C = d.C, K = d.K, S = K - 1;
+
+    // ---- 0. start the recurrent state load (registers) and the replay-log staging: neither
+    //         depends on this pass's activations, so they overlap the conv / norm / gate work
+    float Sc[kDK];
+    const bool preload = rep == 1;
+    const int j = tid;
+    if (preload) {
+        const float *rec0 = L.rec + (size_t)(kh * rep) * kDK * kDV + j;
+#pragma unroll
+        for (int i = 0; i < kDK; i++) Sc[i] = rec0[(size_t)i * kDV];
+    }
+    // ---- 1a. gates (only need b and a)
+    for (int u = tid; u < n * rep; u += nthr) {
+        const int t = u / rep, r = u % rep, h = kh * rep + r;
+        const float b = y[(size_t)t * d.ldy + C + d.vd + h];
+        const float a = y[(size_t)t * d.ldy + C + d.vd + d.nv + h];
+        s.beta[t * rep + r] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(T, -b)));
+        const float xs = __fadd_rn(a, L.dt_bias[h]);
+        const float sp = xs > 20.0f ? xs : glibc_log1pf(T, glibc_expf(T, xs));
+        s.decay[t * rep + r] = glibc_expf(T, __fmul_rn(L.A[h], sp));
+    }
 
     // ---- 1. conv + SiLU
     const int nch = 2 * kDK + rep * kDV;
@@ -742,8 +870,10 @@ __global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, Libm
             const bool act = u < 2 * n;
             float *vec = act ? ((u & 1) ? s.ck : s.cq) + (u >> 1) * kDK : s.cq;
             float c = 0.0f;
-            if (act)
+            if (act) {
+#pragma unroll 8
                 for (int i = l; i < kDK; i += 4) c = madd(c, vec[i], vec[i]);
+            }
             const int base = lane & ~3;
             const float c0 = __shfl_sync(0xffffffffu, c, base), c1 = __shfl_sync(0xffffffffu, c, base + 1);
             const float c2 = __shfl_sync(0xffffffffu, c, base + 2), c3 = __shfl_sync(0xffffffffu, c, base + 3);
@@ -756,37 +886,33 @@ __global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, Libm
             }
         }
     }
-    // ---- 3. gates
-    for (int u = tid; u < n * rep; u += nthr) {
-        const int t = u / rep, r = u % rep, h = kh * rep + r;
-        const float b = y[(size_t)t * d.ldy + C + d.vd + h];
-        const float a = y[(size_t)t * d.ldy + C + d.vd + d.nv + h];
-        s.beta[t * rep + r] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(T, -b)));
-        const float xs = __fadd_rn(a, L.dt_bias[h]);
-        const float sp = xs > 20.0f ? xs : glibc_log1pf(T, glibc_expf(T, xs));
-        s.decay[t * rep + r] = glibc_expf(T, __fmul_rn(L.A[h], sp));
-    }
     __syncthreads();
-
     // ---- 4. recurrence, value heads of this key head one after another
     const size_t logw = (size_t)kDK + kDV + 1;
-    const int j = tid;
     for (int r = 0; r < rep; r++) {
         const int h = kh * rep + r;
-        float Sc[kDK];
         float *rec = L.rec + (size_t)h * kDK * kDV + j;
+        if (!preload) {
 #pragma unroll
-        for (int i = 0; i < kDK; i++) Sc[i] = rec[(size_t)i * kDV];
-        for (int tp = 1; tp <= pend_keep; tp++) {   // deferred commit: rows 1..keep of half wr^1
-            const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp) * d.nv + h) * logw;
+            for (int i = 0; i < kDK; i++) Sc[i] = rec[(size_t)i * kDV];
+        }
+        if (pend_keep > 0) {   // deferred commit: rows 1..keep of half wr^1 (<= kMaxRows - 1)
+            float dl[kMaxRows];
             __syncthreads();
-            s.kp[j] = u[j];
-            if (j == 0) s.pdec[0] = u[kDK + kDV];
+            for (int tp = 1; tp <= pend_keep; tp++) {
+                const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp) * d.nv + h) * logw;
+                s.kp[(tp - 1) * kDK + j] = u[j];
+                dl[tp - 1] = u[kDK + j];
+                if (j == 0) s.pdec[tp - 1] = u[kDK + kDV];
+            }
             __syncthreads();
-            const float dl = u[kDK + j], pd = s.pdec[0];
+            for (int tp = 0; tp < pend_keep; tp++) {
+                const float pd = s.pdec[tp], dv_ = dl[tp];
+                const float *kr = s.kp + tp * kDK;
 #pragma unroll
-            for (int i = 0; i < kDK; i++)
-                Sc[i] = __fadd_rn(__fmul_rn(Sc[i], pd), __fmul_rn(s.kp[i], dl));
+                for (int i = 0; i < kDK; i++)
+                    Sc[i] = __fadd_rn(__fmul_rn(Sc[i], pd), __fmul_rn(kr[i], dv_));
+            }
         }
         for (int t = 0; t < n; t++) {
             const float *qt = s.cq + t * kDK, *kt = s.ck + t * kDK;
@@ -1075,6 +1201,357 @@ __global__ void k_attn(AttnLayer L, AttnDims d, const float *y, const float *qbu
 }
 
 
+// Second part of the attention (attend / score_task / softmax_task / pv_task,
+// forward_attn.c:95-229), per (token, query head), hd threads:
+//  scores   pf_dot(q, K row) * (1/sqrt(hd)): each thread keeps pf_dot's 16 interleaved partial
+//           sums of one position in registers (forward_ops.c:265-287), K rows read as float4;
+//  softmax  max, pf_expf(a - max), the 4-lane sum (forward_ops.c:320-353), p = a * (1/sum);
+//  P.V      row order from zero, per column; V rows stream into a per-thread cp.async ring in
+//           shared memory (`ring` rows in flight), so the sequential chain reads on-chip data;
+//  o *= sigmoid(gate), then A8 blocks of 32 for o_proj.
+
+constexpr int kAttnHd = 256;
+constexpr int kVRing = 96;
+constexpr int kVGroup = 8;
+
+__global__ void __launch_bounds__(kAttnHd) k_attn2(AttnLayer L, AttnDims d, const float *y,
+                                                   const float *qbuf, const Step *st, Act out) {
+    const int t = blockIdx.x;
+    if (t >= st->n) return;
+    constexpr int HD = kAttnHd;
+    const int h = blockIdx.y, tid = threadIdx.x;
+    const int g = h / (d.nq / d.nkv);
+    const int pos = st->pos0 + t;
+    if (pos >= d.max_ctx) return;
+    const int np = pos + 1;
+    extern __shared__ __align__(16) float asm_[];
+    float *q = asm_, *att = asm_ + HD, *vring = att + ((d.max_ctx + 3) & ~3);
+    __shared__ float red[32];
+    __shared__ float s_mx, s_inv;
+    const float *V = L.vc + (size_t)g * d.max_ctx * HD + tid;
+    // start the V stream right away (groups of kVGroup rows): it does not depend on the scores
+    const int ngroups = (np + kVGroup - 1) / kVGroup;
+    for (int gi = 0; gi < kVRing / kVGroup; gi++) {
+        for (int r = 0; r < kVGroup; r++) {
+            const int j = gi * kVGroup + r;
+            if (j < np) cp_async4(vring + (size_t)j * HD + tid, V + (size_t)j * HD);
+        }
+        cp_async_commit();
+    }
+    q[tid] = qbuf[((size_t)t * d.nq + h) * HD + tid];
+    __syncthreads();
+    const float scale = inv_sqrt_ref((float)HD);
+    const float *K = L.kc + (size_t)g * d.max_ctx * HD;
+    const float4 *q4 = reinterpret_cast<const float4 *>(q);
+    for (int p = tid; p < np; p += HD) {
+        const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)p * HD);
+        float c[16];
+#pragma unroll
+        for (int l = 0; l < 16; l++) c[l] = 0.0f;
+#pragma unroll 4
+        for (int i = 0; i < HD / 16; i++) {
+            const float4 k0 = __ldg(kr + 4 * i), k1 = __ldg(kr + 4 * i + 1);
+            const float4 k2 = __ldg(kr + 4 * i + 2), k3 = __ldg(kr + 4 * i + 3);
+            const float4 a0 = q4[4 * i], a1 = q4[4 * i + 1], a2 = q4[4 * i + 2], a3 = q4[4 * i + 3];
+            c[0] = madd(c[0], a0.x, k0.x); c[1] = madd(c[1], a0.y, k0.y);
+            c[2] = madd(c[2], a0.z, k0.z); c[3] = madd(c[3], a0.w, k0.w);
+            c[4] = madd(c[4], a1.x, k1.x); c[5] = madd(c[5], a1.y, k1.y);
+            c[6] = madd(c[6], a1.z, k1.z); c[7] = madd(c[7], a1.w, k1.w);
+            c[8] = madd(c[8], a2.x, k2.x); c[9] = madd(c[9], a2.y, k2.y);
+            c[10] = madd(c[10], a2.z, k2.z); c[11] = madd(c[11], a2.w, k2.w);
+            c[12] = madd(c[12], a3.x, k3.x); c[13] = madd(c[13], a3.y, k3.y);
+            c[14] = madd(c[14], a3.z, k3.z); c[15] = madd(c[15], a3.w, k3.w);
+        }
+        float hh[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            hh[k] = __fadd_rn(__fadd_rn(c[4 * k], c[4 * k + 1]), __fadd_rn(c[4 * k + 2], c[4 * k + 3]));
+        const float s = __fadd_rn(__fadd_rn(hh[0], hh[1]), __fadd_rn(hh[2], hh[3]));
+        att[p] = __fmul_rn(__fadd_rn(s, 0.0f), scale);
+    }
+    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5, nw = HD >> 5;
+    float m = -INFINITY;
+    for (int p = tid; p < np; p += HD) m = fmaxf(m, att[p]);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid < 32) {
+        float mm = tid < nw ? red[tid] : -INFINITY;
+        for (int o = 16; o; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        if (tid == 0) s_mx = mm;
+    }
+    __syncthreads();
+    const float mx = s_mx;
+    for (int p = tid; p < np; p += HD) att[p] = pf_expf(__fadd_rn(att[p], -mx));
+    __syncthreads();
+    if (tid < 32) {
+        const float sum = sum4_ref(att, np);
+        if (tid == 0) s_inv = __fdiv_rn(1.0f, sum);
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    for (int p = tid; p < np; p += HD) att[p] = __fmul_rn(att[p], inv);
+    __syncthreads();
+    float o = 0.0f;
+    for (int gi = 0; gi < ngroups; gi++) {
+        cp_async_wait<kVRing / kVGroup - 1>();
+        const int j0 = gi * kVGroup;
+        float *slot = vring + (size_t)(j0 % kVRing) * HD + tid;
+        float v[kVGroup];
+#pragma unroll
+        for (int r = 0; r < kVGroup; r++) v[r] = slot[(size_t)r * HD];
+#pragma unroll
+        for (int r = 0; r < kVGroup; r++)
+            if (j0 + r < np) o = madd(o, att[j0 + r], v[r]);
+        const int jn = j0 + kVRing;
+#pragma unroll
+        for (int r = 0; r < kVGroup; r++)
+            if (jn + r < np) cp_async4(slot + (size_t)r * HD, V + (size_t)(jn + r) * HD);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    const float gate = y[(size_t)t * d.ldy + (size_t)2 * HD * h + HD + tid];
+    o = __fmul_rn(o, pf_sigmoid(gate));
+    const int col = h * HD + tid, nbo = out.cols >> 5;
+    quant_block_warp(o, lane, out.q + (size_t)t * out.cols + (col & ~31),
+                     out.d + (size_t)t * nbo + (col >> 5), out.fs + (size_t)t * nbo + (col >> 5));
+}
+
+size_t attn2_smem(int max_ctx) {
+    return sizeof(float) * ((size_t)kAttnHd + ((max_ctx + 3) & ~3) + (size_t)kVRing * kAttnHd);
+}
+
+// Gated DeltaNet layer, latency-oriented form of k_deltanet with identical per-element
+// arithmetic (same citations). Differences are scheduling only:
+//  - one cp.async batch brings this key head's q / k / v / z / b / a rows of every token into
+//    shared memory while the 64 KB state column loads into registers;
+//  - the conv runs with its taps in registers (conv_k == KC);
+//  - the deferred-commit replay is folded into token 0's first sweep (kern_lin.c replay_first,
+//    :42-62: per element the same operations in the same order), and token t's second sweep
+//    (S += k delta; o += S q) runs in the same loop as token t+1's first sweep (S *= decay;
+//    kv += S k), two independent add chains per iteration.
+// rep == 1 only (one value head per key head, every Qwen3.5 size); KC taps.
+constexpr int kMaxReplay = 8;   // a verify pass holds at most PINFER_SPEC_MAX_K + 1 rows
+
+template <int KC>
+__global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, LibmTables T,
+                                                      const float *y, Step *st, Act out) {
+    constexpr int S = KC - 1;
+    const int n = st->n;
+    if (n <= 0) return;
+    const int logged = st->logged, pend_keep = st->pend_keep, pend_conv = st->pend_conv;
+    const int wr = st->wr;
+    const int h = blockIdx.x, j = threadIdx.x;
+    const int C = d.C;
+    __shared__ __align__(16) float sq[kMaxRows][kDK], sk[kMaxRows][kDK], sv[kMaxRows][kDV];
+    __shared__ __align__(16) float sz[kMaxRows][kDV], so[kMaxRows][kDV];
+    __shared__ float sb[kMaxRows], sa[kMaxRows], sbeta[kMaxRows], sdec[kMaxRows], srn[kMaxRows];
+    __shared__ __align__(16) float skp[kMaxReplay][kDK];
+    __shared__ float spd[kMaxReplay];
+    extern __shared__ __align__(16) float Ssm[];   // [kDK][kDV]: this head's state, row-major
+    const size_t logw = (size_t)kDK + kDV + 1;
+
+    // ---- prefetch: activations of every token (cp.async), replay log rows, state column
+    for (int t = 0; t < n; t++) {
+        const float *yr = y + (size_t)t * d.ldy;
+        cp_async4(&sq[t][j], yr + h * kDK + j);
+        cp_async4(&sk[t][j], yr + d.kd + h * kDK + j);
+        cp_async4(&sv[t][j], yr + 2 * d.kd + h * kDV + j);
+        cp_async4(&sz[t][j], yr + C + h * kDV + j);
+        if (j == 0) cp_async4(&sb[t], yr + C + d.vd + h);
+        if (j == 1) cp_async4(&sa[t], yr + C + d.vd + d.nv + h);
+    }
+    cp_async_commit();
+    float dl[kMaxReplay];
+    for (int tp = 1; tp <= pend_keep && tp <= kMaxReplay; tp++) {   // deferred commit: rows 1..keep of half wr^1
+        const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp) * d.nv + h) * logw;
+        skp[tp - 1][j] = u[j];
+        dl[tp - 1] = u[kDK + j];
+        if (j == 0) spd[tp - 1] = u[kDK + kDV];
+    }
+    const float *rec_h = L.rec + (size_t)h * kDK * kDV;
+    for (int i4 = j * 4; i4 < kDK * kDV; i4 += 128 * 4)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Ssm + i4)), "l"(rec_h + i4) : "memory");
+    cp_async_commit();
+    float *rec = L.rec + (size_t)h * kDK * kDV + j;
+    float *Sj = Ssm + j;   // column j: Sj[i * kDV]
+    // conv state / taps of this thread's three channels (q, k, v column j of this head)
+    const int chan[3] = {h * kDK + j, d.kd + h * kDK + j, 2 * d.kd + h * kDV + j};
+    float cst[3][S > 0 ? S : 1], cw[3][KC];
+#pragma unroll
+    for (int c3 = 0; c3 < 3; c3++) {
+#pragma unroll
+        for (int r = 0; r < S; r++) cst[c3][r] = L.conv_state[(size_t)r * C + chan[c3]];
+#pragma unroll
+        for (int r = 0; r < KC; r++) cw[c3][r] = L.conv_w[(size_t)chan[c3] * KC + r];
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- gates (thread t < n)
+    if (j < n) {
+        const float b = sb[j], a = sa[j];
+        sbeta[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(T, -b)));
+        const float xs = __fadd_rn(a, L.dt_bias[h]);
+        const float sp = xs > 20.0f ? xs : glibc_log1pf(T, glibc_expf(T, xs));
+        sdec[j] = glibc_expf(T, __fmul_rn(L.A[h], sp));
+    }
+    // ---- pending conv commit, then conv + SiLU for the three channels
+#pragma unroll
+    for (int c3 = 0; c3 < 3; c3++) {
+        float (&stt)[S > 0 ? S : 1] = cst[c3];
+        const int c = chan[c3];
+        if (pend_conv > 1) {
+            const int e1 = pend_conv - 1;
+            float ns[S > 0 ? S : 1];
+#pragma unroll
+            for (int r = 0; r < S; r++) {
+                const int src = r + e1;
+                ns[r] = src < S ? stt[src < S ? src : 0] : L.xin[(size_t)(src - S + 1) * C + c];
+            }
+#pragma unroll
+            for (int r = 0; r < S; r++) stt[r] = ns[r];
+        }
+        float (*dst)[kDK] = c3 == 0 ? sq : (c3 == 1 ? sk : sv);
+        float live[S > 0 ? S : 1];
+        for (int t = 0; t < n; t++) {
+            const float xc = dst[t][j];
+            float acc = __fmul_rn(cw[c3][0], S > 0 ? stt[0] : xc);
+#pragma unroll
+            for (int r = 1; r < KC; r++) acc = madd(acc, cw[c3][r], r < S ? stt[r < S ? r : 0] : xc);
+#pragma unroll
+            for (int r = 0; r + 1 < S; r++) stt[r] = stt[r + 1];
+            if (S > 0) stt[S - 1] = xc;
+            dst[t][j] = pf_silu(acc);
+            if (logged) {
+                if (t == 0) {
+#pragma unroll
+                    for (int r = 0; r < S; r++) live[r] = stt[r];
+                } else {
+                    L.xin[(size_t)t * C + c] = xc;
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < S; r++) L.conv_state[(size_t)r * C + c] = logged ? live[r] : stt[r];
+    }
+    __syncthreads();
+    // ---- L2 norm of q and k: 4 lanes per (token, vector)
+    {
+        const int lane = j & 31, warp = j >> 5;
+        const float qscale = inv_sqrt_ref((float)kDK);
+        for (int u0 = warp * 8; u0 < 2 * n; u0 += 4 * 8) {
+            const int u = u0 + (lane >> 2), l = lane & 3;
+            const bool act = u < 2 * n;
+            float *vec = act ? ((u & 1) ? sk[u >> 1] : sq[u >> 1]) : sq[0];
+            float c = 0.0f;
+            if (act) {
+#pragma unroll 8
+                for (int i = l; i < kDK; i += 4) c = madd(c, vec[i], vec[i]);
+            }
+            const int base = lane & ~3;
+            const float c0 = __shfl_sync(0xffffffffu, c, base), c1 = __shfl_sync(0xffffffffu, c, base + 1);
+            const float c2 = __shfl_sync(0xffffffffu, c, base + 2), c3 = __shfl_sync(0xffffffffu, c, base + 3);
+            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+            const float r = inv_sqrt_ref(__fadd_rn(ss, 1e-6f));
+            __syncwarp();
+            if (act) {
+                const float sc = (u & 1) ? 1.0f : qscale;
+                for (int i = l; i < kDK; i += 4) vec[i] = __fmul_rn(__fmul_rn(vec[i], r), sc);
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- recurrence: replay + token 0 first sweep, then fused sweeps (column j in smem)
+    float kv = 0.0f;
+    {
+        const float dec = sdec[0];
+        const float *k0 = sk[0];
+        const int keep = pend_keep < kMaxReplay ? pend_keep : kMaxReplay;
+#pragma unroll 4
+        for (int i = 0; i < kDK; i++) {
+            float sv_ = Sj[i * kDV];
+            for (int tp = 0; tp < keep; tp++)
+                sv_ = __fadd_rn(__fmul_rn(sv_, spd[tp]), __fmul_rn(skp[tp][i], dl[tp]));
+            sv_ = __fmul_rn(sv_, dec);
+            Sj[i * kDV] = sv_;
+            kv = madd(kv, sv_, k0[i]);
+        }
+    }
+    for (int t = 0; t < n; t++) {
+        const float delta = __fmul_rn(__fadd_rn(sv[t][j], -kv), sbeta[t]);
+        const float *kt = sk[t], *qt = sq[t];
+        float o = 0.0f, kvn = 0.0f;
+        const bool next = t + 1 < n;
+        const float decn = next ? sdec[t + 1] : 0.0f;
+        const float *kn = sk[next ? t + 1 : t];
+        const bool store_live = logged && t == 0;
+        if (next) {
+#pragma unroll 4
+            for (int i = 0; i < kDK; i++) {
+                float sv_ = __fadd_rn(Sj[i * kDV], __fmul_rn(kt[i], delta));
+                o = madd(o, sv_, qt[i]);
+                if (store_live) rec[(size_t)i * kDV] = sv_;
+                sv_ = __fmul_rn(sv_, decn);
+                kvn = madd(kvn, sv_, kn[i]);
+                Sj[i * kDV] = sv_;
+            }
+        } else {
+#pragma unroll 4
+            for (int i = 0; i < kDK; i++) {
+                const float sv_ = __fadd_rn(Sj[i * kDV], __fmul_rn(kt[i], delta));
+                o = madd(o, sv_, qt[i]);
+                Sj[i * kDV] = sv_;
+                if (store_live || !logged) rec[(size_t)i * kDV] = sv_;
+            }
+        }
+        so[t][j] = o;
+        if (logged && t > 0) {
+            float *u = L.upd + (((size_t)wr * d.cap + t) * d.nv + h) * logw;
+            u[kDK + j] = delta;
+            u[j] = kt[j];
+            if (j == 0) u[kDK + kDV] = sdec[t];
+        }
+        kv = kvn;
+    }
+    __syncthreads();
+
+    // ---- gated RMSNorm and A8
+    {
+        const int lane = j & 31, warp = j >> 5;
+        for (int u0 = warp * 8; u0 < n; u0 += 4 * 8) {
+            const int u = u0 + (lane >> 2), l = lane & 3;
+            const bool act = u < n;
+            const float *vec = so[act ? u : 0];
+            float c = 0.0f;
+            if (act) {
+#pragma unroll 8
+                for (int i = l; i < kDV; i += 4) c = madd(c, vec[i], vec[i]);
+            }
+            const int base = lane & ~3;
+            const float c0 = __shfl_sync(0xffffffffu, c, base), c1 = __shfl_sync(0xffffffffu, c, base + 1);
+            const float c2 = __shfl_sync(0xffffffffu, c, base + 2), c3 = __shfl_sync(0xffffffffu, c, base + 3);
+            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+            if (act && l == 0) srn[u] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)kDV), d.eps));
+        }
+    }
+    __syncthreads();
+    {
+        const int lane = j & 31, warp = j >> 5, nbo = out.cols >> 5;
+        const float w = L.norm_w[j];
+        for (int t = 0; t < n; t++) {
+            float v = __fmul_rn(__fmul_rn(so[t][j], srn[t]), w);
+            v = __fmul_rn(v, pf_silu(sz[t][j]));
+            const int col = h * kDV + j;
+            quant_block_warp(v, lane, out.q + (size_t)t * out.cols + (col & ~31),
+                             out.d + (size_t)t * nbo + (col >> 5), out.fs + (size_t)t * nbo + (col >> 5));
+            (void)warp;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ generation control
 // splitmix64 output function and the synthetic drafter of the benchmark: the draft for output
 // index j is, with probability p24 / 2^24, the target's greedy token greedy[j], else a uniform
@@ -1218,50 +1695,101 @@ int num_sms() {
     return sms;
 }
 
-template <int NMAX>
-void head_t2(const Mat &W, Act in, const Step *st, float *y, int ldy, unsigned long long *partial,
-             int *nan0, cudaStream_t s) {
-    const int grid = std::min(2 * num_sms(), (W.npanels + kTallWarps - 1) / kTallWarps);
-    k_mv_head<NMAX><<<std::max(grid, 1), kTallWarps * 32, tall_smem(W.cols, NMAX), s>>>(
-        W, in, const_cast<Step *>(st), y, ldy, partial, nan0);
+// The per-block shared memory opt-in limit of sm_100 (static + dynamic).
+constexpr int kSmemOptin = 227 * 1024;
+
+// The largest dynamic shared memory a kernel may launch with: the opt-in limit less its static
+// __shared__ arrays.
+template <class K>
+int dyn_smem_limit(K kern) {
+    cudaFuncAttributes a{};
+    if (cudaFuncGetAttributes(&a, kern) != cudaSuccess) return 0;
+    return kSmemOptin - (int)a.sharedSizeBytes;
 }
 
-template <int NMAX, int EPI>
-bool panel_t(const Mat &W0, const Mat &W1, Act in, const Step *st, float *y, int ldy, Act out,
-             cudaStream_t s) {
+template <class K>
+void raise_smem(K kern, size_t want = 0) {
+    const int lim = dyn_smem_limit(kern);
+    const int v = want ? (int)std::min<size_t>(want, (size_t)std::max(lim, 0)) : lim;
+    if (v > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+}
+
+template <int NMAX, bool NORM>
+void head_t2(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int ldy,
+             unsigned long long *partial, int *nan0, cudaStream_t s) {
+    const int grid = std::min(2 * num_sms(), (W.npanels + kTallWarps - 1) / kTallWarps);
+    k_mv_head<NMAX, NORM><<<std::max(grid, 1), kTallWarps * 32, tall_smem(W.cols, NMAX, NORM), s>>>(
+        W, in, nin, const_cast<Step *>(st), y, ldy, partial, nan0);
+}
+
+template <int NMAX, int EPI, bool NORM>
+bool panel_t(const Mat &W0, const Mat &W1, Act in, NormIn nin, const Step *st, float *y, int ldy,
+             Act out, cudaStream_t s) {
     const int nmat = EPI == 3 ? 2 : 1;
     const int nw = std::min(W0.nsb * nmat, kPanelWarps);
-    const size_t sm = panel_smem(nw, W0.cols / 32, nmat, NMAX);
-    if (sm > 227 * 1024) return false;
-    k_mv_panel<NMAX, EPI><<<W0.npanels, nw * 32, sm, s>>>(W0, W1, in, const_cast<Step *>(st), y, ldy, out);
+    const size_t sm = panel_smem(nw, W0.cols, nmat, NMAX, NORM);
+    static const int lim = dyn_smem_limit(k_mv_panel<NMAX, EPI, NORM>);
+    if (sm > (size_t)lim) return false;
+    k_mv_panel<NMAX, EPI, NORM><<<W0.npanels, nw * 32, sm, s>>>(W0, W1, in, nin, const_cast<Step *>(st),
+                                                                y, ldy, out);
     return true;
 }
 
 void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode, int nmax,
                    cudaStream_t s) {
     Act none;
+    NormIn nn{};
     bool done = false;
-    if (nmax <= 1) done = mode ? panel_t<1, 1>(W, W, in, st, y, ldy, none, s) : panel_t<1, 0>(W, W, in, st, y, ldy, none, s);
-    else if (nmax <= 4) done = mode ? panel_t<4, 1>(W, W, in, st, y, ldy, none, s) : panel_t<4, 0>(W, W, in, st, y, ldy, none, s);
+    if (nmax <= 1) done = mode ? panel_t<1, 1, false>(W, W, in, nn, st, y, ldy, none, s) : panel_t<1, 0, false>(W, W, in, nn, st, y, ldy, none, s);
+    else if (nmax <= 4) done = mode ? panel_t<4, 1, false>(W, W, in, nn, st, y, ldy, none, s) : panel_t<4, 0, false>(W, W, in, nn, st, y, ldy, none, s);
     if (!done) launch_matvec_chunked(W, in, st, y, ldy, mode, nmax, s);
 }
-void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Act out, int nmax,
-                          cudaStream_t s) {
+
+void launch_matvec_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
+                        float *y, int ldy, int nmax, Act scratch, cudaStream_t s) {
+    Act none;
+    const NormIn nin{x, w, eps};
     bool done = false;
-    if (nmax <= 1) done = panel_t<1, 3>(G, U, in, st, nullptr, 0, out, s);
-    else if (nmax <= 4) done = panel_t<4, 3>(G, U, in, st, nullptr, 0, out, s);
+    if (nmax <= 1) done = panel_t<1, 0, true>(W, W, none, nin, st, y, ldy, none, s);
+    else if (nmax <= 4) done = panel_t<4, 0, true>(W, W, none, nin, st, y, ldy, none, s);
     if (done) return;
-    if (nmax <= 1) swiglu_t<1>(G, U, in, st, out, s);
-    else if (nmax <= 4) swiglu_t<4>(G, U, in, st, out, s);
-    else if (nmax <= 8) swiglu_t<8>(G, U, in, st, out, s);
-    else swiglu_t<16>(G, U, in, st, out, s);
+    launch_norm_quant(x, w, W.cols, eps, st, scratch, s);
+    launch_matvec_chunked(W, scratch, st, y, ldy, 0, nmax, s);
 }
+
+void launch_matvec_swiglu_norm(const Mat &G, const Mat &U, const float *x, const float *w, float eps,
+                               const Step *st, Act out, int nmax, Act scratch, cudaStream_t s) {
+    Act none;
+    const NormIn nin{x, w, eps};
+    bool done = false;
+    if (nmax <= 1) done = panel_t<1, 3, true>(G, U, none, nin, st, nullptr, 0, out, s);
+    else if (nmax <= 4) done = panel_t<4, 3, true>(G, U, none, nin, st, nullptr, 0, out, s);
+    if (done) return;
+    launch_norm_quant(x, w, G.cols, eps, st, scratch, s);
+    if (nmax <= 1) swiglu_t<1>(G, U, scratch, st, out, s);
+    else if (nmax <= 4) swiglu_t<4>(G, U, scratch, st, out, s);
+    else if (nmax <= 8) swiglu_t<8>(G, U, scratch, st, out, s);
+    else swiglu_t<16>(G, U, scratch, st, out, s);
+}
+
 void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int ld,
                         unsigned long long *partial, int *nan0, int nmax, cudaStream_t s) {
-    if (nmax <= 1) head_t2<1>(W, in, st, logits, ld, partial, nan0, s);
-    else if (nmax <= 4) head_t2<4>(W, in, st, logits, ld, partial, nan0, s);
-    else if (nmax <= 8) head_t2<8>(W, in, st, logits, ld, partial, nan0, s);
-    else head_t2<16>(W, in, st, logits, ld, partial, nan0, s);
+    const NormIn nn{};
+    if (nmax <= 1) head_t2<1, false>(W, in, nn, st, logits, ld, partial, nan0, s);
+    else if (nmax <= 4) head_t2<4, false>(W, in, nn, st, logits, ld, partial, nan0, s);
+    else if (nmax <= 8) head_t2<8, false>(W, in, nn, st, logits, ld, partial, nan0, s);
+    else head_t2<16, false>(W, in, nn, st, logits, ld, partial, nan0, s);
+}
+
+void launch_matvec_head_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
+                             float *logits, int ld, unsigned long long *partial, int *nan0, int nmax,
+                             cudaStream_t s) {
+    const NormIn nin{x, w, eps};
+    const Act none;
+    if (nmax <= 1) head_t2<1, true>(W, none, nin, st, logits, ld, partial, nan0, s);
+    else if (nmax <= 4) head_t2<4, true>(W, none, nin, st, logits, ld, partial, nan0, s);
+    else if (nmax <= 8) head_t2<8, true>(W, none, nin, st, logits, ld, partial, nan0, s);
+    else head_t2<16, true>(W, none, nin, st, logits, ld, partial, nan0, s);
 }
 // The first-generation kernel (chunked shared-memory chains, any shape) stays available for
 // the kernel-level ABI's reference timing.
@@ -1281,7 +1809,7 @@ void launch_embed(const Mat &E, const Step *st, float *x, int H, cudaStream_t s)
 }
 void launch_norm_quant(const float *x, const float *w, int H, float eps, const Step *st, Act out,
                        cudaStream_t s) {
-    k_norm_quant<<<kMaxRows, 256, (size_t)H * sizeof(float), s>>>(x, w, H, eps, st, out);
+    k_norm_quant<<<kMaxRows, 256, 2 * (size_t)H * sizeof(float), s>>>(x, w, H, eps, st, out);
 }
 void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s) {
     const int warps = n * (cols / 32);
@@ -1289,10 +1817,14 @@ void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s) 
 }
 size_t deltanet_smem(int rep) {
     return sizeof(float) * ((size_t)kMaxRows * kDK * 2 + (size_t)kMaxRows * rep * kDV * 2 +
-                            (size_t)kMaxRows * rep * 3 + (size_t)kDK + 8);
+                            (size_t)kMaxRows * rep * 3 + (size_t)kMaxRows * kDK + kMaxRows + 8);
 }
 void launch_deltanet(const LinLayer &L, const LinDims &d, const LibmTables &T, const float *y,
                      Step *st, Act out, cudaStream_t s) {
+    if (d.rep == 1 && d.K == 4 && d.dk == kDK && d.dv == kDV) {
+        k_deltanet2<4><<<d.nk, kDV, sizeof(float) * kDK * kDV, s>>>(L, d, T, y, st, out);
+        return;
+    }
     const size_t sm = deltanet_smem(d.rep);
     k_deltanet<<<d.nk, kDV, sm, s>>>(L, d, T, y, st, out);
 }
@@ -1302,6 +1834,11 @@ void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, flo
 }
 void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
                  const Step *st, Act out, cudaStream_t s) {
+    static const int attn2_lim = dyn_smem_limit(k_attn2);
+    if (d.hd == kAttnHd && attn2_smem(d.max_ctx) <= (size_t)attn2_lim) {
+        k_attn2<<<dim3(kMaxRows, d.nq), kAttnHd, attn2_smem(d.max_ctx), s>>>(L, d, y, qbuf, st, out);
+        return;
+    }
     const size_t sm = ((size_t)d.hd + d.max_ctx) * sizeof(float);
     k_attn<<<dim3(kMaxRows, d.nq), d.hd, sm, s>>>(L, d, y, qbuf, st, out);
 }
@@ -1327,37 +1864,49 @@ void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, c
     k_set_pass<<<1, 1, 0, s>>>(st, a);
 }
 void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s) { k_set_gen<<<1, 1, 0, s>>>(st, g); }
-void kernels_init(int max_ctx, int hd, int rep) {
+int kernels_init(int max_ctx, int hd, int rep) {
     // raise the dynamic shared memory limits once, outside any stream capture
-    cudaFuncSetAttribute(k_matvec<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<1>());
-    cudaFuncSetAttribute(k_matvec<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<1>());
-    cudaFuncSetAttribute(k_matvec<4, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
-    cudaFuncSetAttribute(k_matvec<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
-    cudaFuncSetAttribute(k_matvec<8, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
-    cudaFuncSetAttribute(k_matvec<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
-    cudaFuncSetAttribute(k_matvec<16, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
-    cudaFuncSetAttribute(k_matvec<16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
-    cudaFuncSetAttribute(k_matvec_swiglu<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<1>());
-    cudaFuncSetAttribute(k_matvec_swiglu<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
-    cudaFuncSetAttribute(k_matvec_swiglu<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
-    cudaFuncSetAttribute(k_matvec_swiglu<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
-    cudaFuncSetAttribute(k_matvec_head<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<1>());
-    cudaFuncSetAttribute(k_matvec_head<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<4>());
-    cudaFuncSetAttribute(k_matvec_head<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<8>());
-    cudaFuncSetAttribute(k_matvec_head<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mv_smem<16>());
-    cudaFuncSetAttribute(k_mv_head<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_head<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_head<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_head<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_panel<1, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_panel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_panel<1, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_panel<4, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_panel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_mv_panel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (max_ctx <= 0) return;   // matvec kernels only (kernel-level ABI)
-    cudaFuncSetAttribute(k_deltanet, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)deltanet_smem(rep));
-    cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(((size_t)hd + max_ctx) * sizeof(float)));
+    raise_smem(k_matvec<1, 0>, mv_smem<1>());
+    raise_smem(k_matvec<1, 1>, mv_smem<1>());
+    raise_smem(k_matvec<4, 0>, mv_smem<4>());
+    raise_smem(k_matvec<4, 1>, mv_smem<4>());
+    raise_smem(k_matvec<8, 0>, mv_smem<8>());
+    raise_smem(k_matvec<8, 1>, mv_smem<8>());
+    raise_smem(k_matvec<16, 0>, mv_smem<16>());
+    raise_smem(k_matvec<16, 1>, mv_smem<16>());
+    raise_smem(k_matvec_swiglu<1>, mv_smem<1>());
+    raise_smem(k_matvec_swiglu<4>, mv_smem<4>());
+    raise_smem(k_matvec_swiglu<8>, mv_smem<8>());
+    raise_smem(k_matvec_swiglu<16>, mv_smem<16>());
+    raise_smem(k_matvec_head<1>, mv_smem<1>());
+    raise_smem(k_matvec_head<4>, mv_smem<4>());
+    raise_smem(k_matvec_head<8>, mv_smem<8>());
+    raise_smem(k_matvec_head<16>, mv_smem<16>());
+    raise_smem(k_mv_head<1, false>);
+    raise_smem(k_mv_head<1, true>);
+    raise_smem(k_mv_head<4, false>);
+    raise_smem(k_mv_head<4, true>);
+    raise_smem(k_mv_head<8, false>);
+    raise_smem(k_mv_head<8, true>);
+    raise_smem(k_mv_head<16, false>);
+    raise_smem(k_mv_head<16, true>);
+    raise_smem(k_mv_panel<1, 0, false>);
+    raise_smem(k_mv_panel<1, 1, false>);
+    raise_smem(k_mv_panel<1, 3, false>);
+    raise_smem(k_mv_panel<1, 0, true>);
+    raise_smem(k_mv_panel<1, 3, true>);
+    raise_smem(k_mv_panel<4, 0, false>);
+    raise_smem(k_mv_panel<4, 1, false>);
+    raise_smem(k_mv_panel<4, 3, false>);
+    raise_smem(k_mv_panel<4, 0, true>);
+    raise_smem(k_mv_panel<4, 3, true>);
+    if (max_ctx > 0) {
+        raise_smem(k_deltanet2<4>, sizeof(float) * kDK * kDV);
+        raise_smem(k_deltanet, deltanet_smem(rep));
+        raise_smem(k_attn, ((size_t)hd + max_ctx) * sizeof(float));
+        raise_smem(k_attn2, attn2_smem(max_ctx));
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace nb
