@@ -83,6 +83,25 @@ int nb_mv_run(nb_mv *h, const void *W, const float *X, float *Y, void *stream);
 /* Copy the scratch activations out (device buffers: q [n][cols] int8, d / fsum [n][cols/32]). */
 int nb_mv_get_act(nb_mv *h, int8_t *q, float *d, float *fsum, void *stream);
 
+/* Allocation-free Q4K x A8 matmul. No counterpart in the reference (its CPU pf_matmul takes
+ * caller buffers and needs no scratch).
+ * Y [n][rows] = W (device panel layout) x A8(X [n][cols]), the same kernels and the same
+ * bit-exact result as nb_mv_create(rows, cols, n) + nb_mv_set_n + nb_mv_run, but the scratch
+ * (A8 activations and the control block) lives in a fixed array inside the library's device
+ * image, so the call performs no cudaMalloc / cudaFree and calls no allocating library routine.
+ * Meant for hosts that must not allocate device memory while they call it (their own allocator
+ * holds the device's memory, or they cannot take an allocation's device-wide sync).
+ * Limits: n <= NB_MV_STATIC_MAX_N, cols <= NB_MV_STATIC_MAX_COLS; larger sizes return -4 and
+ * set pinfer_b200_last_error. The first call on each device does setup (looks up the scratch's
+ * device address with that device current and sets the kernels' shared-memory limits) and
+ * should come before any stream capture. One scratch per device: calls that overlap in time on
+ * one device (other streams or threads) race on it and must be serialised by the caller.
+ * 0, -4 (arguments), -3 (CUDA error). */
+#define NB_MV_STATIC_MAX_N 16
+#define NB_MV_STATIC_MAX_COLS 8192
+int nb_mv_run_static(const void *W, int rows, int cols, const float *X, int n, float *Y,
+                     void *stream);
+
 #ifdef __cplusplus
 }
 #endif

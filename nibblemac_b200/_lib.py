@@ -119,7 +119,9 @@ _OPTIONAL = {
                                  ctypes.c_void_p]),
     "nb_mv_get_act": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                      ctypes.c_void_p, ctypes.c_void_p]),
-    "nb_libm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_longlong,
+    "nb_mv_run_static": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                        ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "nb_libm_selftest":(ctypes.c_int, [ctypes.c_int, ctypes.c_longlong,
                                         ctypes.POINTER(ctypes.c_longlong)]),
 }
 

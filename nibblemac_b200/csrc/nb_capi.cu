@@ -1,12 +1,72 @@
 // Kernel-level C ABI of the Q4K x A8 matmul (include/nb_b200.h): the pf_matmul contract on
 // device buffers, for the parity tests and the matvec benchmark.
+#include <atomic>
+#include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include "nb_b200.h"
 #include "nb_engine.h"
 
 using namespace nb;
+
+// ------------------------------------------------------------------ allocation-free scratch
+// nb_mv_run_static keeps its scratch in this array of the library's own device image instead of
+// cudaMalloc'd buffers. Layout: [Step control block, padded to 256 B][A8 codes q: 16 x 8192
+// int8][block scales d: 16 x 256 fp32][block sums fsum: 16 x 256 fp32], 164,096 bytes per device.
+namespace {
+constexpr int kStaticMaxCols = NB_MV_STATIC_MAX_COLS;
+constexpr int kStaticMaxN = NB_MV_STATIC_MAX_N;
+static_assert(kStaticMaxN == kMaxRows, "the static scratch holds one full pass of vectors");
+static_assert(kStaticMaxCols % 256 == 0, "whole Q4K superblocks");
+constexpr size_t kStaticQOff = (sizeof(Step) + 255) & ~(size_t)255;
+constexpr size_t kStaticQBytes = (size_t)kStaticMaxN * kStaticMaxCols;
+constexpr size_t kStaticDOff = kStaticQOff + kStaticQBytes;
+constexpr size_t kStaticDBytes = sizeof(float) * kStaticMaxN * (kStaticMaxCols / 32);
+constexpr size_t kStaticFsOff = kStaticDOff + kStaticDBytes;
+constexpr size_t kStaticBytes = kStaticFsOff + kStaticDBytes;
+constexpr int kStaticMaxDevices = 64;
+
+std::mutex g_static_mu;
+std::atomic<unsigned char *> g_static_addr[kStaticMaxDevices];
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_mv_static_scratch[kStaticBytes];
+
+namespace {
+// The scratch's address on the current device. The first call on a device looks the symbol up
+// (which makes the runtime load this library's device image there if it has not yet) and raises
+// the matvec kernels' shared-memory limits on that device; later calls read the cached pointer.
+unsigned char *static_scratch() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kStaticMaxDevices) {
+        set_last_error("nb_mv_run_static: no current CUDA device (or device index >= 64)");
+        return nullptr;
+    }
+    unsigned char *p = g_static_addr[dev].load(std::memory_order_acquire);
+    if (p) return p;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    p = g_static_addr[dev].load(std::memory_order_relaxed);
+    if (p) return p;
+    void *addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, g_mv_static_scratch);
+    if (e != cudaSuccess || !addr) {
+        char b[200];
+        snprintf(b, sizeof b, "nb_mv_run_static: cudaGetSymbolAddress failed on device %d: %s", dev,
+                 cudaGetErrorString(e));
+        set_last_error(b);
+        return nullptr;
+    }
+    if (kernels_init(0, 0, 0) != 0) {
+        set_last_error("nb_mv_run_static: raising the kernels' shared-memory limits failed");
+        return nullptr;
+    }
+    p = static_cast<unsigned char *>(addr);
+    g_static_addr[dev].store(p, std::memory_order_release);
+    return p;
+}
+}  // namespace
 
 struct nb_mv {
     int rows, cols, nmax, n;
@@ -133,6 +193,57 @@ int nb_mv_get_act(nb_mv *h, int8_t *q, float *d, float *fsum, void *stream) {
               cudaMemcpyAsync(d, h->act.d, nb * 4, cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
               cudaMemcpyAsync(fsum, h->act.fs, nb * 4, cudaMemcpyDeviceToDevice, s) == cudaSuccess;
     return ok ? PINFER_OK : PINFER_E_NOMEM;
+}
+
+// The nb_mv_create + nb_mv_set_n + nb_mv_run sequence without an allocation: same kernels, same
+// launches, scratch in g_mv_static_scratch. For callers that must not allocate device memory
+// during the call: a host whose own caching allocator has already reserved the device's memory
+// (a cudaMalloc from the side then fails or fragments that pool), and a host that cannot take
+// the device-wide synchronisation cudaMalloc / cudaFree imply while other streams run.
+// One scratch per device, so two calls in flight at the same time on one device (other
+// streams, other threads) race on it: the caller serialises them.
+int nb_mv_run_static(const void *W, int rows, int cols, const float *X, int n, float *Y,
+                     void *stream) {
+    if (!W || !X || !Y || !nb_q4k_panel_bytes(rows, cols) || n < 1) {
+        set_last_error("nb_mv_run_static: null buffer, n < 1, or rows / cols not multiples of 4 / 256");
+        return PINFER_E_ARG;
+    }
+    if (cols > kStaticMaxCols || n > kStaticMaxN) {
+        char b[200];
+        snprintf(b, sizeof b,
+                 "nb_mv_run_static: n=%d cols=%d exceed the static scratch (n <= %d, cols <= %d); "
+                 "use nb_mv_create", n, cols, kStaticMaxN, kStaticMaxCols);
+        set_last_error(b);
+        return PINFER_E_ARG;
+    }
+    unsigned char *base = static_scratch();
+    if (!base) return PINFER_E_NOMEM;
+    cudaStream_t s = (cudaStream_t)stream;
+    Step *step = reinterpret_cast<Step *>(base);
+    Act act;
+    act.q = reinterpret_cast<int8_t *>(base + kStaticQOff);
+    act.d = reinterpret_cast<float *>(base + kStaticDOff);
+    act.fs = reinterpret_cast<float *>(base + kStaticFsOff);
+    act.cols = cols;
+    // Step::status is the word a kernel sets when a bounded device wait gives up; it must read 0
+    // before the launches. The fields the kernels read (n, pos0, logged, tokens) are written by
+    // k_set_pass, and the A8 rows 0..n-1 by the quantiser, on every call, so nothing else needs
+    // clearing.
+    if (cudaMemsetAsync(&step->status, 0, sizeof(int), s) != cudaSuccess) {
+        set_last_error("nb_mv_run_static: clearing the status word failed");
+        return PINFER_E_NOMEM;
+    }
+    int tok[kMaxRows] = {0};
+    launch_set_pass(step, n, 0, 0, tok, s);
+    launch_quant_act(X, n, cols, act, s);
+    Mat m;
+    m.w = (const uint8_t *)W;
+    m.rows = rows;
+    m.cols = cols;
+    m.npanels = (rows + kPanelRows - 1) / kPanelRows;
+    m.nsb = cols / 256;
+    launch_matvec(m, act, step, Y, rows, 0, n, s);
+    return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
 }
 
 }  // extern "C"

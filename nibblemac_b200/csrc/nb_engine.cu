@@ -52,6 +52,8 @@ int host_threads() {
 // ---------------------------------------------------------------- panel repack
 namespace nb {
 
+void set_last_error(const char *msg) { set_err(msg); }
+
 size_t panel_bytes(int rows, int cols) {
     const size_t np = ((size_t)rows + kPanelRows - 1) / kPanelRows;
     return np * (size_t)(cols / 256) * kUnitBytes;

@@ -136,7 +136,9 @@ void launch_pass_end(Step *st, cudaStream_t s);
 size_t deltanet_smem(int rep);
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s);
 void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s);
-int kernels_init(int max_ctx, int hd, int rep);   // 0, or -1 if a CUDA call failed
+int kernels_init(int max_ctx, int hd, int rep);
+// Records the message pinfer_b200_last_error returns on this thread.
+void set_last_error(const char *msg);   // 0, or -1 if a CUDA call failed
 void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s);
 // small-n standalone entry points for the C-ABI kernel tests
 void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s);

@@ -1,0 +1,68 @@
+"""nb_mv_run_static, the allocation-free matmul entry point, through the C ABI.
+
+Collected last (file name) so that it also runs after every other test has used the device.
+Each case makes two calls in a row with different inputs and vector counts and compares both
+with the handle-based entry point (nb_mv_create / nb_mv_set_n / nb_mv_run) bit for bit, and
+with the CPU oracle.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+E_ARG = -4
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch
+    assert torch.cuda.is_available()
+    return torch
+
+
+def _bits(a: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+@pytest.mark.parametrize("rows,cols,ns", [(3584, 1024, (4, 1)), (256, 8192, (16, 3)),
+                                         (1024, 2048, (1, 7))])
+def test_static_matches_handle_api(lib, torch, q4k_oracle, rows, cols, ns):
+    w = q4k_oracle.kb_matrix(rows, cols, 42 + cols)
+    panels = np.zeros(lib.nb_q4k_panel_bytes(rows, cols), np.uint8)
+    assert lib.nb_q4k_repack(w.ctypes.data, rows, cols, panels.ctypes.data) == 0
+    dW = torch.from_numpy(panels).cuda()
+    stream = torch.cuda.current_stream().cuda_stream
+    h = lib.nb_mv_create(rows, cols, 16)
+    assert h, lib.last_error()
+    rng = np.random.default_rng(rows + cols)
+    try:
+        for call, n in enumerate(ns):
+            x = rng.standard_normal((n, cols)).astype(np.float32)
+            x[0, :32] = 0.0                          # an all-zero A8 block (amax == 0)
+            dX = torch.from_numpy(x).cuda()
+            y_handle = torch.full((n, rows), float("nan"), dtype=torch.float32, device="cuda")
+            y_static = torch.full((n, rows), float("nan"), dtype=torch.float32, device="cuda")
+            assert lib.nb_mv_set_n(h, n, stream) == 0
+            assert lib.nb_mv_run(h, dW.data_ptr(), dX.data_ptr(), y_handle.data_ptr(), stream) == 0
+            rc = lib.nb_mv_run_static(dW.data_ptr(), rows, cols, dX.data_ptr(), n, y_static.data_ptr(),
+                                      stream)
+            assert rc == 0, lib.last_error()
+            torch.cuda.synchronize()
+            a, b = y_handle.cpu().numpy(), y_static.cpu().numpy()
+            assert np.array_equal(_bits(a), _bits(b)), f"call {call}: static != handle entry point"
+            assert np.array_equal(_bits(b), _bits(q4k_oracle.matmul(w, rows, cols, x))), \
+                f"call {call}: static != oracle"
+    finally:
+        lib.nb_mv_destroy(h)
+
+
+def test_static_rejects_sizes_beyond_scratch(lib, torch):
+    buf = torch.zeros(16, dtype=torch.float32, device="cuda")
+    p = buf.data_ptr()
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.nb_mv_run_static(p, 256, 8192 + 256, p, 1, p, stream) == E_ARG
+    assert "static scratch" in lib.last_error()
+    assert lib.nb_mv_run_static(p, 256, 1024, p, 17, p, stream) == E_ARG
+    assert "static scratch" in lib.last_error()
+    assert lib.nb_mv_run_static(p, 256, 1000, p, 1, p, stream) == E_ARG
+    assert lib.nb_mv_run_static(None, 256, 1024, p, 1, p, stream) == E_ARG
