@@ -51,6 +51,36 @@ __device__ __forceinline__ void quant_block_warp(float x, int lane, int8_t *qdst
     }
 }
 
+// The same A8 of one 32-column block held by a group of 8 lanes, 4 consecutive columns per lane
+// (sub = lane & 7): max, division, rounding and code sum are order-independent, so the bits
+// match quant_block_warp. Four blocks per warp at a time, 3-step shuffles; every lane of the
+// warp must call it. qdst: the block's 32 codes; lane sub writes bytes 4 sub .. 4 sub + 3 and
+// sub 0 writes (d, fsum), unless store is false (a padding group).
+__device__ __forceinline__ void quant_block_oct(const float (&x)[4], int sub, bool store, int8_t *qdst,
+                                                float2 *df) {
+    float a = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+    const float id = a > 0.0f ? __fdiv_rn(127.0f, a) : 0.0f;
+    int sum = 0;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int q = __float2int_rn(__fmul_rn(x[i], id));
+        sum += q;
+        packed |= (uint32_t)(uint8_t)(int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q)) << (8 * i);
+    }
+    if (store) *reinterpret_cast<uint32_t *>(qdst + 4 * sub) = packed;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (store && sub == 0) {
+        const float d = __fdiv_rn(a, 127.0f);
+        *df = make_float2(d, __fmul_rn(d, (float)sum));
+    }
+}
+
 // Order-preserving key of a (logit, row) pair: larger logit wins, then the lower row, NaN
 // never wins (pf_argmax, engine/src/forward_ops.c:387-409: first maximum, NaN skipped).
 __device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
@@ -322,13 +352,18 @@ __device__ __forceinline__ void norm_quant_smem(const float *sx, const float *sw
         if (v < n && l == 0) srr[v] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)cols), eps));
     }
     __syncthreads();
-    const int nb = cols >> 5;
-    for (int u = warp; u < n * nb; u += nw) {
-        const int v = u / nb, b = u % nb, i = b * 32 + lane;
-        const float yv = __fmul_rn(__fmul_rn(sx[(size_t)v * cols + i], srr[v]), sw[i]);
-        float d, f;
-        quant_block_warp(yv, lane, sq + (size_t)v * cols + b * 32, &d, &f);
-        if (lane == 0) sdf[(size_t)v * nb + b] = make_float2(d, f);
+    const int nb = cols >> 5, sub = lane & 7;
+    // four blocks per warp per step; every lane of the warp takes part in the shuffles
+    for (int u0 = warp * 4; u0 < n * nb; u0 += nw * 4) {
+        const int u = u0 + (lane >> 3);
+        const bool act = u < n * nb;
+        const int v = act ? u / nb : 0, b = act ? u % nb : 0, i = b * 32 + 4 * sub;
+        const float4 xv = *reinterpret_cast<const float4 *>(sx + (size_t)v * cols + i);
+        const float4 wv = *reinterpret_cast<const float4 *>(sw + i);
+        const float r = srr[v];
+        const float x4[4] = {__fmul_rn(__fmul_rn(xv.x, r), wv.x), __fmul_rn(__fmul_rn(xv.y, r), wv.y),
+                             __fmul_rn(__fmul_rn(xv.z, r), wv.z), __fmul_rn(__fmul_rn(xv.w, r), wv.w)};
+        quant_block_oct(x4, sub, act, sq + (size_t)v * cols + b * 32, sdf + (size_t)v * nb + b);
     }
 }
 
@@ -1322,6 +1357,161 @@ size_t attn2_smem(int max_ctx) {
     return sizeof(float) * ((size_t)kAttnHd + ((max_ctx + 3) & ~3) + (size_t)kVRing * kAttnHd);
 }
 
+// ------------------------------------------------------------------ attention, one cluster per (token, head)
+// The same arithmetic as k_attn2 spread over a thread-block cluster of kAttnCL CTAs, so that one
+// (token, head) pair draws on kAttnCL SMs' L2 bandwidth instead of one:
+//   1. CTA c scores the positions of its slice [c per, (c + 1) per): 4 lanes per position, lane
+//      k4 holding the pf_dot partial sums 4 k4 .. 4 k4 + 3 (element 16 i + l feeds sum l), the
+//      tree of partial sums finished with quad shuffles (IEEE addition commutes, so every lane
+//      of the quad forms the identical value). Meanwhile CTA c's 32 output columns of V
+//      (rows 0..np-1) stream into its shared memory with cp.async.
+//   2. cluster barrier; every CTA gathers the np scores from the cluster's shared memory
+//      (distributed shared memory loads) and runs the reference softmax on its own copy:
+//      fmaxf max, pf_expf, sum4_ref, one division, scaling (identical code to k_attn2);
+//   3. warp 0 runs the ordered PV chain o += att[p] * V[p][col] for its 32 columns, gates it
+//      and A8-quantises the 32-column block (one block per CTA).
+// The whole cluster leaves together: t and pos are uniform over it, and every CTA waits on the
+// cluster barrier before exit so no peer reads shared memory that is gone.
+constexpr int kAttnCL = 8;
+constexpr int kAttnSlice = kAttnHd / kAttnCL;   // 32 output columns per CTA
+
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// a float of CTA `rank`'s shared memory at the offset of `local` in this CTA's
+__device__ __forceinline__ float ld_dsmem(const float *local, uint32_t rank) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+
+size_t attn3_smem(int max_ctx) {
+    const size_t per = ((size_t)max_ctx + kAttnCL - 1) / kAttnCL;
+    return sizeof(float) * ((size_t)kAttnHd + ((per + 3) & ~(size_t)3) + (((size_t)max_ctx + 3) & ~(size_t)3) +
+                            (size_t)max_ctx * kAttnSlice);
+}
+
+__global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
+    k_attn3(AttnLayer L, AttnDims d, const float *y, const float *qbuf, const Step *st, Act out) {
+    constexpr int HD = kAttnHd;
+    const int t = blockIdx.z, h = blockIdx.y, tid = threadIdx.x;
+    if (t >= st->n) return;                 // uniform over the cluster
+    const int pos = st->pos0 + t;
+    if (pos >= d.max_ctx) return;           // uniform over the cluster
+    const uint32_t c = cluster_rank();
+    const int np = pos + 1, g = h / (d.nq / d.nkv);
+    const int per = (d.max_ctx + kAttnCL - 1) / kAttnCL;
+    extern __shared__ __align__(16) float asm3[];
+    float *q = asm3, *part = q + HD, *att = part + ((per + 3) & ~3);
+    float *vs = att + ((d.max_ctx + 3) & ~3);   // [np][32]
+    __shared__ float red[32];
+    __shared__ float s_mx, s_inv;
+
+    // V columns c*32 .. c*32+31 of rows 0..np-1 (8 x 16 bytes per row)
+    const float *V = L.vc + (size_t)g * d.max_ctx * HD + c * kAttnSlice;
+    for (int i = tid; i < np * 8; i += HD) {
+        const int r = i >> 3, k = i & 7;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                     ::"r"(smem_u32(vs + (size_t)r * kAttnSlice + 4 * k)), "l"(V + (size_t)r * HD + 4 * k) : "memory");
+    }
+    cp_async_commit();
+    q[tid] = qbuf[((size_t)t * d.nq + h) * HD + tid];
+    const float gate = tid < kAttnSlice ? y[(size_t)t * d.ldy + (size_t)2 * HD * h + HD + c * kAttnSlice + tid] : 0.0f;
+    __syncthreads();
+
+    // 1. scores of this CTA's positions
+    const float scale = inv_sqrt_ref((float)HD);
+    const float *K = L.kc + (size_t)g * d.max_ctx * HD;
+    const int p0 = (int)c * per, p1 = min(np, p0 + per);
+    const int k4 = tid & 3;
+    const float4 *q4 = reinterpret_cast<const float4 *>(q);
+    for (int base = p0; base < p1; base += HD / 4) {
+        const int pp = base + (tid >> 2);
+        const bool act = pp < p1;
+        const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)(act ? pp : p0) * HD) + k4;
+        float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < HD / 16; i++) {
+            const float4 kv = __ldg(kr + 4 * i), qv = q4[4 * i + k4];
+            c0 = madd(c0, qv.x, kv.x);
+            c1 = madd(c1, qv.y, kv.y);
+            c2 = madd(c2, qv.z, kv.z);
+            c3 = madd(c3, qv.w, kv.w);
+        }
+        const float hh = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
+        const float pr = __fadd_rn(hh, __shfl_xor_sync(0xffffffffu, hh, 1));
+        const float sc = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 2));
+        if (act && k4 == 0) part[pp - p0] = __fmul_rn(__fadd_rn(sc, 0.0f), scale);
+    }
+    cluster_arrive();
+    cluster_wait();
+
+    // 2. gather every score, then the softmax (as k_attn2)
+    for (int p = tid; p < np; p += HD) {
+        const int owner = p / per;
+        att[p] = ld_dsmem(part + (p - owner * per), (uint32_t)owner);
+    }
+    cluster_arrive();   // this CTA is done reading its peers; waited on before exit
+    __syncthreads();
+    const int lane = tid & 31, warp = tid >> 5, nw = HD >> 5;
+    float m = -INFINITY;
+    for (int p = tid; p < np; p += HD) m = fmaxf(m, att[p]);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid < 32) {
+        float mm = tid < nw ? red[tid] : -INFINITY;
+        for (int o = 16; o; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        if (tid == 0) s_mx = mm;
+    }
+    __syncthreads();
+    const float mx = s_mx;
+    for (int p = tid; p < np; p += HD) att[p] = pf_expf(__fadd_rn(att[p], -mx));
+    __syncthreads();
+    if (tid < 32) {
+        const float sum = sum4_ref(att, np);
+        if (tid == 0) s_inv = __fdiv_rn(1.0f, sum);
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    for (int p = tid; p < np; p += HD) att[p] = __fmul_rn(att[p], inv);
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // 3. ordered PV chain for this CTA's 32 columns, gate, A8
+    if (warp == 0) {
+        float o = 0.0f;
+        const float *vp = vs + lane;
+        int p = 0;
+        for (; p + 8 <= np; p += 8) {
+            float v[8], a[8];
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                v[r] = vp[(size_t)(p + r) * kAttnSlice];
+                a[r] = att[p + r];
+            }
+#pragma unroll
+            for (int r = 0; r < 8; r++) o = madd(o, a[r], v[r]);
+        }
+        for (; p < np; p++) o = madd(o, att[p], vp[(size_t)p * kAttnSlice]);
+        o = __fmul_rn(o, pf_sigmoid(gate));
+        const int col = h * HD + (int)c * kAttnSlice, nbo = out.cols >> 5;
+        quant_block_warp(o, lane, out.q + (size_t)t * out.cols + col, out.d + (size_t)t * nbo + (col >> 5),
+                         out.fs + (size_t)t * nbo + (col >> 5));
+    }
+    cluster_wait();
+}
+
 // Gated DeltaNet layer, latency-oriented form of k_deltanet with identical per-element
 // arithmetic (same citations). Differences are scheduling only:
 //  - one cp.async batch brings this key head's q / k / v / z / b / a rows of every token into
@@ -1834,6 +2024,11 @@ void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, flo
 }
 void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
                  const Step *st, Act out, cudaStream_t s) {
+    static const int attn3_lim = dyn_smem_limit(k_attn3);
+    if (d.hd == kAttnHd && attn3_smem(d.max_ctx) <= (size_t)attn3_lim) {
+        k_attn3<<<dim3(kAttnCL, d.nq, kMaxRows), kAttnHd, attn3_smem(d.max_ctx), s>>>(L, d, y, qbuf, st, out);
+        return;
+    }
     static const int attn2_lim = dyn_smem_limit(k_attn2);
     if (d.hd == kAttnHd && attn2_smem(d.max_ctx) <= (size_t)attn2_lim) {
         k_attn2<<<dim3(kMaxRows, d.nq), kAttnHd, attn2_smem(d.max_ctx), s>>>(L, d, y, qbuf, st, out);
@@ -1905,6 +2100,7 @@ int kernels_init(int max_ctx, int hd, int rep) {
         raise_smem(k_deltanet, deltanet_smem(rep));
         raise_smem(k_attn, ((size_t)hd + max_ctx) * sizeof(float));
         raise_smem(k_attn2, attn2_smem(max_ctx));
+        raise_smem(k_attn3, attn3_smem(max_ctx));
     }
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
