@@ -1524,6 +1524,86 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
 // rep == 1 only (one value head per key head, every Qwen3.5 size); KC taps.
 constexpr int kMaxReplay = 8;   // a verify pass holds at most PINFER_SPEC_MAX_K + 1 rows
 
+// One conv channel of k_deltanet2 held in registers (every array index a constant): the state
+// rows, the taps, and the conv-log rows a pending commit shifts in (pf_lin_commit's conv part,
+// kern_lin.c: new state row r = old row r + e1 while that exists, else logged input row
+// r + e1 - S + 1, e1 = pend_conv - 1).
+template <int KC>
+struct ConvCh {
+    static constexpr int S = KC - 1;
+    float st[S > 0 ? S : 1], w[KC], xr[S > 0 ? S : 1];
+    int c;
+};
+template <int KC>
+__device__ __forceinline__ void conv_load(ConvCh<KC> &ch, const LinLayer &L, int C, int c, int pend_conv) {
+    constexpr int S = KC - 1;
+    ch.c = c;
+#pragma unroll
+    for (int r = 0; r < S; r++) ch.st[r] = L.conv_state[(size_t)r * C + c];
+#pragma unroll
+    for (int r = 0; r < KC; r++) ch.w[r] = L.conv_w[(size_t)c * KC + r];
+    const int e1 = pend_conv - 1;
+#pragma unroll
+    for (int r = 0; r < S; r++) {
+        const int src = r + e1;
+        ch.xr[r] = (pend_conv > 1 && src >= S) ? L.xin[(size_t)(src - S + 1) * C + c] : 0.0f;
+    }
+}
+template <int KC>
+__device__ __forceinline__ void conv_commit(ConvCh<KC> &ch, int pend_conv) {
+    constexpr int S = KC - 1;
+    if (pend_conv > 1) {
+        const int e1 = pend_conv - 1;
+        float ns[S > 0 ? S : 1];
+#pragma unroll
+        for (int r = 0; r < S; r++) {
+            const int src = r + e1;
+            float v = ch.xr[r];
+#pragma unroll
+            for (int q2 = 0; q2 < S; q2++)
+                if (src == q2) v = ch.st[q2];
+            ns[r] = v;
+        }
+#pragma unroll
+        for (int r = 0; r < S; r++) ch.st[r] = ns[r];
+    }
+}
+// conv tap sum of token t (state rows, then the token's own input), state shift, SiLU
+template <int KC>
+__device__ __forceinline__ float conv_step(ConvCh<KC> &ch, float xc) {
+    constexpr int S = KC - 1;
+    float acc = __fmul_rn(ch.w[0], S > 0 ? ch.st[0] : xc);
+#pragma unroll
+    for (int r = 1; r < KC; r++) acc = madd(acc, ch.w[r], r < S ? ch.st[r < S ? r : 0] : xc);
+#pragma unroll
+    for (int r = 0; r + 1 < S; r++) ch.st[r] = ch.st[r + 1];
+    if (S > 0) ch.st[S - 1] = xc;
+    return pf_silu(acc);
+}
+template <int KC>
+__device__ __forceinline__ void conv_store(const ConvCh<KC> &ch, const LinLayer &L, int C, const float *live,
+                                           int logged) {
+    constexpr int S = KC - 1;
+#pragma unroll
+    for (int r = 0; r < S; r++) L.conv_state[(size_t)r * C + ch.c] = logged ? live[r] : ch.st[r];
+}
+
+
+// 8 rows i0..i0+7 of a state column (stride kDV) / 8 consecutive floats (16-byte aligned)
+__device__ __forceinline__ void ld8col(float (&v)[8], const float *col, int i0) {
+#pragma unroll
+    for (int r = 0; r < 8; r++) v[r] = col[(size_t)(i0 + r) * kDV];
+}
+__device__ __forceinline__ void st8col(float *col, int i0, const float (&v)[8]) {
+#pragma unroll
+    for (int r = 0; r < 8; r++) col[(size_t)(i0 + r) * kDV] = v[r];
+}
+__device__ __forceinline__ void ld8(float (&v)[8], const float *p) {
+    const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
 template <int KC>
 __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, LibmTables T,
                                                       const float *y, Step *st, Act out) {
@@ -1536,7 +1616,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, Lib
     const int C = d.C;
     __shared__ __align__(16) float sq[kMaxRows][kDK], sk[kMaxRows][kDK], sv[kMaxRows][kDV];
     __shared__ __align__(16) float sz[kMaxRows][kDV], so[kMaxRows][kDV];
-    __shared__ float sb[kMaxRows], sa[kMaxRows], sbeta[kMaxRows], sdec[kMaxRows], srn[kMaxRows];
+    __shared__ float sbeta[kMaxRows], sdec[kMaxRows], srn[kMaxRows];
     __shared__ __align__(16) float skp[kMaxReplay][kDK];
     __shared__ float spd[kMaxReplay];
     extern __shared__ __align__(16) float Ssm[];   // [kDK][kDV]: this head's state, row-major
@@ -1549,16 +1629,19 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, Lib
         cp_async4(&sk[t][j], yr + d.kd + h * kDK + j);
         cp_async4(&sv[t][j], yr + 2 * d.kd + h * kDV + j);
         cp_async4(&sz[t][j], yr + C + h * kDV + j);
-        if (j == 0) cp_async4(&sb[t], yr + C + d.vd + h);
-        if (j == 1) cp_async4(&sa[t], yr + C + d.vd + d.nv + h);
     }
     cp_async_commit();
+    const int keep = pend_keep < kMaxReplay ? pend_keep : kMaxReplay;
     float dl[kMaxReplay];
-    for (int tp = 1; tp <= pend_keep && tp <= kMaxReplay; tp++) {   // deferred commit: rows 1..keep of half wr^1
-        const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp) * d.nv + h) * logw;
-        skp[tp - 1][j] = u[j];
-        dl[tp - 1] = u[kDK + j];
-        if (j == 0) spd[tp - 1] = u[kDK + kDV];
+#pragma unroll
+    for (int tp = 0; tp < kMaxReplay; tp++) {   // deferred commit: rows 1..keep of half wr^1
+        dl[tp] = 0.0f;
+        if (tp < keep) {
+            const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp + 1) * d.nv + h) * logw;
+            skp[tp][j] = u[j];
+            dl[tp] = u[kDK + j];
+            if (j == 0) spd[tp] = u[kDK + kDV];
+        }
     }
     const float *rec_h = L.rec + (size_t)h * kDK * kDV;
     for (int i4 = j * 4; i4 < kDK * kDV; i4 += 128 * 4)
@@ -1567,64 +1650,55 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, Lib
     float *rec = L.rec + (size_t)h * kDK * kDV + j;
     float *Sj = Ssm + j;   // column j: Sj[i * kDV]
     // conv state / taps of this thread's three channels (q, k, v column j of this head)
-    const int chan[3] = {h * kDK + j, d.kd + h * kDK + j, 2 * d.kd + h * kDV + j};
-    float cst[3][S > 0 ? S : 1], cw[3][KC];
-#pragma unroll
-    for (int c3 = 0; c3 < 3; c3++) {
-#pragma unroll
-        for (int r = 0; r < S; r++) cst[c3][r] = L.conv_state[(size_t)r * C + chan[c3]];
-#pragma unroll
-        for (int r = 0; r < KC; r++) cw[c3][r] = L.conv_w[(size_t)chan[c3] * KC + r];
+    ConvCh<KC> cq, ck, cv;   // this thread's three channels: q, k, v column j of this head
+    conv_load(cq, L, C, h * kDK + j, pend_conv);
+    conv_load(ck, L, C, d.kd + h * kDK + j, pend_conv);
+    conv_load(cv, L, C, 2 * d.kd + h * kDV + j, pend_conv);
+    // ---- gates of token t on thread kDV - kMaxRows + t (warp 3), while the state streams in
+    if (j >= kDV - kMaxRows && j - (kDV - kMaxRows) < n) {
+        const int t = j - (kDV - kMaxRows);
+        const float *yr = y + (size_t)t * d.ldy;
+        const float b = yr[C + d.vd + h], a = yr[C + d.vd + d.nv + h];
+        sbeta[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(T, -b)));
+        const float xs = __fadd_rn(a, L.dt_bias[h]);
+        const float sp = xs > 20.0f ? xs : glibc_log1pf(T, glibc_expf(T, xs));
+        sdec[t] = glibc_expf(T, __fmul_rn(L.A[h], sp));
     }
     cp_async_wait<0>();
     __syncthreads();
-
-    // ---- gates (thread t < n)
-    if (j < n) {
-        const float b = sb[j], a = sa[j];
-        sbeta[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(T, -b)));
-        const float xs = __fadd_rn(a, L.dt_bias[h]);
-        const float sp = xs > 20.0f ? xs : glibc_log1pf(T, glibc_expf(T, xs));
-        sdec[j] = glibc_expf(T, __fmul_rn(L.A[h], sp));
-    }
     // ---- pending conv commit, then conv + SiLU for the three channels
+    // (the three channels advance together: three independent chains per token)
+    conv_commit(cq, pend_conv);
+    conv_commit(ck, pend_conv);
+    conv_commit(cv, pend_conv);
+    {
+        float lq[S > 0 ? S : 1], lk[S > 0 ? S : 1], lv[S > 0 ? S : 1];
 #pragma unroll
-    for (int c3 = 0; c3 < 3; c3++) {
-        float (&stt)[S > 0 ? S : 1] = cst[c3];
-        const int c = chan[c3];
-        if (pend_conv > 1) {
-            const int e1 = pend_conv - 1;
-            float ns[S > 0 ? S : 1];
-#pragma unroll
-            for (int r = 0; r < S; r++) {
-                const int src = r + e1;
-                ns[r] = src < S ? stt[src < S ? src : 0] : L.xin[(size_t)(src - S + 1) * C + c];
-            }
-#pragma unroll
-            for (int r = 0; r < S; r++) stt[r] = ns[r];
-        }
-        float (*dst)[kDK] = c3 == 0 ? sq : (c3 == 1 ? sk : sv);
-        float live[S > 0 ? S : 1];
+        for (int r = 0; r < S; r++) lq[r] = lk[r] = lv[r] = 0.0f;
         for (int t = 0; t < n; t++) {
-            const float xc = dst[t][j];
-            float acc = __fmul_rn(cw[c3][0], S > 0 ? stt[0] : xc);
-#pragma unroll
-            for (int r = 1; r < KC; r++) acc = madd(acc, cw[c3][r], r < S ? stt[r < S ? r : 0] : xc);
-#pragma unroll
-            for (int r = 0; r + 1 < S; r++) stt[r] = stt[r + 1];
-            if (S > 0) stt[S - 1] = xc;
-            dst[t][j] = pf_silu(acc);
+            const float xq = sq[t][j], xk = sk[t][j], xv = sv[t][j];
+            const float oq = conv_step(cq, xq), ok = conv_step(ck, xk), ov = conv_step(cv, xv);
+            sq[t][j] = oq;
+            sk[t][j] = ok;
+            sv[t][j] = ov;
             if (logged) {
                 if (t == 0) {
 #pragma unroll
-                    for (int r = 0; r < S; r++) live[r] = stt[r];
+                    for (int r = 0; r < S; r++) {
+                        lq[r] = cq.st[r];
+                        lk[r] = ck.st[r];
+                        lv[r] = cv.st[r];
+                    }
                 } else {
-                    L.xin[(size_t)t * C + c] = xc;
+                    L.xin[(size_t)t * C + cq.c] = xq;
+                    L.xin[(size_t)t * C + ck.c] = xk;
+                    L.xin[(size_t)t * C + cv.c] = xv;
                 }
             }
         }
-#pragma unroll
-        for (int r = 0; r < S; r++) L.conv_state[(size_t)r * C + c] = logged ? live[r] : stt[r];
+        conv_store(cq, L, C, lq, logged);
+        conv_store(ck, L, C, lk, logged);
+        conv_store(cv, L, C, lv, logged);
     }
     __syncthreads();
     // ---- L2 norm of q and k: 4 lanes per (token, vector)
@@ -1654,20 +1728,39 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, Lib
     }
     __syncthreads();
 
-    // ---- recurrence: replay + token 0 first sweep, then fused sweeps (column j in smem)
+    // ---- recurrence: replay + token 0 first sweep, then fused sweeps (column j in smem).
+    // The column moves through registers 8 rows at a time, the next 8 rows loaded before this
+    // chunk is stored back (the compiler cannot prove the state and the q / k rows disjoint, so
+    // it would not hoist those loads itself); per element the operations and their order are
+    // unchanged, and the dot-product chains still run over i = 0..kDK-1 in order.
     float kv = 0.0f;
     {
         const float dec = sdec[0];
         const float *k0 = sk[0];
-        const int keep = pend_keep < kMaxReplay ? pend_keep : kMaxReplay;
-#pragma unroll 4
-        for (int i = 0; i < kDK; i++) {
-            float sv_ = Sj[i * kDV];
-            for (int tp = 0; tp < keep; tp++)
-                sv_ = __fadd_rn(__fmul_rn(sv_, spd[tp]), __fmul_rn(skp[tp][i], dl[tp]));
-            sv_ = __fmul_rn(sv_, dec);
-            Sj[i * kDV] = sv_;
-            kv = madd(kv, sv_, k0[i]);
+        float sc[8];
+        ld8col(sc, Sj, 0);
+        for (int i0 = 0; i0 < kDK; i0 += 8) {
+            float sn[8], k8[8];
+            ld8col(sn, Sj, i0 + 8 < kDK ? i0 + 8 : i0);
+            ld8(k8, k0 + i0);
+#pragma unroll
+            for (int tp = 0; tp < kMaxReplay; tp++) {
+                if (tp < keep) {
+                    float kp[8];
+                    ld8(kp, skp[tp] + i0);
+                    const float pd = spd[tp];
+#pragma unroll
+                    for (int r = 0; r < 8; r++) sc[r] = __fadd_rn(__fmul_rn(sc[r], pd), __fmul_rn(kp[r], dl[tp]));
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                sc[r] = __fmul_rn(sc[r], dec);
+                kv = madd(kv, sc[r], k8[r]);
+            }
+            st8col(Sj, i0, sc);
+#pragma unroll
+            for (int r = 0; r < 8; r++) sc[r] = sn[r];
         }
     }
     for (int t = 0; t < n; t++) {
@@ -1678,24 +1771,38 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, Lib
         const float decn = next ? sdec[t + 1] : 0.0f;
         const float *kn = sk[next ? t + 1 : t];
         const bool store_live = logged && t == 0;
-        if (next) {
-#pragma unroll 4
-            for (int i = 0; i < kDK; i++) {
-                float sv_ = __fadd_rn(Sj[i * kDV], __fmul_rn(kt[i], delta));
-                o = madd(o, sv_, qt[i]);
-                if (store_live) rec[(size_t)i * kDV] = sv_;
-                sv_ = __fmul_rn(sv_, decn);
-                kvn = madd(kvn, sv_, kn[i]);
-                Sj[i * kDV] = sv_;
+        const bool store_rec = store_live || (!next && !logged);
+        float sc[8];
+        ld8col(sc, Sj, 0);
+        for (int i0 = 0; i0 < kDK; i0 += 8) {
+            float sn[8], k8[8], q8[8];
+            ld8col(sn, Sj, i0 + 8 < kDK ? i0 + 8 : i0);
+            ld8(k8, kt + i0);
+            ld8(q8, qt + i0);
+            if (next) {
+                float n8[8];
+                ld8(n8, kn + i0);
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    float sv_ = __fadd_rn(sc[r], __fmul_rn(k8[r], delta));
+                    o = madd(o, sv_, q8[r]);
+                    if (store_live) rec[(size_t)(i0 + r) * kDV] = sv_;
+                    sv_ = __fmul_rn(sv_, decn);
+                    kvn = madd(kvn, sv_, n8[r]);
+                    sc[r] = sv_;
+                }
+            } else {
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    const float sv_ = __fadd_rn(sc[r], __fmul_rn(k8[r], delta));
+                    o = madd(o, sv_, q8[r]);
+                    sc[r] = sv_;
+                    if (store_rec) rec[(size_t)(i0 + r) * kDV] = sv_;
+                }
             }
-        } else {
-#pragma unroll 4
-            for (int i = 0; i < kDK; i++) {
-                const float sv_ = __fadd_rn(Sj[i * kDV], __fmul_rn(kt[i], delta));
-                o = madd(o, sv_, qt[i]);
-                Sj[i * kDV] = sv_;
-                if (store_live || !logged) rec[(size_t)i * kDV] = sv_;
-            }
+            st8col(Sj, i0, sc);
+#pragma unroll
+            for (int r = 0; r < 8; r++) sc[r] = sn[r];
         }
         so[t][j] = o;
         if (logged && t > 0) {
