@@ -83,6 +83,16 @@ int nb_mv_run(nb_mv *h, const void *W, const float *X, float *Y, void *stream);
 /* Copy the scratch activations out (device buffers: q [n][cols] int8, d / fsum [n][cols/32]). */
 int nb_mv_get_act(nb_mv *h, int8_t *q, float *d, float *fsum, void *stream);
 
+/* Test hooks for the glibc expf / log1pf restatement the DeltaNet gates use
+ * (engine/src/forward_lin.c:19,290-293 call the C library's expf and log1pf).
+ * nb_libm_selftest: the restatement compiled for the host against the C library on every
+ * `stride`-th 32-bit input (stride 1 = all 2^32), `threads` host threads; mismatch count in
+ * *mismatches; 0 or -1. nb_libm_eval_host: the C library's values (fn 0 expf, 1 log1pf) of host
+ * arrays. nb_libm_eval_device: the device restatement on device arrays, on `stream`. */
+int nb_libm_selftest(int threads, long long stride, long long *mismatches);
+int nb_libm_eval_host(int fn, const float *x, float *y, long long n);
+int nb_libm_eval_device(int fn, const float *x, float *y, long long n, void *stream);
+
 /* Allocation-free Q4K x A8 matmul. No counterpart in the reference (its CPU pf_matmul takes
  * caller buffers and needs no scratch).
  * Y [n][rows] = W (device panel layout) x A8(X [n][cols]), the same kernels and the same

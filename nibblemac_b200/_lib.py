@@ -121,8 +121,10 @@ _OPTIONAL = {
                                      ctypes.c_void_p, ctypes.c_void_p]),
     "nb_mv_run_static": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
-    "nb_libm_selftest":(ctypes.c_int, [ctypes.c_int, ctypes.c_longlong,
-                                        ctypes.POINTER(ctypes.c_longlong)]),
+    "nb_libm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_longlong, ctypes.POINTER(ctypes.c_longlong)]),
+    "nb_libm_eval_host": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong]),
+    "nb_libm_eval_device": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
+                                           ctypes.c_void_p]),
 }
 
 

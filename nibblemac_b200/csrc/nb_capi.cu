@@ -1,5 +1,6 @@
 // Kernel-level C ABI of the Q4K x A8 matmul (include/nb_b200.h): the pf_matmul contract on
 // device buffers, for the parity tests and the matvec benchmark.
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstring>
@@ -67,6 +68,12 @@ unsigned char *static_scratch() {
     return p;
 }
 }  // namespace
+
+// The device's restated expf / log1pf on an array (the DeltaNet gates' functions), for tests.
+__global__ void k_libm_eval(int fn, const float *x, float *y, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = fn == 0 ? glibc_expf(x[i]) : glibc_log1pf(x[i]);
+}
 
 struct nb_mv {
     int rows, cols, nmax, n;
@@ -193,6 +200,14 @@ int nb_mv_get_act(nb_mv *h, int8_t *q, float *d, float *fsum, void *stream) {
               cudaMemcpyAsync(d, h->act.d, nb * 4, cudaMemcpyDeviceToDevice, s) == cudaSuccess &&
               cudaMemcpyAsync(fsum, h->act.fs, nb * 4, cudaMemcpyDeviceToDevice, s) == cudaSuccess;
     return ok ? PINFER_OK : PINFER_E_NOMEM;
+}
+
+int nb_libm_eval_device(int fn, const float *x, float *y, long long n, void *stream) {
+    if ((fn != 0 && fn != 1) || !x || !y || n < 0) return PINFER_E_ARG;
+    if (n == 0) return PINFER_OK;
+    const long long blocks = std::min<long long>((n + 255) / 256, 4096);
+    k_libm_eval<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(fn, x, y, n);
+    return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
 }
 
 // The nb_mv_create + nb_mv_set_n + nb_mv_run sequence without an allocation: same kernels, same

@@ -42,11 +42,6 @@ void set_err(const char *msg) {
         }                                                                              \
     } while (0)
 
-int host_threads() {
-    const long n = sysconf(_SC_NPROCESSORS_ONLN);
-    return n < 1 ? 1 : (int)std::min<long>(n, 64);
-}
-
 }  // namespace
 
 // ---------------------------------------------------------------- panel repack
@@ -134,8 +129,6 @@ struct pinfer_ctx {
     Step *h_step = nullptr;   // pinned mirror for reads
     int *d_out = nullptr, *d_greedy = nullptr;
     int out_cap = 0;
-    LibmTables tables{};
-    HostLibm host_tables;
 
     // graphs of one verify round per draft depth k (index k), no graph = not captured yet
     cudaGraphExec_t round_graph[PINFER_SPEC_MAX_K + 1] = {};
@@ -333,24 +326,6 @@ int alloc_and_upload(pinfer_ctx *c) {
     CUDA_OK(cudaMallocHost(&c->h_step, sizeof(Step)));
     memset(c->h_step, 0, sizeof(Step));
 
-    // glibc correction tables for the DeltaNet gates
-    char err[160];
-    if (libm_tables_get(&c->host_tables, host_threads(), err, sizeof err)) {
-        set_err(err);
-        return PINFER_E_NOMEM;
-    }
-    uint32_t *eb, *lb, *ok;
-    float *ov;
-    const HostLibm &T = c->host_tables;
-    if ((rc = c->dalloc(&eb, T.exp_words * 4)) || (rc = c->dalloc(&lb, T.log1p_words * 4)) ||
-        (rc = c->dalloc(&ok, sizeof(uint32_t) * 2 * (T.n_ovf + 1))) || (rc = c->dalloc(&ov, sizeof(float) * (T.n_ovf + 1))))
-        return rc;
-    CUDA_OK(cudaMemcpy(eb, T.exp_bits, T.exp_words * 4, cudaMemcpyHostToDevice));
-    CUDA_OK(cudaMemcpy(lb, T.log1p_bits, T.log1p_words * 4, cudaMemcpyHostToDevice));
-    CUDA_OK(cudaMemcpy(ok, T.ovf_key, sizeof(uint32_t) * 2 * T.n_ovf, cudaMemcpyHostToDevice));
-    CUDA_OK(cudaMemcpy(ov, T.ovf_val, sizeof(float) * T.n_ovf, cudaMemcpyHostToDevice));
-    c->tables = LibmTables{eb, lb, ok, ov, T.n_ovf};
-    libm_tables_free(&c->host_tables);
     if (kernels_init(c->max_ctx, c->hd, c->lind.rep) != 0) return PINFER_E_NOMEM;
     return PINFER_OK;
 }
@@ -377,7 +352,7 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head) {
         } else {
             const Act o = mid_act(c, c->vd);
             launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->lind.ldy, nmax, c->act_h, s);
-            launch_deltanet(c->lin[D.lin], c->lind, c->tables, c->y, c->step, o, s);
+            launch_deltanet(c->lin[D.lin], c->lind, c->y, c->step, o, s);
             launch_matvec(D.out, o, c->step, c->x, c->H, 1, nmax, s);
         }
         const Act h = mid_act(c, c->ffn);
@@ -652,7 +627,6 @@ void pinfer_free(pinfer_ctx *c) {
     cudaFree(c->ck_buf);
     if (c->h_step) cudaFreeHost(c->h_step);
     if (c->stream) cudaStreamDestroy(c->stream);
-    libm_tables_free(&c->host_tables);
     c->file.close_file();
     delete c;
 }

@@ -124,7 +124,7 @@ void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int
                         unsigned long long *partial, int *nan0, int nmax, cudaStream_t s);
 void launch_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
                          Step *st, cudaStream_t s);
-void launch_deltanet(const LinLayer &L, const LinDims &d, const LibmTables &T, const float *y,
+void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
                      Step *st, Act out, cudaStream_t s);
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
                       const Step *st, cudaStream_t s);
@@ -149,15 +149,5 @@ size_t panel_bytes(int rows, int cols);
 // layout; `out` has panel_bytes(rows, cols) bytes; rows beyond `rows` are zero.
 void repack_q4k(const uint8_t *pq, int rows, int cols, uint8_t *out);
 
-// libm tables (nb_libm.cpp)
-struct HostLibm {
-    uint32_t *exp_bits = nullptr, *log1p_bits = nullptr;
-    size_t exp_words = 0, log1p_words = 0;
-    uint32_t *ovf_key = nullptr;   // pairs (fn, bits)
-    float *ovf_val = nullptr;
-    int n_ovf = 0;
-};
-int libm_tables_get(HostLibm *out, int threads, char *err, size_t errlen);
-void libm_tables_free(HostLibm *t);
 
 }  // namespace nb

@@ -303,6 +303,15 @@ __device__ __forceinline__ void tma_load_1d(void *dst, const void *src, uint32_t
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
+// one arrival that also announces `bytes` of bulk copies still to complete on the barrier
+__device__ __forceinline__ void mbar_arrive_expect(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// bulk copy global -> shared completing on `bar` (no arrival of its own)
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
 // wait for phase `parity` of the barrier; false after kSpinLimit polls (the caller reports
 // the timeout instead of hanging)
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
@@ -812,8 +821,8 @@ struct DnSmem {   // carved from dynamic shared memory
     float *rn;                 // [nmax][rep] gated-norm factors
 };
 
-__global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, LibmTables T,
-                                                  const float *y, Step *st, Act out) {
+__global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, const float *y, Step *st,
+                                                  Act out) {
     const int n = st->n;
     if (n <= 0) return;
     const int logged = st->logged, pend_keep = st->pend_keep, pend_conv = st->pend_conv;
@@ -847,10 +856,10 @@ __global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, Libm
         const int t = u / rep, r = u % rep, h = kh * rep + r;
         const float b = y[(size_t)t * d.ldy + C + d.vd + h];
         const float a = y[(size_t)t * d.ldy + C + d.vd + d.nv + h];
-        s.beta[t * rep + r] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(T, -b)));
+        s.beta[t * rep + r] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-b)));
         const float xs = __fadd_rn(a, L.dt_bias[h]);
-        const float sp = xs > 20.0f ? xs : glibc_log1pf(T, glibc_expf(T, xs));
-        s.decay[t * rep + r] = glibc_expf(T, __fmul_rn(L.A[h], sp));
+        const float sp = xs > 20.0f ? xs : glibc_log1pf(glibc_expf(xs));
+        s.decay[t * rep + r] = glibc_expf(__fmul_rn(L.A[h], sp));
     }
 
     // ---- 1. conv + SiLU
@@ -1528,6 +1537,15 @@ constexpr int kMaxReplay = 8;   // a verify pass holds at most PINFER_SPEC_MAX_K
 // rows, the taps, and the conv-log rows a pending commit shifts in (pf_lin_commit's conv part,
 // kern_lin.c: new state row r = old row r + e1 while that exists, else logged input row
 // r + e1 - S + 1, e1 = pend_conv - 1).
+// A global load issued where it is written: volatile asm keeps its place among the other
+// volatile asm of the kernel (the cp.async copies), so the compiler cannot sink it to the first
+// use to save registers; the value is waited for only where it is used.
+__device__ __forceinline__ float ld_early(const float *p) {
+    float v;
+    asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
 template <int KC>
 struct ConvCh {
     static constexpr int S = KC - 1;
@@ -1535,18 +1553,23 @@ struct ConvCh {
     int c;
 };
 template <int KC>
-__device__ __forceinline__ void conv_load(ConvCh<KC> &ch, const LinLayer &L, int C, int c, int pend_conv) {
+__device__ __forceinline__ void conv_load(ConvCh<KC> &ch, const LinLayer &L, int C, int c) {
     constexpr int S = KC - 1;
     ch.c = c;
 #pragma unroll
-    for (int r = 0; r < S; r++) ch.st[r] = L.conv_state[(size_t)r * C + c];
+    for (int r = 0; r < S; r++) ch.st[r] = ld_early(L.conv_state + (size_t)r * C + c);
 #pragma unroll
-    for (int r = 0; r < KC; r++) ch.w[r] = L.conv_w[(size_t)c * KC + r];
+    for (int r = 0; r < KC; r++) ch.w[r] = ld_early(L.conv_w + (size_t)c * KC + r);
+}
+template <int KC>
+__device__ __forceinline__ void conv_load_log(ConvCh<KC> &ch, const LinLayer &L, int C, int pend_conv) {
+    constexpr int S = KC - 1;
+    const int c = ch.c;
     const int e1 = pend_conv - 1;
 #pragma unroll
     for (int r = 0; r < S; r++) {
         const int src = r + e1;
-        ch.xr[r] = (pend_conv > 1 && src >= S) ? L.xin[(size_t)(src - S + 1) * C + c] : 0.0f;
+        ch.xr[r] = (pend_conv > 1 && src >= S) ? ld_early(L.xin + (size_t)(src - S + 1) * C + c) : 0.0f;
     }
 }
 template <int KC>
@@ -1605,15 +1628,24 @@ __device__ __forceinline__ void ld8(float (&v)[8], const float *p) {
 }
 
 template <int KC>
-__global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, LibmTables T,
-                                                      const float *y, Step *st, Act out) {
+__global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, const float *y, Step *st,
+                                                      Act out) {
     constexpr int S = KC - 1;
+    const int h = blockIdx.x, j = threadIdx.x;
+    const int C = d.C;
+    // conv taps and state rows of this thread's three channels (q, k, v column j of this
+    // head): independent of the step and the first thing the kernel needs, so requested first
+    ConvCh<KC> cq, ck, cv;
+    conv_load(cq, L, C, h * kDK + j);
+    conv_load(ck, L, C, d.kd + h * kDK + j);
+    conv_load(cv, L, C, 2 * d.kd + h * kDV + j);
     const int n = st->n;
     if (n <= 0) return;
     const int logged = st->logged, pend_keep = st->pend_keep, pend_conv = st->pend_conv;
     const int wr = st->wr;
-    const int h = blockIdx.x, j = threadIdx.x;
-    const int C = d.C;
+    conv_load_log(cq, L, C, pend_conv);
+    conv_load_log(ck, L, C, pend_conv);
+    conv_load_log(cv, L, C, pend_conv);
     __shared__ __align__(16) float sq[kMaxRows][kDK], sk[kMaxRows][kDK], sv[kMaxRows][kDV];
     __shared__ __align__(16) float sz[kMaxRows][kDV], so[kMaxRows][kDV];
     __shared__ float sbeta[kMaxRows], sdec[kMaxRows], srn[kMaxRows];
@@ -1622,15 +1654,31 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, Lib
     extern __shared__ __align__(16) float Ssm[];   // [kDK][kDV]: this head's state, row-major
     const size_t logw = (size_t)kDK + kDV + 1;
 
-    // ---- prefetch: activations of every token (cp.async), replay log rows, state column
-    for (int t = 0; t < n; t++) {
-        const float *yr = y + (size_t)t * d.ldy;
-        cp_async4(&sq[t][j], yr + h * kDK + j);
-        cp_async4(&sk[t][j], yr + d.kd + h * kDK + j);
-        cp_async4(&sv[t][j], yr + 2 * d.kd + h * kDV + j);
-        cp_async4(&sz[t][j], yr + C + h * kDV + j);
+    // ---- prefetch by TMA bulk copies: this head's q / k / v / z rows of every token on
+    // sbar[0], the 64 KB state on sbar[1] (waited for only before the recurrence). Bulk copies
+    // do not queue in the SM's load / store path, so the loads and stores below do not wait
+    // behind the state. Rows are 512 B at 16-byte aligned offsets (launch_deltanet checks ldy).
+    __shared__ __align__(8) uint64_t sbar[2];
+    if (j == 0) {
+        mbar_init(&sbar[0], 1);
+        mbar_init(&sbar[1], 1);
+        fence_mbar_init();
     }
-    cp_async_commit();
+    __syncthreads();
+    const float *rec_h = L.rec + (size_t)h * kDK * kDV;
+    if (j == 0) {
+        mbar_arrive_expect(&sbar[0], (uint32_t)n * 4u * kDK * 4u);
+        for (int t = 0; t < n; t++) {
+            const float *yr = y + (size_t)t * d.ldy;
+            bulk_g2s(sq[t], yr + h * kDK, kDK * 4, &sbar[0]);
+            bulk_g2s(sk[t], yr + d.kd + h * kDK, kDK * 4, &sbar[0]);
+            bulk_g2s(sv[t], yr + 2 * d.kd + h * kDV, kDV * 4, &sbar[0]);
+            bulk_g2s(sz[t], yr + C + h * kDV, kDV * 4, &sbar[0]);
+        }
+        mbar_arrive_expect(&sbar[1], kDK * kDV * 4);
+        for (int q4 = 0; q4 < 4; q4++)
+            bulk_g2s(Ssm + q4 * (kDK * kDV / 4), rec_h + q4 * (kDK * kDV / 4), kDK * kDV, &sbar[1]);
+    }
     const int keep = pend_keep < kMaxReplay ? pend_keep : kMaxReplay;
     float dl[kMaxReplay];
 #pragma unroll
@@ -1643,28 +1691,19 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, Lib
             if (j == 0) spd[tp] = u[kDK + kDV];
         }
     }
-    const float *rec_h = L.rec + (size_t)h * kDK * kDV;
-    for (int i4 = j * 4; i4 < kDK * kDV; i4 += 128 * 4)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(Ssm + i4)), "l"(rec_h + i4) : "memory");
-    cp_async_commit();
     float *rec = L.rec + (size_t)h * kDK * kDV + j;
     float *Sj = Ssm + j;   // column j: Sj[i * kDV]
-    // conv state / taps of this thread's three channels (q, k, v column j of this head)
-    ConvCh<KC> cq, ck, cv;   // this thread's three channels: q, k, v column j of this head
-    conv_load(cq, L, C, h * kDK + j, pend_conv);
-    conv_load(ck, L, C, d.kd + h * kDK + j, pend_conv);
-    conv_load(cv, L, C, 2 * d.kd + h * kDV + j, pend_conv);
     // ---- gates of token t on thread kDV - kMaxRows + t (warp 3), while the state streams in
     if (j >= kDV - kMaxRows && j - (kDV - kMaxRows) < n) {
         const int t = j - (kDV - kMaxRows);
         const float *yr = y + (size_t)t * d.ldy;
         const float b = yr[C + d.vd + h], a = yr[C + d.vd + d.nv + h];
-        sbeta[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(T, -b)));
+        sbeta[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-b)));
         const float xs = __fadd_rn(a, L.dt_bias[h]);
-        const float sp = xs > 20.0f ? xs : glibc_log1pf(T, glibc_expf(T, xs));
-        sdec[t] = glibc_expf(T, __fmul_rn(L.A[h], sp));
+        const float sp = xs > 20.0f ? xs : glibc_log1pf(glibc_expf(xs));
+        sdec[t] = glibc_expf(__fmul_rn(L.A[h], sp));
     }
-    cp_async_wait<0>();
+    if (!mbar_wait(&sbar[0], 0) && j == 0) st->status = -90;   // timed out: reported, no hang
     __syncthreads();
     // ---- pending conv commit, then conv + SiLU for the three channels
     // (the three channels advance together: three independent chains per token)
@@ -1726,6 +1765,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, Lib
             }
         }
     }
+    if (!mbar_wait(&sbar[1], 0) && j == 0) st->status = -90;   // the state
     __syncthreads();
 
     // ---- recurrence: replay + token 0 first sweep, then fused sweeps (column j in smem).
@@ -2116,14 +2156,15 @@ size_t deltanet_smem(int rep) {
     return sizeof(float) * ((size_t)kMaxRows * kDK * 2 + (size_t)kMaxRows * rep * kDV * 2 +
                             (size_t)kMaxRows * rep * 3 + (size_t)kMaxRows * kDK + kMaxRows + 8);
 }
-void launch_deltanet(const LinLayer &L, const LinDims &d, const LibmTables &T, const float *y,
+void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
                      Step *st, Act out, cudaStream_t s) {
-    if (d.rep == 1 && d.K == 4 && d.dk == kDK && d.dv == kDV) {
-        k_deltanet2<4><<<d.nk, kDV, sizeof(float) * kDK * kDV, s>>>(L, d, T, y, st, out);
+    if (d.rep == 1 && d.K == 4 && d.dk == kDK && d.dv == kDV && d.ldy % 4 == 0 && d.kd % 4 == 0 &&
+        d.C % 4 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)L.rec & 15) == 0) {
+        k_deltanet2<4><<<d.nk, kDV, sizeof(float) * kDK * kDV, s>>>(L, d, y, st, out);
         return;
     }
     const size_t sm = deltanet_smem(d.rep);
-    k_deltanet<<<d.nk, kDV, sm, s>>>(L, d, T, y, st, out);
+    k_deltanet<<<d.nk, kDV, sm, s>>>(L, d, y, st, out);
 }
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
                       const Step *st, cudaStream_t s) {

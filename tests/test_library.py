@@ -2,6 +2,7 @@
 files (the reference's tests/test_malformed.py pattern: patched headers and directories must
 fail with PINFER_E_FORMAT, never crash), host-side helpers, and the glibc tables."""
 import ctypes
+import os
 import re
 import shutil
 import struct
@@ -160,12 +161,14 @@ def test_valid_model_without_device_fails_loudly(lib, tiny_model):
     assert "no CUDA device" in lib.last_error()
 
 
-def test_glibc_tables_reproduce_glibc(lib):
-    """The device's expf / log1pf correction tables, queried on the host like the kernels do,
-    give glibc's results on random inputs across the whole float range."""
+def test_glibc_restatement_matches_c_library(lib):
+    """The restated glibc expf / log1pf of the DeltaNet gates, compiled for the host from the
+    source the device uses, equal the C library's on every 4099th 32-bit input (about a million
+    per function, every sign and exponent); NB_LIBM_EXHAUSTIVE=1 checks all 2^32."""
     mism = ctypes.c_longlong(-1)
-    n_ovf = lib.nb_libm_selftest(8, 300000, ctypes.byref(mism))
-    assert n_ovf >= 0 and mism.value == 0
+    stride = 1 if os.environ.get("NB_LIBM_EXHAUSTIVE") == "1" else 4099
+    assert lib.nb_libm_selftest(max(1, os.cpu_count() or 1), stride, ctypes.byref(mism)) == 0
+    assert mism.value == 0
 
 
 def test_repack_roundtrip(lib, q4k_oracle):
