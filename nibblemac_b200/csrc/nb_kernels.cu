@@ -55,9 +55,9 @@ __device__ __forceinline__ void quant_block_warp(float x, int lane, int8_t *qdst
 // (sub = lane & 7): max, division, rounding and code sum are order-independent, so the bits
 // match quant_block_warp. Four blocks per warp at a time, 3-step shuffles; every lane of the
 // warp must call it. qdst: the block's 32 codes; lane sub writes bytes 4 sub .. 4 sub + 3 and
-// sub 0 writes (d, fsum), unless store is false (a padding group).
+// sub 0 writes d and fsum, unless store is false (a padding group).
 __device__ __forceinline__ void quant_block_oct(const float (&x)[4], int sub, bool store, int8_t *qdst,
-                                                float2 *df) {
+                                                float *ddst, float *fdst) {
     float a = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
     a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
     a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
@@ -77,7 +77,8 @@ __device__ __forceinline__ void quant_block_oct(const float (&x)[4], int sub, bo
     sum += __shfl_xor_sync(0xffffffffu, sum, 4);
     if (store && sub == 0) {
         const float d = __fdiv_rn(a, 127.0f);
-        *df = make_float2(d, __fmul_rn(d, (float)sum));
+        *ddst = d;
+        *fdst = __fmul_rn(d, (float)sum);
     }
 }
 
@@ -343,7 +344,7 @@ struct NormIn {          // RMSNorm input of a NORM panel kernel
 // RMSNorm + A8 of n rows into shared memory (pf_rmsnorm, forward_ops.c:191-200, then
 // kern_quant_act). sx: [n][cols] fp32 and sw: [cols] already staged. Threads of the CTA.
 __device__ __forceinline__ void norm_quant_smem(const float *sx, const float *sw, int n, int cols,
-                                                float eps, int8_t *sq, float2 *sdf, float *srr) {
+                                                float eps, int8_t *sq, float *sd, float *sfs, float *srr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     if (warp == 0) {
         // lanes 4v..4v+3: the four interleaved partial sums of row v (cols % 4 == 0)
@@ -372,16 +373,17 @@ __device__ __forceinline__ void norm_quant_smem(const float *sx, const float *sw
         const float r = srr[v];
         const float x4[4] = {__fmul_rn(__fmul_rn(xv.x, r), wv.x), __fmul_rn(__fmul_rn(xv.y, r), wv.y),
                              __fmul_rn(__fmul_rn(xv.z, r), wv.z), __fmul_rn(__fmul_rn(xv.w, r), wv.w)};
-        quant_block_oct(x4, sub, act, sq + (size_t)v * cols + b * 32, sdf + (size_t)v * nb + b);
+        quant_block_oct(x4, sub, act, sq + (size_t)v * cols + b * 32, sd + (size_t)v * nb + b,
+                        sfs + (size_t)v * nb + b);
     }
 }
 
 // One superblock of one row (this lane) for every vector: decode the 6-bit scales, integer
 // block dots against the A8 activations (staged in shared memory), and the ordered fused chain
-// into acc[v]. sq: [NMAX][cols] int8, sdf: [NMAX][nb] (d, fsum).
+// into acc[v]. sq: [NMAX][cols] int8, sd / sfs: [NMAX][nb] block scales d and sums fsum.
 template <int NMAX>
 __device__ __forceinline__ void sb_accumulate(const uint4 sc, const uint4 (&cd)[8], const int8_t *sq,
-                                              const float2 *sdf, int cols, int sb, int n,
+                                              const float *sd, const float *sfs, int cols, int sb, int n,
                                               float (&acc)[NMAX]) {
     const int nb = cols >> 5;
     const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
@@ -410,12 +412,40 @@ __device__ __forceinline__ void sb_accumulate(const uint4 sc, const uint4 (&cd)[
                 sacc = __dp4a(hi1, x1.y, sacc);
                 sacc = __dp4a(hi2, x1.z, sacc);
                 sacc = __dp4a(hi3, x1.w, sacc);
-                const float2 df = sdf[(size_t)v * nb + b];
-                acc[v] = __fmaf_rn((float)sacc, __fmul_rn(ds, df.x), acc[v]);
-                acc[v] = __fmaf_rn(-os, df.y, acc[v]);
+                acc[v] = __fmaf_rn((float)sacc, __fmul_rn(ds, sd[(size_t)v * nb + b]), acc[v]);
+                acc[v] = __fmaf_rn(-os, sfs[(size_t)v * nb + b], acc[v]);
             }
         }
     }
+}
+
+// Activations of a panel / head kernel into shared memory by TMA bulk copies completing on
+// `abar` (thread 0 issues them; every thread then waits): NORM the residual rows x [n][cols]
+// fp32 and the norm weight [cols], else the A8 rows q [n][cols] and their block scales d and
+// sums fsum [n][cols / 32]. Returns false if the wait timed out.
+template <bool NORM>
+__device__ __forceinline__ bool stage_act(uint64_t *abar, int n, int cols, const Act &in, const NormIn &nin,
+                                          float *sx, float *sw, int8_t *sq, float *sd, float *sfs) {
+    const int nb = cols >> 5;
+    if (threadIdx.x == 0) {
+        mbar_init(abar, 1);
+        fence_mbar_init();
+        if (NORM) {
+            mbar_arrive_expect(abar, (uint32_t)(n + 1) * cols * 4u);
+            bulk_g2s(sx, nin.x, (uint32_t)n * cols * 4u, abar);
+            bulk_g2s(sw, nin.w, (uint32_t)cols * 4u, abar);
+        } else {
+            const int nbi = in.cols >> 5;
+            mbar_arrive_expect(abar, (uint32_t)n * (cols + 8u * nb));
+            for (int v = 0; v < n; v++) {
+                bulk_g2s(sq + (size_t)v * cols, in.q + (size_t)v * in.cols, (uint32_t)cols, abar);
+                bulk_g2s(sd + (size_t)v * nb, in.d + (size_t)v * nbi, (uint32_t)nb * 4u, abar);
+                bulk_g2s(sfs + (size_t)v * nb, in.fs + (size_t)v * nbi, (uint32_t)nb * 4u, abar);
+            }
+        }
+    }
+    __syncthreads();
+    return mbar_wait(abar, 0);
 }
 
 size_t tall_smem(int cols, int nmax, bool norm) {
@@ -440,7 +470,9 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Nor
     uint64_t *bars = reinterpret_cast<uint64_t *>(tsm + (size_t)kTallWarps * kRing * kUnitBytes) + warp * kRing;
     const int cols = W0.cols, nb = cols >> 5, nsb = W0.nsb;
     int8_t *sq = reinterpret_cast<int8_t *>(tsm + kTallSmem);
-    float2 *sdf = reinterpret_cast<float2 *>(tsm + kTallSmem + (size_t)NMAX * cols);
+    float *sd = reinterpret_cast<float *>(tsm + kTallSmem + (size_t)NMAX * cols);   // [NMAX][nb]
+    float *sfs = sd + (size_t)NMAX * nb;                                               // [NMAX][nb]
+    uint64_t *abar = reinterpret_cast<uint64_t *>(sfs + (size_t)NMAX * nb);         // in the 16 B slack
     const int gw = warp * gridDim.x + blockIdx.x, tw = gridDim.x * kTallWarps;
     const int npw = W0.npanels > gw ? (W0.npanels - 1 - gw) / tw + 1 : 0;
     const int total = npw * nsb;
@@ -456,25 +488,11 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Nor
     // stage the activations while the first weight units are in flight: the A8 input, or
     // (NORM) the final RMSNorm of the residual rows computed here
     __shared__ float srr[NMAX];
-    if (NORM) {
-        const size_t off = ((kTallSmem + (size_t)NMAX * cols + (size_t)nb * NMAX * 8 + 16) + 15) & ~(size_t)15;
-        float *sx = reinterpret_cast<float *>(tsm + off), *sw = sx + (size_t)NMAX * cols;
-        for (int i = threadIdx.x; i < n * cols / 4; i += blockDim.x)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sx + 4 * i)), "l"(nin.x + 4 * i) : "memory");
-        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sw + 4 * i)), "l"(nin.w + 4 * i) : "memory");
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncthreads();
-        norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sdf, srr);
-    } else {
-        for (int i = threadIdx.x; i < n * cols / 16; i += blockDim.x) {
-            const int v = i / (cols / 16), j = i % (cols / 16);
-            reinterpret_cast<int4 *>(sq)[i] = __ldg(reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols) + j);
-        }
-        for (int i = threadIdx.x; i < n * nb; i += blockDim.x)
-            sdf[i] = make_float2(__ldg(in.d + i), __ldg(in.fs + i));
-    }
+    const size_t off = ((kTallSmem + (size_t)NMAX * cols + (size_t)nb * NMAX * 8 + 16) + 15) & ~(size_t)15;
+    float *sx = reinterpret_cast<float *>(tsm + off), *sw = sx + (size_t)NMAX * cols;   // NORM only
+    if (!stage_act<NORM>(abar, n, cols, in, nin, sx, sw, sq, sd, sfs) && threadIdx.x == 0)
+        st->status = -90;   // device wait timed out: reported, no hang
+    if (NORM) norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sd, sfs, srr);
     __syncthreads();
     float acc[NMAX];
 #pragma unroll
@@ -500,7 +518,7 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Nor
 #pragma unroll
             for (int v = 0; v < NMAX; v++) acc[v] = 0.0f;
         }
-        sb_accumulate<NMAX>(sc, cd, sq, sdf, cols, sb, n, acc);
+        sb_accumulate<NMAX>(sc, cd, sq, sd, sfs, cols, sb, n, acc);
         if (sb != nsb - 1) continue;
         const int panel = gw + (u / nsb) * tw, row = panel * kPanelRows + lane;
 #pragma unroll
@@ -539,11 +557,13 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
     const int nmat = EPI == 3 ? 2 : 1, nunit = nsb * nmat;
     uint8_t *units = wsm;
     uint64_t *bars = reinterpret_cast<uint64_t *>(wsm + (size_t)nw * kUnitBytes);
-    int32_t *isum = reinterpret_cast<int32_t *>(wsm + (size_t)nw * kUnitBytes + (((size_t)nw * 8 + 15) & ~(size_t)15));
+    uint64_t *abar = bars + nw;   // the activations
+    int32_t *isum = reinterpret_cast<int32_t *>(wsm + (size_t)nw * kUnitBytes + (((size_t)nw * 8 + 8 + 15) & ~(size_t)15));
     float *ds = reinterpret_cast<float *>(isum + (size_t)nmat * nb * NMAX * 32);   // [nmat][nb][32]
     float *os = ds + (size_t)nmat * nb * 32;
-    float2 *sdf = reinterpret_cast<float2 *>(os + (size_t)nmat * nb * 32);   // [NMAX][nb]
-    int8_t *sq = reinterpret_cast<int8_t *>(sdf + (size_t)NMAX * nb);         // [NMAX][cols]
+    float *sd = os + (size_t)nmat * nb * 32;                                     // [NMAX][nb]
+    float *sfs = sd + (size_t)NMAX * nb;                                          // [NMAX][nb]
+    int8_t *sq = reinterpret_cast<int8_t *>(sfs + (size_t)NMAX * nb);          // [NMAX][cols]
     float *sx = reinterpret_cast<float *>(sq + (size_t)NMAX * cols);           // NORM: [NMAX][cols]
     float *sw = sx + (size_t)NMAX * cols;                                       // NORM: [cols]
     __shared__ float srr[NMAX];
@@ -557,23 +577,9 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
         }
     }
     // activations into shared memory while the weights are in flight
-    if (NORM) {
-        for (int i = threadIdx.x; i < n * cols / 4; i += blockDim.x)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sx + 4 * i)), "l"(nin.x + 4 * i) : "memory");
-        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sw + 4 * i)), "l"(nin.w + 4 * i) : "memory");
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncthreads();
-        norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sdf, srr);
-    } else {
-        for (int i = threadIdx.x; i < n * cols / 16; i += blockDim.x) {
-            const int v = i / (cols / 16), jj = i % (cols / 16);
-            reinterpret_cast<int4 *>(sq)[i] = __ldg(reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols) + jj);
-        }
-        for (int i = threadIdx.x; i < n * nb; i += blockDim.x)
-            sdf[i] = make_float2(__ldg(in.d + i), __ldg(in.fs + i));
-    }
+    if (!stage_act<NORM>(abar, n, cols, in, nin, sx, sw, sq, sd, sfs) && threadIdx.x == 0)
+        st->status = -90;   // device wait timed out: reported, no hang
+    if (NORM) norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sd, sfs, srr);
     __syncthreads();
     for (int u = warp, it = 0; u < nunit; u += nw, it++) {
         const int m = u / nsb, sb = u % nsb;
@@ -633,13 +639,12 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
             float a = 0.0f;
             const int32_t *is = isum + ((size_t)m * nb * NMAX + v) * 32 + lane;
             const float *dsp = ds + (size_t)m * nb * 32 + lane, *osp = os + (size_t)m * nb * 32 + lane;
-            const float2 *df = sdf + (size_t)v * nb;
+            const float *dv = sd + (size_t)v * nb, *fv = sfs + (size_t)v * nb;
 #pragma unroll 4
             for (int b = 0; b < nb; b++) {
                 const float s = (float)is[(size_t)b * NMAX * 32];
-                const float2 f = df[b];
-                a = __fmaf_rn(s, __fmul_rn(dsp[b * 32], f.x), a);
-                a = __fmaf_rn(-osp[b * 32], f.y, a);
+                a = __fmaf_rn(s, __fmul_rn(dsp[b * 32], dv[b]), a);
+                a = __fmaf_rn(-osp[b * 32], fv[b], a);
             }
             acc[m] = a;
         }
@@ -657,7 +662,7 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
 
 size_t panel_smem(int nw, int cols, int nmat, int nmax, bool norm) {
     const size_t nb = cols / 32;
-    size_t b = (size_t)nw * kUnitBytes + (((size_t)nw * 8 + 15) & ~(size_t)15) + (size_t)nmat * nb * nmax * 32 * 4 +
+    size_t b = (size_t)nw * kUnitBytes + (((size_t)nw * 8 + 8 + 15) & ~(size_t)15) + (size_t)nmat * nb * nmax * 32 * 4 +
                (size_t)nmat * nb * 32 * 8 + (size_t)nmax * nb * 8 + (size_t)nmax * cols;
     b = (b + 15) & ~(size_t)15;
     if (norm) b += (size_t)nmax * cols * 4 + (size_t)cols * 4;
