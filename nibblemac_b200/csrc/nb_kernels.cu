@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <utility>
 #include <cstdio>
 
 #include "nb_engine.h"
@@ -14,6 +15,32 @@
 namespace nb {
 
 namespace {
+
+// ------------------------------------------------------------------ programmatic dependent launch
+// Every kernel of the forward is launched with programmatic stream serialisation, so it can be
+// resident while its predecessor on the stream finishes. Each kernel calls pdl_wait() before it
+// touches anything another kernel writes (griddepcontrol.wait returns once every prerequisite
+// grid has completed and its memory is visible) and only then pdl_trigger(), which lets the
+// next kernel launch. Hence, while a kernel runs code placed before its pdl_wait(), every kernel
+// earlier than its immediate predecessor has completed, and that code reads only data the
+// predecessor does not write (weights, and state the predecessor never touches).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <class... KArgs, class... Args>
+void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------------ warp helpers
 __device__ __forceinline__ float warp_max_abs(float v) {
@@ -195,6 +222,8 @@ __device__ __forceinline__ void mv_panel(const Mat &W, const Act &in, int n, int
 template <int NMAX, int MODE>
 __global__ void __launch_bounds__(kMvThreads) k_matvec(Mat W, Act in, const Step *st, float *y,
                                                        int ldy) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
     MvSmem<NMAX> &sm = *reinterpret_cast<MvSmem<NMAX> *>(smraw);
     const int n = st->n;
@@ -222,6 +251,8 @@ __global__ void __launch_bounds__(kMvThreads) k_matvec_head(Mat W, Act in, const
                                                             float *logits, int ld,
                                                             unsigned long long *partial,
                                                             int *nan0) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
     MvSmem<NMAX> &sm = *reinterpret_cast<MvSmem<NMAX> *>(smraw);
     const int n = st->n;
@@ -251,6 +282,8 @@ __global__ void __launch_bounds__(kMvThreads) k_matvec_head(Mat W, Act in, const
 template <int NMAX>
 __global__ void __launch_bounds__(kMvThreads) k_matvec_swiglu(Mat G, Mat U, Act in,
                                                               const Step *st, Act out) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(16) unsigned char smraw[];
     MvSmem<NMAX> &sm = *reinterpret_cast<MvSmem<NMAX> *>(smraw);
     const int n = st->n;
@@ -463,8 +496,6 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Nor
                                                              float *y, int ldy,
                                                              unsigned long long *partial, int *nan0) {
     extern __shared__ __align__(128) uint8_t tsm[];
-    const int n = st->n;
-    if (n <= 0) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t *ring = tsm + (size_t)warp * kRing * kUnitBytes;
     uint64_t *bars = reinterpret_cast<uint64_t *>(tsm + (size_t)kTallWarps * kRing * kUnitBytes) + warp * kRing;
@@ -484,6 +515,14 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Nor
         for (int i = 0; i < kRing; i++) mbar_init(bars + i, 1);
         fence_mbar_init();
         for (int u = 0; u < kRing && u < total; u++) tma_load_1d(ring + (size_t)u * kUnitBytes, src(u), kUnitBytes, bars + u);
+    }
+    pdl_wait();   // the ring above holds weights only
+    pdl_trigger();
+    const int n = st->n;
+    if (n <= 0) {   // nothing to do: let the weight copies land before this CTA's shared memory goes
+        __syncwarp();
+        for (int u = 0; u < kRing && u < total; u++) mbar_wait(bars + u, 0);
+        return;
     }
     // stage the activations while the first weight units are in flight: the A8 input, or
     // (NORM) the final RMSNorm of the residual rows computed here
@@ -550,8 +589,6 @@ template <int NMAX, int EPI, bool NORM>
 __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, Act in, NormIn nin,
                                                                Step *st, float *y, int ldy, Act out) {
     extern __shared__ __align__(128) uint8_t wsm[];
-    const int n = st->n;
-    if (n <= 0) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const int nsb = W0.nsb, cols = W0.cols, nb = cols >> 5, panel = blockIdx.x;
     const int nmat = EPI == 3 ? 2 : 1, nunit = nsb * nmat;
@@ -570,11 +607,19 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
     if (lane == 0) {
         mbar_init(bars + warp, 1);
         fence_mbar_init();
-        if (warp < nunit) {   // first unit of every warp, before anything else
+        if (warp < nunit) {   // first unit of every warp (weights: safe before pdl_wait)
             const int m = warp / nsb, sb = warp % nsb;
             tma_load_1d(units + (size_t)warp * kUnitBytes,
                         (m ? W1 : W0).w + ((size_t)panel * nsb + sb) * kUnitBytes, kUnitBytes, bars + warp);
         }
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int n = st->n;
+    if (n <= 0) {   // nothing to do: let the weight copy land before this CTA's shared memory goes
+        __syncwarp();
+        if (warp < nunit) mbar_wait(bars + warp, 0);
+        return;
     }
     // activations into shared memory while the weights are in flight
     if (!stage_act<NORM>(abar, n, cols, in, nin, sx, sw, sq, sd, sfs) && threadIdx.x == 0)
@@ -672,6 +717,8 @@ size_t panel_smem(int nw, int cols, int nmat, int nmax, bool norm) {
 // ------------------------------------------------------------------ argmax over the panels
 __global__ void k_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
                                Step *st) {
+    pdl_wait();
+    pdl_trigger();
     const int v = blockIdx.x;
     if (v >= st->n) return;
     __shared__ unsigned long long red[32];
@@ -695,6 +742,8 @@ __global__ void k_argmax_final(const unsigned long long *partial, const int *nan
 // kern_get_row_q, Q4K branch (engine/src/kern_act.c:76-85): dd = D * s6, mm = M * m6,
 // x = dd * u - mm (two roundings), read from the panel layout.
 __global__ void k_embed(Mat E, const Step *st, float *x, int H) {
+    pdl_wait();
+    pdl_trigger();
     const int v = blockIdx.x;
     if (v >= st->n) return;
     int tok = st->tokens[v];
@@ -758,6 +807,8 @@ __device__ float sum4_ref(const float *a, int n) {
 // A8 blocks of 32 (kern_quant_act). One CTA per row, H floats of shared memory.
 __global__ void k_norm_quant(const float *x, const float *w, int H, float eps, const Step *st,
                              Act out) {
+    pdl_wait();
+    pdl_trigger();
     const int v = blockIdx.x;
     if (v >= st->n) return;
     extern __shared__ float xs[];   // [H] x, then [H] w
@@ -786,6 +837,8 @@ __global__ void k_norm_quant(const float *x, const float *w, int H, float eps, c
 
 // plain A8 quantisation of n rows (kernel-level C-ABI entry point)
 __global__ void k_quant_act(const float *x, int n, int cols, Act out) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int nb = cols >> 5;
@@ -828,6 +881,8 @@ struct DnSmem {   // carved from dynamic shared memory
 
 __global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, const float *y, Step *st,
                                                   Act out) {
+    pdl_wait();
+    pdl_trigger();
     const int n = st->n;
     if (n <= 0) return;
     const int logged = st->logged, pend_keep = st->pend_keep, pend_conv = st->pend_conv;
@@ -1044,6 +1099,8 @@ struct FlushArgs {
 };
 
 __global__ void k_flush(FlushArgs fa, LinDims d, const Step *st) {
+    pdl_wait();
+    pdl_trigger();
     const int keep = st->pend_keep, pend_conv = st->pend_conv, wr = st->wr;
     const LinLayer &L = fa.layers[blockIdx.y];
     const int kh = blockIdx.x, rep = d.rep, tid = threadIdx.x, nthr = blockDim.x;
@@ -1082,12 +1139,16 @@ __global__ void k_flush(FlushArgs fa, LinDims d, const Step *st) {
 
 // End of a pass: its deferred commit has been consumed by every layer.
 __global__ void k_pass_end(Step *st) {
+    pdl_wait();
+    pdl_trigger();
     if (st->n <= 0) return;   // no pass ran (generation finished): the commit is still owed
     st->pend_keep = 0;
     st->pend_conv = 0;
 }
 
 __global__ void k_clear_pending(Step *st) {
+    pdl_wait();
+    pdl_trigger();
     st->pend_keep = 0;
     st->pend_conv = 0;
 }
@@ -1098,6 +1159,8 @@ struct PassArgs {
     int tokens[kMaxRows];
 };
 __global__ void k_set_pass(Step *st, PassArgs a) {
+    pdl_wait();
+    pdl_trigger();
     st->n = a.n;
     st->pos0 = a.pos0;
     st->logged = a.logged;
@@ -1106,6 +1169,8 @@ __global__ void k_set_pass(Step *st, PassArgs a) {
 
 // Generation parameters before k_gen_start.
 __global__ void k_set_gen(Step *st, GenArgs g) {
+    pdl_wait();
+    pdl_trigger();
     st->n_max = g.n_max;
     st->k = g.k;
     st->eos = g.eos;
@@ -1128,6 +1193,8 @@ __global__ void k_set_gen(Step *st, GenArgs g) {
 // exactly as pf_rope_tables does (forward.c:19-32). grid (rows, nq + nkv), hd threads.
 __global__ void k_attn_prep(AttnLayer L, AttnDims d, const float *y, float *qbuf,
                             const Step *st) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     if (t >= st->n) return;
     const int idx = blockIdx.y, hd = d.hd, tid = threadIdx.x;
@@ -1179,6 +1246,8 @@ __global__ void k_attn_prep(AttnLayer L, AttnDims d, const float *y, float *qbuf
 // dynamic shared memory: q [hd] + att [max_ctx].
 __global__ void k_attn(AttnLayer L, AttnDims d, const float *y, const float *qbuf,
                        const Step *st, Act out) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     if (t >= st->n) return;
     const int h = blockIdx.y, hd = d.hd, tid = threadIdx.x;
@@ -1265,6 +1334,8 @@ constexpr int kVGroup = 8;
 
 __global__ void __launch_bounds__(kAttnHd) k_attn2(AttnLayer L, AttnDims d, const float *y,
                                                    const float *qbuf, const Step *st, Act out) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     if (t >= st->n) return;
     constexpr int HD = kAttnHd;
@@ -1417,6 +1488,8 @@ size_t attn3_smem(int max_ctx) {
 
 __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     k_attn3(AttnLayer L, AttnDims d, const float *y, const float *qbuf, const Step *st, Act out) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int HD = kAttnHd;
     const int t = blockIdx.z, h = blockIdx.y, tid = threadIdx.x;
     if (t >= st->n) return;                 // uniform over the cluster
@@ -1644,8 +1717,32 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     conv_load(cq, L, C, h * kDK + j);
     conv_load(ck, L, C, d.kd + h * kDK + j);
     conv_load(cv, L, C, 2 * d.kd + h * kDV + j);
+    // ---- prefetch by TMA bulk copies: the 64 KB state on sbar[1] (before pdl_wait: only this
+    // kernel writes it), after pdl_wait this head's q / k / v / z rows of every token on
+    // sbar[0]. Bulk copies do not queue in the SM's load / store path, so the loads and stores
+    // below do not wait behind the state. Rows are 512 B at 16-byte aligned offsets
+    // (launch_deltanet checks ldy).
+    __shared__ __align__(8) uint64_t sbar[2];
+    extern __shared__ __align__(16) float Ssm[];   // [kDK][kDV]: this head's state, row-major
+    if (j == 0) {
+        mbar_init(&sbar[0], 1);
+        mbar_init(&sbar[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const float *rec_h = L.rec + (size_t)h * kDK * kDV;
+    if (j == 0) {
+        mbar_arrive_expect(&sbar[1], kDK * kDV * 4);
+        for (int q4 = 0; q4 < 4; q4++)
+            bulk_g2s(Ssm + q4 * (kDK * kDV / 4), rec_h + q4 * (kDK * kDV / 4), kDK * kDV, &sbar[1]);
+    }
+    pdl_wait();
+    pdl_trigger();
     const int n = st->n;
-    if (n <= 0) return;
+    if (n <= 0) {   // nothing to do: let the state copy land before this CTA's shared memory goes
+        mbar_wait(&sbar[1], 0);
+        return;
+    }
     const int logged = st->logged, pend_keep = st->pend_keep, pend_conv = st->pend_conv;
     const int wr = st->wr;
     conv_load_log(cq, L, C, pend_conv);
@@ -1656,21 +1753,8 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     __shared__ float sbeta[kMaxRows], sdec[kMaxRows], srn[kMaxRows];
     __shared__ __align__(16) float skp[kMaxReplay][kDK];
     __shared__ float spd[kMaxReplay];
-    extern __shared__ __align__(16) float Ssm[];   // [kDK][kDV]: this head's state, row-major
     const size_t logw = (size_t)kDK + kDV + 1;
 
-    // ---- prefetch by TMA bulk copies: this head's q / k / v / z rows of every token on
-    // sbar[0], the 64 KB state on sbar[1] (waited for only before the recurrence). Bulk copies
-    // do not queue in the SM's load / store path, so the loads and stores below do not wait
-    // behind the state. Rows are 512 B at 16-byte aligned offsets (launch_deltanet checks ldy).
-    __shared__ __align__(8) uint64_t sbar[2];
-    if (j == 0) {
-        mbar_init(&sbar[0], 1);
-        mbar_init(&sbar[1], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-    const float *rec_h = L.rec + (size_t)h * kDK * kDV;
     if (j == 0) {
         mbar_arrive_expect(&sbar[0], (uint32_t)n * 4u * kDK * 4u);
         for (int t = 0; t < n; t++) {
@@ -1680,9 +1764,6 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             bulk_g2s(sv[t], yr + 2 * d.kd + h * kDV, kDV * 4, &sbar[0]);
             bulk_g2s(sz[t], yr + C + h * kDV, kDV * 4, &sbar[0]);
         }
-        mbar_arrive_expect(&sbar[1], kDK * kDV * 4);
-        for (int q4 = 0; q4 < 4; q4++)
-            bulk_g2s(Ssm + q4 * (kDK * kDV / 4), rec_h + q4 * (kDK * kDV / 4), kDK * kDV, &sbar[1]);
     }
     const int keep = pend_keep < kMaxReplay ? pend_keep : kMaxReplay;
     float dl[kMaxReplay];
@@ -1943,6 +2024,8 @@ __device__ void prepare_round(Step *st, const int *greedy) {
 
 // After the prefill pass: the first token is the argmax of the prompt's last row.
 __global__ void k_gen_start(Step *st, const int *greedy, int *out) {
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x != 0) return;
     const int n = st->n;
     st->cur = st->argmax[n - 1];
@@ -1963,6 +2046,8 @@ __global__ void k_gen_start(Step *st, const int *greedy, int *out) {
 // committed (recurrent updates deferred, conv shifted at the next pass) and n_past advances
 // by e (stale KV rows above it are overwritten later).
 __global__ void k_accept(Step *st, const int *greedy, int *out) {
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x != 0) return;
     const int n = st->n;
     if (n <= 0) return;
@@ -2008,21 +2093,21 @@ template <int NMAX>
 void matvec_t(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode, cudaStream_t s) {
     const size_t sm = mv_smem<NMAX>();
     if (mode == 0) {
-        k_matvec<NMAX, 0><<<mv_grid(W), kMvThreads, sm, s>>>(W, in, st, y, ldy);
+        launch_k(k_matvec<NMAX, 0>, mv_grid(W), kMvThreads, sm, s, W, in, st, y, ldy);
     } else {
-        k_matvec<NMAX, 1><<<mv_grid(W), kMvThreads, sm, s>>>(W, in, st, y, ldy);
+        launch_k(k_matvec<NMAX, 1>, mv_grid(W), kMvThreads, sm, s, W, in, st, y, ldy);
     }
 }
 template <int NMAX>
 void swiglu_t(const Mat &G, const Mat &U, Act in, const Step *st, Act out, cudaStream_t s) {
     const size_t sm = mv_smem<NMAX>();
-    k_matvec_swiglu<NMAX><<<mv_grid(G), kMvThreads, sm, s>>>(G, U, in, st, out);
+    launch_k(k_matvec_swiglu<NMAX>, mv_grid(G), kMvThreads, sm, s, G, U, in, st, out);
 }
 template <int NMAX>
 void head_t(const Mat &W, Act in, const Step *st, float *logits, int ld, unsigned long long *partial,
             int *nan0, cudaStream_t s) {
     const size_t sm = mv_smem<NMAX>();
-    k_matvec_head<NMAX><<<mv_grid(W), kMvThreads, sm, s>>>(W, in, st, logits, ld, partial, nan0);
+    launch_k(k_matvec_head<NMAX>, mv_grid(W), kMvThreads, sm, s, W, in, st, logits, ld, partial, nan0);
 }
 }  // namespace
 
@@ -2060,7 +2145,7 @@ template <int NMAX, bool NORM>
 void head_t2(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int ldy,
              unsigned long long *partial, int *nan0, cudaStream_t s) {
     const int grid = std::min(2 * num_sms(), (W.npanels + kTallWarps - 1) / kTallWarps);
-    k_mv_head<NMAX, NORM><<<std::max(grid, 1), kTallWarps * 32, tall_smem(W.cols, NMAX, NORM), s>>>(
+    launch_k(k_mv_head<NMAX, NORM>, std::max(grid, 1), kTallWarps * 32, tall_smem(W.cols, NMAX, NORM), s, 
         W, in, nin, const_cast<Step *>(st), y, ldy, partial, nan0);
 }
 
@@ -2072,7 +2157,7 @@ bool panel_t(const Mat &W0, const Mat &W1, Act in, NormIn nin, const Step *st, f
     const size_t sm = panel_smem(nw, W0.cols, nmat, NMAX, NORM);
     static const int lim = dyn_smem_limit(k_mv_panel<NMAX, EPI, NORM>);
     if (sm > (size_t)lim) return false;
-    k_mv_panel<NMAX, EPI, NORM><<<W0.npanels, nw * 32, sm, s>>>(W0, W1, in, nin, const_cast<Step *>(st),
+    launch_k(k_mv_panel<NMAX, EPI, NORM>, W0.npanels, nw * 32, sm, s, W0, W1, in, nin, const_cast<Step *>(st),
                                                                 y, ldy, out);
     return true;
 }
@@ -2144,18 +2229,18 @@ void launch_matvec_chunked(const Mat &W, Act in, const Step *st, float *y, int l
 }
 void launch_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
                          Step *st, cudaStream_t s) {
-    k_argmax_final<<<kMaxRows, 256, 0, s>>>(partial, nan0, npanels, st);
+    launch_k(k_argmax_final, kMaxRows, 256, 0, s, partial, nan0, npanels, st);
 }
 void launch_embed(const Mat &E, const Step *st, float *x, int H, cudaStream_t s) {
-    k_embed<<<kMaxRows, 256, 0, s>>>(E, st, x, H);
+    launch_k(k_embed, kMaxRows, 256, 0, s, E, st, x, H);
 }
 void launch_norm_quant(const float *x, const float *w, int H, float eps, const Step *st, Act out,
                        cudaStream_t s) {
-    k_norm_quant<<<kMaxRows, 256, 2 * (size_t)H * sizeof(float), s>>>(x, w, H, eps, st, out);
+    launch_k(k_norm_quant, kMaxRows, 256, 2 * (size_t)H * sizeof(float), s, x, w, H, eps, st, out);
 }
 void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s) {
     const int warps = n * (cols / 32);
-    k_quant_act<<<(warps * 32 + 255) / 256, 256, 0, s>>>(x, n, cols, out);
+    launch_k(k_quant_act, (warps * 32 + 255) / 256, 256, 0, s, x, n, cols, out);
 }
 size_t deltanet_smem(int rep) {
     return sizeof(float) * ((size_t)kMaxRows * kDK * 2 + (size_t)kMaxRows * rep * kDV * 2 +
@@ -2165,53 +2250,53 @@ void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
                      Step *st, Act out, cudaStream_t s) {
     if (d.rep == 1 && d.K == 4 && d.dk == kDK && d.dv == kDV && d.ldy % 4 == 0 && d.kd % 4 == 0 &&
         d.C % 4 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)L.rec & 15) == 0) {
-        k_deltanet2<4><<<d.nk, kDV, sizeof(float) * kDK * kDV, s>>>(L, d, y, st, out);
+        launch_k(k_deltanet2<4>, d.nk, kDV, sizeof(float) * kDK * kDV, s, L, d, y, st, out);
         return;
     }
     const size_t sm = deltanet_smem(d.rep);
-    k_deltanet<<<d.nk, kDV, sm, s>>>(L, d, y, st, out);
+    launch_k(k_deltanet, d.nk, kDV, sm, s, L, d, y, st, out);
 }
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
                       const Step *st, cudaStream_t s) {
-    k_attn_prep<<<dim3(kMaxRows, d.nq + d.nkv), d.hd, (size_t)d.hd * sizeof(float), s>>>(L, d, y, qbuf, st);
+    launch_k(k_attn_prep, dim3(kMaxRows, d.nq + d.nkv), d.hd, (size_t)d.hd * sizeof(float), s, L, d, y, qbuf, st);
 }
 void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
                  const Step *st, Act out, cudaStream_t s) {
     static const int attn3_lim = dyn_smem_limit(k_attn3);
     if (d.hd == kAttnHd && attn3_smem(d.max_ctx) <= (size_t)attn3_lim) {
-        k_attn3<<<dim3(kAttnCL, d.nq, kMaxRows), kAttnHd, attn3_smem(d.max_ctx), s>>>(L, d, y, qbuf, st, out);
+        launch_k(k_attn3, dim3(kAttnCL, d.nq, kMaxRows), kAttnHd, attn3_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
         return;
     }
     static const int attn2_lim = dyn_smem_limit(k_attn2);
     if (d.hd == kAttnHd && attn2_smem(d.max_ctx) <= (size_t)attn2_lim) {
-        k_attn2<<<dim3(kMaxRows, d.nq), kAttnHd, attn2_smem(d.max_ctx), s>>>(L, d, y, qbuf, st, out);
+        launch_k(k_attn2, dim3(kMaxRows, d.nq), kAttnHd, attn2_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
         return;
     }
     const size_t sm = ((size_t)d.hd + d.max_ctx) * sizeof(float);
-    k_attn<<<dim3(kMaxRows, d.nq), d.hd, sm, s>>>(L, d, y, qbuf, st, out);
+    launch_k(k_attn, dim3(kMaxRows, d.nq), d.hd, sm, s, L, d, y, qbuf, st, out);
 }
 void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s) {
-    k_gen_start<<<1, 32, 0, s>>>(st, greedy, out);
+    launch_k(k_gen_start, 1, 32, 0, s, st, greedy, out);
 }
 void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s) {
-    k_accept<<<1, 32, 0, s>>>(st, greedy, out);
+    launch_k(k_accept, 1, 32, 0, s, st, greedy, out);
 }
 void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s) {
     FlushArgs fa;
     for (int i = 0; i < n_lin && i < kMaxLayers; i++) fa.layers[i] = layers[i];
-    if (n_lin > 0) k_flush<<<dim3(d.nk, n_lin), kDV, 0, s>>>(fa, d, st);
-    k_clear_pending<<<1, 1, 0, s>>>(st);
+    if (n_lin > 0) launch_k(k_flush, dim3(d.nk, n_lin), kDV, 0, s, fa, d, st);
+    launch_k(k_clear_pending, 1, 1, 0, s, st);
 }
-void launch_pass_end(Step *st, cudaStream_t s) { k_pass_end<<<1, 1, 0, s>>>(st); }
+void launch_pass_end(Step *st, cudaStream_t s) { launch_k(k_pass_end, 1, 1, 0, s, st); }
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s) {
     PassArgs a;
     a.n = n;
     a.pos0 = pos0;
     a.logged = logged;
     for (int i = 0; i < kMaxRows; i++) a.tokens[i] = i < n ? tokens[i] : 0;
-    k_set_pass<<<1, 1, 0, s>>>(st, a);
+    launch_k(k_set_pass, 1, 1, 0, s, st, a);
 }
-void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s) { k_set_gen<<<1, 1, 0, s>>>(st, g); }
+void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s) { launch_k(k_set_gen, 1, 1, 0, s, st, g); }
 int kernels_init(int max_ctx, int hd, int rep) {
     // raise the dynamic shared memory limits once, outside any stream capture
     raise_smem(k_matvec<1, 0>, mv_smem<1>());
