@@ -377,7 +377,9 @@ struct NormIn {          // RMSNorm input of a NORM panel kernel
 // RMSNorm + A8 of n rows into shared memory (pf_rmsnorm, forward_ops.c:191-200, then
 // kern_quant_act). sx: [n][cols] fp32 and sw: [cols] already staged. Threads of the CTA.
 __device__ __forceinline__ void norm_quant_smem(const float *sx, const float *sw, int n, int cols,
-                                                float eps, int8_t *sq, float *sd, float *sfs, float *srr) {
+                                                float eps, int8_t *sq, float *sd, float *sfs, float *srr,
+                                                int qstride = 0) {
+    if (qstride == 0) qstride = cols;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     if (warp == 0) {
         // lanes 4v..4v+3: the four interleaved partial sums of row v (cols % 4 == 0)
@@ -406,7 +408,7 @@ __device__ __forceinline__ void norm_quant_smem(const float *sx, const float *sw
         const float r = srr[v];
         const float x4[4] = {__fmul_rn(__fmul_rn(xv.x, r), wv.x), __fmul_rn(__fmul_rn(xv.y, r), wv.y),
                              __fmul_rn(__fmul_rn(xv.z, r), wv.z), __fmul_rn(__fmul_rn(xv.w, r), wv.w)};
-        quant_block_oct(x4, sub, act, sq + (size_t)v * cols + b * 32, sd + (size_t)v * nb + b,
+        quant_block_oct(x4, sub, act, sq + (size_t)v * qstride + b * 32, sd + (size_t)v * nb + b,
                         sfs + (size_t)v * nb + b);
     }
 }
@@ -458,8 +460,10 @@ __device__ __forceinline__ void sb_accumulate(const uint4 sc, const uint4 (&cd)[
 // sums fsum [n][cols / 32]. Returns false if the wait timed out.
 template <bool NORM>
 __device__ __forceinline__ bool stage_act(uint64_t *abar, int n, int cols, const Act &in, const NormIn &nin,
-                                          float *sx, float *sw, int8_t *sq, float *sd, float *sfs) {
+                                          float *sx, float *sw, int8_t *sq, float *sd, float *sfs,
+                                          int qstride = 0) {
     const int nb = cols >> 5;
+    if (qstride == 0) qstride = cols;
     if (threadIdx.x == 0) {
         mbar_init(abar, 1);
         fence_mbar_init();
@@ -471,7 +475,7 @@ __device__ __forceinline__ bool stage_act(uint64_t *abar, int n, int cols, const
             const int nbi = in.cols >> 5;
             mbar_arrive_expect(abar, (uint32_t)n * (cols + 8u * nb));
             for (int v = 0; v < n; v++) {
-                bulk_g2s(sq + (size_t)v * cols, in.q + (size_t)v * in.cols, (uint32_t)cols, abar);
+                bulk_g2s(sq + (size_t)v * qstride, in.q + (size_t)v * in.cols, (uint32_t)cols, abar);
                 bulk_g2s(sd + (size_t)v * nb, in.d + (size_t)v * nbi, (uint32_t)nb * 4u, abar);
                 bulk_g2s(sfs + (size_t)v * nb, in.fs + (size_t)v * nbi, (uint32_t)nb * 4u, abar);
             }
@@ -568,6 +572,170 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Nor
             const unsigned long long best = warp_max_u64(key);
             if (lane == 0) partial[(size_t)v * W0.npanels + panel] = best;
             if (panel == 0 && lane == 0) nan0[v] = acc[v] != acc[v];
+        }
+    }
+}
+
+// The LM head for n <= 4 rows with the exact int8 block dots on the tensor cores.
+// Same persistent schedule as k_mv_head (a warp owns whole panels and walks their units through a
+// TMA ring) and the same float arithmetic, but each 32-row x 32-column block of a unit is one
+// ldmatrix (the 16-byte row entries of rows 0..31) and two mma.sync.m16n8k32.s8 (rows 0-15 and
+// 16-31) against the A8 activations, instead of 32 dp4a and 8 shared loads per row. MMA
+// fragments: A row groupID (+8), columns 4 t..4 t+3 (+16) of the block = the low (high) nibbles
+// of bytes 4 t..4 t+3 of the row entry, exactly one ldmatrix word; B column n = vector n & 3
+// (columns 4..7 repeat vectors 0..3 so every lane receives useful sums); C: thread (g, t)
+// takes rows g (t < 2) or g + 8 (t >= 2) of each half for vectors 2 (t & 1), 2 (t & 1) + 1.
+// Integer sums are exact, so each (row, vector) chain
+//   acc = fma((float)isum, (D s6) d, acc); acc = fma(-(M m6), fsum, acc)   (blocks in order)
+// is bit-identical to kern_q4k and to k_mv_head. Then per-panel (max, first index) keys.
+constexpr int kHeadQPad = 16;   // bytes of padding per activation row: conflict-free B loads
+
+size_t head_mma_smem(int cols, bool norm) {
+    const size_t nb = cols / 32;
+    size_t b = kTallSmem + 16 + 4 * ((size_t)cols + kHeadQPad) + nb * 2 * 16 + 2 * 4 * nb * 4;
+    b = (b + 15) & ~(size_t)15;
+    if (norm) b += 4 * (size_t)cols * 4 + (size_t)cols * 4;
+    return b;
+}
+
+__device__ __forceinline__ void mma_s8_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
+}
+
+template <bool NORM>
+__global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in, NormIn nin, Step *st,
+                                                                 float *y, int ldy,
+                                                                 unsigned long long *partial, int *nan0) {
+    extern __shared__ __align__(128) uint8_t hsm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3, tv = t & 1;   // MMA group / thread in group; vector pair
+    uint8_t *ring = hsm + (size_t)warp * kRing * kUnitBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(hsm + (size_t)kTallWarps * kRing * kUnitBytes) + warp * kRing;
+    const int cols = W0.cols, nb = cols >> 5, nsb = W0.nsb, qs = cols + kHeadQPad;
+    uint64_t *abar = reinterpret_cast<uint64_t *>(hsm + kTallSmem);
+    int8_t *sq = reinterpret_cast<int8_t *>(hsm + kTallSmem + 16);                  // [4][qs]
+    float4 *sdfq = reinterpret_cast<float4 *>(sq + 4 * (size_t)qs);                 // [nb][2]
+    float *sd = reinterpret_cast<float *>(sdfq + (size_t)nb * 2), *sfs = sd + 4 * (size_t)nb;
+    const size_t off = (kTallSmem + 16 + 4 * (size_t)qs + (size_t)nb * 32 + 2 * 4 * (size_t)nb * 4 + 15) & ~(size_t)15;
+    float *sx = reinterpret_cast<float *>(hsm + off), *sw = sx + 4 * (size_t)cols;   // NORM only
+    const int gw = warp * gridDim.x + blockIdx.x, tw = gridDim.x * kTallWarps;
+    const int npw = W0.npanels > gw ? (W0.npanels - 1 - gw) / tw + 1 : 0;
+    const int total = npw * nsb;
+    auto src = [&](int u) -> const uint8_t * {
+        const int panel = gw + (u / nsb) * tw;
+        return W0.w + ((size_t)panel * nsb + (u % nsb)) * kUnitBytes;
+    };
+    if (lane == 0) {
+        for (int i = 0; i < kRing; i++) mbar_init(bars + i, 1);
+        fence_mbar_init();
+        for (int u = 0; u < kRing && u < total; u++) tma_load_1d(ring + (size_t)u * kUnitBytes, src(u), kUnitBytes, bars + u);
+    }
+    pdl_wait();   // the ring above holds weights only
+    pdl_trigger();
+    const int n = st->n;
+    if (n <= 0) {   // nothing to do: let the weight copies land before this CTA's shared memory goes
+        __syncwarp();
+        for (int u = 0; u < kRing && u < total; u++) mbar_wait(bars + u, 0);
+        return;
+    }
+    __shared__ float srr[4];
+    if (!stage_act<NORM>(abar, n, cols, in, nin, sx, sw, sq, sd, sfs, qs) && threadIdx.x == 0)
+        st->status = -90;   // device wait timed out: reported, no hang
+    if (NORM) norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sd, sfs, srr, qs);
+    __syncthreads();
+    // (d, fsum) of vectors 2 p and 2 p + 1 for block b at sdfq[2 b + p]
+    for (int i = threadIdx.x; i < 2 * nb; i += blockDim.x) {
+        const int b = i >> 1, p = i & 1;
+        sdfq[i] = make_float4(sd[(2 * p) * nb + b], sfs[(2 * p) * nb + b], sd[(2 * p + 1) * nb + b],
+                              sfs[(2 * p + 1) * nb + b]);
+    }
+    __syncthreads();
+    const int8_t *bq = sq + (size_t)(g & 3) * qs + 4 * t;   // B fragment base of this lane
+    const int r0 = (t < 2 ? 0 : 8) + g;                     // this lane's row in each 16-row half
+    float acc[2][2];                                         // [half][vector of the pair]
+    for (int u = 0; u < total; u++) {
+        const int slot = u % kRing;
+        if (!mbar_wait(bars + slot, (uint32_t)(u / kRing) & 1u)) {
+            if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
+            return;
+        }
+        const uint8_t *sp = ring + (size_t)slot * kUnitBytes;
+        const int sb = u % nsb;
+        if (sb == 0) {
+            acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.0f;
+        }
+        // scale entries of this lane's two rows
+        const uint4 sc0 = lds128(sp + 16 * r0), sc1 = lds128(sp + 16 * (r0 + 16));
+        const unsigned long long A0 = (unsigned long long)sc0.x | ((unsigned long long)sc0.y << 32);
+        const unsigned long long B0 = (unsigned long long)sc0.z | ((unsigned long long)sc0.w << 32);
+        const unsigned long long A1 = (unsigned long long)sc1.x | ((unsigned long long)sc1.y << 32);
+        const unsigned long long B1 = (unsigned long long)sc1.z | ((unsigned long long)sc1.w << 32);
+        const float D0 = half_bits_to_float((uint32_t)(A0 >> 48)), M0 = half_bits_to_float((uint32_t)(B0 >> 48));
+        const float D1 = half_bits_to_float((uint32_t)(A1 >> 48)), M1 = half_bits_to_float((uint32_t)(B1 >> 48));
+        uint32_t am[8][4];
+#pragma unroll
+        for (int k = 0; k < 8; k++) ldsm_x4(am[k], sp + 512 * (k + 1) + 16 * lane);
+        __syncwarp();
+        if (lane == 0 && u + kRing < total) {
+            fence_proxy_async();
+            tma_load_1d(ring + (size_t)slot * kUnitBytes, src(u + kRing), kUnitBytes, bars + slot);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int b = sb * 8 + k;
+            const uint32_t b0 = *reinterpret_cast<const uint32_t *>(bq + b * 32);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t *>(bq + b * 32 + 16);
+            int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+            mma_s8_16832(c0, am[k][0] & 0x0f0f0f0fu, am[k][1] & 0x0f0f0f0fu, (am[k][0] >> 4) & 0x0f0f0f0fu,
+                         (am[k][1] >> 4) & 0x0f0f0f0fu, b0, b1);
+            mma_s8_16832(c1, am[k][2] & 0x0f0f0f0fu, am[k][3] & 0x0f0f0f0fu, (am[k][2] >> 4) & 0x0f0f0f0fu,
+                         (am[k][3] >> 4) & 0x0f0f0f0fu, b0, b1);
+            const float4 df = sdfq[2 * b + tv];
+            const int i00 = t < 2 ? c0[0] : c0[2], i01 = t < 2 ? c0[1] : c0[3];
+            const int i10 = t < 2 ? c1[0] : c1[2], i11 = t < 2 ? c1[1] : c1[3];
+            const float ds0 = __fmul_rn(D0, (float)(uint32_t)((A0 >> (6 * k)) & 63u));
+            const float os0 = __fmul_rn(M0, (float)(uint32_t)((B0 >> (6 * k)) & 63u));
+            const float ds1 = __fmul_rn(D1, (float)(uint32_t)((A1 >> (6 * k)) & 63u));
+            const float os1 = __fmul_rn(M1, (float)(uint32_t)((B1 >> (6 * k)) & 63u));
+            acc[0][0] = __fmaf_rn((float)i00, __fmul_rn(ds0, df.x), acc[0][0]);
+            acc[0][0] = __fmaf_rn(-os0, df.y, acc[0][0]);
+            acc[0][1] = __fmaf_rn((float)i01, __fmul_rn(ds0, df.z), acc[0][1]);
+            acc[0][1] = __fmaf_rn(-os0, df.w, acc[0][1]);
+            acc[1][0] = __fmaf_rn((float)i10, __fmul_rn(ds1, df.x), acc[1][0]);
+            acc[1][0] = __fmaf_rn(-os1, df.y, acc[1][0]);
+            acc[1][1] = __fmaf_rn((float)i11, __fmul_rn(ds1, df.z), acc[1][1]);
+            acc[1][1] = __fmaf_rn(-os1, df.w, acc[1][1]);
+        }
+        if (sb != nsb - 1) continue;
+        // panel done: logits and the per-panel keys (rows r0 and r0 + 16, vectors 2 tv, 2 tv + 1)
+        const int panel = gw + (u / nsb) * tw, rowa = panel * kPanelRows + r0, rowb = rowa + 16;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int v = 2 * tv + j;
+            const bool live = v < n;
+            if (live && y) {
+                if (rowa < W0.rows) y[(size_t)v * ldy + rowa] = acc[0][j];
+                if (rowb < W0.rows) y[(size_t)v * ldy + rowb] = acc[1][j];
+            }
+            const unsigned long long ka = rowa < W0.rows ? argmax_key(acc[0][j], rowa) : 0ull;
+            const unsigned long long kb = rowb < W0.rows ? argmax_key(acc[1][j], rowb) : 0ull;
+            unsigned long long best = ka > kb ? ka : kb;
+            // lanes holding the same vector pair: t and t ^ 2 over every g
+#pragma unroll
+            for (int o = 2; o <= 16; o <<= 1) {
+                const unsigned long long w = __shfl_xor_sync(0xffffffffu, best, o);
+                best = w > best ? w : best;
+            }
+            if (live && lane == tv) partial[(size_t)v * W0.npanels + panel] = best;
+            if (live && panel == 0 && lane == tv) nan0[v] = acc[0][j] != acc[0][j];
         }
     }
 }
@@ -2149,6 +2317,14 @@ void head_t2(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int ldy
         W, in, nin, const_cast<Step *>(st), y, ldy, partial, nan0);
 }
 
+template <bool NORM>
+void head_mma_t(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int ldy,
+                unsigned long long *partial, int *nan0, cudaStream_t s) {
+    const int grid = std::min(2 * num_sms(), (W.npanels + kTallWarps - 1) / kTallWarps);
+    launch_k(k_mv_head_mma<NORM>, std::max(grid, 1), kTallWarps * 32, head_mma_smem(W.cols, NORM), s, W, in, nin,
+             const_cast<Step *>(st), y, ldy, partial, nan0);
+}
+
 template <int NMAX, int EPI, bool NORM>
 bool panel_t(const Mat &W0, const Mat &W1, Act in, NormIn nin, const Step *st, float *y, int ldy,
              Act out, cudaStream_t s) {
@@ -2202,8 +2378,7 @@ void launch_matvec_swiglu_norm(const Mat &G, const Mat &U, const float *x, const
 void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int ld,
                         unsigned long long *partial, int *nan0, int nmax, cudaStream_t s) {
     const NormIn nn{};
-    if (nmax <= 1) head_t2<1, false>(W, in, nn, st, logits, ld, partial, nan0, s);
-    else if (nmax <= 4) head_t2<4, false>(W, in, nn, st, logits, ld, partial, nan0, s);
+    if (nmax <= 4) head_mma_t<false>(W, in, nn, st, logits, ld, partial, nan0, s);
     else if (nmax <= 8) head_t2<8, false>(W, in, nn, st, logits, ld, partial, nan0, s);
     else head_t2<16, false>(W, in, nn, st, logits, ld, partial, nan0, s);
 }
@@ -2213,8 +2388,7 @@ void launch_matvec_head_norm(const Mat &W, const float *x, const float *w, float
                              cudaStream_t s) {
     const NormIn nin{x, w, eps};
     const Act none;
-    if (nmax <= 1) head_t2<1, true>(W, none, nin, st, logits, ld, partial, nan0, s);
-    else if (nmax <= 4) head_t2<4, true>(W, none, nin, st, logits, ld, partial, nan0, s);
+    if (nmax <= 4) head_mma_t<true>(W, none, nin, st, logits, ld, partial, nan0, s);
     else if (nmax <= 8) head_t2<8, true>(W, none, nin, st, logits, ld, partial, nan0, s);
     else head_t2<16, true>(W, none, nin, st, logits, ld, partial, nan0, s);
 }
@@ -2323,6 +2497,8 @@ int kernels_init(int max_ctx, int hd, int rep) {
     raise_smem(k_mv_head<8, true>);
     raise_smem(k_mv_head<16, false>);
     raise_smem(k_mv_head<16, true>);
+    raise_smem(k_mv_head_mma<false>);
+    raise_smem(k_mv_head_mma<true>);
     raise_smem(k_mv_panel<1, 0, false>);
     raise_smem(k_mv_panel<1, 1, false>);
     raise_smem(k_mv_panel<1, 3, false>);

@@ -109,3 +109,36 @@ def test_rows_independent_of_batch(lib, torch, q4k_oracle):
             assert np.array_equal(yb[v].view(np.uint32), dev.run(dW, x[v:v + 1])[0].view(np.uint32))
     finally:
         dev.close()
+
+
+@pytest.mark.parametrize("rows,cols", [(4100, 1024), (2048, 2048)])
+@pytest.mark.parametrize("n", [1, 2, 3, 4])
+def test_head_kernel_bit_exact_and_argmax(lib, torch, q4k_oracle, rows, cols, n):
+    """The LM-head kernel (per-panel argmax keys, optional logits) through the kernel ABI:
+    logits bit-identical to the oracle, and the argmax from the keys equal to the first maximum
+    of the oracle's logits (pf_argmax); rows 4100 leaves a partial last panel."""
+    w = q4k_oracle.kb_matrix(rows, cols, 5)
+    dev = Dev(lib, torch, rows, cols, nmax=4)
+    try:
+        dW = dev.upload(w)
+        x = np.random.default_rng(rows + n).standard_normal((n, cols)).astype(np.float32)
+        dX = torch.from_numpy(x).cuda()
+        npan = (rows + 31) // 32
+        y = torch.zeros((n, rows), dtype=torch.float32, device="cuda")
+        part = torch.zeros((n, npan), dtype=torch.int64, device="cuda")
+        nan0 = torch.zeros(16, dtype=torch.int32, device="cuda")
+        s = dev.stream
+        assert lib.nb_mv_set_n(dev.h, n, s) == 0 and lib.nb_mv_quant(dev.h, dX.data_ptr(), s) == 0
+        assert lib.nb_mv_head_repeat(dev.h, dW.data_ptr(), 0, 1, y.data_ptr(), 1, part.data_ptr(),
+                                     nan0.data_ptr(), s) == 0
+        torch.cuda.synchronize()
+        want = q4k_oracle.matmul(w, rows, cols, x)
+        got = y.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        keys = part.cpu().numpy().view(np.uint64)
+        for v in range(n):
+            best = int(keys[v].max())
+            assert 0xFFFFFFFF - (best & 0xFFFFFFFF) == int(np.argmax(want[v]))
+        assert not nan0.cpu().numpy()[:n].any()
+    finally:
+        dev.close()
