@@ -103,6 +103,7 @@ struct pinfer_ctx {
     int eos = 0;
     int has_mtp = 0;
     uint64_t fp = 0;
+    PqHeader hdr{};   // copy of the file header (the mapping is released after upload)
     cudaStream_t stream = nullptr;
 
     // weights (panel layout) and float parameters on the device
@@ -605,6 +606,7 @@ pinfer_ctx *pinfer_load(const char *path, const pinfer_params *params, int *err)
         }
         if (rc == PINFER_OK) rc = alloc_and_upload(c);
         if (rc == PINFER_OK) {
+            c->hdr = *c->file.hdr;
             c->file.close_file();   // everything lives in HBM now
             if (cudaDeviceSynchronize() != cudaSuccess) rc = PINFER_E_NOMEM;
         }
@@ -715,17 +717,115 @@ int pinfer_generate_greedy(pinfer_ctx *c, const int32_t *prompt, int n_prompt, i
 }
 
 // ---- conversation state -------------------------------------------------------------------
-size_t pinfer_state_size(const pinfer_ctx *c) {
-    (void)c;
-    return 0;
+// The reference's blob (engine/src/state.c:20-118), so blobs move between the two engines:
+//   72-byte header: "PINFERS", version 2, n_past, kv_dtype, MTP rows, model dims, full-attention
+//                   mask, pf_model_fingerprint of the file
+//   per linear-attention layer (layer order): conv state [(K-1)][C], recurrent state [nv][dk][dv]
+//   per full-attention layer: K rows [n_kv][n_past][hd], then V rows (fp32 storage)
+// This build keeps no MTP cache, so the MTP row count is 0. Every generation ends with its
+// deferred DeltaNet commit flushed, so the device state is complete whenever the API returns.
+namespace {
+struct StateHdr {
+    char magic[8];
+    uint32_t version, n_past, kv_dtype, mtp_rows;
+    uint32_t n_layers, hidden, n_kv, head_dim, lk_heads, lv_heads, lk_dim, lv_dim, conv_k;
+    uint32_t full_mask;
+    uint64_t model_fp;
+};
+static_assert(sizeof(StateHdr) == 72, "state header layout of engine/src/state.c:24-30");
+constexpr uint32_t kStateVersion = 2;
+
+size_t lin_state_floats(const pinfer_ctx *c) {
+    return (size_t)std::max(c->K - 1, 1) * c->C + (size_t)c->nv * c->dk * c->dv;
 }
+size_t state_bytes(const pinfer_ctx *c, int n_past) {
+    int n_full = 0;
+    for (int l = 0; l < c->n_layers; l++) n_full += c->layers[l].is_full;
+    return sizeof(StateHdr) + (size_t)c->n_lin * lin_state_floats(c) * 4 +
+           (size_t)n_full * 2 * c->nkv * (size_t)n_past * c->hd * 4;
+}
+StateHdr state_header(const pinfer_ctx *c) {
+    const PqHeader *h = &c->hdr;
+    StateHdr s{};
+    memcpy(s.magic, "PINFERS", 8);
+    s.version = kStateVersion;
+    s.n_past = (uint32_t)c->n_past;
+    s.kv_dtype = PINFER_KV_F32;
+    s.mtp_rows = 0;
+    s.n_layers = h->n_layers;
+    s.hidden = h->hidden;
+    s.n_kv = h->n_kv_heads;
+    s.head_dim = h->head_dim;
+    s.lk_heads = h->lin_k_heads;
+    s.lv_heads = h->lin_v_heads;
+    s.lk_dim = h->lin_k_dim;
+    s.lv_dim = h->lin_v_dim;
+    s.conv_k = h->conv_k;
+    s.full_mask = h->full_attn_mask;
+    s.model_fp = c->fp;
+    return s;
+}
+// dir 0: device -> blob, 1: blob -> device; rows [0, n_past) of every cache
+int state_copy(pinfer_ctx *c, char *cur, int n_past, int dir) {
+    const auto kind = dir == 0 ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
+    auto mv = [&](void *dev, size_t bytes) -> int {
+        if (bytes == 0) return PINFER_OK;
+        CUDA_OK(dir == 0 ? cudaMemcpyAsync(cur, dev, bytes, kind, c->stream)
+                         : cudaMemcpyAsync(dev, cur, bytes, kind, c->stream));
+        cur += bytes;
+        return PINFER_OK;
+    };
+    int rc;
+    const size_t conv = (size_t)std::max(c->K - 1, 1) * c->C * 4, rec = (size_t)c->nv * c->dk * c->dv * 4;
+    for (int i = 0; i < c->n_lin; i++)
+        if ((rc = mv(c->lin[i].conv_state, conv)) || (rc = mv(c->lin[i].rec, rec))) return rc;
+    const size_t rows = (size_t)n_past * c->hd * 4, gstride = (size_t)c->max_ctx * c->hd;
+    for (int l = 0; l < c->n_layers; l++) {
+        if (!c->layers[l].is_full) continue;
+        for (int kv = 0; kv < 2; kv++)
+            for (int g = 0; g < c->nkv; g++)
+                if ((rc = mv((kv ? c->att[l].vc : c->att[l].kc) + g * gstride, rows))) return rc;
+    }
+    CUDA_OK(cudaStreamSynchronize(c->stream));
+    return PINFER_OK;
+}
+}  // namespace
+
+size_t pinfer_state_size(const pinfer_ctx *c) { return c ? state_bytes(c, c->n_past) : 0; }
+
 int pinfer_state_save(const pinfer_ctx *c, void *buf, size_t cap) {
-    (void)c; (void)buf; (void)cap;
-    return PINFER_E_ARG;
+    if (!c || !buf) return PINFER_E_ARG;
+    if (cap < state_bytes(c, c->n_past)) return PINFER_E_ARG;
+    pinfer_ctx *m = const_cast<pinfer_ctx *>(c);   // the stream is used, the state is not changed
+    const StateHdr h = state_header(c);
+    memcpy(buf, &h, sizeof h);
+    return state_copy(m, static_cast<char *>(buf) + sizeof h, c->n_past, 0);
 }
+
 int pinfer_state_load(pinfer_ctx *c, const void *buf, size_t len) {
-    (void)c; (void)buf; (void)len;
-    return PINFER_E_FORMAT;
+    if (!c || !buf || len < sizeof(StateHdr)) return PINFER_E_ARG;
+    StateHdr h;
+    memcpy(&h, buf, sizeof h);
+    const StateHdr mine = state_header(c);
+    if (memcmp(h.magic, "PINFERS", 8) != 0 || h.version != kStateVersion) return PINFER_E_FORMAT;
+    if (h.n_layers != mine.n_layers || h.hidden != mine.hidden || h.n_kv != mine.n_kv ||
+        h.head_dim != mine.head_dim || h.lk_heads != mine.lk_heads || h.lv_heads != mine.lv_heads ||
+        h.lk_dim != mine.lk_dim || h.lv_dim != mine.lv_dim || h.conv_k != mine.conv_k ||
+        h.full_mask != mine.full_mask || h.kv_dtype != mine.kv_dtype || h.model_fp != mine.model_fp)
+        return PINFER_E_FORMAT;   // another model file, or another KV storage format
+    if (h.n_past > (uint32_t)c->max_ctx) return PINFER_E_CTX_FULL;
+    // MTP rows (saved by an engine with the draft head's cache) are dropped: this build keeps
+    // no MTP cache, like a model converted without the head (state.c:137-140)
+    if (h.mtp_rows > h.n_past) return PINFER_E_FORMAT;
+    const size_t mtp = 2 * (size_t)h.n_kv * h.mtp_rows * h.head_dim * 4;
+    if (len < state_bytes(c, (int)h.n_past) + mtp) return PINFER_E_FORMAT;
+    launch_flush(c->lin, 0, c->lind, c->step, c->stream);   // drop any pending commit
+    const int rc = state_copy(c, const_cast<char *>(static_cast<const char *>(buf)) + sizeof h,
+                              (int)h.n_past, 1);
+    if (rc) return rc;
+    c->n_past = (int)h.n_past;
+    c->ck_valid = 0;   // the KV rows below the checkpoint were replaced
+    return PINFER_OK;
 }
 
 int pinfer_checkpoint(pinfer_ctx *c) {

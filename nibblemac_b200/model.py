@@ -138,6 +138,20 @@ class Model:
             raise PinferError(n, "pinfer_b200_generate_synthetic_ex", self.lib.last_error())
         return out[:n].tolist(), st, status.value, ms.value
 
+    def save_state(self) -> bytes:
+        """The conversation state blob (pinfer_state_save; the reference's format)."""
+        n = self.lib.pinfer_state_size(self.ctx)
+        buf = ctypes.create_string_buffer(n)
+        rc = self.lib.pinfer_state_save(self.ctx, buf, n)
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_state_save", self.lib.last_error())
+        return buf.raw
+
+    def load_state(self, data: bytes) -> None:
+        rc = self.lib.pinfer_state_load(self.ctx, data, len(data))
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_state_load", self.lib.last_error())
+
     def checkpoint(self) -> None:
         rc = self.lib.pinfer_checkpoint(self.ctx)
         if rc != PINFER_OK:

@@ -98,6 +98,10 @@ class RefEngine:
         L.ref_spec_generate.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P,
                                         ctypes.c_uint64, ctypes.c_uint32, _P]
         L.ref_forward_all.argtypes = [_P, _P, ctypes.c_int, _P]
+        L.pinfer_state_size.restype = ctypes.c_size_t
+        L.pinfer_state_size.argtypes = [_P]
+        L.pinfer_state_save.argtypes = [_P, _P, ctypes.c_size_t]
+        L.pinfer_state_load.argtypes = [_P, _P, ctypes.c_size_t]
         L.nb_synth_draft.restype = ctypes.c_int32
         L.nb_synth_draft.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_int32,
                                      ctypes.c_int32]
@@ -131,6 +135,17 @@ class RefEngine:
         if rc:
             raise RuntimeError(f"reference pinfer_eval: {rc}")
         return out
+
+    def save_state(self) -> bytes:
+        n = self.lib.pinfer_state_size(self.ctx)
+        buf = ctypes.create_string_buffer(n)
+        rc = self.lib.pinfer_state_save(self.ctx, buf, n)
+        if rc:
+            raise RuntimeError(f"reference pinfer_state_save: {rc}")
+        return buf.raw
+
+    def load_state(self, data: bytes) -> int:
+        return self.lib.pinfer_state_load(self.ctx, data, len(data))
 
     def forward_all(self, tokens) -> np.ndarray:
         t = np.ascontiguousarray(tokens, np.int32)

@@ -2,6 +2,8 @@
 own C sources run on the host CPU): logits bit for bit, greedy tokens identical, and
 speculative decoding with the synthetic drafter identical to plain decoding with the same
 acceptance counts as the reference's own speculative loop."""
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -105,3 +107,39 @@ def test_context_full(pair):
     with pytest.raises(PinferError) as e:
         dev.eval(np.zeros(513, np.int32))
     assert e.value.code == -5 and dev.n_past == 0
+
+
+def test_state_blob_equals_reference_and_round_trips(pair):
+    """pinfer_state_save after the same prompt gives the reference engine's blob byte for byte
+    (header with the model fingerprint, conv and recurrent states, K/V rows); loading either
+    blob and continuing gives the reference's logits; bad blobs are refused like the reference
+    (engine/src/state.c:120-160)."""
+    from nibblemac_b200._lib import PINFER_E_ARG, PINFER_E_FORMAT
+    from nibblemac_b200.model import PinferError
+    name, dev, ref = pair
+    a, b = prompt(dev.n_vocab, 37, 21), prompt(dev.n_vocab, 6, 22)
+    dev.reset()
+    ref.reset()
+    dev.eval(a)
+    ref.eval(a)
+    blob, rblob = dev.save_state(), ref.save_state()
+    assert len(blob) == len(rblob) == dev.lib.pinfer_state_size(dev.ctx)
+    assert blob == rblob, f"{name}: state blob differs from the reference's"
+    want = ref.eval(b)
+    assert np.array_equal(bits(dev.eval(b)), bits(want))
+    dev.eval(prompt(dev.n_vocab, 9, 23))          # move on, then come back
+    dev.load_state(rblob)
+    assert dev.n_past == len(a)
+    assert np.array_equal(bits(dev.eval(b)), bits(want))
+    dev.reset()
+    dev.load_state(blob)
+    assert np.array_equal(bits(dev.eval(b)), bits(want))
+    bad = bytearray(blob)
+    bad[0] ^= 1
+    for data, code in ((bytes(bad), PINFER_E_FORMAT), (blob[:len(blob) - 4], PINFER_E_FORMAT),
+                       (blob[:40], PINFER_E_ARG)):
+        with pytest.raises(PinferError) as e:
+            dev.load_state(data)
+        assert e.value.code == code
+    small = ctypes.create_string_buffer(16)
+    assert dev.lib.pinfer_state_save(dev.ctx, small, 16) == PINFER_E_ARG
