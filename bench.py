@@ -210,7 +210,7 @@ def cpu_baseline_sample(path: Path) -> dict:
     assert toks == greedy
     sec = ref.last_decode_s
     ref.close()
-    return {"value": round(len(toks) / sec, 3), "unit": UNIT, "cores": 1, "kind": "reference",
+    return {"value": round((len(toks) - 1) / sec, 3), "unit": UNIT, "cores": 1, "kind": "reference",
             "sample": "reference engine (scalar C, oracle/_ref) on the 0.8B model: 32-token "
                       "context, 16 tokens at k=3 p=0.8, decode loop timed"}
 
@@ -230,7 +230,7 @@ def run_reference(args, rank: int, world: int) -> None:
         assert out == greedy
         if i >= args.warmup:
             secs.append(ref.last_decode_s)
-            toks += len(out)
+            toks += len(out) - 1   # the decode loop's tokens (the first comes from the prefill)
     ref.close()
     total = sum(secs)
     value = toks / total
@@ -331,15 +331,29 @@ def main() -> None:
         tt = torch.tensor([t_dev, t_wall], dtype=torch.float64, device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_dev, t_wall = tt.tolist()
-    tokens = N_GEN * args.steps * world
-    value = tokens / t_dev
-    e2e = tokens / t_wall
+    # the device-timed loop emits N_GEN - 1 tokens (the first comes from the one-token prefill);
+    # the end-to-end call produces all N_GEN
+    value = (N_GEN - 1) * args.steps * world / t_dev
+    e2e = N_GEN * args.steps * world / t_wall
 
     sweep = {}
     for p in P_SWEEP:
         ms, _, st = step(p, 77)
-        sweep[str(p)] = {"tok_s": round(N_GEN / (ms / 1000.0), 1),
-                         "tokens_per_round": round(N_GEN / st.rounds, 3)}
+        sweep[str(p)] = {"tok_s": round((N_GEN - 1) / (ms / 1000.0), 1),
+                         "tokens_per_round": round((N_GEN - 1) / st.rounds, 3)}
+
+    # plain greedy decode (no speculation, batch 1) of a 64-token uniform-random
+    # prompt, 128 tokens; decode steps timed on the device like the reference's pinfer_run
+    # (prefill excluded, N - 1 decode steps)
+    p64 = context_tokens(rank + 7, m.n_vocab)[:64]
+    c2 = []
+    for _ in range(3):
+        m.reset()
+        _, _, st2, ms2 = m.generate_synthetic_ex(p64, N_GEN, 0, np.zeros(N_GEN, np.int32), 0, 0.0)
+        assert st2 == 0
+        c2.append(ms2)
+    config2 = {"tok_s": round((N_GEN - 1) / (statistics.median(c2) / 1000.0), 1), "prompt": 64,
+               "generated": N_GEN, "k": 0, "ms": round(statistics.median(c2), 3)}
 
     roof = None
     extra = {}
@@ -368,7 +382,7 @@ def main() -> None:
                         "h2d_bytes_per_step": 4 * (1 + N_GEN), "d2h_bytes_per_step": 4 * N_GEN},
                 "gpu_launches": int(rounds * kernels_per_round * world),
                 "kernels_per_round": kernels_per_round, "rounds": rounds,
-                "sweep": sweep, "roofline": roof, "clocks": clk.summary()}
+                "sweep": sweep, "config2_plain": config2, "roofline": roof, "clocks": clk.summary()}
         line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(path)
