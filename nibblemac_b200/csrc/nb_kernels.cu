@@ -1627,6 +1627,8 @@ size_t attn2_smem(int max_ctx) {
 // cluster barrier before exit so no peer reads shared memory that is gone.
 constexpr int kAttnCL = 8;
 constexpr int kAttnSlice = kAttnHd / kAttnCL;   // 32 output columns per CTA
+constexpr int kAttnChunk = 32;                   // V rows per cp.async group (one 16 B copy per thread)
+constexpr int kAttnRing = 16;                    // chunks in the V ring (512 rows, 64 KB)
 
 __device__ __forceinline__ void cluster_arrive() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
@@ -1651,7 +1653,7 @@ __device__ __forceinline__ float ld_dsmem(const float *local, uint32_t rank) {
 size_t attn3_smem(int max_ctx) {
     const size_t per = ((size_t)max_ctx + kAttnCL - 1) / kAttnCL;
     return sizeof(float) * ((size_t)kAttnHd + ((per + 3) & ~(size_t)3) + (((size_t)max_ctx + 3) & ~(size_t)3) +
-                            (size_t)max_ctx * kAttnSlice);
+                            (size_t)kAttnRing * kAttnChunk * kAttnSlice);
 }
 
 __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
@@ -1668,18 +1670,25 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     const int per = (d.max_ctx + kAttnCL - 1) / kAttnCL;
     extern __shared__ __align__(16) float asm3[];
     float *q = asm3, *part = q + HD, *att = part + ((per + 3) & ~3);
-    float *vs = att + ((d.max_ctx + 3) & ~3);   // [np][32]
+    float *vs = att + ((d.max_ctx + 3) & ~3);   // V ring: [kAttnRing][kAttnChunk rows][32]
     __shared__ float red[32];
     __shared__ float s_mx, s_inv;
 
-    // V columns c*32 .. c*32+31 of rows 0..np-1 (8 x 16 bytes per row)
+    // V columns c*32 .. c*32+31 stream through a ring of kAttnRing chunks of kAttnChunk rows
+    // (8 x 16 bytes per row, one copy per thread per chunk, one cp.async group per chunk); the
+    // first kAttnRing - 1 chunks start now, behind the scores
     const float *V = L.vc + (size_t)g * d.max_ctx * HD + c * kAttnSlice;
-    for (int i = tid; i < np * 8; i += HD) {
-        const int r = i >> 3, k = i & 7;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                     ::"r"(smem_u32(vs + (size_t)r * kAttnSlice + 4 * k)), "l"(V + (size_t)r * HD + 4 * k) : "memory");
-    }
-    cp_async_commit();
+    const int nch = (np + kAttnChunk - 1) / kAttnChunk;
+    auto issue_chunk = [&](int ch) {
+        const int r = ch * kAttnChunk + (tid >> 3), k = tid & 7;
+        if (ch < nch && r < np)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                         ::"r"(smem_u32(vs + ((size_t)(ch % kAttnRing) * kAttnChunk + (tid >> 3)) * kAttnSlice + 4 * k)),
+                         "l"(V + (size_t)r * HD + 4 * k) : "memory");
+        cp_async_commit();   // one group per chunk, empty past the end
+    };
+    static_assert(kAttnChunk * 8 == kAttnHd, "one 16-byte copy per thread per chunk");
+    for (int ch = 0; ch < kAttnRing - 1; ch++) issue_chunk(ch);
     q[tid] = qbuf[((size_t)t * d.nq + h) * HD + tid];
     const float gate = tid < kAttnSlice ? y[(size_t)t * d.ldy + (size_t)2 * HD * h + HD + c * kAttnSlice + tid] : 0.0f;
     __syncthreads();
@@ -1740,25 +1749,34 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     __syncthreads();
     const float inv = s_inv;
     for (int p = tid; p < np; p += HD) att[p] = __fmul_rn(att[p], inv);
-    cp_async_wait<0>();
-    __syncthreads();
 
-    // 3. ordered PV chain for this CTA's 32 columns, gate, A8
-    if (warp == 0) {
-        float o = 0.0f;
-        const float *vp = vs + lane;
-        int p = 0;
-        for (; p + 8 <= np; p += 8) {
-            float v[8], a[8];
+    // 3. ordered PV chain for this CTA's 32 columns (warp 0, chunk by chunk through the ring;
+    // every thread waits for its copy of chunk ch, refills the slot chunk ch - 1 used), gate, A8
+    float o = 0.0f;
+    const float *vp = vs + lane;
+    for (int ch = 0; ch < nch; ch++) {
+        cp_async_wait<kAttnRing - 2>();
+        __syncthreads();
+        issue_chunk(ch + kAttnRing - 1);
+        if (warp == 0) {
+            const float *cv = vp + (size_t)(ch % kAttnRing) * kAttnChunk * kAttnSlice;
+            const int p0c = ch * kAttnChunk, rows = min(kAttnChunk, np - p0c);
+            int i = 0;
+            for (; i + 8 <= rows; i += 8) {
+                float v[8], a[8];
 #pragma unroll
-            for (int r = 0; r < 8; r++) {
-                v[r] = vp[(size_t)(p + r) * kAttnSlice];
-                a[r] = att[p + r];
+                for (int r = 0; r < 8; r++) {
+                    v[r] = cv[(size_t)(i + r) * kAttnSlice];
+                    a[r] = att[p0c + i + r];
+                }
+#pragma unroll
+                for (int r = 0; r < 8; r++) o = madd(o, a[r], v[r]);
             }
-#pragma unroll
-            for (int r = 0; r < 8; r++) o = madd(o, a[r], v[r]);
+            for (; i < rows; i++) o = madd(o, att[p0c + i], cv[(size_t)i * kAttnSlice]);
         }
-        for (; p < np; p++) o = madd(o, att[p], vp[(size_t)p * kAttnSlice]);
+    }
+    cp_async_wait<0>();   // the empty trailing groups
+    if (warp == 0) {
         o = __fmul_rn(o, pf_sigmoid(gate));
         const int col = h * HD + (int)c * kAttnSlice, nbo = out.cols >> 5;
         quant_block_warp(o, lane, out.q + (size_t)t * out.cols + col, out.d + (size_t)t * nbo + (col >> 5),

@@ -143,3 +143,26 @@ def test_state_blob_equals_reference_and_round_trips(pair):
         assert e.value.code == code
     small = ctypes.create_string_buffer(16)
     assert dev.lib.pinfer_state_save(dev.ctx, small, 16) == PINFER_E_ARG
+
+
+def test_long_context_attention_bit_exact(small_model):
+    """Attention over ~1300 positions (the V stream wraps its 512-row ring of the cluster kernel
+    more than twice): last-token logits after a long prompt and after a speculative generation
+    continuing it, against the reference engine."""
+    from nibblemac_b200.model import Model
+    from oracle import RefEngine
+    dev = Model(small_model, max_ctx=2048)
+    ref = RefEngine(small_model, max_ctx=2048)
+    try:
+        p = prompt(dev.n_vocab, 1300, 31)
+        assert np.array_equal(bits(dev.eval(p)), bits(ref.eval(p)))
+        q = prompt(dev.n_vocab, 7, 32)
+        assert np.array_equal(bits(dev.eval(q)), bits(ref.eval(q)))
+        dev.reset()
+        ref.reset()
+        greedy = ref.generate(p, 24)
+        toks, st, status = dev.generate_synthetic(p, 24, 3, greedy, seed=5, p=0.8)
+        assert status == 0 and toks == greedy
+    finally:
+        dev.close()
+        ref.close()
