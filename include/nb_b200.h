@@ -50,6 +50,23 @@ int pinfer_b200_forward_all(pinfer_ctx *ctx, const int32_t *tokens, int n, float
 /* The CUDA stream every call on ctx runs on (for timing with events on the same stream). */
 void *pinfer_b200_stream(pinfer_ctx *ctx);
 
+/* ---- vocab-sharded LM head ------------------------------------------
+ * No reference counterpart (the reference runs on one device). One context per GPU, each with
+ * the same model and fed the same tokens: every GPU runs the layers, and its LM head covers only
+ * vocabulary rows [rank * V / world, (rank + 1) * V / world); the greedy argmax of each verify
+ * row is merged with one NCCL all-reduce (max) of 64-bit (order-preserving value, first index)
+ * keys, so every rank accepts the same tokens, and pinfer_eval's logits are all-gathered.
+ * libnccl.so.2 is loaded on first use.
+ * pinfer_b200_nccl_id: a 128-byte NCCL unique id, made on one rank and sent to the others by the
+ * caller. pinfer_b200_shard_head: collective over the `world` ranks (each calls it with the same
+ * id); requires V % (32 * world) == 0; world == 1 undoes sharding. 0, -4 (arguments), -3 (NCCL
+ * or CUDA failure, message in pinfer_b200_last_error). */
+int pinfer_b200_nccl_id(void *id);
+int pinfer_b200_shard_head(pinfer_ctx *ctx, int rank, int world, const void *id);
+/* The 64-bit argmax key of (logit v, vocabulary row) the device uses (host function, for
+ * checks): unsigned maximum over any partition of the rows = the pf_argmax of all of them. */
+unsigned long long nb_argmax_key(float v, int row);
+
 /* ---- kernel-level ABI: the Q4K x A8 matmul on device buffers ----------------------------
  * The pf_matmul contract for dtype Q4K_G32 (engine/src/ops.h:49-52: Y[n][rows] = W X, weights
  * read once for all n) with the reference's arithmetic (kern_quant_act, kern_act.c:14-41;

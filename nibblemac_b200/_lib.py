@@ -103,6 +103,8 @@ _OPTIONAL = {
     "pinfer_b200_round_kernels": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "pinfer_b200_forward_all": (ctypes.c_int, [ctypes.c_void_p, _c_int32_p, ctypes.c_int, _c_float_p]),
     "pinfer_b200_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "pinfer_b200_nccl_id": (ctypes.c_int, [ctypes.c_void_p]),
+    "pinfer_b200_shard_head": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "nb_q4k_panel_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
     "nb_q4k_repack": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "nb_mv_create": (ctypes.c_void_p, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
@@ -121,6 +123,7 @@ _OPTIONAL = {
                                      ctypes.c_void_p, ctypes.c_void_p]),
     "nb_mv_run_static": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    "nb_argmax_key": (ctypes.c_ulonglong, [ctypes.c_float, ctypes.c_int]),
     "nb_libm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_longlong, ctypes.POINTER(ctypes.c_longlong)]),
     "nb_libm_eval_host": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong]),
     "nb_libm_eval_device": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,

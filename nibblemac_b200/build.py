@@ -56,7 +56,7 @@ def build_quant() -> Path:
 def build_engine() -> Path:
     out = LIB / "libpinfer.so"
     cu = ["nb_kernels.cu", "nb_engine.cu", "nb_capi.cu"]
-    cpp = ["nb_model.cpp", "nb_libm.cpp"]
+    cpp = ["nb_model.cpp", "nb_libm.cpp", "nb_nccl.cpp"]
     headers = sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
     BUILD.mkdir(exist_ok=True)
     objs = []
@@ -73,7 +73,7 @@ def build_engine() -> Path:
     if not newer(out, objs + [CSRC / "pinfer.map"]):
         run([NVCC, *ARCH, "-shared", "-o", out, *objs,
              "-Xlinker", "-soname=libpinfer.so.0.3",
-             "-Xlinker", f"--version-script={CSRC / 'pinfer.map'}", "-lpthread"])
+             "-Xlinker", f"--version-script={CSRC / 'pinfer.map'}", "-lpthread", "-ldl"])
     return out
 
 

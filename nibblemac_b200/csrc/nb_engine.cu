@@ -16,6 +16,7 @@
 
 #include "nb_engine.h"
 #include "nb_model.h"
+#include "nb_nccl.h"
 #include "pinfer.h"
 #include "nb_b200.h"
 
@@ -133,6 +134,13 @@ struct pinfer_ctx {
 
     // graphs of one verify round per draft depth k (index k), no graph = not captured yet
     cudaGraphExec_t round_graph[PINFER_SPEC_MAX_K + 1] = {};
+
+    // vocab-sharded LM head (pinfer_b200_shard_head): this GPU's rows [head_row0, +head_view.rows)
+    int device = 0;
+    int shard_rank = 0, shard_world = 1, head_row0 = 0;
+    Mat head_view;
+    ncclComm_t nccl = nullptr;
+    unsigned long long *d_keys = nullptr;   // [2][kMaxRows]: best key, row-0 NaN flag
     int round_nmax[PINFER_SPEC_MAX_K + 1] = {};
 
     // checkpoint slot (pinfer_checkpoint)
@@ -361,15 +369,36 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head) {
         launch_matvec(D.down, h, c->step, c->x, c->H, 1, nmax, s);
     }
     if (head) {
+        // sharded: this GPU's vocabulary rows only, logits at their global columns
+        const bool sharded = c->shard_world > 1;
+        const Mat &HW = sharded ? c->head_view : c->head;
+        float *lg = head == 1 ? c->logits + c->head_row0 : nullptr;
         if (nmax <= 4) {
-            launch_matvec_head_norm(c->head, c->x, c->norm, c->eps, c->step, head == 1 ? c->logits : nullptr,
-                                    c->vocab, c->partial, c->nan0, nmax, s);
+            launch_matvec_head_norm(HW, c->x, c->norm, c->eps, c->step, lg, c->vocab, c->partial, c->nan0,
+                                    nmax, s, c->head_row0);
         } else {
             launch_norm_quant(c->x, c->norm, c->H, c->eps, c->step, c->act_h, s);
-            launch_matvec_head(c->head, c->act_h, c->step, head == 1 ? c->logits : nullptr, c->vocab,
-                               c->partial, c->nan0, nmax, s);
+            launch_matvec_head(HW, c->act_h, c->step, lg, c->vocab, c->partial, c->nan0, nmax, s,
+                               c->head_row0);
         }
-        launch_argmax_final(c->partial, c->nan0, c->head.npanels, c->step, s);
+        if (!sharded) {
+            launch_argmax_final(c->partial, c->nan0, c->head.npanels, c->step, s);
+        } else {
+            // one all-reduce (max) of the (value, first index) keys across the shards: the
+            // tie and NaN rules of pf_argmax hold because the keys order exactly as they do
+            const NcclApi *n = nccl_api(nullptr, 0);
+            launch_argmax_keys(c->partial, c->nan0, HW.npanels, c->step, c->d_keys, s);
+            n->all_reduce(c->d_keys, c->d_keys, 2 * kMaxRows, ncclUint64, ncclMax, c->nccl, s);
+            launch_keys_argmax(c->d_keys, c->step, s);
+            if (head == 1) {   // logits of every row for the API: in-place all-gather of the shards
+                const size_t S = (size_t)c->head_view.rows;
+                n->group_start();
+                for (int v = 0; v < nmax; v++)
+                    n->all_gather(c->logits + (size_t)v * c->vocab + c->head_row0, c->logits + (size_t)v * c->vocab,
+                                  S, ncclFloat, c->nccl, s);
+                n->group_end();
+            }
+        }
     }
     launch_pass_end(c->step, s);
 }
@@ -600,6 +629,7 @@ pinfer_ctx *pinfer_load(const char *path, const pinfer_params *params, int *err)
             set_err("no CUDA device: this library runs on an NVIDIA B200 and has no CPU path");
             rc = PINFER_E_NOMEM;
         }
+        if (rc == PINFER_OK) cudaGetDevice(&c->device);
         if (rc == PINFER_OK && cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
             set_err("cannot create a CUDA stream");
             rc = PINFER_E_NOMEM;
@@ -623,6 +653,10 @@ void pinfer_free(pinfer_ctx *c) {
     if (!c) return;
     if (c->stream) cudaStreamSynchronize(c->stream);
     drop_graphs(c);
+    if (c->nccl) {
+        const NcclApi *n = nccl_api(nullptr, 0);
+        if (n) n->comm_destroy(c->nccl);
+    }
     for (void *p : c->allocs) cudaFree(p);
     cudaFree(c->d_out);
     cudaFree(c->d_greedy);
@@ -947,5 +981,69 @@ int pinfer_b200_forward_all(pinfer_ctx *c, const int32_t *tokens, int n, float *
 }
 
 void *pinfer_b200_stream(pinfer_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+int pinfer_b200_nccl_id(void *id) {
+    if (!id) return PINFER_E_ARG;
+    char err[200];
+    const NcclApi *n = nccl_api(err, sizeof err);
+    if (!n) {
+        set_err(err);
+        return PINFER_E_NOMEM;
+    }
+    ncclUniqueId u;
+    const ncclResult_t r = n->get_unique_id(&u);
+    if (r != ncclSuccess) {
+        set_err(n->error_string(r));
+        return PINFER_E_NOMEM;
+    }
+    memcpy(id, &u, sizeof u);
+    return PINFER_OK;
+}
+
+int pinfer_b200_shard_head(pinfer_ctx *c, int rank, int world, const void *id) {
+    if (!c || world < 1 || rank < 0 || rank >= world || (world > 1 && !id)) return PINFER_E_ARG;
+    if (world > 1 && c->vocab % (kPanelRows * world) != 0) {
+        set_err("the vocabulary must split into equal shards of whole 32-row panels");
+        return PINFER_E_ARG;
+    }
+    CUDA_OK(cudaStreamSynchronize(c->stream));
+    drop_graphs(c);   // captured rounds hold the old head
+    if (c->nccl) {
+        const NcclApi *n = nccl_api(nullptr, 0);
+        if (n) n->comm_destroy(c->nccl);
+        c->nccl = nullptr;
+    }
+    c->shard_rank = 0;
+    c->shard_world = 1;
+    c->head_row0 = 0;
+    if (world == 1) return PINFER_OK;
+    char err[200];
+    const NcclApi *n = nccl_api(err, sizeof err);
+    if (!n) {
+        set_err(err);
+        return PINFER_E_NOMEM;
+    }
+    int rc;
+    if (!c->d_keys && (rc = c->dalloc(&c->d_keys, sizeof(unsigned long long) * 2 * kMaxRows))) return rc;
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof u);
+    CUDA_OK(cudaSetDevice(c->device));
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = n->comm_init_rank(&comm, world, u, rank);
+    if (r != ncclSuccess) {
+        set_err(n->error_string(r));
+        return PINFER_E_NOMEM;
+    }
+    const int rows = c->vocab / world;
+    c->nccl = comm;
+    c->shard_rank = rank;
+    c->shard_world = world;
+    c->head_row0 = rank * rows;
+    c->head_view = c->head;
+    c->head_view.w = c->head.w + (size_t)(c->head_row0 / kPanelRows) * c->head.nsb * kUnitBytes;
+    c->head_view.rows = rows;
+    c->head_view.npanels = rows / kPanelRows;
+    return PINFER_OK;
+}
 
 }  // extern "C"

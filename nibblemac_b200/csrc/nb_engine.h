@@ -115,15 +115,21 @@ void launch_matvec_swiglu_norm(const Mat &G, const Mat &U, const float *x, const
                                const Step *st, Act out, int nmax, Act scratch, cudaStream_t s);
 void launch_matvec_head_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
                              float *logits, int ld, unsigned long long *partial, int *nan0, int nmax,
-                             cudaStream_t s);
+                             cudaStream_t s, int row_base = 0);
 // gate / up with SwiGLU and A8 quantisation of the product
 void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Act out, int nmax,
                           cudaStream_t s);
-// tied head: logits (may be null) [v][ld] and per-panel argmax partials
+// tied head: logits (may be null) [v][ld] and per-panel argmax partials; row_base is the
+// vocabulary index of W's row 0 (a vocab shard), which the argmax keys carry
 void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int ld,
-                        unsigned long long *partial, int *nan0, int nmax, cudaStream_t s);
+                        unsigned long long *partial, int *nan0, int nmax, cudaStream_t s, int row_base = 0);
 void launch_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
                          Step *st, cudaStream_t s);
+// vocab-sharded head: per-row best keys and NaN flags into keys [2][kMaxRows] (to be merged by
+// an all-reduce max across the shards), then the merged keys into Step::argmax
+void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int npanels, const Step *st,
+                        unsigned long long *keys, cudaStream_t s);
+void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s);
 void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
                      Step *st, Act out, cudaStream_t s);
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,

@@ -109,15 +109,6 @@ __device__ __forceinline__ void quant_block_oct(const float (&x)[4], int sub, bo
     }
 }
 
-// Order-preserving key of a (logit, row) pair: larger logit wins, then the lower row, NaN
-// never wins (pf_argmax, engine/src/forward_ops.c:387-409: first maximum, NaN skipped).
-__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
-    uint32_t u = __float_as_uint(v);
-    if (v != v) u = 0u;
-    else if (v == 0.0f) u = 0x80000000u;                 // +0 and -0 compare equal
-    else u = (u >> 31) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)u << 32) | (0xffffffffu - (uint32_t)row);
-}
 
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
     return __half2float(__ushort_as_half((unsigned short)h));
@@ -498,7 +489,8 @@ size_t tall_smem(int cols, int nmax, bool norm) {
 template <int NMAX, bool NORM>
 __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, NormIn nin, Step *st,
                                                              float *y, int ldy,
-                                                             unsigned long long *partial, int *nan0) {
+                                                             unsigned long long *partial, int *nan0,
+                                                             int row_base) {
     extern __shared__ __align__(128) uint8_t tsm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t *ring = tsm + (size_t)warp * kRing * kUnitBytes;
@@ -568,10 +560,10 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Nor
         for (int v = 0; v < NMAX; v++) {
             if (v >= n) break;
             if (y && row < W0.rows) y[(size_t)v * ldy + row] = acc[v];
-            const unsigned long long key = row < W0.rows ? argmax_key(acc[v], row) : 0ull;
+            const unsigned long long key = row < W0.rows ? argmax_key(acc[v], row_base + row) : 0ull;
             const unsigned long long best = warp_max_u64(key);
             if (lane == 0) partial[(size_t)v * W0.npanels + panel] = best;
-            if (panel == 0 && lane == 0) nan0[v] = acc[v] != acc[v];
+            if (panel == 0 && lane == 0 && row_base == 0) nan0[v] = acc[v] != acc[v];
         }
     }
 }
@@ -613,7 +605,8 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
 template <bool NORM>
 __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in, NormIn nin, Step *st,
                                                                  float *y, int ldy,
-                                                                 unsigned long long *partial, int *nan0) {
+                                                                 unsigned long long *partial, int *nan0,
+                                                                 int row_base) {
     extern __shared__ __align__(128) uint8_t hsm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3, tv = t & 1;   // MMA group / thread in group; vector pair
@@ -725,8 +718,8 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in,
                 if (rowa < W0.rows) y[(size_t)v * ldy + rowa] = acc[0][j];
                 if (rowb < W0.rows) y[(size_t)v * ldy + rowb] = acc[1][j];
             }
-            const unsigned long long ka = rowa < W0.rows ? argmax_key(acc[0][j], rowa) : 0ull;
-            const unsigned long long kb = rowb < W0.rows ? argmax_key(acc[1][j], rowb) : 0ull;
+            const unsigned long long ka = rowa < W0.rows ? argmax_key(acc[0][j], row_base + rowa) : 0ull;
+            const unsigned long long kb = rowb < W0.rows ? argmax_key(acc[1][j], row_base + rowb) : 0ull;
             unsigned long long best = ka > kb ? ka : kb;
             // lanes holding the same vector pair: t and t ^ 2 over every g
 #pragma unroll
@@ -735,7 +728,7 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in,
                 best = w > best ? w : best;
             }
             if (live && lane == tv) partial[(size_t)v * W0.npanels + panel] = best;
-            if (live && panel == 0 && lane == tv) nan0[v] = acc[0][j] != acc[0][j];
+            if (live && panel == 0 && lane == tv && row_base == 0) nan0[v] = acc[0][j] != acc[0][j];
         }
     }
 }
@@ -883,6 +876,41 @@ size_t panel_smem(int nw, int cols, int nmat, int nmax, bool norm) {
 }
 
 // ------------------------------------------------------------------ argmax over the panels
+// Vocab-sharded head: this GPU's best key per verify row and its row-0 NaN flag, for the
+// all-reduce (max) across the shards; k_keys_argmax turns the merged keys into tokens exactly
+// as k_argmax_final does.
+__global__ void k_argmax_keys(const unsigned long long *partial, const int *nan0, int npanels,
+                              const Step *st, unsigned long long *keys) {
+    pdl_wait();
+    pdl_trigger();
+    const int v = blockIdx.x;
+    if (v >= st->n) return;
+    __shared__ unsigned long long red[32];
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < npanels; i += blockDim.x) {
+        const unsigned long long k = partial[(size_t)v * npanels + i];
+        best = k > best ? k : best;
+    }
+    best = warp_max_u64(best);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        unsigned long long b = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+        b = warp_max_u64(b);
+        if (threadIdx.x == 0) {
+            keys[v] = b;
+            keys[kMaxRows + v] = nan0[v] ? 1ull : 0ull;
+        }
+    }
+}
+__global__ void k_keys_argmax(const unsigned long long *keys, Step *st) {
+    pdl_wait();
+    pdl_trigger();
+    const int v = threadIdx.x;
+    if (v >= st->n) return;
+    st->argmax[v] = keys[kMaxRows + v] ? 0 : (int)(0xffffffffu - (uint32_t)(keys[v] & 0xffffffffu));
+}
+
 __global__ void k_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
                                Step *st) {
     pdl_wait();
@@ -2329,18 +2357,18 @@ void raise_smem(K kern, size_t want = 0) {
 
 template <int NMAX, bool NORM>
 void head_t2(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int ldy,
-             unsigned long long *partial, int *nan0, cudaStream_t s) {
+             unsigned long long *partial, int *nan0, int row_base, cudaStream_t s) {
     const int grid = std::min(2 * num_sms(), (W.npanels + kTallWarps - 1) / kTallWarps);
-    launch_k(k_mv_head<NMAX, NORM>, std::max(grid, 1), kTallWarps * 32, tall_smem(W.cols, NMAX, NORM), s, 
-        W, in, nin, const_cast<Step *>(st), y, ldy, partial, nan0);
+    launch_k(k_mv_head<NMAX, NORM>, std::max(grid, 1), kTallWarps * 32, tall_smem(W.cols, NMAX, NORM), s,
+             W, in, nin, const_cast<Step *>(st), y, ldy, partial, nan0, row_base);
 }
 
 template <bool NORM>
 void head_mma_t(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int ldy,
-                unsigned long long *partial, int *nan0, cudaStream_t s) {
+                unsigned long long *partial, int *nan0, int row_base, cudaStream_t s) {
     const int grid = std::min(2 * num_sms(), (W.npanels + kTallWarps - 1) / kTallWarps);
     launch_k(k_mv_head_mma<NORM>, std::max(grid, 1), kTallWarps * 32, head_mma_smem(W.cols, NORM), s, W, in, nin,
-             const_cast<Step *>(st), y, ldy, partial, nan0);
+             const_cast<Step *>(st), y, ldy, partial, nan0, row_base);
 }
 
 template <int NMAX, int EPI, bool NORM>
@@ -2394,21 +2422,21 @@ void launch_matvec_swiglu_norm(const Mat &G, const Mat &U, const float *x, const
 }
 
 void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int ld,
-                        unsigned long long *partial, int *nan0, int nmax, cudaStream_t s) {
+                        unsigned long long *partial, int *nan0, int nmax, cudaStream_t s, int row_base) {
     const NormIn nn{};
-    if (nmax <= 4) head_mma_t<false>(W, in, nn, st, logits, ld, partial, nan0, s);
-    else if (nmax <= 8) head_t2<8, false>(W, in, nn, st, logits, ld, partial, nan0, s);
-    else head_t2<16, false>(W, in, nn, st, logits, ld, partial, nan0, s);
+    if (nmax <= 4) head_mma_t<false>(W, in, nn, st, logits, ld, partial, nan0, row_base, s);
+    else if (nmax <= 8) head_t2<8, false>(W, in, nn, st, logits, ld, partial, nan0, row_base, s);
+    else head_t2<16, false>(W, in, nn, st, logits, ld, partial, nan0, row_base, s);
 }
 
 void launch_matvec_head_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
                              float *logits, int ld, unsigned long long *partial, int *nan0, int nmax,
-                             cudaStream_t s) {
+                             cudaStream_t s, int row_base) {
     const NormIn nin{x, w, eps};
     const Act none;
-    if (nmax <= 4) head_mma_t<true>(W, none, nin, st, logits, ld, partial, nan0, s);
-    else if (nmax <= 8) head_t2<8, true>(W, none, nin, st, logits, ld, partial, nan0, s);
-    else head_t2<16, true>(W, none, nin, st, logits, ld, partial, nan0, s);
+    if (nmax <= 4) head_mma_t<true>(W, none, nin, st, logits, ld, partial, nan0, row_base, s);
+    else if (nmax <= 8) head_t2<8, true>(W, none, nin, st, logits, ld, partial, nan0, row_base, s);
+    else head_t2<16, true>(W, none, nin, st, logits, ld, partial, nan0, row_base, s);
 }
 // The first-generation kernel (chunked shared-memory chains, any shape) stays available for
 // the kernel-level ABI's reference timing.
@@ -2478,6 +2506,13 @@ void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st,
     for (int i = 0; i < n_lin && i < kMaxLayers; i++) fa.layers[i] = layers[i];
     if (n_lin > 0) launch_k(k_flush, dim3(d.nk, n_lin), kDV, 0, s, fa, d, st);
     launch_k(k_clear_pending, 1, 1, 0, s, st);
+}
+void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int npanels, const Step *st,
+                        unsigned long long *keys, cudaStream_t s) {
+    launch_k(k_argmax_keys, kMaxRows, 256, 0, s, partial, nan0, npanels, st, keys);
+}
+void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s) {
+    launch_k(k_keys_argmax, 1, kMaxRows, 0, s, keys, st);
 }
 void launch_pass_end(Step *st, cudaStream_t s) { launch_k(k_pass_end, 1, 1, 0, s, st); }
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s) {

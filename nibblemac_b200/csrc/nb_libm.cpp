@@ -59,4 +59,7 @@ int nb_libm_eval_host(int fn, const float *x, float *y, long long n) {
     return 0;
 }
 
+// The argmax key of (v, row) as the device computes it (for host-side checks of the merge).
+unsigned long long nb_argmax_key(float v, int row) { return nb::argmax_key(v, row); }
+
 }  // extern "C"

@@ -89,6 +89,17 @@ NB_HD double libm_u2d(uint64_t u) {
 #endif
 }
 
+// Order-preserving key of a (logit, row) pair: larger logit wins, then the lower row, NaN never
+// wins (pf_argmax, engine/src/forward_ops.c:387-409: first maximum, NaN skipped); the maximum
+// over any split of the rows (panels, warps, vocab shards) is the maximum over all of them.
+NB_HD unsigned long long argmax_key(float v, int row) {
+    uint32_t u = libm_f2u(v);
+    if (v != v) u = 0u;
+    else if (v == 0.0f) u = 0x80000000u;                 // +0 and -0 compare equal
+    else u = (u >> 31) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (0xffffffffu - (uint32_t)row);
+}
+
 // bits of 2^(i/32) rounded to the nearest double, minus i << 47 (so that adding k << 47 for
 // k = 32 m + i gives 2^(k/32) directly)
 #define NB_EXP2_TAB {                                                             \

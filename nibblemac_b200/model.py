@@ -162,6 +162,20 @@ class Model:
         if rc != PINFER_OK:
             raise PinferError(rc, "pinfer_rewind", self.lib.last_error())
 
+    def nccl_id(self) -> bytes:
+        """A fresh NCCL unique id (128 bytes) for shard_head, to be sent to every rank."""
+        buf = ctypes.create_string_buffer(128)
+        rc = self.lib.pinfer_b200_nccl_id(buf)
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_b200_nccl_id", self.lib.last_error())
+        return buf.raw
+
+    def shard_head(self, rank: int, world: int, nccl_id: bytes | None) -> None:
+        """Vocab-shard the LM head over `world` GPUs (collective: every rank calls it)."""
+        rc = self.lib.pinfer_b200_shard_head(self.ctx, rank, world, nccl_id)
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_b200_shard_head", self.lib.last_error())
+
     def round_kernels(self, k: int) -> int:
         return self.lib.pinfer_b200_round_kernels(self.ctx, k)
 
