@@ -102,11 +102,15 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def model_path(rank: int, dist) -> Path:
+def model_path(rank: int, dist, preset: str = "0.8b") -> Path:
+    """The synthetic model of `preset`, written once by rank 0 (to a temporary name, then
+    renamed, so no rank opens a partial file)."""
     from nibblemac_b200 import pq
-    path = ROOT / "_models" / f"bench-0.8b-s{SEED_MODEL}.pq"
+    path = ROOT / "_models" / f"bench-{preset}-s{SEED_MODEL}.pq"
     if rank == 0 and not path.exists():
-        pq.make_synthetic(path, pq.QWEN35_08B, SEED_MODEL, std=0.02)
+        tmp = path.with_suffix(".tmp")
+        pq.make_synthetic(tmp, pq.PRESETS[preset], SEED_MODEL, std=0.02)
+        os.replace(tmp, path)
     if dist is not None:
         dist.barrier()
     while not path.exists():
@@ -248,6 +252,78 @@ def run_reference(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+CTX5 = 4096
+
+
+def run_config5(args, rank: int, world: int, local: int) -> None:
+    """the 2B-shaped model, k = 3 at p = 0.8 on a 4096-token context, the
+    LM head vocab-sharded over the `world` GPUs with the argmax merged by one NCCL all-reduce
+    per verify pass (pinfer_b200_shard_head). Every rank runs the same single stream (batch 1;
+    the configured batch of 8 sequences needs multi-stream batching, not built), so the total
+    work is fixed: strong scaling. value = the stream's tokens / max over ranks of the device
+    time of the verify loop."""
+    import datetime
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=900))
+    from nibblemac_b200.model import Model
+    path = model_path(rank, dist, "2b")
+    m = Model(path, max_ctx=CTX5 + N_GEN + 16)
+    if world > 1:
+        obj = [m.nccl_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        m.shard_head(rank, world, obj[0])
+    ctx = np.random.default_rng(4321).integers(0, m.n_vocab, CTX5).astype(np.int32)   # same on every rank
+    m.reset()
+    m.eval(ctx[:-1], logits=False)
+    m.checkpoint()
+    greedy, _, st0, _ = m.generate_synthetic_ex(ctx[-1:], N_GEN, 0, np.zeros(N_GEN, np.int32), 0, 0.0,
+                                                append=True)
+    assert st0 == 0 and len(greedy) == N_GEN
+
+    def step(seed: int):
+        m.rewind()
+        toks, st, status, ms = m.generate_synthetic_ex(ctx[-1:], N_GEN, K_DRAFT, greedy, seed, P_MAIN,
+                                                       append=True)
+        assert status == 0 and toks == greedy, "speculative output differs from plain greedy"
+        return ms, st
+
+    for i in range(args.warmup):
+        step(500 + i)
+    if dist is not None:
+        dist.barrier()
+    ms_all, rounds = [], 0
+    for i in range(args.steps):
+        ms, st = step(600 + i)
+        ms_all.append(ms)
+        rounds += st.rounds
+    t_dev = sum(ms_all) / 1000.0
+    if dist is not None:
+        t = torch.tensor([t_dev], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_dev = float(t.item())
+    m.close()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "greedy spec-decode tok/s (k=3), 2B shape, LM head vocab-sharded",
+            "value": round((N_GEN - 1) * args.steps / t_dev, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_dev * 1000.0 / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "q4k x int8 -> fp32",
+            "data": "synthetic (random-init 2B-shaped weights, uniform-random context, synthetic drafter)",
+            "config": {"workload": f"configs[4]: Qwen3.5-2B-shaped Q4K, k=3, p={P_MAIN}, {CTX5}-token "
+                                   f"context, {N_GEN} generated, batch 1 (of the configured 8)",
+                       "head_rows_per_gpu": 248320 // world, "collective": "ncclAllReduce max, 32 x u64 per verify pass" if world > 1 else None,
+                       "rounds": rounds}}), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -255,6 +331,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config5", action="store_true",
+                    help="BASELINE configs[4]: 2B shape, 4096-token context, LM head vocab-sharded "
+                         "over the torchrun ranks (one JSON line, strong scaling)")
     ap.add_argument("--profile", action="store_true",
                     help="setup, then exactly one generation inside cudaProfilerStart/Stop (for "
                          "ncu --profile-from-start off); prints nothing else")
@@ -265,6 +344,9 @@ def main() -> None:
     if args.impl == "reference":
         sys.path.insert(0, str(ROOT / "oracle"))
         run_reference(args, rank, world)
+        return
+    if args.config5:
+        run_config5(args, rank, world, local)
         return
 
     import torch
