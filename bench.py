@@ -253,6 +253,112 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 CTX5 = 4096
+N_SEQ4, GEN4 = 256, 256
+
+
+def run_config4(args, rank: int, world: int, local: int) -> None:
+    """256 independent requests per GPU (uniform-random prompts of length
+    U[32, 1024], 256 generated tokens each, k = 3 at p = 0.8) on the 0.8B-shaped model, served by
+    `--streams` concurrent contexts that share one copy of the weights (pinfer_b200_clone), one
+    host thread and CUDA stream each; replicas across GPUs (weak scaling). The greedy streams the
+    drafter needs come from an untimed plain pass. value = generated tokens (prefill included in
+    the time) / the span of the timed phase from CUDA events on every context's stream, max over
+    ranks. (Requests are served concurrently, not merged into one >= 64-row verify batch.)"""
+    import datetime
+    import threading
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=1800))
+    from nibblemac_b200.model import Model
+    path = model_path(rank, dist)
+    max_ctx = 1024 + GEN4 + 16
+    base = Model(path, max_ctx=max_ctx)
+    S = max(1, args.streams)
+    ctxs = [base] + [base.clone(max_ctx) for _ in range(S - 1)]
+    rng = np.random.default_rng(777 + rank)
+    lens = rng.integers(32, 1025, N_SEQ4)
+    prompts = [rng.integers(0, base.n_vocab, int(n)).astype(np.int32) for n in lens]
+    greedy = [None] * N_SEQ4
+
+    def phase(fn):
+        errs = []
+
+        def worker(i):
+            try:
+                for j in range(i, N_SEQ4, S):
+                    fn(ctxs[i], j)
+            except Exception as e:   # reported below
+                errs.append(repr(e))
+
+        ths = [threading.Thread(target=worker, args=(i,)) for i in range(S)]
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+        assert not errs, errs[:3]
+
+    def plain(m, j):
+        greedy[j], st = m.generate(prompts[j], GEN4)   # shorter if the random model emits EOS
+        assert st == 0 and 0 < len(greedy[j]) <= GEN4
+
+    def padded(j):
+        return np.array(greedy[j] + [0] * (GEN4 - len(greedy[j])), np.int32)
+
+    lock = threading.Lock()
+
+    def spec(m, j):
+        toks, st, status = m.generate_synthetic(prompts[j], GEN4, K_DRAFT, padded(j), 9000 + j, P_MAIN)
+        assert status == 0 and toks == greedy[j], "speculative output differs from plain greedy"
+        with lock:
+            stats[0] += st.rounds
+
+    stats = [0]
+    phase(plain)                           # untimed: the greedy streams
+    for i, m in enumerate(ctxs):           # untimed: each context captures its k = 3 round graph
+        toks, _, status = m.generate_synthetic(prompts[i], 8, K_DRAFT, padded(i), 1, P_MAIN)
+        assert status == 0
+    streams = [torch.cuda.ExternalStream(m.stream()) for m in ctxs]
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in ctxs]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in ctxs]
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    for e, st in zip(ev0, streams):
+        e.record(st)
+    with Clocks(local) as clk:
+        phase(spec)
+        for e, st in zip(ev1, streams):
+            e.record(st)
+        torch.cuda.synchronize()
+    t0 = min(range(S), key=lambda i: ev0[0].elapsed_time(ev0[i]))
+    span_ms = max(ev0[t0].elapsed_time(e) for e in ev1)
+    t = span_ms / 1000.0
+    if dist is not None:
+        tt = torch.tensor([t], dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    for m in ctxs[1:]:
+        m.close()
+    base.close()
+    if rank == 0:
+        tokens = sum(len(g) for g in greedy) * world
+        print(json.dumps({
+            "metric": "greedy spec-decode tok/s (k=3), multi-stream, per job", "value": round(tokens / t, 1),
+            "unit": UNIT, "n_gpus": world, "steps": 1, "warmup": 1, "ms_per_step": round(t * 1000.0, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4k x int8 -> fp32",
+            "data": "synthetic (random-init 0.8B-shaped weights, uniform-random prompts, synthetic drafter)",
+            "config": {"workload": f"configs[3]: {N_SEQ4} requests per GPU, prompts U[32,1024], {GEN4} "
+                                   f"generated each, k=3, p={P_MAIN}; prefill inside the timed span",
+                       "streams_per_gpu": S, "parallelism": f"replicas x{world}" if world > 1 else "single replica",
+                       "rounds_per_gpu": stats[0], "mean_prompt": float(lens.mean())},
+            "clocks": clk.summary()}), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_config5(args, rank: int, world: int, local: int) -> None:
@@ -331,6 +437,10 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config4", action="store_true",
+                    help="BASELINE configs[3]: 256 requests per GPU served by --streams concurrent "
+                         "contexts (one JSON line)")
+    ap.add_argument("--streams", type=int, default=16)
     ap.add_argument("--config5", action="store_true",
                     help="BASELINE configs[4]: 2B shape, 4096-token context, LM head vocab-sharded "
                          "over the torchrun ranks (one JSON line, strong scaling)")
@@ -347,6 +457,9 @@ def main() -> None:
         return
     if args.config5:
         run_config5(args, rank, world, local)
+        return
+    if args.config4:
+        run_config4(args, rank, world, local)
         return
 
     import torch

@@ -50,6 +50,13 @@ int pinfer_b200_forward_all(pinfer_ctx *ctx, const int32_t *tokens, int n, float
 /* The CUDA stream every call on ctx runs on (for timing with events on the same stream). */
 void *pinfer_b200_stream(pinfer_ctx *ctx);
 
+/* A second context on the same model and device (no reference counterpart): it shares the
+ * source's weights in device memory (refcounted; either may be freed first) and owns its own
+ * recurrent/conv states, KV cache (max_ctx positions, at most the source's; 0 = the source's),
+ * stream and round graphs, so independent request streams can run concurrently, one host thread
+ * per context. NULL on failure with *err set. */
+pinfer_ctx *pinfer_b200_clone(const pinfer_ctx *src, int max_ctx, int *err);
+
 /* ---- vocab-sharded LM head ------------------------------------------
  * No reference counterpart (the reference runs on one device). One context per GPU, each with
  * the same model and fed the same tokens: every GPU runs the layers, and its LM head covers only

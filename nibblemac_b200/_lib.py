@@ -103,6 +103,7 @@ _OPTIONAL = {
     "pinfer_b200_round_kernels": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "pinfer_b200_forward_all": (ctypes.c_int, [ctypes.c_void_p, _c_int32_p, ctypes.c_int, _c_float_p]),
     "pinfer_b200_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "pinfer_b200_clone": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, _c_int_p]),
     "pinfer_b200_nccl_id": (ctypes.c_int, [ctypes.c_void_p]),
     "pinfer_b200_shard_head": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "nb_q4k_panel_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),

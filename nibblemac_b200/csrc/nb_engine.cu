@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <vector>
 #include <new>
@@ -95,6 +96,15 @@ void repack_q4k(const uint8_t *pq, int rows, int cols, uint8_t *out) {
 }  // namespace nb
 
 // ---------------------------------------------------------------- the context
+// Device buffers of the model parameters (weights, norms, RoPE tables), shared by a context and
+// its clones (pinfer_b200_clone) and freed with the last of them.
+struct WeightStore {
+    std::vector<void *> ptrs;
+    ~WeightStore() {
+        for (void *p : ptrs) cudaFree(p);
+    }
+};
+
 struct pinfer_ctx {
     PqFile file;
     int H = 0, ffn = 0, n_layers = 0, vocab = 0, nq = 0, nkv = 0, hd = 0, rot = 0;
@@ -120,7 +130,8 @@ struct pinfer_ctx {
     int n_lin = 0;
     LinDims lind{};
     AttnDims attd{};
-    std::vector<void *> allocs;
+    std::vector<void *> allocs;                 // this context's buffers
+    std::shared_ptr<WeightStore> weights;       // the model's parameters (shared with clones)
 
     // activations and scratch
     float *x = nullptr, *y = nullptr, *qbuf = nullptr, *logits = nullptr;
@@ -149,14 +160,14 @@ struct pinfer_ctx {
     int ck_valid = 0, ck_n_past = -1;
 
     template <class T>
-    int dalloc(T **p, size_t bytes) {
+    int dalloc(T **p, size_t bytes, bool weight = false) {
         void *q = nullptr;
         if (cudaMalloc(&q, bytes ? bytes : 16) != cudaSuccess) {
             set_err("device allocation failed");
             return PINFER_E_NOMEM;
         }
         cudaMemset(q, 0, bytes ? bytes : 16);
-        allocs.push_back(q);
+        (weight ? weights->ptrs : allocs).push_back(q);
         *p = (T *)q;
         return PINFER_OK;
     }
@@ -165,7 +176,7 @@ struct pinfer_ctx {
 namespace {
 
 int upload_floats(pinfer_ctx *c, const float *h, size_t n, float **d) {
-    int rc = c->dalloc(d, n * sizeof(float));
+    int rc = c->dalloc(d, n * sizeof(float), true);
     if (rc) return rc;
     CUDA_OK(cudaMemcpy(*d, h, n * sizeof(float), cudaMemcpyHostToDevice));
     return PINFER_OK;
@@ -184,7 +195,7 @@ int upload_mats(pinfer_ctx *c, const PqMat *const *parts, int nparts, Mat *out) 
         r0 += parts[i]->rows;
     }
     uint8_t *d = nullptr;
-    int rc = c->dalloc(&d, bytes);
+    int rc = c->dalloc(&d, bytes, true);
     if (rc) return rc;
     CUDA_OK(cudaMemcpy(d, buf.data(), bytes, cudaMemcpyHostToDevice));
     out->w = d;
@@ -243,8 +254,11 @@ int check_limits(const pinfer_ctx *c) {
     return PINFER_OK;
 }
 
+int alloc_state(pinfer_ctx *c);
+
 int alloc_and_upload(pinfer_ctx *c) {
     const PqFile &f = c->file;
+    c->weights = std::make_shared<WeightStore>();
     int rc = upload_mat(c, f.embed, &c->embed);
     if (rc) return rc;
     if (f.hdr->tied_embeddings) c->head = c->embed;
@@ -289,8 +303,6 @@ int alloc_and_upload(pinfer_ctx *c) {
             if ((rc = upload_floats(c, L.q_norm, c->hd, &qn)) || (rc = upload_floats(c, L.k_norm, c->hd, &kn))) return rc;
             A.q_norm = qn;
             A.k_norm = kn;
-            const size_t kv = (size_t)c->nkv * c->max_ctx * c->hd * sizeof(float);
-            if ((rc = c->dalloc(&A.kc, kv)) || (rc = c->dalloc(&A.vc, kv))) return rc;
         } else {
             const PqMat *parts[4] = {&L.qkv, &L.z, &L.b, &L.a};
             if ((rc = upload_mats(c, parts, 4, &D.win)) || (rc = upload_mat(c, L.out, &D.out))) return rc;
@@ -308,6 +320,24 @@ int alloc_and_upload(pinfer_ctx *c) {
             N.A = dA;
             N.dt_bias = dt;
             N.norm_w = nw;
+        }
+    }
+    return alloc_state(c);
+}
+
+// This context's own buffers: recurrent and conv states, logs, KV caches, activations, the step
+// block (everything but the model's parameters).
+int alloc_state(pinfer_ctx *c) {
+    int rc;
+    const int cap = PINFER_SPEC_MAX_K + 1;
+    for (int l = 0; l < c->n_layers; l++) {
+        const auto &D = c->layers[l];
+        if (D.is_full) {
+            AttnLayer &A = c->att[l];
+            const size_t kv = (size_t)c->nkv * c->max_ctx * c->hd * sizeof(float);
+            if ((rc = c->dalloc(&A.kc, kv)) || (rc = c->dalloc(&A.vc, kv))) return rc;
+        } else {
+            LinLayer &N = c->lin[D.lin];
             if ((rc = c->dalloc(&N.conv_state, sizeof(float) * (size_t)std::max(c->K - 1, 1) * c->C)) ||
                 (rc = c->dalloc(&N.rec, sizeof(float) * (size_t)c->nv * c->dk * c->dv)) ||
                 (rc = c->dalloc(&N.xin, sizeof(float) * (size_t)cap * c->C)) ||
@@ -981,6 +1011,54 @@ int pinfer_b200_forward_all(pinfer_ctx *c, const int32_t *tokens, int n, float *
 }
 
 void *pinfer_b200_stream(pinfer_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+pinfer_ctx *pinfer_b200_clone(const pinfer_ctx *src, int max_ctx, int *err) {
+    int dummy;
+    if (!err) err = &dummy;
+    *err = PINFER_OK;
+    if (!src || max_ctx < 0 || max_ctx > src->max_ctx) {
+        set_err("pinfer_b200_clone: max_ctx must be in [0, the source's max_ctx]");
+        *err = PINFER_E_ARG;
+        return nullptr;
+    }
+    pinfer_ctx *c = new (std::nothrow) pinfer_ctx();
+    if (!c) {
+        *err = PINFER_E_NOMEM;
+        return nullptr;
+    }
+    // the model: dimensions, parameter pointers (shared), no file
+    c->H = src->H; c->ffn = src->ffn; c->n_layers = src->n_layers; c->vocab = src->vocab;
+    c->nq = src->nq; c->nkv = src->nkv; c->hd = src->hd; c->rot = src->rot;
+    c->nk = src->nk; c->nv = src->nv; c->dk = src->dk; c->dv = src->dv; c->K = src->K;
+    c->kd = src->kd; c->vd = src->vd; c->C = src->C;
+    c->max_ctx = max_ctx > 0 ? max_ctx : src->max_ctx;
+    c->eps = src->eps; c->eos = src->eos; c->has_mtp = src->has_mtp; c->fp = src->fp; c->hdr = src->hdr;
+    c->embed = src->embed; c->head = src->head; c->norm = src->norm;
+    for (int l = 0; l < kMaxLayers; l++) {
+        c->layers[l] = src->layers[l];
+        c->lin[l] = src->lin[l];   // parameter pointers; the state buffers are replaced below
+        c->att[l] = src->att[l];
+    }
+    c->n_lin = src->n_lin;
+    c->lind = src->lind;
+    c->attd = src->attd;
+    c->attd.max_ctx = c->max_ctx;   // the RoPE tables cover the source's (larger) context
+    c->weights = src->weights;
+    c->device = src->device;
+    int rc = cudaSetDevice(c->device) == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
+    if (rc == PINFER_OK && cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        set_err("cannot create a CUDA stream");
+        rc = PINFER_E_NOMEM;
+    }
+    if (rc == PINFER_OK) rc = alloc_state(c);
+    if (rc == PINFER_OK && cudaStreamSynchronize(c->stream) != cudaSuccess) rc = PINFER_E_NOMEM;
+    if (rc != PINFER_OK) {
+        pinfer_free(c);
+        *err = rc;
+        return nullptr;
+    }
+    return c;
+}
 
 int pinfer_b200_nccl_id(void *id) {
     if (!id) return PINFER_E_ARG;

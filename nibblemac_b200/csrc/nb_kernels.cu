@@ -2348,11 +2348,13 @@ int dyn_smem_limit(K kern) {
     return kSmemOptin - (int)a.sharedSizeBytes;
 }
 
+// Allow the kernel the whole opt-in limit: the attribute only bounds what a launch may request,
+// and contexts with different sizes (max_ctx) share the kernels, so it is never lowered.
 template <class K>
 void raise_smem(K kern, size_t want = 0) {
+    (void)want;
     const int lim = dyn_smem_limit(kern);
-    const int v = want ? (int)std::min<size_t>(want, (size_t)std::max(lim, 0)) : lim;
-    if (v > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+    if (lim > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
 }
 
 template <int NMAX, bool NORM>

@@ -35,6 +35,17 @@ class Model:
         self.n_vocab = self.lib.pinfer_n_vocab(self.ctx)
         self.eos_id = self.lib.pinfer_eos_id(self.ctx)
 
+    def clone(self, max_ctx: int = 0) -> "Model":
+        """Another context on the same weights (pinfer_b200_clone): own states, KV cache,
+        stream and graphs, for running independent request streams concurrently."""
+        err = ctypes.c_int(0)
+        ctx = self.lib.pinfer_b200_clone(self.ctx, max_ctx, ctypes.byref(err))
+        if not ctx:
+            raise PinferError(err.value, "pinfer_b200_clone", self.lib.last_error())
+        m = Model.__new__(Model)
+        m.lib, m.ctx, m.n_vocab, m.eos_id = self.lib, ctx, self.n_vocab, self.eos_id
+        return m
+
     def close(self) -> None:
         if self.ctx:
             self.lib.pinfer_free(self.ctx)

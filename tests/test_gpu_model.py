@@ -166,3 +166,42 @@ def test_long_context_attention_bit_exact(small_model):
     finally:
         dev.close()
         ref.close()
+
+
+def test_clones_share_weights_and_run_concurrently(small_model):
+    """pinfer_b200_clone: contexts on the source's weights with their own states, freed in
+    either order; four of them generating at once from four host threads give the same tokens
+    and statistics as one context alone."""
+    import threading
+    from nibblemac_b200.model import Model
+    src = Model(small_model, max_ctx=512)
+    clones = [src.clone(256) for _ in range(4)]
+    try:
+        prompts = [prompt(src.n_vocab, 20 + 7 * i, 40 + i) for i in range(4)]
+        want = []
+        for p in prompts:
+            g, _ = src.generate(p, 32)
+            t, st, _ = src.generate_synthetic(p, 32, 3, g, seed=3, p=0.6)
+            assert t == g
+            want.append((g, (st.rounds, st.drafted, st.accepted)))
+        got = [None] * 4
+
+        def run(i):
+            m, p = clones[i], prompts[i]
+            g, _ = m.generate(p, 32)
+            t, st, _ = m.generate_synthetic(p, 32, 3, g, seed=3, p=0.6)
+            got[i] = (t, (st.rounds, st.drafted, st.accepted))
+
+        ths = [threading.Thread(target=run, args=(i,)) for i in range(4)]
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join(120)
+        assert got == want
+        src.close()                          # the weights live on with the clones
+        g, _ = clones[0].generate(prompts[0], 32)
+        assert g == want[0][0]
+    finally:
+        src.close()
+        for m in clones:
+            m.close()
