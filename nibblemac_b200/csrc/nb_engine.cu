@@ -143,6 +143,22 @@ struct pinfer_ctx {
     int *d_out = nullptr, *d_greedy = nullptr;
     int out_cap = 0;
 
+    // MTP draft head (speculative generation with k > 0): parameters shared with clones, KV
+    // cache and buffers per context
+    bool mtp_ok = false;
+    Mat mtp_fc;
+    float *mtp_norm_emb = nullptr, *mtp_norm_hid = nullptr, *mtp_norm_out = nullptr;
+    Layer mtp_layer;
+    AttnLayer mtp_att{};
+    int mtp_rows = 0;                          // positions [0, mtp_rows) hold MTP KV rows
+    float *hn = nullptr, *mrows = nullptr;     // [kMaxRows][H]: main final-normed rows, MTP output rows
+    float *mcur = nullptr;                     // [H]: the m the next draft chain starts from
+    Act act_cat;                               // [kMaxRows][2H]: MTP input rows, A8
+    Step *msteps = nullptr;                    // [K+1]: 0 the pass over committed rows, s chain step s
+    Mat mtp_head;                              // the head's first nv rows (draft vocabulary)
+    cudaGraphExec_t round_graph_mtp[PINFER_SPEC_MAX_K + 1] = {};
+    int graph_nv[PINFER_SPEC_MAX_K + 1] = {};
+
     // graphs of one verify round per draft depth k (index k), no graph = not captured yet
     cudaGraphExec_t round_graph[PINFER_SPEC_MAX_K + 1] = {};
 
@@ -157,7 +173,7 @@ struct pinfer_ctx {
     // checkpoint slot (pinfer_checkpoint)
     float *ck_buf = nullptr;
     size_t ck_floats = 0;
-    int ck_valid = 0, ck_n_past = -1;
+    int ck_valid = 0, ck_n_past = -1, ck_mtp_rows = 0;
 
     template <class T>
     int dalloc(T **p, size_t bytes, bool weight = false) {
@@ -322,6 +338,27 @@ int alloc_and_upload(pinfer_ctx *c) {
             N.norm_w = nw;
         }
     }
+    if (f.hdr->has_mtp && f.mtp.ok) {   // the MTP head (mtp.c:8-32)
+        const PqMtp &M = f.mtp;
+        auto &D = c->mtp_layer;
+        D.is_full = 1;
+        const PqMat *parts[3] = {&M.layer.q, &M.layer.k, &M.layer.v};
+        float *qn, *kn;
+        if ((rc = upload_mat(c, M.fc, &c->mtp_fc)) ||
+            (rc = upload_floats(c, M.norm_emb, c->H, &c->mtp_norm_emb)) ||
+            (rc = upload_floats(c, M.norm_hid, c->H, &c->mtp_norm_hid)) ||
+            (rc = upload_floats(c, M.norm_out, c->H, &c->mtp_norm_out)) ||
+            (rc = upload_floats(c, M.layer.in_norm, c->H, &D.in_norm)) ||
+            (rc = upload_floats(c, M.layer.post_norm, c->H, &D.post_norm)) ||
+            (rc = upload_mat(c, M.layer.gate, &D.gate)) || (rc = upload_mat(c, M.layer.up, &D.up)) ||
+            (rc = upload_mat(c, M.layer.down, &D.down)) || (rc = upload_mats(c, parts, 3, &D.win)) ||
+            (rc = upload_mat(c, M.layer.o, &D.out)) || (rc = upload_floats(c, M.layer.q_norm, c->hd, &qn)) ||
+            (rc = upload_floats(c, M.layer.k_norm, c->hd, &kn)))
+            return rc;
+        c->mtp_att.q_norm = qn;
+        c->mtp_att.k_norm = kn;
+        c->mtp_ok = true;
+    }
     return alloc_state(c);
 }
 
@@ -344,6 +381,19 @@ int alloc_state(pinfer_ctx *c) {
                 (rc = c->dalloc(&N.upd, sizeof(float) * 2 * (size_t)cap * c->nv * (c->dk + c->dv + 1))))
                 return rc;
         }
+    }
+    if (c->mtp_ok) {
+        const size_t kv = (size_t)c->nkv * c->max_ctx * c->hd * sizeof(float);
+        if ((rc = c->dalloc(&c->mtp_att.kc, kv)) || (rc = c->dalloc(&c->mtp_att.vc, kv)) ||
+            (rc = c->dalloc(&c->hn, sizeof(float) * kMaxRows * c->H)) ||
+            (rc = c->dalloc(&c->mrows, sizeof(float) * kMaxRows * c->H)) ||
+            (rc = c->dalloc(&c->mcur, sizeof(float) * c->H)) ||
+            (rc = c->dalloc(&c->act_cat.q, (size_t)kMaxRows * 2 * c->H)) ||
+            (rc = c->dalloc(&c->act_cat.d, sizeof(float) * kMaxRows * (2 * c->H / 32))) ||
+            (rc = c->dalloc(&c->act_cat.fs, sizeof(float) * kMaxRows * (2 * c->H / 32))) ||
+            (rc = c->dalloc(&c->msteps, sizeof(Step) * (PINFER_SPEC_MAX_K + 1))))
+            return rc;
+        c->act_cat.cols = 2 * c->H;
     }
     // activations
     const int ldy = std::max(c->lind.ldy, c->attd.ldy);
@@ -377,7 +427,7 @@ Act mid_act(pinfer_ctx *c, int cols) {
 
 // One forward pass over the rows described by the Step block (<= nmax rows).
 // head: 0 none, 1 logits + argmax, 2 argmax only (no logits written)
-void enqueue_forward(pinfer_ctx *c, int nmax, int head) {
+void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = false) {
     cudaStream_t s = c->stream;
     launch_embed(c->embed, c->step, c->x, c->H, s);
     for (int l = 0; l < c->n_layers; l++) {
@@ -398,6 +448,7 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head) {
         launch_matvec_swiglu_norm(D.gate, D.up, c->x, D.post_norm, c->eps, c->step, h, nmax, c->act_h, s);
         launch_matvec(D.down, h, c->step, c->x, c->H, 1, nmax, s);
     }
+    if (export_normed) launch_norm_rows(c->x, c->norm, c->H, c->eps, c->step, c->hn, s);   // pf_forward_h normed
     if (head) {
         // sharded: this GPU's vocabulary rows only, logits at their global columns
         const bool sharded = c->shard_world > 1;
@@ -431,6 +482,43 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head) {
         }
     }
     launch_pass_end(c->step, s);
+}
+
+// One MTP pass (pf_mtp_forward, mtp.c:62-100) over the rows of step block ms: h [n][H] hidden
+// rows, ms->tokens the tokens that follow them, positions ms->pos0..; writes the MTP KV rows,
+// the normed outputs m (c->mrows) and, with head, the argmax over the draft vocabulary
+// (ms->argmax). Uses the main pass's scratch buffers, so it runs between main passes.
+void enqueue_mtp(pinfer_ctx *c, Step *ms, const float *h, int nmax, bool head) {
+    cudaStream_t s = c->stream;
+    const auto &D = c->mtp_layer;
+    launch_mtp_input(c->embed, h, ms, c->mtp_norm_emb, c->mtp_norm_hid, c->H, c->eps, c->act_cat, s);
+    launch_matvec(c->mtp_fc, c->act_cat, ms, c->x, c->H, 0, nmax, s);   // u = fc [e | h]
+    const Act o = mid_act(c, c->nq * c->hd);
+    launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, ms, c->y, c->attd.ldy, nmax, c->act_h, s);
+    launch_attn_prep(c->mtp_att, c->attd, c->y, c->qbuf, ms, s);
+    launch_attn(c->mtp_att, c->attd, c->y, c->qbuf, ms, o, s);
+    launch_matvec(D.out, o, ms, c->x, c->H, 1, nmax, s);
+    const Act hm = mid_act(c, c->ffn);
+    launch_matvec_swiglu_norm(D.gate, D.up, c->x, D.post_norm, c->eps, ms, hm, nmax, c->act_h, s);
+    launch_matvec(D.down, hm, ms, c->x, c->H, 1, nmax, s);
+    launch_norm_rows(c->x, c->mtp_norm_out, c->H, c->eps, ms, c->mrows, s);   // m = mtp.norm(u)
+    if (head) {
+        if (nmax <= 4) {
+            launch_matvec_head_norm(c->mtp_head, c->x, c->mtp_norm_out, c->eps, ms, nullptr, c->vocab,
+                                    c->partial, c->nan0, nmax, s);
+        } else {
+            launch_norm_quant(c->x, c->mtp_norm_out, c->H, c->eps, ms, c->act_h, s);
+            launch_matvec_head(c->mtp_head, c->act_h, ms, nullptr, c->vocab, c->partial, c->nan0, nmax, s);
+        }
+        launch_argmax_final(c->partial, c->nan0, c->mtp_head.npanels, ms, s);
+    }
+}
+
+// The head's first nv rows, the draft vocabulary (spec.c:88-91, mtp.c:92-97).
+void set_mtp_head(pinfer_ctx *c, int nv) {
+    c->mtp_head = c->head;
+    c->mtp_head.rows = nv;
+    c->mtp_head.npanels = (nv + kPanelRows - 1) / kPanelRows;
 }
 
 int sync(pinfer_ctx *c) {
@@ -484,21 +572,45 @@ int ensure_out(pinfer_ctx *c, int n_max) {
     return PINFER_OK;
 }
 
-int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out) {
-    if (c->round_graph[k]) {
-        *out = c->round_graph[k];
+int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int nv = 0) {
+    if (drafter == 1 && c->round_graph_mtp[k] && c->graph_nv[k] != nv) {
+        cudaGraphExecDestroy(c->round_graph_mtp[k]);
+        c->round_graph_mtp[k] = nullptr;
+    }
+    cudaGraphExec_t &slot = drafter == 1 ? c->round_graph_mtp[k] : c->round_graph[k];
+    if (slot) {
+        *out = slot;
         return PINFER_OK;
     }
     const int nmax = k + 1 <= 1 ? 1 : k + 1 <= 4 ? 4 : k + 1 <= 8 ? 8 : 16;
+    cudaStream_t s = c->stream;
     cudaGraph_t g;
-    CUDA_OK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    enqueue_forward(c, nmax, 2);
-    launch_accept(c->step, c->d_greedy, c->d_out, c->stream);
-    CUDA_OK(cudaStreamEndCapture(c->stream, &g));
+    CUDA_OK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    if (drafter == 1) {
+        // pf_spec_decode with MTP drafts (spec.c:300-374): the chain drafts 2..ke, the verify
+        // pass (with its normed rows), acceptance, then the MTP pass over the committed rows,
+        // which drafts the next round's first token
+        set_mtp_head(c, nv);
+        for (int i = 1; i < k; i++) {
+            launch_mtp_chain_set(c->step, c->msteps + i, i, s);
+            enqueue_mtp(c, c->msteps + i, c->mcur, 1, true);
+            launch_mtp_chain_take(c->step, c->msteps + i, i, c->mrows, c->mcur, c->H, s);
+        }
+        enqueue_forward(c, nmax, 2, true);
+        launch_accept(c->step, c->d_greedy, c->d_out, s);
+        launch_mtp_pending_set(c->step, c->msteps, s);
+        enqueue_mtp(c, c->msteps, c->hn, nmax, true);
+        launch_mtp_pending_take(c->step, c->msteps, c->mrows, c->mcur, c->H, s);
+    } else {
+        enqueue_forward(c, nmax, 2);
+        launch_accept(c->step, c->d_greedy, c->d_out, s);
+    }
+    CUDA_OK(cudaStreamEndCapture(s, &g));
     cudaGraphExec_t ex;
     CUDA_OK(cudaGraphInstantiate(&ex, g, 0));
     cudaGraphDestroy(g);
-    c->round_graph[k] = ex;
+    slot = ex;
+    if (drafter == 1) c->graph_nv[k] = nv;
     c->round_nmax[k] = nmax;
     *out = ex;
     return PINFER_OK;
@@ -507,6 +619,44 @@ int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out) {
 void drop_graphs(pinfer_ctx *c) {
     for (auto &g : c->round_graph)
         if (g) { cudaGraphExecDestroy(g); g = nullptr; }
+    for (auto &g : c->round_graph_mtp)
+        if (g) { cudaGraphExecDestroy(g); g = nullptr; }
+}
+
+// Zero MTP KV rows [from, to) of every group (spec.c:166-170: positions consumed without the
+// MTP head hold no MTP rows, and drafts must not attend to stale memory).
+int zero_mtp_rows(pinfer_ctx *c, int from, int to) {
+    if (!c->mtp_ok || to <= from) return PINFER_OK;
+    const size_t row = (size_t)c->hd * sizeof(float), gstride = (size_t)c->max_ctx * c->hd;
+    for (int g = 0; g < c->nkv; g++) {
+        CUDA_OK(cudaMemsetAsync(c->mtp_att.kc + g * gstride + (size_t)from * c->hd, 0, (size_t)(to - from) * row, c->stream));
+        CUDA_OK(cudaMemsetAsync(c->mtp_att.vc + g * gstride + (size_t)from * c->hd, 0, (size_t)(to - from) * row, c->stream));
+    }
+    return PINFER_OK;
+}
+
+// The prompt with the MTP head (pf_spec_prefill, spec.c:172-195): chunk by chunk the main pass
+// with its normed rows, then the MTP pass over the same rows (row i with token i + 1; the last
+// row with the first generated token), which fills the MTP KV rows and drafts d1.
+int forward_tokens_mtp(pinfer_ctx *c, const int32_t *tokens, int n) {
+    int rc;
+    if ((rc = zero_mtp_rows(c, c->mtp_rows, c->n_past))) return rc;
+    int next[kMaxRows];
+    for (int t0 = 0; t0 < n; t0 += kMaxRows) {
+        const int nb = std::min(kMaxRows, n - t0);
+        const bool last = t0 + nb == n;
+        launch_set_pass(c->step, nb, c->n_past, 0, tokens + t0, c->stream);
+        enqueue_forward(c, kMaxRows, last ? 2 : 0, true);
+        for (int i = 0; i < nb; i++) next[i] = t0 + i + 1 < n ? tokens[t0 + i + 1] : 0;
+        launch_set_pass(c->msteps, nb, c->n_past, 0, next, c->stream);
+        if (last) launch_mtp_prefill_fix(c->step, c->msteps, c->stream);
+        enqueue_mtp(c, c->msteps, c->hn, kMaxRows, last);
+        if (last) launch_mtp_pending_take(c->step, c->msteps, c->mrows, c->mcur, c->H, c->stream);
+        c->n_past += nb;
+    }
+    c->mtp_rows = c->n_past;
+    CUDA_OK(cudaGetLastError());
+    return PINFER_OK;
 }
 
 struct GenRequest {
@@ -522,6 +672,8 @@ struct GenRequest {
     int append;
     long long stats[3];
     float decode_ms;          // device time of the round loop (events on the context's stream)
+    int drafter = 0;          // 0 synthetic drafts, 1 the MTP head
+    int nv = 0;               // MTP draft vocabulary
 };
 
 // Generation (generate / pf_spec_prefill / pf_spec_decode, spec.c:153-416): prefill, then
@@ -552,12 +704,18 @@ int generate_impl(pinfer_ctx *c, GenRequest *r, int *status) {
     g.vocab = c->vocab;
     g.p24 = r->p24;
     g.seed = r->seed;
+    g.drafter = r->drafter;
     if (host_loop) g.eos = -1;   // the host decides when to stop (one token per round)
     launch_set_gen(c->step, g, c->stream);
-    if ((rc = forward_tokens(c, r->prompt, r->n_prompt, 2))) return *status = rc;
+    if (r->drafter == 1) {
+        set_mtp_head(c, r->nv);
+        if ((rc = forward_tokens_mtp(c, r->prompt, r->n_prompt))) return *status = rc;
+    } else if ((rc = forward_tokens(c, r->prompt, r->n_prompt, 2))) {
+        return *status = rc;
+    }
     launch_gen_start(c->step, c->d_greedy, c->d_out, c->stream);
     cudaGraphExec_t ex;
-    if ((rc = round_graph(c, r->k, &ex))) return *status = rc;
+    if ((rc = round_graph(c, r->k, &ex, r->drafter, r->nv))) return *status = rc;
     int count = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     cudaEventCreate(&ev0);
@@ -607,6 +765,7 @@ int generate_impl(pinfer_ctx *c, GenRequest *r, int *status) {
     r->stats[2] = c->h_step->accepted;
     *status = c->h_step->status;
     c->n_past = c->h_step->pos0;
+    if (r->drafter == 1) c->mtp_rows = c->n_past;   // every committed row had its MTP pass
     flush_pending(c);
     if ((rc = sync(c))) return *status = rc;
     return count;
@@ -705,6 +864,7 @@ void pinfer_reset(pinfer_ctx *c) {
     }
     launch_flush(nullptr, 0, c->lind, c->step, c->stream);   // clears any owed commit
     c->n_past = 0;
+    c->mtp_rows = 0;
     c->ck_valid = 0;
 }
 
@@ -751,13 +911,24 @@ static int generate_api(pinfer_ctx *c, const int32_t *prompt, int n_prompt, int3
     if (!status) status = &dummy;
     if (sp && (sp->k < 0 || sp->k > PINFER_SPEC_MAX_K || sp->ngram < 0 || sp->ngram > PINFER_SPEC_MAX_K))
         return *status = PINFER_E_ARG;
-    if (sp && sp->k > 0 && c && !c->has_mtp) return *status = PINFER_E_FORMAT;
-    // Drafts come from the MTP head or prompt lookup in the reference; this build verifies
-    // synthetic drafts (pinfer_b200_generate_synthetic) and decodes other requests greedily,
-    // which yields the same tokens (the output never depends on the drafts, pinfer.h:70-73).
+    if (sp && sp->k > 0 && c && !(c->has_mtp && c->mtp_ok)) return *status = PINFER_E_FORMAT;
+    // k > 0: drafts from the MTP head, k per round (pf_spec_decode). Prompt-lookup (n-gram)
+    // drafts and the adaptive policy are not built: such requests draft with the MTP head at a
+    // fixed k, or decode plainly when k = 0; the tokens are the same either way (the output
+    // never depends on the drafts, pinfer.h:70-73), only the statistics differ.
     GenRequest r{prompt, n_prompt, out, n_max, 0, nullptr, 0, 0, opts, append, {0, 0, 0}, 0.0f};
+    if (sp && sp->k > 0) {
+        r.k = sp->k;
+        r.drafter = 1;
+        const int v = sp->draft_vocab;   // spec.c:88-91
+        r.nv = v >= 4 && v < c->vocab ? (v & ~3) : c->vocab;
+    }
     const int n = generate_impl(c, &r, status);
-    (void)stats;
+    if (stats && n >= 0 && r.k > 0) {   // accumulated, never reset (pinfer.h:110-116)
+        stats->rounds += r.stats[0];
+        stats->drafted += r.stats[1];
+        stats->accepted += r.stats[2];
+    }
     return n;
 }
 
@@ -802,11 +973,14 @@ constexpr uint32_t kStateVersion = 2;
 size_t lin_state_floats(const pinfer_ctx *c) {
     return (size_t)std::max(c->K - 1, 1) * c->C + (size_t)c->nv * c->dk * c->dv;
 }
-size_t state_bytes(const pinfer_ctx *c, int n_past) {
+size_t state_bytes(const pinfer_ctx *c, int n_past, int n_mtp = 0) {
     int n_full = 0;
     for (int l = 0; l < c->n_layers; l++) n_full += c->layers[l].is_full;
     return sizeof(StateHdr) + (size_t)c->n_lin * lin_state_floats(c) * 4 +
-           (size_t)n_full * 2 * c->nkv * (size_t)n_past * c->hd * 4;
+           (size_t)(n_full * (size_t)n_past + n_mtp) * 2 * c->nkv * c->hd * 4;
+}
+int mtp_rows_saved(const pinfer_ctx *c) {   // state.c:51-53
+    return c->mtp_ok && c->mtp_rows > 0 ? std::min(c->mtp_rows, c->n_past) : 0;
 }
 StateHdr state_header(const pinfer_ctx *c) {
     const PqHeader *h = &c->hdr;
@@ -815,7 +989,7 @@ StateHdr state_header(const pinfer_ctx *c) {
     s.version = kStateVersion;
     s.n_past = (uint32_t)c->n_past;
     s.kv_dtype = PINFER_KV_F32;
-    s.mtp_rows = 0;
+    s.mtp_rows = (uint32_t)mtp_rows_saved(c);
     s.n_layers = h->n_layers;
     s.hidden = h->hidden;
     s.n_kv = h->n_kv_heads;
@@ -830,7 +1004,7 @@ StateHdr state_header(const pinfer_ctx *c) {
     return s;
 }
 // dir 0: device -> blob, 1: blob -> device; rows [0, n_past) of every cache
-int state_copy(pinfer_ctx *c, char *cur, int n_past, int dir) {
+int state_copy(pinfer_ctx *c, char *cur, int n_past, int dir, int n_mtp = 0) {
     const auto kind = dir == 0 ? cudaMemcpyDeviceToHost : cudaMemcpyHostToDevice;
     auto mv = [&](void *dev, size_t bytes) -> int {
         if (bytes == 0) return PINFER_OK;
@@ -850,20 +1024,27 @@ int state_copy(pinfer_ctx *c, char *cur, int n_past, int dir) {
             for (int g = 0; g < c->nkv; g++)
                 if ((rc = mv((kv ? c->att[l].vc : c->att[l].kc) + g * gstride, rows))) return rc;
     }
+    const size_t mrows_b = (size_t)n_mtp * c->hd * 4;   // the MTP head's K then V rows
+    for (int kv = 0; kv < 2 && n_mtp > 0; kv++)
+        for (int g = 0; g < c->nkv; g++)
+            if ((rc = mv((kv ? c->mtp_att.vc : c->mtp_att.kc) + g * gstride, mrows_b))) return rc;
     CUDA_OK(cudaStreamSynchronize(c->stream));
     return PINFER_OK;
 }
 }  // namespace
 
-size_t pinfer_state_size(const pinfer_ctx *c) { return c ? state_bytes(c, c->n_past) : 0; }
+size_t pinfer_state_size(const pinfer_ctx *c) {
+    return c ? state_bytes(c, c->n_past, mtp_rows_saved(c)) : 0;
+}
 
 int pinfer_state_save(const pinfer_ctx *c, void *buf, size_t cap) {
     if (!c || !buf) return PINFER_E_ARG;
-    if (cap < state_bytes(c, c->n_past)) return PINFER_E_ARG;
+    const int n_mtp = mtp_rows_saved(c);
+    if (cap < state_bytes(c, c->n_past, n_mtp)) return PINFER_E_ARG;
     pinfer_ctx *m = const_cast<pinfer_ctx *>(c);   // the stream is used, the state is not changed
     const StateHdr h = state_header(c);
     memcpy(buf, &h, sizeof h);
-    return state_copy(m, static_cast<char *>(buf) + sizeof h, c->n_past, 0);
+    return state_copy(m, static_cast<char *>(buf) + sizeof h, c->n_past, 0, n_mtp);
 }
 
 int pinfer_state_load(pinfer_ctx *c, const void *buf, size_t len) {
@@ -878,16 +1059,17 @@ int pinfer_state_load(pinfer_ctx *c, const void *buf, size_t len) {
         h.full_mask != mine.full_mask || h.kv_dtype != mine.kv_dtype || h.model_fp != mine.model_fp)
         return PINFER_E_FORMAT;   // another model file, or another KV storage format
     if (h.n_past > (uint32_t)c->max_ctx) return PINFER_E_CTX_FULL;
-    // MTP rows (saved by an engine with the draft head's cache) are dropped: this build keeps
-    // no MTP cache, like a model converted without the head (state.c:137-140)
-    if (h.mtp_rows > h.n_past) return PINFER_E_FORMAT;
-    const size_t mtp = 2 * (size_t)h.n_kv * h.mtp_rows * h.head_dim * 4;
-    if (len < state_bytes(c, (int)h.n_past) + mtp) return PINFER_E_FORMAT;
+    if (h.mtp_rows > h.n_past || len < state_bytes(c, (int)h.n_past, (int)h.mtp_rows)) return PINFER_E_FORMAT;
+    // MTP rows go to the MTP cache, or are dropped without the head (state.c:137-140)
+    const int n_mtp = c->mtp_ok ? (int)h.mtp_rows : 0;
     launch_flush(c->lin, 0, c->lind, c->step, c->stream);   // drop any pending commit
-    const int rc = state_copy(c, const_cast<char *>(static_cast<const char *>(buf)) + sizeof h,
-                              (int)h.n_past, 1);
+    int rc = state_copy(c, const_cast<char *>(static_cast<const char *>(buf)) + sizeof h,
+                        (int)h.n_past, 1, n_mtp);
     if (rc) return rc;
+    // rows without saved values must not hold stale memory (state.c:149-152)
+    if ((rc = zero_mtp_rows(c, n_mtp, (int)h.n_past)) || (rc = sync(c))) return rc;
     c->n_past = (int)h.n_past;
+    c->mtp_rows = n_mtp;
     c->ck_valid = 0;   // the KV rows below the checkpoint were replaced
     return PINFER_OK;
 }
@@ -909,6 +1091,7 @@ int pinfer_checkpoint(pinfer_ctx *c) {
     }
     c->ck_valid = 1;
     c->ck_n_past = c->n_past;
+    c->ck_mtp_rows = std::min(c->mtp_rows, c->n_past);
     return sync(c);
 }
 
@@ -920,6 +1103,7 @@ int pinfer_rewind(pinfer_ctx *c) {
         CUDA_OK(cudaMemcpyAsync(c->lin[i].rec, c->ck_buf + i * (conv + rec) + conv, rec * 4, cudaMemcpyDeviceToDevice, c->stream));
     }
     c->n_past = c->ck_n_past;
+    c->mtp_rows = c->ck_mtp_rows;
     return sync(c);
 }
 
@@ -1040,6 +1224,14 @@ pinfer_ctx *pinfer_b200_clone(const pinfer_ctx *src, int max_ctx, int *err) {
         c->att[l] = src->att[l];
     }
     c->n_lin = src->n_lin;
+    c->mtp_ok = src->mtp_ok;   // the MTP head's parameters (its KV cache is allocated below)
+    c->mtp_fc = src->mtp_fc;
+    c->mtp_norm_emb = src->mtp_norm_emb;
+    c->mtp_norm_hid = src->mtp_norm_hid;
+    c->mtp_norm_out = src->mtp_norm_out;
+    c->mtp_layer = src->mtp_layer;
+    c->mtp_att.q_norm = src->mtp_att.q_norm;
+    c->mtp_att.k_norm = src->mtp_att.k_norm;
     c->lind = src->lind;
     c->attd = src->attd;
     c->attd.max_ctx = c->max_ctx;   // the RoPE tables cover the source's (larger) context

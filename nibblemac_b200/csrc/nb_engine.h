@@ -61,10 +61,15 @@ struct Step {
     unsigned p24;          // synthetic drafter acceptance threshold (p * 2^24)
     unsigned long long seed;
     long long rounds, drafted, accepted;
+    // MTP drafting (drafter 1): the last MTP pass's draft and the last verify's committed rows
+    int drafter;           // 0 synthetic (seed, p24, greedy stream), 1 the MTP head
+    int mtp_d1;
+    int last_pos, last_e;
+    int last_tok[kMaxRows];
 };
 
 struct GenArgs {
-    int n_max, k, eos, n_stop, max_ctx, vocab;
+    int n_max, k, eos, n_stop, max_ctx, vocab, drafter;
     int stop_ids[8];
     unsigned p24;
     unsigned long long seed;
@@ -139,6 +144,17 @@ void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const fl
 void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s);
 void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s);
 void launch_pass_end(Step *st, cudaStream_t s);
+// MTP draft head (see the kernels' comments)
+void launch_norm_rows(const float *x, const float *w, int H, float eps, const Step *st, float *out,
+                      cudaStream_t s);
+void launch_mtp_input(const Mat &E, const float *h, const Step *ms, const float *w_emb, const float *w_hid,
+                      int H, float eps, Act out, cudaStream_t s);
+void launch_mtp_chain_set(const Step *st, Step *ms, int step, cudaStream_t s);
+void launch_mtp_chain_take(Step *st, const Step *ms, int step, const float *mrows, float *mcur, int H,
+                           cudaStream_t s);
+void launch_mtp_pending_set(const Step *st, Step *ms, cudaStream_t s);
+void launch_mtp_pending_take(Step *st, const Step *ms, const float *mrows, float *mcur, int H, cudaStream_t s);
+void launch_mtp_prefill_fix(const Step *st, Step *ms, cudaStream_t s);
 size_t deltanet_smem(int rep);
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s);
 void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s);

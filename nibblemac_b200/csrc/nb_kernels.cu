@@ -1380,6 +1380,8 @@ __global__ void k_set_gen(Step *st, GenArgs g) {
     st->count = 0;
     st->done = 0;
     st->status = 0;
+    st->drafter = g.drafter;
+    st->last_e = 0;
 }
 
 // ------------------------------------------------------------------ attention
@@ -2189,6 +2191,133 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     }
 }
 
+
+// ------------------------------------------------------------------ MTP draft head
+// The Qwen3.5 MTP head (engine/src/mtp.c:60-100, semantics engine/src/mtp.h): row t at position
+// pos0 + t takes a final-normed hidden h[t] and the token that follows that position;
+//   u = fc([rmsnorm(embed(tok), norm_emb) | rmsnorm(h, norm_hid)]), one full-attention decoder
+//   block with its own KV cache, m = rmsnorm(u, norm_out), logits = head[0:nv) m.
+// The block and the head reuse the main model's kernels; these kernels add the input rows, the
+// normed-row export, and the hand-offs between the passes of a verify round (draft chain, then
+// the pass over the accepted rows that leaves the next round's first draft).
+
+// one dequantised row element of a Q4K embedding (kern_get_row_q, engine/src/kern_act.c:53-86)
+__device__ __forceinline__ float embed_val(const Mat &E, int tok, int c) {
+    const int panel = tok >> 5, r = tok & 31;
+    const int sb = c >> 8, k = (c >> 5) & 7, j = c & 31;
+    const uint8_t *u = E.w + ((size_t)panel * E.nsb + sb) * kUnitBytes + r * 16;
+    const uint4 sc = *reinterpret_cast<const uint4 *>(u);
+    const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
+    const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
+    const float dd = __fmul_rn(half_bits_to_float((uint32_t)(A >> 48)), (float)(uint32_t)((A >> (6 * k)) & 63u));
+    const float mm = __fmul_rn(half_bits_to_float((uint32_t)(B >> 48)), (float)(uint32_t)((B >> (6 * k)) & 63u));
+    const uint8_t byte = u[512 * (k + 1) + (j & 15)];
+    const float q = (float)(j < 16 ? (byte & 15) : (byte >> 4));
+    return __fadd_rn(__fmul_rn(dd, q), -mm);
+}
+
+// pf_norm_rows without quantisation: out [n][H] = (x r) w, r = 1 / sqrtf(sumsq / H + eps)
+__global__ void k_norm_rows(const float *x, const float *w, int H, float eps, const Step *st, float *out) {
+    pdl_wait();
+    pdl_trigger();
+    const int v = blockIdx.x;
+    if (v >= st->n) return;
+    extern __shared__ float xr[];   // [H]
+    __shared__ float rr;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xr[i] = x[(size_t)v * H + i];
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const float s = sumsq_ref(xr, H);
+        if (threadIdx.x == 0) rr = inv_sqrt_ref(__fadd_rn(__fdiv_rn(s, (float)H), eps));
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < H; i += blockDim.x) out[(size_t)v * H + i] = __fmul_rn(__fmul_rn(xr[i], rr), w[i]);
+}
+
+// MTP input rows (mtp.c:76-83): [rmsnorm(embed(tok)) | rmsnorm(h)] (2H columns), A8-quantised
+// for the fc projection. h [n][H] rows, tokens from the pass's step block.
+__global__ void k_mtp_input(Mat E, const float *h, const Step *ms, const float *w_emb, const float *w_hid,
+                            int H, float eps, Act out) {
+    pdl_wait();
+    pdl_trigger();
+    const int v = blockIdx.x;
+    if (v >= ms->n) return;
+    extern __shared__ float cat[];   // [2H]: embedding row, hidden row
+    __shared__ float r2[2];
+    int tok = ms->tokens[v];
+    if (tok < 0 || tok >= E.rows) tok = 0;   // ids come from the argmax of this head
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+        cat[c] = embed_val(E, tok, c);
+        cat[H + c] = h[(size_t)v * H + c];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (warp < 2) {
+        const float s = sumsq_ref(cat + warp * H, H);
+        if (lane == 0) r2[warp] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(s, (float)H), eps));
+    }
+    __syncthreads();
+    const int nb = (2 * H) >> 5;
+    for (int b = warp; b < nb; b += nw) {
+        const int i = b * 32 + lane;
+        const float y = i < H ? __fmul_rn(__fmul_rn(cat[i], r2[0]), w_emb[i])
+                              : __fmul_rn(__fmul_rn(cat[i], r2[1]), w_hid[i - H]);
+        quant_block_warp(y, lane, out.q + (size_t)v * out.cols + b * 32, out.d + (size_t)v * nb + b,
+                         out.fs + (size_t)v * nb + b);
+    }
+}
+
+// Chain step s of a verify round (spec.c:300-321): draft s + 1 from (m of draft s, draft s) at
+// position P - 1 + s; runs only while s < ke (verify rows - 1).
+__global__ void k_mtp_chain_set(const Step *st, Step *ms, int s) {
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x != 0) return;
+    const int n = st->n;
+    ms->n = (n > 0 && s < n - 1) ? 1 : 0;
+    ms->pos0 = st->pos0 - 1 + s;
+    ms->tokens[0] = st->tokens[s];
+    ms->logged = 0;
+}
+__global__ void k_mtp_chain_take(Step *st, const Step *ms, int s, const float *mrows, float *mcur, int H) {
+    pdl_wait();
+    pdl_trigger();
+    if (ms->n <= 0) return;
+    if (threadIdx.x == 0) st->tokens[s + 1] = ms->argmax[0];
+    for (int i = threadIdx.x; i < H; i += blockDim.x) mcur[i] = mrows[i];
+}
+// The pass over the rows the last verify committed (spec.c:369-374, mtp_pending): their main
+// hiddens, the tokens that followed them, their positions.
+__global__ void k_mtp_pending_set(const Step *st, Step *ms) {
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x != 0) return;
+    const int e = st->last_e;
+    ms->n = e;
+    ms->pos0 = st->last_pos;
+    for (int t = 0; t < e && t < kMaxRows; t++) ms->tokens[t] = st->last_tok[t];
+    ms->logged = 0;
+}
+// Its last row drafts the next round's first token; its m seeds the next chain.
+__global__ void k_mtp_pending_take(Step *st, const Step *ms, const float *mrows, float *mcur, int H) {
+    pdl_wait();
+    pdl_trigger();
+    const int n = ms->n;
+    if (n <= 0) return;
+    if (threadIdx.x == 0) {
+        const int d1 = ms->argmax[n - 1];
+        st->mtp_d1 = d1;
+        if (st->n >= 2) st->tokens[1] = d1;
+    }
+    for (int i = threadIdx.x; i < H; i += blockDim.x) mcur[i] = mrows[(size_t)(n - 1) * H + i];
+}
+// Prefill: the prompt's last row pairs with the first generated token (spec.c:186-190).
+__global__ void k_mtp_prefill_fix(const Step *st, Step *ms) {
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0 && ms->n > 0 && st->n > 0) ms->tokens[ms->n - 1] = st->argmax[st->n - 1];
+}
+
 // ------------------------------------------------------------------ generation control
 // splitmix64 output function and the synthetic drafter of the benchmark: the draft for output
 // index j is, with probability p24 / 2^24, the target's greedy token greedy[j], else a uniform
@@ -2228,9 +2357,14 @@ __device__ void prepare_round(Step *st, const int *greedy) {
     }
     const int ke = st->k < left ? st->k : left;
     st->tokens[0] = st->cur;
-    for (int s = 1; s <= ke; s++) {
-        const long long j = st->count - 1 + s;
-        st->tokens[s] = synth_draft(st->seed, j, st->p24, st->vocab, greedy ? greedy[j] : 0);
+    if (st->drafter == 1) {
+        // MTP drafts: d1 from the last MTP pass; drafts 2..ke come from this round's chain
+        if (ke >= 1) st->tokens[1] = st->mtp_d1;
+    } else {
+        for (int s = 1; s <= ke; s++) {
+            const long long j = st->count - 1 + s;
+            st->tokens[s] = synth_draft(st->seed, j, st->p24, st->vocab, greedy ? greedy[j] : 0);
+        }
     }
     st->n = ke + 1;
     st->logged = 1;
@@ -2247,6 +2381,7 @@ __global__ void k_gen_start(Step *st, const int *greedy, int *out) {
     st->count = 0;
     st->done = 0;
     st->status = 0;
+    st->last_e = 0;
     if (emit_tok(st, out, st->cur)) {
         st->done = 1;
         st->n = 0;
@@ -2264,7 +2399,10 @@ __global__ void k_accept(Step *st, const int *greedy, int *out) {
     pdl_trigger();
     if (threadIdx.x != 0) return;
     const int n = st->n;
-    if (n <= 0) return;
+    if (n <= 0) {
+        st->last_e = 0;
+        return;
+    }
     const int ke = n - 1;
     int vt[kMaxRows + 1];
     for (int i = 0; i < n; i++) vt[i] = st->tokens[i];
@@ -2276,6 +2414,9 @@ __global__ void k_accept(Step *st, const int *greedy, int *out) {
     vt[a + 1] = g;
     int e = 0, done = 0;
     while (e <= a && !done) done = emit_tok(st, out, vt[++e]);
+    st->last_pos = st->pos0;   // for the MTP pass over the committed rows
+    st->last_e = e;
+    for (int i = 0; i < e; i++) st->last_tok[i] = vt[i + 1];
     st->pend_keep = e - 1;   // pf_lin_commit (forward_lin.c:413-432)
     st->pend_conv = e;
     st->wr ^= 1;
@@ -2515,6 +2656,30 @@ void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int 
 }
 void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s) {
     launch_k(k_keys_argmax, 1, kMaxRows, 0, s, keys, st);
+}
+void launch_norm_rows(const float *x, const float *w, int H, float eps, const Step *st, float *out,
+                      cudaStream_t s) {
+    launch_k(k_norm_rows, kMaxRows, 256, (size_t)H * sizeof(float), s, x, w, H, eps, st, out);
+}
+void launch_mtp_input(const Mat &E, const float *h, const Step *ms, const float *w_emb, const float *w_hid,
+                      int H, float eps, Act out, cudaStream_t s) {
+    launch_k(k_mtp_input, kMaxRows, 256, 2 * (size_t)H * sizeof(float), s, E, h, ms, w_emb, w_hid, H, eps, out);
+}
+void launch_mtp_chain_set(const Step *st, Step *ms, int step, cudaStream_t s) {
+    launch_k(k_mtp_chain_set, 1, 32, 0, s, st, ms, step);
+}
+void launch_mtp_chain_take(Step *st, const Step *ms, int step, const float *mrows, float *mcur, int H,
+                           cudaStream_t s) {
+    launch_k(k_mtp_chain_take, 1, 256, 0, s, st, ms, step, mrows, mcur, H);
+}
+void launch_mtp_pending_set(const Step *st, Step *ms, cudaStream_t s) {
+    launch_k(k_mtp_pending_set, 1, 32, 0, s, st, ms);
+}
+void launch_mtp_pending_take(Step *st, const Step *ms, const float *mrows, float *mcur, int H, cudaStream_t s) {
+    launch_k(k_mtp_pending_take, 1, 256, 0, s, st, ms, mrows, mcur, H);
+}
+void launch_mtp_prefill_fix(const Step *st, Step *ms, cudaStream_t s) {
+    launch_k(k_mtp_prefill_fix, 1, 32, 0, s, st, ms);
 }
 void launch_pass_end(Step *st, cudaStream_t s) { launch_k(k_pass_end, 1, 1, 0, s, st); }
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s) {

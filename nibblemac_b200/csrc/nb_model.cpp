@@ -133,13 +133,19 @@ int PqFile::mat(const char *name, uint32_t rows, uint32_t cols, PqMat *out) cons
     return PINFER_OK;
 }
 
-static int build_layer(const PqFile &m, int i, PqLayer *L) {   // model.c:156-205
+// model.c:156-205; prefix "layers.<i>." for the main layers, "mtp.layers.0." (always a
+// full-attention block) for the MTP head's.
+static int build_layer(const PqFile &m, int i, PqLayer *L, const char *prefix = nullptr) {
     const PqHeader *h = m.hdr;
-    char nm[128];
+    char nm[160];
     int rc = 0;
-    auto N = [&](const char *s) { snprintf(nm, sizeof nm, "layers.%d.%s", i, s); return nm; };
+    auto N = [&](const char *s) {
+        if (prefix) snprintf(nm, sizeof nm, "%s%s", prefix, s);
+        else snprintf(nm, sizeof nm, "layers.%d.%s", i, s);
+        return nm;
+    };
     const uint32_t H = h->hidden;
-    L->is_full = (h->full_attn_mask >> i) & 1;
+    L->is_full = prefix ? 1 : (h->full_attn_mask >> i) & 1;
     rc |= m.vec(N("input_layernorm.weight"), H, &L->in_norm);
     rc |= m.vec(N("post_attention_layernorm.weight"), H, &L->post_norm);
     rc |= m.mat(N("mlp.gate_proj.weight"), h->ffn, H, &L->gate);
@@ -206,7 +212,26 @@ int PqFile::open_file(const char *path) {
     }
     if (rc == PINFER_OK) rc = vec("norm.weight", hdr->hidden, &norm);
     for (uint32_t i = 0; rc == PINFER_OK && i < hdr->n_layers; i++) rc = build_layer(*this, (int)i, &layers[i]);
-    if (rc != PINFER_OK) close_file();
+    if (rc != PINFER_OK) {
+        close_file();
+        return rc;
+    }
+    // The MTP head is mapped lazily by the reference (pf_mtp_init at the first speculative
+    // generation), so a missing or malformed head does not fail the load: generation with
+    // k > 0 then returns PINFER_E_FORMAT.
+    if (hdr->has_mtp) {
+        const uint32_t H = hdr->hidden;
+        int m = PINFER_OK;
+        m |= find("mtp.fc.weight") ? mat("mtp.fc.weight", H, 2 * H, &mtp.fc) : PINFER_E_FORMAT;
+        m |= find("mtp.pre_fc_norm_embedding.weight") ? vec("mtp.pre_fc_norm_embedding.weight", H, &mtp.norm_emb) : PINFER_E_FORMAT;
+        m |= find("mtp.pre_fc_norm_hidden.weight") ? vec("mtp.pre_fc_norm_hidden.weight", H, &mtp.norm_hid) : PINFER_E_FORMAT;
+        m |= find("mtp.norm.weight") ? vec("mtp.norm.weight", H, &mtp.norm_out) : PINFER_E_FORMAT;
+        if (m == PINFER_OK && find("mtp.layers.0.self_attn.q_proj.weight"))
+            m = build_layer(*this, 0, &mtp.layer, "mtp.layers.0.");
+        else
+            m = PINFER_E_FORMAT;
+        mtp.ok = m == PINFER_OK;
+    }
     return rc;
 }
 
@@ -217,6 +242,7 @@ void PqFile::close_file() {
     hdr = nullptr;
     dir = nullptr;
     for (auto &L : layers) L = PqLayer();
+    mtp = PqMtp();
 }
 
 // pf_model_fingerprint (model.c:142-154): FNV-1a over the header, the directory and three

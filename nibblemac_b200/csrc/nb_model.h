@@ -52,6 +52,14 @@ struct PqLayer {
     const float *q_norm = nullptr, *k_norm = nullptr;
 };
 
+// The MTP draft head (engine/src/mtp.c:8-32): fc [H][2H], three norms, one full-attention block.
+struct PqMtp {
+    bool ok = false;   // every mtp.* tensor present with the right shape
+    PqMat fc;
+    const float *norm_emb = nullptr, *norm_hid = nullptr, *norm_out = nullptr;
+    PqLayer layer;
+};
+
 struct PqFile {
     void *map = nullptr;
     size_t map_bytes = 0;
@@ -60,6 +68,7 @@ struct PqFile {
     PqMat embed, head;
     const float *norm = nullptr;
     PqLayer layers[32];
+    PqMtp mtp;
 
     int open_file(const char *path);   // PINFER_OK / PINFER_E_IO / PINFER_E_FORMAT
     void close_file();

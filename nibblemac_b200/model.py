@@ -89,12 +89,14 @@ class Model:
         return out
 
     def generate(self, prompt, n_max: int, k: int = 0, stop_ids=None, on_token=None,
+                 draft_vocab: int = 0, stats: SpecStats | None = None, append: bool = False
                  ) -> tuple[list[int], int]:
-        """pinfer_generate_greedy_ex: (tokens, status)."""
+        """pinfer_generate_greedy_ex (append: _cont): (tokens, status). k > 0 drafts with the
+        MTP head over the first draft_vocab ids (0: all); statistics accumulate into stats."""
         t = _i32(prompt)
         out = np.zeros(n_max, np.int32)
-        sp = SpecParams(k, 0, 0, 0)
-        st = SpecStats()
+        sp = SpecParams(k, draft_vocab, 0, 0)
+        st = stats if stats is not None else SpecStats()
         status = ctypes.c_int(0)
         opts = None
         keep = []
@@ -105,10 +107,9 @@ class Model:
                 type(GenOpts().on_token)(lambda tok, user: int(bool(on_token(int(tok)))))
             keep.append(cb)
             opts = GenOpts(ids.ctypes.data_as(_c_int32_p) if len(ids) else None, len(ids), cb, None)
-        n = self.lib.pinfer_generate_greedy_ex(self.ctx, t.ctypes.data_as(_c_int32_p), len(t),
-                                               out.ctypes.data_as(_c_int32_p), n_max,
-                                               ctypes.byref(sp), ctypes.byref(opts) if opts else None,
-                                               ctypes.byref(st), ctypes.byref(status))
+        fn = self.lib.pinfer_generate_greedy_cont if append else self.lib.pinfer_generate_greedy_ex
+        n = fn(self.ctx, t.ctypes.data_as(_c_int32_p), len(t), out.ctypes.data_as(_c_int32_p), n_max,
+               ctypes.byref(sp), ctypes.byref(opts) if opts else None, ctypes.byref(st), ctypes.byref(status))
         if n < 0:
             raise PinferError(n, "pinfer_generate_greedy_ex", self.lib.last_error())
         return out[:n].tolist(), status.value

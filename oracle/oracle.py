@@ -79,6 +79,16 @@ class _Params(ctypes.Structure):
                 ("kv_dtype", ctypes.c_int), ("gpu_split", ctypes.c_float)]
 
 
+class _SpecParams(ctypes.Structure):
+    _fields_ = [("k", ctypes.c_int), ("draft_vocab", ctypes.c_int), ("adaptive", ctypes.c_int),
+                ("ngram", ctypes.c_int)]
+
+
+class _SpecStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int64) for n in ("rounds", "drafted", "accepted", "ngram_rounds",
+                                              "ngram_drafted", "ngram_accepted")]
+
+
 class RefEngine:
     """The reference engine (scalar build + Q4K restatement) on one model file."""
 
@@ -98,6 +108,8 @@ class RefEngine:
         L.ref_spec_generate.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P,
                                         ctypes.c_uint64, ctypes.c_uint32, _P]
         L.ref_forward_all.argtypes = [_P, _P, ctypes.c_int, _P]
+        L.pinfer_generate_greedy_ex.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, _P, _P, _P, _P]
+        L.pinfer_generate_greedy_cont.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, _P, _P, _P, _P]
         L.pinfer_state_size.restype = ctypes.c_size_t
         L.pinfer_state_size.argtypes = [_P]
         L.pinfer_state_save.argtypes = [_P, _P, ctypes.c_size_t]
@@ -162,6 +174,22 @@ class RefEngine:
         if n < 0:
             raise RuntimeError(f"reference generate: {n}")
         return out[:n].tolist()
+
+    def generate_mtp(self, prompt, n_max: int, k: int, draft_vocab: int = 0, append: bool = False):
+        """The reference's own speculative decoding with its MTP head (pinfer_generate_greedy_ex
+        / _cont, fixed k, no prompt lookup, no adaptive policy): (tokens, [rounds, drafted,
+        accepted], status)."""
+        t = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(n_max, np.int32)
+        sp = _SpecParams(k, draft_vocab, 0, 0)
+        st = _SpecStats()
+        status = ctypes.c_int(0)
+        fn = self.lib.pinfer_generate_greedy_cont if append else self.lib.pinfer_generate_greedy_ex
+        n = fn(self.ctx, _ptr(t), len(t), _ptr(out), n_max, ctypes.byref(sp), None, ctypes.byref(st),
+               ctypes.byref(status))
+        if n < 0:
+            raise RuntimeError(f"reference generate: {n}")
+        return out[:n].tolist(), [st.rounds, st.drafted, st.accepted], status.value
 
     def spec_generate(self, prompt, n_max: int, k: int, greedy, seed: int, p: float):
         t = np.ascontiguousarray(prompt, np.int32)

@@ -205,3 +205,29 @@ def test_clones_share_weights_and_run_concurrently(small_model):
         src.close()
         for m in clones:
             m.close()
+
+
+@pytest.mark.parametrize("k,nv", [(1, 0), (2, 0), (3, 0), (4, 0), (3, 1000)])
+def test_mtp_speculation_matches_reference(pair, k, nv):
+    """pinfer_generate_greedy_ex with k > 0: drafts from the MTP head (draft chain, verify,
+    pass over the committed rows, all on the device) give the plain greedy tokens and exactly the
+    reference's rounds / drafted / accepted counts (its MTP drafts are bit-identical), and the
+    state after it, MTP KV rows included, equals the reference's byte for byte."""
+    from nibblemac_b200._lib import SpecStats
+    name, dev, ref = pair
+    p = prompt(dev.n_vocab, 29, 50 + k)
+    dev.reset()
+    plain, _ = dev.generate(p, 40)
+    st = SpecStats()
+    toks, status = dev.generate(p, 40, k=k, draft_vocab=nv, stats=st)
+    rtoks, rst, rstatus = ref.generate_mtp(p, 40, k, nv)
+    assert status == rstatus == 0
+    assert toks == plain == rtoks
+    assert [st.rounds, st.drafted, st.accepted] == rst, f"{name} k={k}: stats {st.rounds, st.drafted, st.accepted} vs {rst}"
+    assert dev.save_state() == ref.save_state()
+    # a continuation keeps drafting from the MTP rows of the first call
+    q = prompt(dev.n_vocab, 3, 60 + k)
+    st2 = SpecStats()
+    toks2, _ = dev.generate(q, 24, k=k, draft_vocab=nv, stats=st2, append=True)
+    rtoks2, rst2, _ = ref.generate_mtp(q, 24, k, nv, append=True)
+    assert toks2 == rtoks2 and [st2.rounds, st2.drafted, st2.accepted] == rst2
