@@ -85,7 +85,10 @@ int nb_q4k_repack(const uint8_t *pq, int rows, int cols, uint8_t *panels);
 
 typedef struct nb_mv nb_mv;
 /* Activation scratch (A8 of up to nmax vectors of `cols`) and a control block on the device.
- * nmax <= 16. NULL on failure (no device, bad shape). */
+ * nmax <= NB_MV_MAX_N. NULL on failure (no device, bad shape). Calls with n <= 16 vectors run
+ * the CUDA-core matvec kernels; n > 16 (which needs nmax > 16 at creation) runs the tcgen05
+ * tensor-core GEMM, with bit-identical results. */
+#define NB_MV_MAX_N 65536
 nb_mv *nb_mv_create(int rows, int cols, int nmax);
 void nb_mv_destroy(nb_mv *h);
 /* Set the vector count n (1..nmax) used by the next calls (one tiny kernel on `stream`). */
@@ -102,6 +105,18 @@ int nb_mv_matmul_repeat(nb_mv *h, const void *W, size_t stride, int copies, floa
  * [n][rows/32] uint64, NaN flags into nan0 [n]). */
 int nb_mv_head_repeat(nb_mv *h, const void *W, size_t stride, int copies, float *Y, int iters,
                       void *partial, int *nan0, void *stream);
+/* The tensor-core GEMM with one of its epilogues on the current n (> 16) vectors:
+ * epi 0: Y [n][rows] = W0 x;  1: Y += W0 x (residual add);
+ * 3: gate W0 / up W1 (both rows x cols, rows % 32 == 0): A8 of silu(W0 x) * (W1 x) into
+ *    q [n][rows] int8, d / fs [n][rows / 32] (pf_silu_mul then kern_quant_act);
+ * 4: LM head: logits into Y (may be NULL), argmax keys into partial [n][rows / 32] uint64 and
+ *    row-0 NaN flags into nan0 [n], as nb_mv_head_repeat.
+ * 0, or -4 (arguments; n <= 16). */
+int nb_mv_gemm(nb_mv *h, int epi, const void *W0, const void *W1, float *Y, void *q, void *d, void *fs,
+               void *partial, int *nan0, void *stream);
+/* The status word of the tensor-core path (0, or -91 after a bounded device wait gave up);
+ * synchronous. */
+int nb_mv_status(nb_mv *h);
 /* nb_mv_quant + nb_mv_matmul. */
 int nb_mv_run(nb_mv *h, const void *W, const float *X, float *Y, void *stream);
 /* Copy the scratch activations out (device buffers: q [n][cols] int8, d / fsum [n][cols/32]). */

@@ -79,7 +79,21 @@ struct nb_mv {
     int rows, cols, nmax, n;
     Act act;
     Step *step;
+    GemmMaps maps;   // nmax > kMaxRows: TMA descriptors of the activation scratch
+    int *status;     // the GEMM's device-wait status word
 };
+
+namespace {
+Mat panel_mat(const void *W, int rows, int cols) {
+    Mat m;
+    m.w = (const uint8_t *)W;
+    m.rows = rows;
+    m.cols = cols;
+    m.npanels = (rows + kPanelRows - 1) / kPanelRows;
+    m.nsb = cols / 256;
+    return m;
+}
+}  // namespace
 
 extern "C" {
 
@@ -97,7 +111,7 @@ int nb_q4k_repack(const uint8_t *pq, int rows, int cols, uint8_t *panels) {
 nb_mv *nb_mv_create(int rows, int cols, int nmax) {
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev < 1) return nullptr;
-    if (!nb_q4k_panel_bytes(rows, cols) || nmax < 1 || nmax > kMaxRows) return nullptr;
+    if (!nb_q4k_panel_bytes(rows, cols) || nmax < 1 || nmax > NB_MV_MAX_N) return nullptr;
     nb_mv *h = new (std::nothrow) nb_mv();
     if (!h) return nullptr;
     h->rows = rows;
@@ -105,16 +119,19 @@ nb_mv *nb_mv_create(int rows, int cols, int nmax) {
     h->nmax = nmax;
     h->n = 0;
     h->act.cols = cols;
-    bool ok = cudaMalloc(&h->act.q, (size_t)kMaxRows * cols) == cudaSuccess &&
-              cudaMalloc(&h->act.d, sizeof(float) * kMaxRows * (cols / 32)) == cudaSuccess &&
-              cudaMalloc(&h->act.fs, sizeof(float) * kMaxRows * (cols / 32)) == cudaSuccess &&
+    const size_t nr = (size_t)std::max(nmax, kMaxRows);
+    bool ok = cudaMalloc(&h->act.q, nr * cols) == cudaSuccess &&
+              cudaMalloc(&h->act.d, sizeof(float) * nr * (cols / 32)) == cudaSuccess &&
+              cudaMalloc(&h->act.fs, sizeof(float) * nr * (cols / 32)) == cudaSuccess &&
               cudaMalloc(&h->step, sizeof(Step)) == cudaSuccess &&
-              cudaMemset(h->step, 0, sizeof(Step)) == cudaSuccess;
+              cudaMemset(h->step, 0, sizeof(Step)) == cudaSuccess &&
+              cudaMalloc(&h->status, sizeof(int)) == cudaSuccess &&
+              cudaMemset(h->status, 0, sizeof(int)) == cudaSuccess;
     if (!ok) {
         nb_mv_destroy(h);
         return nullptr;
     }
-    if (kernels_init(0, 0, 0) != 0) {
+    if (kernels_init(0, 0, 0) != 0 || (nmax > kMaxRows && gemm_maps(h->act, (int)nr, &h->maps) != 0)) {
         nb_mv_destroy(h);
         return nullptr;
     }
@@ -127,12 +144,14 @@ void nb_mv_destroy(nb_mv *h) {
     cudaFree(h->act.d);
     cudaFree(h->act.fs);
     cudaFree(h->step);
+    cudaFree(h->status);
     delete h;
 }
 
 int nb_mv_set_n(nb_mv *h, int n, void *stream) {
     if (!h || n < 1 || n > h->nmax) return PINFER_E_ARG;
     h->n = n;
+    if (n > kMaxRows) return PINFER_OK;   // the tensor-core path takes n as an argument
     int tok[kMaxRows] = {0};
     launch_set_pass(h->step, n, 0, 0, tok, (cudaStream_t)stream);
     return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
@@ -146,27 +165,66 @@ int nb_mv_quant(nb_mv *h, const float *X, void *stream) {
 
 int nb_mv_matmul(nb_mv *h, const void *W, float *Y, void *stream) {
     if (!h || !W || !Y || h->n < 1) return PINFER_E_ARG;
-    Mat m;
-    m.w = (const uint8_t *)W;
-    m.rows = h->rows;
-    m.cols = h->cols;
-    m.npanels = (h->rows + kPanelRows - 1) / kPanelRows;
-    m.nsb = h->cols / 256;
-    launch_matvec(m, h->act, h->step, Y, h->rows, 0, h->nmax, (cudaStream_t)stream);
+    const Mat m = panel_mat(W, h->rows, h->cols);
+    if (h->n > kMaxRows) {   // tcgen05 tiles
+        GemmArgs g;
+        g.W0 = g.W1 = m;
+        g.n = h->n;
+        g.y = Y;
+        g.ldy = h->rows;
+        g.status = h->status;
+        launch_gemm(0, h->maps, g, (cudaStream_t)stream);
+    } else {
+        launch_matvec(m, h->act, h->step, Y, h->rows, 0, h->nmax, (cudaStream_t)stream);
+    }
     return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
+}
+
+int nb_mv_gemm(nb_mv *h, int epi, const void *W0, const void *W1, float *Y, void *q, void *d, void *fs,
+               void *partial, int *nan0, void *stream) {
+    if (!h || !W0 || h->n < 1 || h->nmax <= kMaxRows || (epi != 0 && epi != 1 && epi != 3 && epi != 4) ||
+        ((epi == 0 || epi == 1) && !Y) || (epi == 3 && (!W1 || !q || !d || !fs || h->rows % 32)) ||
+        (epi == 4 && (!partial || !nan0)))
+        return PINFER_E_ARG;
+    GemmArgs g;
+    g.W0 = panel_mat(W0, h->rows, h->cols);
+    g.W1 = epi == 3 ? panel_mat(W1, h->rows, h->cols) : g.W0;
+    g.n = h->n;
+    g.y = Y;
+    g.ldy = h->rows;
+    g.out.q = (int8_t *)q;
+    g.out.d = (float *)d;
+    g.out.fs = (float *)fs;
+    g.out.cols = h->rows;
+    g.partial = (unsigned long long *)partial;
+    g.nan0 = nan0;
+    g.status = h->status;
+    launch_gemm(epi, h->maps, g, (cudaStream_t)stream);
+    return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
+}
+
+int nb_mv_status(nb_mv *h) {
+    int v = 0;
+    if (!h || cudaMemcpy(&v, h->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return PINFER_E_ARG;
+    return v;
 }
 
 int nb_mv_matmul_repeat(nb_mv *h, const void *W, size_t stride, int copies, float *Y, int iters,
                         void *stream) {
     if (!h || !W || !Y || h->n < 1 || copies < 1 || iters < 1) return PINFER_E_ARG;
-    Mat m;
-    m.rows = h->rows;
-    m.cols = h->cols;
-    m.npanels = (h->rows + kPanelRows - 1) / kPanelRows;
-    m.nsb = h->cols / 256;
     for (int i = 0; i < iters; i++) {
-        m.w = (const uint8_t *)W + (size_t)(i % copies) * stride;
-        launch_matvec(m, h->act, h->step, Y, h->rows, 0, h->nmax, (cudaStream_t)stream);
+        const Mat m = panel_mat((const uint8_t *)W + (size_t)(i % copies) * stride, h->rows, h->cols);
+        if (h->n > kMaxRows) {
+            GemmArgs g;
+            g.W0 = g.W1 = m;
+            g.n = h->n;
+            g.y = Y;
+            g.ldy = h->rows;
+            g.status = h->status;
+            launch_gemm(0, h->maps, g, (cudaStream_t)stream);
+        } else {
+            launch_matvec(m, h->act, h->step, Y, h->rows, 0, h->nmax, (cudaStream_t)stream);
+        }
     }
     return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
 }

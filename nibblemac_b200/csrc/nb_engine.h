@@ -4,6 +4,7 @@
 #include <cstddef>
 #include <cstdint>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "nb_math.cuh"
@@ -164,6 +165,29 @@ void set_last_error(const char *msg);   // 0, or -1 if a CUDA call failed
 void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s);
 // small-n standalone entry points for the C-ABI kernel tests
 void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s);
+
+// ---- tensor-core GEMM for passes of many rows (nb_gemm.cu) --------------------------------
+// TMA descriptors of an A8 activation buffer of `rows` rows (codes, block scales, block sums).
+struct GemmMaps {
+    CUtensorMap q, d, fs;
+    int rows = 0, cols = 0;
+};
+struct GemmArgs {
+    Mat W0, W1;                             // W1: the up matrix of the SwiGLU epilogue
+    int n = 0;                              // activation rows
+    float *y = nullptr;                     // epilogue 0 / 1 output, 4: logits (may be null)
+    int ldy = 0;
+    Act out;                                // epilogue 3: A8 of the SwiGLU product
+    unsigned long long *partial = nullptr;  // epilogue 4: argmax keys [n][npanels]
+    int *nan0 = nullptr;
+    int row_base = 0;
+    int *status = nullptr;                  // set to -91 when a bounded device wait gives up
+};
+int gemm_maps(const Act &a, int rows, GemmMaps *m);   // 0 or -1 (message in last error)
+int gemm_init();                                       // shared-memory limits; 0 or -1
+// Y = W A8(x) over g.n rows with the given epilogue (0 store, 1 residual add, 3 SwiGLU + A8,
+// 4 head keys); the A8 rows come through `maps`
+void launch_gemm(int epi, const GemmMaps &maps, const GemmArgs &g, cudaStream_t s);
 
 // ---- host-side helpers -----------------------------------------------------------------------
 size_t panel_bytes(int rows, int cols);
