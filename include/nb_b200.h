@@ -105,15 +105,19 @@ int nb_mv_matmul_repeat(nb_mv *h, const void *W, size_t stride, int copies, floa
  * [n][rows/32] uint64, NaN flags into nan0 [n]). */
 int nb_mv_head_repeat(nb_mv *h, const void *W, size_t stride, int copies, float *Y, int iters,
                       void *partial, int *nan0, void *stream);
-/* The tensor-core GEMM with one of its epilogues on the current n (> 16) vectors:
+/* Tensor-core path, two steps. nb_mv_prepare widens W0 (rows x cols, panel layout), or the row
+ * concatenation W0 ++ W1 when W1 is not NULL (gate / up, rows % 32 == 0), into the handle's
+ * tile image (the int8 codes in the tensor cores' shared-memory layout plus the scale entries;
+ * needs nmax > 16). nb_mv_gemm then runs on the current n (> 16) vectors:
  * epi 0: Y [n][rows] = W0 x;  1: Y += W0 x (residual add);
- * 3: gate W0 / up W1 (both rows x cols, rows % 32 == 0): A8 of silu(W0 x) * (W1 x) into
- *    q [n][rows] int8, d / fs [n][rows / 32] (pf_silu_mul then kern_quant_act);
+ * 3 (prepared with W1): A8 of silu(W0 x) * (W1 x) into q [n][rows] int8, d / fs [n][rows / 32]
+ *    (pf_silu_mul then kern_quant_act);
  * 4: LM head: logits into Y (may be NULL), argmax keys into partial [n][rows / 32] uint64 and
  *    row-0 NaN flags into nan0 [n], as nb_mv_head_repeat.
- * 0, or -4 (arguments; n <= 16). */
-int nb_mv_gemm(nb_mv *h, int epi, const void *W0, const void *W1, float *Y, void *q, void *d, void *fs,
-               void *partial, int *nan0, void *stream);
+ * nb_mv_matmul with n > 16 is nb_mv_prepare(W) + nb_mv_gemm(0). 0, or -4 (arguments). */
+int nb_mv_prepare(nb_mv *h, const void *W0, const void *W1, void *stream);
+int nb_mv_gemm(nb_mv *h, int epi, float *Y, void *q, void *d, void *fs, void *partial, int *nan0,
+               void *stream);
 /* The status word of the tensor-core path (0, or -91 after a bounded device wait gave up);
  * synchronous. */
 int nb_mv_status(nb_mv *h);

@@ -81,6 +81,9 @@ struct nb_mv {
     Step *step;
     GemmMaps maps;   // nmax > kMaxRows: TMA descriptors of the activation scratch
     int *status;     // the GEMM's device-wait status word
+    uint8_t *tiled;  // nmax > kMaxRows: tile image of the prepared weights (room for 2 x rows)
+    GemmW w;         // the prepared weights (nb_mv_prepare)
+    float *ypair;    // epilogue 3: gate / up rows [nmax][2 rows]
 };
 
 namespace {
@@ -131,9 +134,18 @@ nb_mv *nb_mv_create(int rows, int cols, int nmax) {
         nb_mv_destroy(h);
         return nullptr;
     }
-    if (kernels_init(0, 0, 0) != 0 || (nmax > kMaxRows && gemm_maps(h->act, (int)nr, &h->maps) != 0)) {
+    if (kernels_init(0, 0, 0) != 0) {
         nb_mv_destroy(h);
         return nullptr;
+    }
+    if (nmax > kMaxRows) {
+        const size_t rows2 = (size_t)((rows + 31) / 32) * 32 * 2;
+        if (gemm_maps(h->act, (int)nr, &h->maps) != 0 ||
+            cudaMalloc(&h->tiled, gemm_tiled_bytes((int)rows2, cols)) != cudaSuccess ||
+            cudaMalloc(&h->ypair, sizeof(float) * nr * rows2) != cudaSuccess) {
+            nb_mv_destroy(h);
+            return nullptr;
+        }
     }
     return h;
 }
@@ -145,6 +157,8 @@ void nb_mv_destroy(nb_mv *h) {
     cudaFree(h->act.fs);
     cudaFree(h->step);
     cudaFree(h->status);
+    cudaFree(h->tiled);
+    cudaFree(h->ypair);
     delete h;
 }
 
@@ -166,40 +180,51 @@ int nb_mv_quant(nb_mv *h, const float *X, void *stream) {
 int nb_mv_matmul(nb_mv *h, const void *W, float *Y, void *stream) {
     if (!h || !W || !Y || h->n < 1) return PINFER_E_ARG;
     const Mat m = panel_mat(W, h->rows, h->cols);
-    if (h->n > kMaxRows) {   // tcgen05 tiles
-        GemmArgs g;
-        g.W0 = g.W1 = m;
-        g.n = h->n;
-        g.y = Y;
-        g.ldy = h->rows;
-        g.status = h->status;
-        launch_gemm(0, h->maps, g, (cudaStream_t)stream);
+    if (h->n > kMaxRows) {   // tcgen05 tiles: widen the weights, then the GEMM
+        const int rc = nb_mv_prepare(h, W, nullptr, stream);
+        if (rc) return rc;
+        return nb_mv_gemm(h, 0, Y, nullptr, nullptr, nullptr, nullptr, nullptr, stream);
     } else {
         launch_matvec(m, h->act, h->step, Y, h->rows, 0, h->nmax, (cudaStream_t)stream);
     }
     return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
 }
 
-int nb_mv_gemm(nb_mv *h, int epi, const void *W0, const void *W1, float *Y, void *q, void *d, void *fs,
-               void *partial, int *nan0, void *stream) {
-    if (!h || !W0 || h->n < 1 || h->nmax <= kMaxRows || (epi != 0 && epi != 1 && epi != 3 && epi != 4) ||
-        ((epi == 0 || epi == 1) && !Y) || (epi == 3 && (!W1 || !q || !d || !fs || h->rows % 32)) ||
-        (epi == 4 && (!partial || !nan0)))
+int nb_mv_prepare(nb_mv *h, const void *W0, const void *W1, void *stream) {
+    if (!h || !W0 || h->nmax <= kMaxRows || (W1 && h->rows % 32)) return PINFER_E_ARG;
+    const Mat m0 = panel_mat(W0, h->rows, h->cols);
+    Mat m1;
+    if (W1) m1 = panel_mat(W1, h->rows, h->cols);
+    launch_gemm_tile(m0, m1, h->tiled, (cudaStream_t)stream);
+    h->w = gemm_w(m0, m1, h->tiled);
+    return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
+}
+
+int nb_mv_gemm(nb_mv *h, int epi, float *Y, void *q, void *d, void *fs, void *partial, int *nan0,
+               void *stream) {
+    if (!h || !h->w.t || h->n < 1 || h->nmax <= kMaxRows || (epi != 0 && epi != 1 && epi != 3 && epi != 4) ||
+        ((epi == 0 || epi == 1) && (!Y || h->w.rows != h->rows)) ||
+        (epi == 3 && (!q || !d || !fs || h->w.rows != 2 * h->rows)) ||
+        (epi == 4 && (!partial || !nan0 || h->w.rows != h->rows)))
         return PINFER_E_ARG;
+    cudaStream_t s = (cudaStream_t)stream;
     GemmArgs g;
-    g.W0 = panel_mat(W0, h->rows, h->cols);
-    g.W1 = epi == 3 ? panel_mat(W1, h->rows, h->cols) : g.W0;
+    g.W = h->w;
     g.n = h->n;
-    g.y = Y;
-    g.ldy = h->rows;
-    g.out.q = (int8_t *)q;
-    g.out.d = (float *)d;
-    g.out.fs = (float *)fs;
-    g.out.cols = h->rows;
+    g.y = epi == 3 ? h->ypair : Y;
+    g.ldy = h->w.rows;
     g.partial = (unsigned long long *)partial;
     g.nan0 = nan0;
     g.status = h->status;
-    launch_gemm(epi, h->maps, g, (cudaStream_t)stream);
+    launch_gemm(epi == 3 ? 0 : epi, h->maps, g, s);
+    if (epi == 3) {
+        Act out;
+        out.q = (int8_t *)q;
+        out.d = (float *)d;
+        out.fs = (float *)fs;
+        out.cols = h->rows;
+        launch_swiglu_quant(h->ypair, h->w.rows, h->rows, h->n, out, s);
+    }
     return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
 }
 
@@ -215,13 +240,8 @@ int nb_mv_matmul_repeat(nb_mv *h, const void *W, size_t stride, int copies, floa
     for (int i = 0; i < iters; i++) {
         const Mat m = panel_mat((const uint8_t *)W + (size_t)(i % copies) * stride, h->rows, h->cols);
         if (h->n > kMaxRows) {
-            GemmArgs g;
-            g.W0 = g.W1 = m;
-            g.n = h->n;
-            g.y = Y;
-            g.ldy = h->rows;
-            g.status = h->status;
-            launch_gemm(0, h->maps, g, (cudaStream_t)stream);
+            const int rc = nb_mv_matmul(h, m.w, Y, stream);
+            if (rc) return rc;
         } else {
             launch_matvec(m, h->act, h->step, Y, h->rows, 0, h->nmax, (cudaStream_t)stream);
         }

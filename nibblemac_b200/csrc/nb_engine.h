@@ -172,12 +172,18 @@ struct GemmMaps {
     CUtensorMap q, d, fs;
     int rows = 0, cols = 0;
 };
+// A matrix (or the row concatenation of two) in the tensor-core tile image: per tile of 128
+// rows and superblock of 256 columns, the codes widened to int8 in the MMA's swizzled layout
+// and the 4 panels' scale entries (gemm_tiled_bytes; made by launch_gemm_tile).
+struct GemmW {
+    const uint8_t *t = nullptr;
+    int rows = 0, cols = 0, npanels = 0, nsb = 0, mtiles = 0;
+};
 struct GemmArgs {
-    Mat W0, W1;                             // W1: the up matrix of the SwiGLU epilogue
+    GemmW W;
     int n = 0;                              // activation rows
     float *y = nullptr;                     // epilogue 0 / 1 output, 4: logits (may be null)
     int ldy = 0;
-    Act out;                                // epilogue 3: A8 of the SwiGLU product
     unsigned long long *partial = nullptr;  // epilogue 4: argmax keys [n][npanels]
     int *nan0 = nullptr;
     int row_base = 0;
@@ -185,9 +191,15 @@ struct GemmArgs {
 };
 int gemm_maps(const Act &a, int rows, GemmMaps *m);   // 0 or -1 (message in last error)
 int gemm_init();                                       // shared-memory limits; 0 or -1
-// Y = W A8(x) over g.n rows with the given epilogue (0 store, 1 residual add, 3 SwiGLU + A8,
-// 4 head keys); the A8 rows come through `maps`
+size_t gemm_tiled_bytes(int rows, int cols);
+// the tile image of W0 ++ W1 (W1.npanels = 0: W0 alone; with W1, W0.rows % 32 == 0)
+GemmW gemm_w(const Mat &W0, const Mat &W1, uint8_t *tiled);
+void launch_gemm_tile(const Mat &W0, const Mat &W1, uint8_t *tiled, cudaStream_t s);
+// Y = W A8(x) over g.n rows with the given epilogue (0 store, 1 residual add, 4 head keys); the
+// A8 rows come through `maps`
 void launch_gemm(int epi, const GemmMaps &maps, const GemmArgs &g, cudaStream_t s);
+// A8 of silu(gate) * up, gate = y[v][0, ffn), up = y[v][ffn, 2 ffn)
+void launch_swiglu_quant(const float *y, int ldy, int ffn, int n, Act out, cudaStream_t s);
 
 // ---- host-side helpers -----------------------------------------------------------------------
 size_t panel_bytes(int rows, int cols);

@@ -9,21 +9,29 @@
 //   acc  = fmaf(-(M_r * m6[b][r]), fsum[b][v], acc)
 // The tensor cores compute the block dots only: one tcgen05.mma of kind::i8 with K = 32 is
 // exactly one block, so every block's int32 dots land in their own TMEM columns, and the ordered
-// FMA chain runs on the CUDA cores, one thread per weight row, reading the dots back with
-// tcgen05.ld. The chain, not the MMA, bounds the kernel.
+// FMA chain runs on the CUDA cores, one thread per (weight row, activation row pair), reading
+// the dots back with tcgen05.ld. The chain, not the MMA, bounds the kernel.
 //
-// One CTA computes a tile of 128 weight rows (4 panels) x 64 activation rows over all columns:
-//   warp 8       producer: per superblock (256 columns) the four 4608-byte weight units by bulk
+// Weights: at 17+ rows the pass is compute-bound, so the tensor-core path reads a second copy
+// of each matrix made once at load, the "tile image": per tile of 128 rows (4 panels) and
+// superblock (256 columns) 34,816 bytes = the 4-bit codes widened to int8 in the tensor cores'
+// K-major 128-byte-swizzled layout (32 KB, exactly the shared-memory image the MMA reads) and
+// the 4 panels' scale entries (2 KB). One bulk copy per stage brings it in; nothing is unpacked
+// on the hot path. (The CUDA-core matvec kernels keep reading the packed panels.)
+//
+// Persistent CTAs, one per SM, walk tiles of 128 weight rows x 64 activation rows (activation
+// tiles fastest, so concurrent CTAs share weight tiles in L2):
+//   warp 16      producer: per stage (one superblock of one tile) the tile-image chunk by bulk
 //                copy, the A8 codes (two 128-column boxes, 128-byte swizzle) and the block
-//                scales d / fsum by TMA tensor copies; then unpacks the 4-bit codes into int8 in
-//                the tensor cores' K-major swizzled layout and pairs (d, fsum) per block.
-//   warp 9       TMEM owner and MMA issuer: 8 MMAs (M 128, N 64, K 32) per superblock into a
-//                ring of 8 TMEM slots of 64 columns, each completion signalled by tcgen05.commit.
-//   warps 0..7   the chains: warp w reads TMEM lanes 32 (w % 4) .. (its 32 weight rows) and
-//                activation rows 32 (w / 4) .. of the tile, and frees a slot as soon as its dots
-//                are in registers.
-// Two shared-memory stages; every wait is bounded (a timeout sets the status word, drains the
-// copies and MMAs in flight, frees TMEM and returns).
+//                scales d / fsum by TMA tensor copies, into a ring of 3 stages.
+//   warp 17      TMEM owner and MMA issuer: pairs (d, fsum) per block for the chains, then 8 MMAs
+//                (M 128, N 64, K 32) per stage into a ring of 8 TMEM slots of 64 columns, each
+//                completion signalled by tcgen05.commit.
+//   warps 0..15  the chains: warp w reads TMEM lanes 32 (w % 4) .. (its 32 weight rows) and
+//                activation rows 16 (w / 4) .. of the tile, frees a TMEM slot as soon as its
+//                dots are in registers, and writes the tile's outputs after the last stage.
+// Every wait is bounded: a timeout sets the status word, lets the copies and MMAs in flight
+// finish, frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -40,29 +48,30 @@ namespace {
 constexpr int kGmM = 128;            // weight rows per tile (4 panels = TMEM lanes)
 constexpr int kGmN = 64;             // activation rows per tile
 constexpr int kGmSlots = 8;          // TMEM ring: one slot of kGmN columns per block
-constexpr int kGmEpiWarps = 8;
+constexpr int kGmStages = 3;         // shared-memory ring
+constexpr int kGmEpiWarps = 16;      // 4 warpgroups; warpgroup g takes activation rows 16 g ..
+constexpr int kGmWg = kGmEpiWarps / 4;
+constexpr int kGmTpt = kGmN / kGmWg;  // activation rows per epilogue thread
 constexpr int kGmProducer = kGmEpiWarps, kGmMma = kGmEpiWarps + 1;
 constexpr int kGmThreads = (kGmEpiWarps + 2) * 32;
 constexpr uint32_t kGmTmemCols = kGmSlots * kGmN;   // 512: the whole TMEM of the SM
 
-// shared memory, from a 1024-byte aligned base (the swizzled operand tiles need it)
-constexpr uint32_t kGmAStage = 2 * kGmM * 128;                 // unpacked codes [2 halves][128][128 B]
-constexpr uint32_t kGmBStage = 2 * kGmN * 128;                 // A8 codes [2 halves][64][128 B]
-constexpr uint32_t kGmRawStage = 4 * kUnitBytes;               // 4 weight units
-constexpr uint32_t kGmQStage = kGmN * 8 * 4;                   // d or fsum [64][8] fp32
-constexpr uint32_t kGmDfStage = 8 * kGmN * 2 * 4;              // (d, fsum) [8][64] pairs
-constexpr uint32_t kGmA = 0;
-constexpr uint32_t kGmB = kGmA + 2 * kGmAStage;
-constexpr uint32_t kGmRaw = kGmB + 2 * kGmBStage;
-constexpr uint32_t kGmDq = kGmRaw + 2 * kGmRawStage;
-constexpr uint32_t kGmFq = kGmDq + 2 * kGmQStage;
-constexpr uint32_t kGmDf = kGmFq + 2 * kGmQStage;
-constexpr uint32_t kGmX = kGmDf + 2 * kGmDfStage;              // SwiGLU hand-off [2][2][32][32] fp32
-constexpr uint32_t kGmBar = kGmX + 2 * 2 * 32 * 32 * 4;
+// one stage of shared memory (1024-byte aligned: the swizzled operand tiles need it)
+constexpr uint32_t kGmACodes = 2 * kGmM * 128;                 // int8 codes [2 halves][128 rows][128 B]
+constexpr uint32_t kGmTileBytes = kGmACodes + 4 * 512;         // + 4 panels' scale entries
+constexpr uint32_t kGmBStage = 2 * kGmN * 128;                 // A8 codes [2 halves][64 rows][128 B]
+constexpr uint32_t kGmQStage = kGmN * 8 * 4;                   // d or fsum [64 rows][8 blocks] fp32
+constexpr uint32_t kGmDfStage = 8 * kGmN * 2 * 4;              // [8 blocks][32] (d_t, d_t+1, fs_t, fs_t+1)
+constexpr uint32_t kGmOffB = kGmTileBytes;
+constexpr uint32_t kGmOffDq = kGmOffB + kGmBStage;
+constexpr uint32_t kGmOffFq = kGmOffDq + kGmQStage;
+constexpr uint32_t kGmOffDf = kGmOffFq + kGmQStage;
+constexpr uint32_t kGmStageBytes = kGmOffDf + kGmDfStage;
+constexpr uint32_t kGmBar = kGmStages * kGmStageBytes;
 constexpr uint32_t kGmMisc = kGmBar + 32 * 8;
 constexpr uint32_t kGmSmem = kGmMisc + 64 + 1024;              // + alignment slack
 static_assert(kGmSmem <= 227 * 1024, "shared memory of one CTA");
-static_assert(kGmB % 1024 == 0 && kGmBStage % 1024 == 0 && kGmAStage % 1024 == 0, "swizzle atoms");
+static_assert(kGmStageBytes % 1024 == 0 && kGmOffB % 1024 == 0 && kGmACodes % 2048 == 0, "swizzle atoms");
 
 // instruction descriptor of tcgen05.mma kind::i8: D s32 (bits 4-5 = 2), A and B s8 (bits 7-9,
 // 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
@@ -106,7 +115,7 @@ __device__ __forceinline__ void tm_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // 32 consecutive columns of this thread's TMEM lane
-__device__ __forceinline__ void tm_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+[[maybe_unused]] __device__ __forceinline__ void tm_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
                  "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
                  "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
@@ -116,18 +125,76 @@ __device__ __forceinline__ void tm_ld32(uint32_t taddr, uint32_t (&r)[32]) {
                    "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                  : "r"(taddr));
 }
+__device__ __forceinline__ void tm_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+                 "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr));
+}
+template <int N>
+__device__ __forceinline__ void tm_ld(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 32) tm_ld32(taddr, r);
+    else tm_ld16(taddr, r);
+}
+// (float)v for |v| < 2^22, exactly, without the conversion unit: the bits of 1.5 * 2^23 + v
+// read as a float are 12582912 + v, and subtracting 12582912 is exact
+__device__ __forceinline__ float int_bits_plus_magic(uint32_t v) { return __int_as_float((int)v + 0x4B400000); }
 __device__ __forceinline__ void tm_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // a bounded wait whose outcome every lane of the (converged) warp agrees on, so the warp stays
 // converged for the .sync.aligned tcgen05 instructions that follow
 __device__ __forceinline__ bool wait_all(uint64_t *bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
-__device__ __forceinline__ void named_bar(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+
+// Widen one tile image chunk per CTA (blockIdx.x = tile, blockIdx.y = superblock): tile t holds
+// panels 4t .. 4t + 3 of the row concatenation W0 ++ W1 (W1.npanels may be 0); rows past the
+// end are zero. Row r of the tile, 16-byte chunk j of a 128-column half lands at
+// (r / 8) * 1024 + (r % 8) * 128 + ((j ^ r % 8) * 16); block k's low nibbles (columns 0..15)
+// are chunk 2 (k % 4) of half k / 4, its high nibbles (columns 16..31) chunk 2 (k % 4) + 1.
+__global__ void k_gemm_tile(Mat W0, Mat W1, uint8_t *dst) {
+    const int mt = blockIdx.x, sb = blockIdx.y;
+    uint8_t *o = dst + ((size_t)mt * W0.nsb + sb) * kGmTileBytes;
+    for (int idx = threadIdx.x; idx < 4 * 9 * 32; idx += blockDim.x) {
+        const int u = idx / 288, k = (idx % 288) / 32 - 1, r = idx % 32;   // k = -1: the scale entry
+        const int p = 4 * mt + u;
+        const Mat *m = p < W0.npanels ? &W0 : (p - W0.npanels < W1.npanels ? &W1 : nullptr);
+        const int pp = p < W0.npanels ? p : p - W0.npanels;
+        uint4 c = make_uint4(0u, 0u, 0u, 0u);
+        if (m) c = *reinterpret_cast<const uint4 *>(m->w + ((size_t)pp * m->nsb + sb) * kUnitBytes + (k + 1) * 512 + r * 16);
+        if (k < 0) {
+            *reinterpret_cast<uint4 *>(o + kGmACodes + u * 512 + r * 16) = c;
+            continue;
+        }
+        const uint4 lo = make_uint4(c.x & 0x0f0f0f0fu, c.y & 0x0f0f0f0fu, c.z & 0x0f0f0f0fu, c.w & 0x0f0f0f0fu);
+        const uint4 hi = make_uint4((c.x >> 4) & 0x0f0f0f0fu, (c.y >> 4) & 0x0f0f0f0fu, (c.z >> 4) & 0x0f0f0f0fu,
+                                    (c.w >> 4) & 0x0f0f0f0fu);
+        const int row = u * 32 + r, rr = row & 7, j0 = (k & 3) * 2;
+        uint8_t *rowp = o + (k >> 2) * (kGmM * 128) + (row >> 3) * 1024 + rr * 128;
+        *reinterpret_cast<uint4 *>(rowp + ((j0 ^ rr) << 4)) = lo;
+        *reinterpret_cast<uint4 *>(rowp + (((j0 + 1) ^ rr) << 4)) = hi;
+    }
 }
 
-// EPI 0: y[v][row] = acc; 1: y[v][row] += acc; 3: SwiGLU of (W0 = gate, W1 = up) and A8 of the
-// product into `out`; 4: LM head, logits into y (may be null) and per-panel argmax keys.
+// SwiGLU of a pass's gate / up rows and A8 of the product (pf_mlp / pf_silu_mul,
+// engine/src/forward.c:49-58, then kern_quant_act): y [n][ldy] holds gate in columns [0, ffn)
+// and up in [ffn, 2 ffn); one warp per (row, 32-column block).
+__global__ void k_swiglu_quant(const float *y, int ldy, int ffn, int n, Act out) {
+    pdl_wait();
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const long long gw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int nbo = ffn >> 5;
+    if (gw >= (long long)n * nbo) return;
+    const int v = (int)(gw / nbo), b = (int)(gw % nbo);
+    const float *yr = y + (size_t)v * ldy + b * 32 + lane;
+    const float h = __fmul_rn(pf_silu(yr[0]), yr[ffn]);
+    quant_block_warp(h, lane, out.q + (size_t)v * out.cols + b * 32, out.d + (size_t)v * nbo + b,
+                     out.fs + (size_t)v * nbo + b);
+}
+
+// EPI 0: y[v][row] = acc; 1: y[v][row] += acc (the residual stream); 4: LM head, logits into y
+// (may be null) and per-panel argmax keys.
 template <int EPI>
 __global__ void __launch_bounds__(kGmThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap td,
@@ -137,21 +204,19 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     const uint32_t sbase = (raw_u + 1023u) & ~1023u;
     uint8_t *sm = gsm_raw + (sbase - raw_u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kGmBar);
-    uint64_t *full = bars, *unp = bars + 2, *sfree = bars + 4, *estage = bars + 6;
-    uint64_t *mdone = bars + 8, *edone = bars + 16, *drain = bars + 24;
+    uint64_t *full = bars, *ready = bars + 3, *sfree = bars + 6, *estage = bars + 9;
+    uint64_t *mdone = bars + 12, *edone = bars + 20, *drain = bars + 28;
     uint32_t *tmem_at = reinterpret_cast<uint32_t *>(sm + kGmMisc);
     volatile int *abort_f = reinterpret_cast<volatile int *>(sm + kGmMisc + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = g.n;
-    const int ntn = (n + kGmN - 1) / kGmN;
-    const int mt = blockIdx.x / ntn, n0 = (blockIdx.x % ntn) * kGmN;
-    const int nsb = g.W0.nsb, nb = nsb * 8;
+    const int n = g.n, nsb = g.W.nsb;
+    const int ntn = (n + kGmN - 1) / kGmN, ntiles = g.W.mtiles * ntn;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < kGmStages; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&unp[i], 32);
+            mbar_init(&ready[i], 32);
             mbar_init(&sfree[i], 1);
             mbar_init(&estage[i], kGmEpiWarps);
         }
@@ -172,202 +237,160 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     pdl_trigger();
 
     if (warp == kGmProducer) {
-        // unit u of the tile: EPI 3 interleaves gate and up panels (quarters 0 / 2 gate, 1 / 3 up)
-        const uint8_t *ubase[4];
-        bool uok[4];
-        uint32_t wbytes = 0;
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const Mat &m = (EPI == 3 && (u & 1)) ? g.W1 : g.W0;
-            const int panel = EPI == 3 ? 2 * mt + (u >> 1) : 4 * mt + u;
-            uok[u] = panel < m.npanels;
-            ubase[u] = m.w + (size_t)panel * m.nsb * kUnitBytes;
-            wbytes += uok[u] ? kUnitBytes : 0;
-        }
-        for (int s = 0; s < nsb; s++) {
-            const int slot = s & 1;
-            if (s >= 2) {
-                const uint32_t par = (uint32_t)((s >> 1) - 1) & 1u;
-                if (!wait_all(&sfree[slot], par) || !wait_all(&estage[slot], par)) {
+        int gs = 0;   // stages issued by this CTA
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            const int mt = tile / ntn, n0 = (tile % ntn) * kGmN;
+            const uint8_t *wt = g.W.t + (size_t)mt * nsb * kGmTileBytes;
+            for (int s = 0; s < nsb; s++, gs++) {
+                const int slot = gs % kGmStages;
+                const uint32_t use = (uint32_t)(gs / kGmStages);
+                if (gs >= kGmStages && (!wait_all(&sfree[slot], (use - 1) & 1u) || !wait_all(&estage[slot], (use - 1) & 1u))) {
                     *abort_f = 1;
+                    ok = false;
                     break;
                 }
+                if (lane == 0) {
+                    uint8_t *st = sm + slot * kGmStageBytes;
+                    mbar_arrive_expect(&full[slot], kGmTileBytes + kGmBStage + 2 * kGmQStage);
+                    bulk_g2s(st, wt + (size_t)s * kGmTileBytes, kGmTileBytes, &full[slot]);
+                    tma_load_2d(st + kGmOffB, &tq, s * 256, n0, &full[slot]);
+                    tma_load_2d(st + kGmOffB + kGmN * 128, &tq, s * 256 + 128, n0, &full[slot]);
+                    tma_load_2d(st + kGmOffDq, &td, s * 8, n0, &full[slot]);
+                    tma_load_2d(st + kGmOffFq, &tf, s * 8, n0, &full[slot]);
+                }
+                __syncwarp();
             }
-            uint8_t *rawp = sm + kGmRaw + slot * kGmRawStage;
-            if (lane == 0) {
-                mbar_arrive_expect(&full[slot], wbytes + kGmBStage + 2 * kGmQStage);
-#pragma unroll
-                for (int u = 0; u < 4; u++)
-                    if (uok[u]) bulk_g2s(rawp + u * kUnitBytes, ubase[u] + (size_t)s * kUnitBytes, kUnitBytes, &full[slot]);
-                uint8_t *bp = sm + kGmB + slot * kGmBStage;
-                tma_load_2d(bp, &tq, s * 256, n0, &full[slot]);
-                tma_load_2d(bp + kGmN * 128, &tq, s * 256 + 128, n0, &full[slot]);
-                tma_load_2d(sm + kGmDq + slot * kGmQStage, &td, s * 8, n0, &full[slot]);
-                tma_load_2d(sm + kGmFq + slot * kGmQStage, &tf, s * 8, n0, &full[slot]);
-            }
-            __syncwarp();
-            if (!wait_all(&full[slot], (uint32_t)(s >> 1) & 1u)) {
-                *abort_f = 1;
-                wait_all(&full[slot], (uint32_t)(s >> 1) & 1u);   // the copies in flight, once more
-                break;
-            }
-            // 4-bit codes -> int8, K-major with the 128-byte swizzle: row r of the tile, 16-byte
-            // chunk j of a 128-column half at (r / 8) * 1024 + (r % 8) * 128 + ((j ^ r % 8) * 16);
-            // block k's low nibbles are chunk 2 (k % 4), its high nibbles chunk 2 (k % 4) + 1
-            uint8_t *ap = sm + kGmA + slot * kGmAStage;
-            for (int idx = lane; idx < 4 * 8 * 32; idx += 32) {
-                const int u = idx >> 8, k = (idx >> 5) & 7, r = idx & 31;
-                const uint4 c = lds128(rawp + u * kUnitBytes + 512 * (k + 1) + r * 16);
-                const uint4 lo = make_uint4(c.x & 0x0f0f0f0fu, c.y & 0x0f0f0f0fu, c.z & 0x0f0f0f0fu, c.w & 0x0f0f0f0fu);
-                const uint4 hi = make_uint4((c.x >> 4) & 0x0f0f0f0fu, (c.y >> 4) & 0x0f0f0f0fu,
-                                            (c.z >> 4) & 0x0f0f0f0fu, (c.w >> 4) & 0x0f0f0f0fu);
-                const int row = u * 32 + r, rr = row & 7, j0 = (k & 3) * 2;
-                uint8_t *rowp = ap + (k >> 2) * (kGmM * 128) + (row >> 3) * 1024 + rr * 128;
-                *reinterpret_cast<uint4 *>(rowp + ((j0 ^ rr) << 4)) = lo;
-                *reinterpret_cast<uint4 *>(rowp + (((j0 + 1) ^ rr) << 4)) = hi;
-            }
-            // (d, fsum) of activation row t and block k side by side: df[k][t]
-            const float *dq = reinterpret_cast<const float *>(sm + kGmDq + slot * kGmQStage);
-            const float *fq = reinterpret_cast<const float *>(sm + kGmFq + slot * kGmQStage);
-            float2 *df = reinterpret_cast<float2 *>(sm + kGmDf + slot * kGmDfStage);
-            for (int idx = lane; idx < 8 * kGmN; idx += 32) {
-                const int k = idx / kGmN, t = idx % kGmN;
-                df[idx] = make_float2(dq[t * 8 + k], fq[t * 8 + k]);
-            }
-            fence_proxy_async();   // the unpacked codes are read by the tensor cores
-            mbar_arrive(&unp[slot]);
         }
+        // the last stages' copies have landed before shared memory is released (normally the
+        // MMA warp already waited for them)
+        for (int i = gs > kGmStages ? gs - kGmStages : 0; i < gs; i++)
+            wait_all(&full[i % kGmStages], (uint32_t)(i / kGmStages) & 1u);
     } else if (warp == kGmMma) {
-        for (int b = 0; b < nb; b++) {
-            const int s = b >> 3, k = b & 7, slot = s & 1, ts = b & (kGmSlots - 1);
-            if (k == 0 && (!wait_all(&unp[slot], (uint32_t)(s >> 1) & 1u) ||
-                           !wait_all(&full[slot], (uint32_t)(s >> 1) & 1u))) {
-                *abort_f = 1;
-                break;
+        int gs = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            for (int s = 0; s < nsb; s++, gs++) {
+                const int slot = gs % kGmStages;
+                const uint32_t use = (uint32_t)(gs / kGmStages);
+                if (!wait_all(&full[slot], use & 1u)) {
+                    *abort_f = 1;
+                    ok = false;
+                    break;
+                }
+                uint8_t *st = sm + slot * kGmStageBytes;
+                // (d_t, d_t+1, fsum_t, fsum_t+1) per block and activation-row pair for the chains
+                const float *dq = reinterpret_cast<const float *>(st + kGmOffDq);
+                const float *fq = reinterpret_cast<const float *>(st + kGmOffFq);
+                float4 *df = reinterpret_cast<float4 *>(st + kGmOffDf);
+                for (int idx = lane; idx < 8 * kGmN / 2; idx += 32) {
+                    const int k = idx / (kGmN / 2), t = (idx % (kGmN / 2)) * 2;
+                    df[idx] = make_float4(dq[t * 8 + k], dq[(t + 1) * 8 + k], fq[t * 8 + k], fq[(t + 1) * 8 + k]);
+                }
+                mbar_arrive(&ready[slot]);
+                for (int k = 0; k < 8; k++) {
+                    if (gs >= 1 && !wait_all(&edone[k], (uint32_t)(gs - 1) & 1u)) {
+                        *abort_f = 1;
+                        ok = false;
+                        break;
+                    }
+                    tm_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a = sbase + slot * kGmStageBytes + (k >> 2) * (kGmM * 128) + (k & 3) * 32;
+                        const uint32_t b = sbase + slot * kGmStageBytes + kGmOffB + (k >> 2) * (kGmN * 128) + (k & 3) * 32;
+                        tm_mma_i8(tmem + k * kGmN, sw128_desc(a), sw128_desc(b), kGmIdesc, 0u);
+                        tm_commit(&mdone[k]);
+                        if (k == 7) tm_commit(&sfree[slot]);
+                    }
+                    __syncwarp();
+                }
+                if (!ok) break;
             }
-            if (b >= kGmSlots && !wait_all(&edone[ts], (uint32_t)((b >> 3) - 1) & 1u)) {
-                *abort_f = 1;
-                break;
-            }
-            tm_fence_after();
-            if (lane == 0) {
-                const uint32_t a = sbase + kGmA + slot * kGmAStage + (k >> 2) * (kGmM * 128) + (k & 3) * 32;
-                const uint32_t bb = sbase + kGmB + slot * kGmBStage + (k >> 2) * (kGmN * 128) + (k & 3) * 32;
-                tm_mma_i8(tmem + ts * kGmN, sw128_desc(a), sw128_desc(bb), kGmIdesc, 0u);
-                tm_commit(&mdone[ts]);
-                if (k == 7) tm_commit(&sfree[slot]);
-            }
-            __syncwarp();
         }
         if (lane == 0) tm_commit(drain);   // every MMA complete before TMEM is released
         __syncwarp();
         wait_all(drain, 0);
     } else {
         const int q = warp & 3, wg = warp >> 2;
-        float acc[32];
+        const float2 magic = make_float2(-12582912.0f, -12582912.0f);
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(wg * kGmTpt);
+        int gs = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            const int mt = tile / ntn, n0 = (tile % ntn) * kGmN;
+            // two activation rows per packed f32x2 chain: acc[j] = rows (2 j, 2 j + 1) of this thread
+            float2 acc[kGmTpt / 2];
 #pragma unroll
-        for (int i = 0; i < 32; i++) acc[i] = 0.0f;
-        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(wg * 32);
-        for (int s = 0; s < nsb; s++) {
-            const int slot = s & 1;
-            if (__any_sync(0xffffffffu, *abort_f)) break;
-            if (!wait_all(&unp[slot], (uint32_t)(s >> 1) & 1u)) {
-                *abort_f = 1;
-                break;
-            }
-            const uint4 sc = lds128(sm + kGmRaw + slot * kGmRawStage + q * kUnitBytes + lane * 16);
-            const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
-            const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
-            const float D = half_bits_to_float((uint32_t)(A >> 48));
-            const float M = half_bits_to_float((uint32_t)(B >> 48));
-            const float4 *dfw = reinterpret_cast<const float4 *>(sm + kGmDf + slot * kGmDfStage) + wg * 16;
-            bool ok = true;
-#pragma unroll 1
-            for (int k = 0; k < 8; k++) {
-                const int b = s * 8 + k;
-                const float ds = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
-                const float os = __fmul_rn(M, (float)(uint32_t)((B >> (6 * k)) & 63u));
-                if (!wait_all(&mdone[k], (uint32_t)(b >> 3) & 1u)) {
+            for (int j = 0; j < kGmTpt / 2; j++) acc[j] = make_float2(0.0f, 0.0f);
+            for (int s = 0; s < nsb; s++, gs++) {
+                const int slot = gs % kGmStages;
+                if (__any_sync(0xffffffffu, *abort_f) || !wait_all(&ready[slot], (uint32_t)(gs / kGmStages) & 1u)) {
+                    *abort_f = 1;
                     ok = false;
                     break;
                 }
-                tm_fence_after();
-                uint32_t is[32];
-                tm_ld32(trow + (uint32_t)(k * kGmN), is);
-                tm_wait_ld();
-                tm_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&edone[k]);
-                const float4 *dk = dfw + k * (kGmN / 2);
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    const float4 p = dk[i >> 1];   // d, fsum of rows i and i + 1
-                    acc[i] = __fmaf_rn(__int2float_rn((int)is[i]), __fmul_rn(ds, p.x), acc[i]);
-                    acc[i] = __fmaf_rn(-os, p.y, acc[i]);
-                    acc[i + 1] = __fmaf_rn(__int2float_rn((int)is[i + 1]), __fmul_rn(ds, p.z), acc[i + 1]);
-                    acc[i + 1] = __fmaf_rn(-os, p.w, acc[i + 1]);
-                }
-            }
-            if (!ok) {
-                *abort_f = 1;
-                break;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&estage[slot]);
-        }
-        const int vb = n0 + wg * 32;
-        // one read of the flag per warp: both warps of a SwiGLU pair pass the named barrier below
-        // whatever they read
-        const bool live = !__any_sync(0xffffffffu, *abort_f);
-        if (EPI == 3) {
-            float *xch = reinterpret_cast<float *>(sm + kGmX) + ((q >> 1) * 2 + wg) * 32 * 32;
-            if ((q & 1) && live) {
-#pragma unroll
-                for (int i = 0; i < 32; i++) xch[i * 32 + lane] = acc[i];
-            }
-            named_bar(1 + (q >> 1) * 2 + wg, 64);
-        }
-        if (live) {
-            if (EPI == 0 || EPI == 1) {
-                const int row = mt * kGmM + q * 32 + lane;
-                if (row < g.W0.rows) {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        if (vb + i < n) {
-                            float *p = g.y + (size_t)(vb + i) * g.ldy + row;
-                            *p = EPI == 0 ? acc[i] : __fadd_rn(*p, acc[i]);
-                        }
-                    }
-                }
-            } else if (EPI == 4) {
-                const int row = mt * kGmM + q * 32 + lane, panel = mt * 4 + q;
-                const bool valid = row < g.W0.rows;
-#pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const int v = vb + i;
-                    if (v < n) {
-                        if (g.y && valid) g.y[(size_t)v * g.ldy + row] = acc[i];
-                        unsigned long long key = valid ? argmax_key(acc[i], g.row_base + row) : 0ull;
-                        key = warp_max_u64(key);
-                        if (lane == 0 && panel < g.W0.npanels) g.partial[(size_t)v * g.W0.npanels + panel] = key;
-                        if (row == 0 && g.row_base == 0) g.nan0[v] = acc[i] != acc[i];
-                    }
-                }
-            } else if (EPI == 3) {
-                float *xch = reinterpret_cast<float *>(sm + kGmX) + ((q >> 1) * 2 + wg) * 32 * 32;
-                const int panel = 2 * mt + (q >> 1);
-                if (!(q & 1) && panel < g.W0.npanels) {
-                    // h = silu(gate) * up in place, then A8 of each activation row's block
-#pragma unroll
-                    for (int i = 0; i < 32; i++) xch[i * 32 + lane] = __fmul_rn(pf_silu(acc[i]), xch[i * 32 + lane]);
-                    __syncwarp();
-                    const int nbo = g.out.cols >> 5;
+                const uint8_t *st = sm + slot * kGmStageBytes;
+                const uint4 sc = lds128(st + kGmACodes + q * 512 + lane * 16);
+                const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
+                const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
+                const float D = half_bits_to_float((uint32_t)(A >> 48));
+                const float M = half_bits_to_float((uint32_t)(B >> 48));
+                const float4 *dfw = reinterpret_cast<const float4 *>(st + kGmOffDf) + wg * (kGmTpt / 2);
 #pragma unroll 1
-                    for (int i = 0; i < 32; i++) {
-                        const int v = vb + i;
-                        if (v >= n) break;
-                        quant_block_warp(xch[i * 32 + lane], lane, g.out.q + (size_t)v * g.out.cols + panel * 32,
-                                         g.out.d + (size_t)v * nbo + panel, g.out.fs + (size_t)v * nbo + panel);
+                for (int k = 0; k < 8; k++) {
+                    const float ds = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
+                    const float os = __fmul_rn(M, (float)(uint32_t)((B >> (6 * k)) & 63u));
+                    const float2 ds2 = make_float2(ds, ds), nos2 = make_float2(-os, -os);
+                    if (!wait_all(&mdone[k], (uint32_t)gs & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tm_fence_after();
+                    uint32_t is[kGmTpt];
+                    tm_ld(trow + (uint32_t)(k * kGmN), is);
+                    tm_wait_ld();
+                    tm_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&edone[k]);
+                    const float4 *dk = dfw + k * (kGmN / 2);
+                    // per row: acc = fmaf((float)isum, ds * d, acc); acc = fmaf(-os, fsum, acc),
+                    // two rows per packed instruction (each lane of f32x2 rounds as the scalar op)
+#pragma unroll
+                    for (int j = 0; j < kGmTpt / 2; j++) {
+                        const float4 p = dk[j];   // d_2j, d_2j+1, fsum_2j, fsum_2j+1
+                        const float2 f = __fadd2_rn(make_float2(int_bits_plus_magic(is[2 * j]),
+                                                                int_bits_plus_magic(is[2 * j + 1])), magic);
+                        acc[j] = __ffma2_rn(f, __fmul2_rn(ds2, make_float2(p.x, p.y)), acc[j]);
+                        acc[j] = __ffma2_rn(nos2, make_float2(p.z, p.w), acc[j]);
+                    }
+                }
+                if (!ok) {
+                    *abort_f = 1;
+                    break;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&estage[slot]);
+            }
+            if (!ok) break;
+            // the tile's outputs (stores of consecutive weight rows by consecutive lanes)
+            const int vb = n0 + wg * kGmTpt, row = mt * kGmM + q * 32 + lane;
+            const bool valid = row < g.W.rows;
+#pragma unroll
+            for (int i = 0; i < kGmTpt; i++) {
+                const int v = vb + i;
+                const float a = (i & 1) ? acc[i >> 1].y : acc[i >> 1].x;
+                if (v < n) {
+                    if (EPI == 0 || EPI == 1) {
+                        if (valid) {
+                            float *p = g.y + (size_t)v * g.ldy + row;
+                            *p = EPI == 0 ? a : __fadd_rn(*p, a);
+                        }
+                    } else {
+                        if (g.y && valid) g.y[(size_t)v * g.ldy + row] = a;
+                        const unsigned long long key = warp_max_u64(valid ? argmax_key(a, g.row_base + row) : 0ull);
+                        const int panel = mt * 4 + q;
+                        if (lane == 0 && panel < g.W.npanels) g.partial[(size_t)v * g.W.npanels + panel] = key;
+                        if (row == 0 && g.row_base == 0) g.nan0[v] = a != a;
                     }
                 }
             }
@@ -396,12 +419,22 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+int sm_count() {
+    static int n = 0;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            n = 148;
+    });
+    return n;
+}
+
 template <int EPI>
 void gemm_t(const GemmMaps &maps, const GemmArgs &g, cudaStream_t s) {
-    const int ntn = (g.n + kGmN - 1) / kGmN;
-    const int mtiles = EPI == 3 ? (g.W0.npanels + 1) / 2 : (g.W0.npanels + 3) / 4;
-    launch_k(k_gemm<EPI>, dim3((unsigned)(mtiles * ntn)), dim3(kGmThreads), (size_t)kGmSmem, s,
-             maps.q, maps.d, maps.fs, g);
+    const int ntiles = g.W.mtiles * ((g.n + kGmN - 1) / kGmN);
+    const int grid = ntiles < sm_count() ? ntiles : sm_count();
+    launch_k(k_gemm<EPI>, dim3((unsigned)grid), dim3(kGmThreads), (size_t)kGmSmem, s, maps.q, maps.d, maps.fs, g);
 }
 
 }  // namespace
@@ -448,19 +481,43 @@ int gemm_init() {
     const int s = (int)kGmSmem;
     if (cudaFuncSetAttribute(k_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) != cudaSuccess ||
         cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) != cudaSuccess ||
-        cudaFuncSetAttribute(k_gemm<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) != cudaSuccess ||
         cudaFuncSetAttribute(k_gemm<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) != cudaSuccess)
         return -1;
     return 0;
+}
+
+size_t gemm_tiled_bytes(int rows, int cols) {
+    const int npanels = (rows + kPanelRows - 1) / kPanelRows;
+    return (size_t)((npanels + 3) / 4) * (cols / 256) * kGmTileBytes;
+}
+
+GemmW gemm_w(const Mat &W0, const Mat &W1, uint8_t *tiled) {
+    GemmW w;
+    w.t = tiled;
+    w.npanels = W0.npanels + W1.npanels;
+    w.rows = W1.npanels ? W0.npanels * kPanelRows + W1.rows : W0.rows;
+    w.cols = W0.cols;
+    w.nsb = W0.nsb;
+    w.mtiles = (w.npanels + 3) / 4;
+    return w;
+}
+
+void launch_gemm_tile(const Mat &W0, const Mat &W1, uint8_t *tiled, cudaStream_t s) {
+    const int mtiles = (W0.npanels + W1.npanels + 3) / 4;
+    launch_k(k_gemm_tile, dim3((unsigned)mtiles, (unsigned)W0.nsb), dim3(256), 0, s, W0, W1, tiled);
 }
 
 void launch_gemm(int epi, const GemmMaps &maps, const GemmArgs &g, cudaStream_t s) {
     switch (epi) {
         case 0: gemm_t<0>(maps, g, s); break;
         case 1: gemm_t<1>(maps, g, s); break;
-        case 3: gemm_t<3>(maps, g, s); break;
         default: gemm_t<4>(maps, g, s); break;
     }
+}
+
+void launch_swiglu_quant(const float *y, int ldy, int ffn, int n, Act out, cudaStream_t s) {
+    const long long warps = (long long)n * (ffn / 32);
+    launch_k(k_swiglu_quant, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, s, y, ldy, ffn, n, out);
 }
 
 }  // namespace nb

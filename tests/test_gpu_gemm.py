@@ -48,8 +48,8 @@ class Gemm:
         if epi == 0:
             assert self.lib.nb_mv_matmul(self.h, dW.data_ptr(), y.data_ptr(), self.s) == 0
         else:
-            assert self.lib.nb_mv_gemm(self.h, epi, dW.data_ptr(), None, y.data_ptr(), None, None, None,
-                                       None, None, self.s) == 0
+            assert self.lib.nb_mv_prepare(self.h, dW.data_ptr(), None, self.s) == 0
+            assert self.lib.nb_mv_gemm(self.h, epi, y.data_ptr(), None, None, None, None, None, self.s) == 0
         self.t.cuda.synchronize()
         assert self.lib.nb_mv_status(self.h) == 0
         return y.cpu().numpy()
@@ -162,8 +162,9 @@ def _pf_silu(x):
 
 
 def test_swiglu_epilogue(lib, torch, q4k_oracle):
-    """Epilogue 3: A8 of silu(gate x) * (up x) (pf_mlp / pf_silu_mul, engine/src/forward.c:49-58,
-    then kern_quant_act), the input of down_proj."""
+    """Gate / up prepared as one concatenated tile image, then A8 of silu(gate x) * (up x)
+    (pf_mlp / pf_silu_mul, engine/src/forward.c:49-58, then kern_quant_act): the input of
+    down_proj."""
     ffn, cols, n = 3584, 1024, 80
     rng = np.random.default_rng(12)
     gq, uq = _rand_q4k(rng, ffn, cols), _rand_q4k(rng, ffn, cols)
@@ -175,8 +176,8 @@ def test_swiglu_epilogue(lib, torch, q4k_oracle):
         q = torch.zeros((n, ffn), dtype=torch.int8, device="cuda")
         d = torch.zeros((n, ffn // 32), dtype=torch.float32, device="cuda")
         f = torch.zeros((n, ffn // 32), dtype=torch.float32, device="cuda")
-        assert lib.nb_mv_gemm(g.h, 3, dG.data_ptr(), dU.data_ptr(), None, q.data_ptr(), d.data_ptr(),
-                              f.data_ptr(), None, None, g.s) == 0
+        assert lib.nb_mv_prepare(g.h, dG.data_ptr(), dU.data_ptr(), g.s) == 0
+        assert lib.nb_mv_gemm(g.h, 3, None, q.data_ptr(), d.data_ptr(), f.data_ptr(), None, None, g.s) == 0
         torch.cuda.synchronize()
         assert lib.nb_mv_status(g.h) == 0
         gate = q4k_oracle.matmul(gq, ffn, cols, x)
@@ -205,8 +206,8 @@ def test_head_epilogue_logits_and_argmax(lib, torch, q4k_oracle, rows, cols, n):
         y = torch.zeros((n, rows), dtype=torch.float32, device="cuda")
         part = torch.zeros((n, npan), dtype=torch.int64, device="cuda")
         nan0 = torch.ones(n, dtype=torch.int32, device="cuda")
-        assert lib.nb_mv_gemm(g.h, 4, dW.data_ptr(), None, y.data_ptr(), None, None, None,
-                              part.data_ptr(), nan0.data_ptr(), g.s) == 0
+        assert lib.nb_mv_prepare(g.h, dW.data_ptr(), None, g.s) == 0
+        assert lib.nb_mv_gemm(g.h, 4, y.data_ptr(), None, None, None, part.data_ptr(), nan0.data_ptr(), g.s) == 0
         torch.cuda.synchronize()
         assert lib.nb_mv_status(g.h) == 0
         want = q4k_oracle.matmul(w, rows, cols, x)
