@@ -74,6 +74,29 @@ int pinfer_b200_shard_head(pinfer_ctx *ctx, int rank, int world, const void *id)
  * checks): unsigned maximum over any partition of the rows = the pf_argmax of all of them. */
 unsigned long long nb_argmax_key(float v, int row);
 
+/* ---- multi-sequence batches (no counterpart in the reference, which serves one sequence per
+ * context) ---------------------------------------------------------------------------------
+ * `slots` (1..2048) sequence slots on a loaded context's weights (shared; the context must outlive the
+ * batch), each with its own DeltaNet / conv states, logs and KV cache of max_ctx positions
+ * (max_ctx <= the context's), for speculative generation with up to max_k drafts per round.
+ * A generation call runs all its sequences in the same passes: the projections of all their
+ * rows are one tcgen05 tensor-core GEMM per matrix. NULL on failure (*err set). */
+typedef struct pinfer_b200_batch pinfer_b200_batch;
+pinfer_b200_batch *pinfer_b200_batch_create(pinfer_ctx *ctx, int slots, int max_ctx, int max_k, int *err);
+void pinfer_b200_batch_free(pinfer_b200_batch *b);
+/* Greedy speculative generation of n_seq (<= slots) independent sequences from fresh states,
+ * with the synthetic drafter of pinfer_b200_generate_synthetic per sequence: prompts
+ * concatenated (sequence i has prompt_lens[i] tokens), greedy [n_seq][n_max] and seeds [n_seq]
+ * (k > 0), p. k = 0: plain greedy (greedy and seeds may be NULL). Sequence i's tokens go to
+ * out[i * n_max ..], their count to counts[i], its generation status to status[i] (may be
+ * NULL); the rounds / drafted / accepted counts of all sequences are added to stats (may be
+ * NULL); decode_ms (may be NULL): device time of the verify rounds. Every sequence's tokens and
+ * counts equal pinfer_b200_generate_synthetic's on its own. 0 or a PINFER_E_* code. */
+int pinfer_b200_batch_generate_synthetic(pinfer_b200_batch *b, int n_seq, const int32_t *prompts,
+                                         const int32_t *prompt_lens, int n_max, int k, const int32_t *greedy,
+                                         const uint64_t *seeds, float p, int32_t *out, int32_t *counts,
+                                         int32_t *status, pinfer_spec_stats *stats, float *decode_ms);
+
 /* ---- kernel-level ABI: the Q4K x A8 matmul on device buffers ----------------------------
  * The pf_matmul contract for dtype Q4K_G32 (engine/src/ops.h:49-52: Y[n][rows] = W X, weights
  * read once for all n) with the reference's arithmetic (kern_quant_act, kern_act.c:14-41;

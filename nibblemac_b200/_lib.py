@@ -104,6 +104,13 @@ _OPTIONAL = {
     "pinfer_b200_forward_all": (ctypes.c_int, [ctypes.c_void_p, _c_int32_p, ctypes.c_int, _c_float_p]),
     "pinfer_b200_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
     "pinfer_b200_clone": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, _c_int_p]),
+    "pinfer_b200_batch_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                   _c_int_p]),
+    "pinfer_b200_batch_free": (None, [ctypes.c_void_p]),
+    "pinfer_b200_batch_generate_synthetic": (ctypes.c_int, [
+        ctypes.c_void_p, ctypes.c_int, _c_int32_p, _c_int32_p, ctypes.c_int, ctypes.c_int, _c_int32_p,
+        ctypes.POINTER(ctypes.c_uint64), ctypes.c_float, _c_int32_p, _c_int32_p, _c_int32_p,
+        ctypes.POINTER(SpecStats), _c_float_p]),
     "pinfer_b200_nccl_id": (ctypes.c_int, [ctypes.c_void_p]),
     "pinfer_b200_shard_head": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "nb_q4k_panel_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),

@@ -48,6 +48,7 @@ struct Step {
     int wr;                // log half the next logged pass writes
     int pend_keep;         // recurrent updates (log rows 1..pend_keep of half wr^1) to replay
     int pend_conv;         // conv commit owed: keep = pend_conv tokens of the last logged pass
+    int row0;              // first row of this sequence's rows in a multi-sequence pass (else 0)
     int tokens[kMaxRows];  // input tokens of the pass
     int argmax[kMaxRows];  // head argmax of every row (first maximum)
     // generation loop (nb_accept)
@@ -91,6 +92,8 @@ struct LinLayer {
 struct LinDims {
     int C, K, kd, vd, nk, nv, rep, dk, dv, cap, ldy;
     float eps;
+    // per-sequence strides (floats) of a multi-sequence batch's states; 0 for one context
+    size_t ss_conv = 0, ss_rec = 0, ss_xin = 0, ss_upd = 0;
 };
 
 struct AttnLayer {
@@ -102,12 +105,16 @@ struct AttnDims {
     int nq, nkv, hd, rot, max_ctx, ldy;
     float eps;
     const float *rope_cos, *rope_sin;   // [max_ctx][rot / 2]
+    int rps = kMaxRows;                 // rows per sequence in the launch grid
+    size_t ss_kv = 0;                   // per-sequence stride (floats) of a batch's KV caches
 };
 
 // ---- launchers (nb_kernels.cu); all asynchronous on `s` ---------------------------------
-void launch_embed(const Mat &E, const Step *st, float *x, int H, cudaStream_t s);
+// Multi-sequence passes: `nseq` Step blocks (st[0..nseq)), sequence i's rows at st[i].row0 ..;
+// `rps` = the most rows any sequence has in the pass.
+void launch_embed(const Mat &E, const Step *st, float *x, int H, cudaStream_t s, int nseq = 1, int rps = kMaxRows);
 void launch_norm_quant(const float *x, const float *w, int H, float eps, const Step *st,
-                       Act out, cudaStream_t s);
+                       Act out, cudaStream_t s, int nseq = 1, int rps = kMaxRows);
 // Y = W A8(x): mode 0 store y[v][ldy], mode 1 residual x[v][ldy] += y
 void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode, int nmax,
                    cudaStream_t s);
@@ -130,21 +137,27 @@ void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Ac
 void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int ld,
                         unsigned long long *partial, int *nan0, int nmax, cudaStream_t s, int row_base = 0);
 void launch_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
-                         Step *st, cudaStream_t s);
+                         Step *st, cudaStream_t s, int nseq = 1, int rps = kMaxRows);
 // vocab-sharded head: per-row best keys and NaN flags into keys [2][kMaxRows] (to be merged by
 // an all-reduce max across the shards), then the merged keys into Step::argmax
 void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int npanels, const Step *st,
                         unsigned long long *keys, cudaStream_t s);
 void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s);
+// nseq > 1 needs the fast kernel's shape (deltanet_batch_ok)
 void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
-                     Step *st, Act out, cudaStream_t s);
+                     Step *st, Act out, cudaStream_t s, int nseq = 1);
+bool deltanet_batch_ok(const LinDims &d);
+// attention grids cover d.rps rows of each of nseq sequences; nseq > 1 needs the cluster kernel
+// (attn_batch_ok)
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
-                      const Step *st, cudaStream_t s);
+                      const Step *st, cudaStream_t s, int nseq = 1);
 void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
-                 const Step *st, Act out, cudaStream_t s);
-void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s);
-void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s);
-void launch_pass_end(Step *st, cudaStream_t s);
+                 const Step *st, Act out, cudaStream_t s, int nseq = 1);
+bool attn_batch_ok(const AttnDims &d);
+// greedy / out: sequence i's at greedy + i * n_max, out + i * n_max
+void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s, int nseq = 1);
+void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s, int nseq = 1);
+void launch_pass_end(Step *st, cudaStream_t s, int nseq = 1);
 // MTP draft head (see the kernels' comments)
 void launch_norm_rows(const float *x, const float *w, int H, float eps, const Step *st, float *out,
                       cudaStream_t s);
@@ -158,11 +171,20 @@ void launch_mtp_pending_take(Step *st, const Step *ms, const float *mrows, float
 void launch_mtp_prefill_fix(const Step *st, Step *ms, cudaStream_t s);
 size_t deltanet_smem(int rep);
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s);
-void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s);
+void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s, int nseq = 1,
+                    const unsigned long long *seeds = nullptr);
 int kernels_init(int max_ctx, int hd, int rep);
 // Records the message pinfer_b200_last_error returns on this thread.
 void set_last_error(const char *msg);   // 0, or -1 if a CUDA call failed
-void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s);
+void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s, int nseq = 1);
+// Host-chosen shapes of a multi-sequence pass: per sequence n, pos0, row0, logged, tokens.
+struct SeqPass {
+    int n, pos0, row0, logged;
+    int tokens[kMaxRows];
+};
+void launch_set_pass_seqs(Step *st, const SeqPass *dev_passes, int nseq, cudaStream_t s);
+// count of sequences with Step::done set, into *ndone
+void launch_count_done(const Step *st, int nseq, int *ndone, cudaStream_t s);
 // small-n standalone entry points for the C-ABI kernel tests
 void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s);
 

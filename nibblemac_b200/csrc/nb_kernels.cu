@@ -773,12 +773,14 @@ __global__ void k_argmax_final(const unsigned long long *partial, const int *nan
                                Step *st) {
     pdl_wait();
     pdl_trigger();
+    st += blockIdx.y;   // the sequence (multi-sequence passes)
     const int v = blockIdx.x;
     if (v >= st->n) return;
+    const int row = st->row0 + v;
     __shared__ unsigned long long red[32];
     unsigned long long best = 0ull;
     for (int i = threadIdx.x; i < npanels; i += blockDim.x) {
-        const unsigned long long k = partial[(size_t)v * npanels + i];
+        const unsigned long long k = partial[(size_t)row * npanels + i];
         best = k > best ? k : best;
     }
     best = warp_max_u64(best);
@@ -788,7 +790,7 @@ __global__ void k_argmax_final(const unsigned long long *partial, const int *nan
         unsigned long long b = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
         b = warp_max_u64(b);
         if (threadIdx.x == 0)
-            st->argmax[v] = nan0[v] ? 0 : (int)(0xffffffffu - (uint32_t)(b & 0xffffffffu));
+            st->argmax[v] = nan0[row] ? 0 : (int)(0xffffffffu - (uint32_t)(b & 0xffffffffu));
     }
 }
 
@@ -798,8 +800,10 @@ __global__ void k_argmax_final(const unsigned long long *partial, const int *nan
 __global__ void k_embed(Mat E, const Step *st, float *x, int H) {
     pdl_wait();
     pdl_trigger();
+    st += blockIdx.y;   // the sequence (multi-sequence passes)
     const int v = blockIdx.x;
     if (v >= st->n) return;
+    const int row = st->row0 + v;
     int tok = st->tokens[v];
     if (tok < 0 || tok >= E.rows) tok = 0;   // host and accept kernel validate ids
     const int panel = tok >> 5, r = tok & 31;
@@ -815,7 +819,7 @@ __global__ void k_embed(Mat E, const Step *st, float *x, int H) {
                                    (float)(uint32_t)((B >> (6 * k)) & 63u));
         const uint8_t byte = u[512 * (k + 1) + (j & 15)];
         const float q = (float)(j < 16 ? (byte & 15) : (byte >> 4));
-        x[(size_t)v * H + c] = __fadd_rn(__fmul_rn(dd, q), -mm);
+        x[(size_t)row * H + c] = __fadd_rn(__fmul_rn(dd, q), -mm);
     }
 }
 
@@ -863,8 +867,9 @@ __global__ void k_norm_quant(const float *x, const float *w, int H, float eps, c
                              Act out) {
     pdl_wait();
     pdl_trigger();
-    const int v = blockIdx.x;
-    if (v >= st->n) return;
+    st += blockIdx.y;   // the sequence (multi-sequence passes)
+    if ((int)blockIdx.x >= st->n) return;
+    const int v = st->row0 + blockIdx.x;
     extern __shared__ float xs[];   // [H] x, then [H] w
     __shared__ float rr;
     float *ws = xs + H;
@@ -1155,8 +1160,14 @@ struct FlushArgs {
 __global__ void k_flush(FlushArgs fa, LinDims d, const Step *st) {
     pdl_wait();
     pdl_trigger();
+    const int seq = blockIdx.z;   // the sequence (multi-sequence batches)
+    st += seq;
     const int keep = st->pend_keep, pend_conv = st->pend_conv, wr = st->wr;
-    const LinLayer &L = fa.layers[blockIdx.y];
+    LinLayer L = fa.layers[blockIdx.y];
+    L.conv_state += seq * d.ss_conv;
+    L.rec += seq * d.ss_rec;
+    L.xin += seq * d.ss_xin;
+    L.upd += seq * d.ss_upd;
     const int kh = blockIdx.x, rep = d.rep, tid = threadIdx.x, nthr = blockDim.x;
     const int C = d.C, S = d.K - 1;
     if (pend_conv > 1) {
@@ -1195,6 +1206,7 @@ __global__ void k_flush(FlushArgs fa, LinDims d, const Step *st) {
 __global__ void k_pass_end(Step *st) {
     pdl_wait();
     pdl_trigger();
+    st += blockIdx.x;   // the sequence (multi-sequence passes)
     if (st->n <= 0) return;   // no pass ran (generation finished): the commit is still owed
     st->pend_keep = 0;
     st->pend_conv = 0;
@@ -1203,8 +1215,41 @@ __global__ void k_pass_end(Step *st) {
 __global__ void k_clear_pending(Step *st) {
     pdl_wait();
     pdl_trigger();
+    st += blockIdx.x;   // the sequence (multi-sequence batches)
     st->pend_keep = 0;
     st->pend_conv = 0;
+}
+
+// Host-chosen shapes of a multi-sequence pass, one CTA per sequence.
+__global__ void k_set_pass_seqs(Step *st, const SeqPass *ps) {
+    pdl_wait();
+    pdl_trigger();
+    const SeqPass &p = ps[blockIdx.x];
+    st += blockIdx.x;
+    if (threadIdx.x == 0) {
+        st->n = p.n;
+        st->pos0 = p.pos0;
+        st->row0 = p.row0;
+        st->logged = p.logged;
+    }
+    if ((int)threadIdx.x < p.n && threadIdx.x < kMaxRows) st->tokens[threadIdx.x] = p.tokens[threadIdx.x];
+}
+
+// Sequences of a batch whose generation has finished.
+__global__ void k_count_done(const Step *st, int nseq, int *ndone) {
+    pdl_wait();
+    pdl_trigger();
+    int c = 0;
+    for (int i = threadIdx.x; i < nseq; i += blockDim.x) c += st[i].done ? 1 : 0;
+    c = warp_sum_int(c);
+    __shared__ int part[32];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += part[w];
+        *ndone = t;
+    }
 }
 
 // Host-chosen pass (prefill chunks, plain eval): shape and tokens by value.
@@ -1222,9 +1267,12 @@ __global__ void k_set_pass(Step *st, PassArgs a) {
 }
 
 // Generation parameters before k_gen_start.
-__global__ void k_set_gen(Step *st, GenArgs g) {
+// blockIdx.x: the sequence of a batch, whose drafter seed is seeds[seq] when seeds is given.
+__global__ void k_set_gen(Step *st, GenArgs g, const unsigned long long *seeds) {
     pdl_wait();
     pdl_trigger();
+    st += blockIdx.x;
+    if (seeds) g.seed = seeds[blockIdx.x];
     st->n_max = g.n_max;
     st->k = g.k;
     st->eos = g.eos;
@@ -1251,17 +1299,21 @@ __global__ void k_attn_prep(AttnLayer L, AttnDims d, const float *y, float *qbuf
                             const Step *st) {
     pdl_wait();
     pdl_trigger();
-    const int t = blockIdx.x;
+    const int t = blockIdx.x % d.rps, seq = blockIdx.x / d.rps;   // row t of sequence seq
+    st += seq;
     if (t >= st->n) return;
     const int idx = blockIdx.y, hd = d.hd, tid = threadIdx.x;
     const int pos = st->pos0 + t;
     if (pos >= d.max_ctx) return;
+    const int row = st->row0 + t;
+    L.kc += seq * d.ss_kv;
+    L.vc += seq * d.ss_kv;
     extern __shared__ float xa[];
     __shared__ float rr;
     const float *src;
     const float *w;
-    if (idx < d.nq) { src = y + (size_t)t * d.ldy + (size_t)2 * hd * idx; w = L.q_norm; }
-    else { src = y + (size_t)t * d.ldy + (size_t)2 * hd * d.nq + (size_t)(idx - d.nq) * hd; w = L.k_norm; }
+    if (idx < d.nq) { src = y + (size_t)row * d.ldy + (size_t)2 * hd * idx; w = L.q_norm; }
+    else { src = y + (size_t)row * d.ldy + (size_t)2 * hd * d.nq + (size_t)(idx - d.nq) * hd; w = L.k_norm; }
     xa[tid] = src[tid];
     __syncthreads();
     if (tid < 32) {
@@ -1285,12 +1337,12 @@ __global__ void k_attn_prep(AttnLayer L, AttnDims d, const float *y, float *qbuf
         v = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, sn));
     }
     if (idx < d.nq) {
-        qbuf[((size_t)t * d.nq + idx) * hd + tid] = v;
+        qbuf[((size_t)row * d.nq + idx) * hd + tid] = v;
     } else {
         const int g = idx - d.nq;
         L.kc[((size_t)g * d.max_ctx + pos) * hd + tid] = v;
         L.vc[((size_t)g * d.max_ctx + pos) * hd + tid] =
-            y[(size_t)t * d.ldy + (size_t)2 * hd * d.nq + (size_t)d.nkv * hd + (size_t)g * hd + tid];
+            y[(size_t)row * d.ldy + (size_t)2 * hd * d.nq + (size_t)d.nkv * hd + (size_t)g * hd + tid];
     }
 }
 
@@ -1549,10 +1601,14 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     pdl_wait();
     pdl_trigger();
     constexpr int HD = kAttnHd;
-    const int t = blockIdx.z, h = blockIdx.y, tid = threadIdx.x;
+    const int t = blockIdx.z % d.rps, seq = blockIdx.z / d.rps, h = blockIdx.y, tid = threadIdx.x;
+    st += seq;                              // row t of sequence seq (multi-sequence passes)
     if (t >= st->n) return;                 // uniform over the cluster
     const int pos = st->pos0 + t;
     if (pos >= d.max_ctx) return;           // uniform over the cluster
+    const int row = st->row0 + t;
+    L.kc += seq * d.ss_kv;
+    L.vc += seq * d.ss_kv;
     const uint32_t c = cluster_rank();
     const int np = pos + 1, g = h / (d.nq / d.nkv);
     const int per = (d.max_ctx + kAttnCL - 1) / kAttnCL;
@@ -1577,8 +1633,8 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     };
     static_assert(kAttnChunk * 8 == kAttnHd, "one 16-byte copy per thread per chunk");
     for (int ch = 0; ch < kAttnRing - 1; ch++) issue_chunk(ch);
-    q[tid] = qbuf[((size_t)t * d.nq + h) * HD + tid];
-    const float gate = tid < kAttnSlice ? y[(size_t)t * d.ldy + (size_t)2 * HD * h + HD + c * kAttnSlice + tid] : 0.0f;
+    q[tid] = qbuf[((size_t)row * d.nq + h) * HD + tid];
+    const float gate = tid < kAttnSlice ? y[(size_t)row * d.ldy + (size_t)2 * HD * h + HD + c * kAttnSlice + tid] : 0.0f;
     __syncthreads();
 
     // 1. scores of this CTA's positions
@@ -1667,8 +1723,8 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     if (warp == 0) {
         o = __fmul_rn(o, pf_sigmoid(gate));
         const int col = h * HD + (int)c * kAttnSlice, nbo = out.cols >> 5;
-        quant_block_warp(o, lane, out.q + (size_t)t * out.cols + col, out.d + (size_t)t * nbo + (col >> 5),
-                         out.fs + (size_t)t * nbo + (col >> 5));
+        quant_block_warp(o, lane, out.q + (size_t)row * out.cols + col, out.d + (size_t)row * nbo + (col >> 5),
+                         out.fs + (size_t)row * nbo + (col >> 5));
     }
     cluster_wait();
 }
@@ -1785,6 +1841,13 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     constexpr int S = KC - 1;
     const int h = blockIdx.x, j = threadIdx.x;
     const int C = d.C;
+    // blockIdx.y: the sequence of a multi-sequence batch (its states, Step block and rows)
+    const int seq = blockIdx.y;
+    st += seq;
+    L.conv_state += seq * d.ss_conv;
+    L.rec += seq * d.ss_rec;
+    L.xin += seq * d.ss_xin;
+    L.upd += seq * d.ss_upd;
     // conv taps and state rows of this thread's three channels (q, k, v column j of this
     // head): independent of the step and the first thing the kernel needs, so requested first
     ConvCh<KC> cq, ck, cv;
@@ -1817,6 +1880,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
         mbar_wait(&sbar[1], 0);
         return;
     }
+    const int row0 = st->row0;
     const int logged = st->logged, pend_keep = st->pend_keep, pend_conv = st->pend_conv;
     const int wr = st->wr;
     conv_load_log(cq, L, C, pend_conv);
@@ -1832,7 +1896,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     if (j == 0) {
         mbar_arrive_expect(&sbar[0], (uint32_t)n * 4u * kDK * 4u);
         for (int t = 0; t < n; t++) {
-            const float *yr = y + (size_t)t * d.ldy;
+            const float *yr = y + (size_t)(row0 + t) * d.ldy;
             bulk_g2s(sq[t], yr + h * kDK, kDK * 4, &sbar[0]);
             bulk_g2s(sk[t], yr + d.kd + h * kDK, kDK * 4, &sbar[0]);
             bulk_g2s(sv[t], yr + 2 * d.kd + h * kDV, kDV * 4, &sbar[0]);
@@ -1856,7 +1920,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     // ---- gates of token t on thread kDV - kMaxRows + t (warp 3), while the state streams in
     if (j >= kDV - kMaxRows && j - (kDV - kMaxRows) < n) {
         const int t = j - (kDV - kMaxRows);
-        const float *yr = y + (size_t)t * d.ldy;
+        const float *yr = y + (size_t)(row0 + t) * d.ldy;
         const float b = yr[C + d.vd + h], a = yr[C + d.vd + d.nv + h];
         sbeta[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-b)));
         const float xs = __fadd_rn(a, L.dt_bias[h]);
@@ -2042,8 +2106,8 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             float v = __fmul_rn(__fmul_rn(so[t][j], srn[t]), w);
             v = __fmul_rn(v, pf_silu(sz[t][j]));
             const int col = h * kDV + j;
-            quant_block_warp(v, lane, out.q + (size_t)t * out.cols + (col & ~31),
-                             out.d + (size_t)t * nbo + (col >> 5), out.fs + (size_t)t * nbo + (col >> 5));
+            quant_block_warp(v, lane, out.q + (size_t)(row0 + t) * out.cols + (col & ~31),
+                             out.d + (size_t)(row0 + t) * nbo + (col >> 5), out.fs + (size_t)(row0 + t) * nbo + (col >> 5));
             (void)warp;
         }
     }
@@ -2233,6 +2297,9 @@ __global__ void k_gen_start(Step *st, const int *greedy, int *out) {
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x != 0) return;
+    st += blockIdx.x;   // the sequence of a batch: its Step, greedy stream and output row
+    if (greedy) greedy += (size_t)blockIdx.x * st->n_max;
+    out += (size_t)blockIdx.x * st->n_max;
     const int n = st->n;
     st->cur = st->argmax[n - 1];
     st->pos0 += n;
@@ -2256,6 +2323,9 @@ __global__ void k_accept(Step *st, const int *greedy, int *out) {
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x != 0) return;
+    st += blockIdx.x;   // the sequence of a batch: its Step, greedy stream and output row
+    if (greedy) greedy += (size_t)blockIdx.x * st->n_max;
+    out += (size_t)blockIdx.x * st->n_max;
     const int n = st->n;
     if (n <= 0) {
         st->last_e = 0;
@@ -2449,15 +2519,15 @@ void launch_matvec_chunked(const Mat &W, Act in, const Step *st, float *y, int l
     else matvec_t<16>(W, in, st, y, ldy, mode, s);
 }
 void launch_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
-                         Step *st, cudaStream_t s) {
-    launch_k(k_argmax_final, kMaxRows, 256, 0, s, partial, nan0, npanels, st);
+                         Step *st, cudaStream_t s, int nseq, int rps) {
+    launch_k(k_argmax_final, dim3(rps, nseq), 256, 0, s, partial, nan0, npanels, st);
 }
-void launch_embed(const Mat &E, const Step *st, float *x, int H, cudaStream_t s) {
-    launch_k(k_embed, kMaxRows, 256, 0, s, E, st, x, H);
+void launch_embed(const Mat &E, const Step *st, float *x, int H, cudaStream_t s, int nseq, int rps) {
+    launch_k(k_embed, dim3(rps, nseq), 256, 0, s, E, st, x, H);
 }
 void launch_norm_quant(const float *x, const float *w, int H, float eps, const Step *st, Act out,
-                       cudaStream_t s) {
-    launch_k(k_norm_quant, kMaxRows, 256, 2 * (size_t)H * sizeof(float), s, x, w, H, eps, st, out);
+                       cudaStream_t s, int nseq, int rps) {
+    launch_k(k_norm_quant, dim3(rps, nseq), 256, 2 * (size_t)H * sizeof(float), s, x, w, H, eps, st, out);
 }
 void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s) {
     const int warps = n * (cols / 32);
@@ -2467,27 +2537,35 @@ size_t deltanet_smem(int rep) {
     return sizeof(float) * ((size_t)kMaxRows * kDK * 2 + (size_t)kMaxRows * rep * kDV * 2 +
                             (size_t)kMaxRows * rep * 3 + (size_t)kMaxRows * kDK + kMaxRows + 8);
 }
+bool deltanet_batch_ok(const LinDims &d) {
+    return d.rep == 1 && d.K == 4 && d.dk == kDK && d.dv == kDV && d.ldy % 4 == 0 && d.kd % 4 == 0 && d.C % 4 == 0 &&
+           d.ss_rec % 4 == 0;
+}
 void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
-                     Step *st, Act out, cudaStream_t s) {
-    if (d.rep == 1 && d.K == 4 && d.dk == kDK && d.dv == kDV && d.ldy % 4 == 0 && d.kd % 4 == 0 &&
-        d.C % 4 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)L.rec & 15) == 0) {
-        launch_k(k_deltanet2<4>, d.nk, kDV, sizeof(float) * kDK * kDV, s, L, d, y, st, out);
+                     Step *st, Act out, cudaStream_t s, int nseq) {
+    if (deltanet_batch_ok(d) && ((uintptr_t)y & 15) == 0 && ((uintptr_t)L.rec & 15) == 0) {
+        launch_k(k_deltanet2<4>, dim3(d.nk, nseq), kDV, sizeof(float) * kDK * kDV, s, L, d, y, st, out);
         return;
     }
+    if (nseq != 1) return;   // callers check deltanet_batch_ok first
     const size_t sm = deltanet_smem(d.rep);
     launch_k(k_deltanet, d.nk, kDV, sm, s, L, d, y, st, out);
 }
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
-                      const Step *st, cudaStream_t s) {
-    launch_k(k_attn_prep, dim3(kMaxRows, d.nq + d.nkv), d.hd, (size_t)d.hd * sizeof(float), s, L, d, y, qbuf, st);
+                      const Step *st, cudaStream_t s, int nseq) {
+    launch_k(k_attn_prep, dim3(d.rps * nseq, d.nq + d.nkv), d.hd, (size_t)d.hd * sizeof(float), s, L, d, y, qbuf, st);
+}
+bool attn_batch_ok(const AttnDims &d) {
+    static const int attn3_lim = dyn_smem_limit(k_attn3);
+    return d.hd == kAttnHd && attn3_smem(d.max_ctx) <= (size_t)attn3_lim;
 }
 void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
-                 const Step *st, Act out, cudaStream_t s) {
-    static const int attn3_lim = dyn_smem_limit(k_attn3);
-    if (d.hd == kAttnHd && attn3_smem(d.max_ctx) <= (size_t)attn3_lim) {
-        launch_k(k_attn3, dim3(kAttnCL, d.nq, kMaxRows), kAttnHd, attn3_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
+                 const Step *st, Act out, cudaStream_t s, int nseq) {
+    if (attn_batch_ok(d)) {
+        launch_k(k_attn3, dim3(kAttnCL, d.nq, d.rps * nseq), kAttnHd, attn3_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
         return;
     }
+    if (nseq != 1) return;   // callers check attn_batch_ok first
     static const int attn2_lim = dyn_smem_limit(k_attn2);
     if (d.hd == kAttnHd && attn2_smem(d.max_ctx) <= (size_t)attn2_lim) {
         launch_k(k_attn2, dim3(kMaxRows, d.nq), kAttnHd, attn2_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
@@ -2496,17 +2574,17 @@ void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const fl
     const size_t sm = ((size_t)d.hd + d.max_ctx) * sizeof(float);
     launch_k(k_attn, dim3(kMaxRows, d.nq), d.hd, sm, s, L, d, y, qbuf, st, out);
 }
-void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s) {
-    launch_k(k_gen_start, 1, 32, 0, s, st, greedy, out);
+void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s, int nseq) {
+    launch_k(k_gen_start, nseq, 32, 0, s, st, greedy, out);
 }
-void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s) {
-    launch_k(k_accept, 1, 32, 0, s, st, greedy, out);
+void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s, int nseq) {
+    launch_k(k_accept, nseq, 32, 0, s, st, greedy, out);
 }
-void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s) {
+void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st, cudaStream_t s, int nseq) {
     FlushArgs fa;
     for (int i = 0; i < n_lin && i < kMaxLayers; i++) fa.layers[i] = layers[i];
-    if (n_lin > 0) launch_k(k_flush, dim3(d.nk, n_lin), kDV, 0, s, fa, d, st);
-    launch_k(k_clear_pending, 1, 1, 0, s, st);
+    if (n_lin > 0) launch_k(k_flush, dim3(d.nk, n_lin, nseq), kDV, 0, s, fa, d, st);
+    launch_k(k_clear_pending, nseq, 1, 0, s, st);
 }
 void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int npanels, const Step *st,
                         unsigned long long *keys, cudaStream_t s) {
@@ -2539,7 +2617,7 @@ void launch_mtp_pending_take(Step *st, const Step *ms, const float *mrows, float
 void launch_mtp_prefill_fix(const Step *st, Step *ms, cudaStream_t s) {
     launch_k(k_mtp_prefill_fix, 1, 32, 0, s, st, ms);
 }
-void launch_pass_end(Step *st, cudaStream_t s) { launch_k(k_pass_end, 1, 1, 0, s, st); }
+void launch_pass_end(Step *st, cudaStream_t s, int nseq) { launch_k(k_pass_end, nseq, 1, 0, s, st); }
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s) {
     PassArgs a;
     a.n = n;
@@ -2548,7 +2626,15 @@ void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, c
     for (int i = 0; i < kMaxRows; i++) a.tokens[i] = i < n ? tokens[i] : 0;
     launch_k(k_set_pass, 1, 1, 0, s, st, a);
 }
-void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s) { launch_k(k_set_gen, 1, 1, 0, s, st, g); }
+void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s, int nseq, const unsigned long long *seeds) {
+    launch_k(k_set_gen, nseq, 1, 0, s, st, g, seeds);
+}
+void launch_set_pass_seqs(Step *st, const SeqPass *dev_passes, int nseq, cudaStream_t s) {
+    launch_k(k_set_pass_seqs, nseq, 32, 0, s, st, dev_passes);
+}
+void launch_count_done(const Step *st, int nseq, int *ndone, cudaStream_t s) {
+    launch_k(k_count_done, 1, 256, 0, s, st, nseq, ndone);
+}
 int kernels_init(int max_ctx, int hd, int rep) {
     // raise the dynamic shared memory limits once, outside any stream capture
     raise_smem(k_matvec<1, 0>, mv_smem<1>());

@@ -188,8 +188,65 @@ class Model:
         if rc != PINFER_OK:
             raise PinferError(rc, "pinfer_b200_shard_head", self.lib.last_error())
 
+    def batch(self, slots: int, max_ctx: int, max_k: int = 3) -> "Batch":
+        """A multi-sequence batch on this context's weights (pinfer_b200_batch_create)."""
+        return Batch(self, slots, max_ctx, max_k)
+
     def round_kernels(self, k: int) -> int:
         return self.lib.pinfer_b200_round_kernels(self.ctx, k)
 
     def stream(self) -> int:
         return self.lib.pinfer_b200_stream(self.ctx) or 0
+
+
+class Batch:
+    """Independent sequences generated together in merged passes (pinfer_b200_batch_*): each
+    sequence's tokens equal what Model.generate_synthetic gives for it alone."""
+
+    def __init__(self, model: Model, slots: int, max_ctx: int, max_k: int = 3) -> None:
+        self.lib, self.model = model.lib, model
+        err = ctypes.c_int(0)
+        self.h = self.lib.pinfer_b200_batch_create(model.ctx, slots, max_ctx, max_k, ctypes.byref(err))
+        if not self.h:
+            raise PinferError(err.value, "pinfer_b200_batch_create", self.lib.last_error())
+        self.slots = slots
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.pinfer_b200_batch_free(self.h)
+            self.h = None
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def generate_synthetic(self, prompts, n_max: int, k: int = 0, greedy=None, seeds=None, p: float = 0.0):
+        """(list of token lists, SpecStats, statuses, decode_ms) for the prompts (a list of
+        token arrays); k > 0 drafts with the synthetic drafter from greedy[i] (n_max tokens
+        each) and seeds[i]."""
+        n = len(prompts)
+        lens = _i32([len(x) for x in prompts])
+        flat = _i32(np.concatenate([np.asarray(x, np.int32) for x in prompts]))
+        out = np.zeros((n, n_max), np.int32)
+        counts = np.zeros(n, np.int32)
+        status = np.zeros(n, np.int32)
+        st = SpecStats()
+        ms = ctypes.c_float(0.0)
+        g = sd = None
+        if k > 0:
+            g = np.zeros((n, n_max), np.int32)
+            for i, row in enumerate(greedy):
+                r = np.asarray(row, np.int32)[:n_max]
+                g[i, :len(r)] = r
+            sd = np.ascontiguousarray(np.asarray(seeds, np.uint64))
+        rc = self.lib.pinfer_b200_batch_generate_synthetic(
+            self.h, n, flat.ctypes.data_as(_c_int32_p), lens.ctypes.data_as(_c_int32_p), n_max, k,
+            g.ctypes.data_as(_c_int32_p) if g is not None else None,
+            sd.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)) if sd is not None else None, p,
+            out.ctypes.data_as(_c_int32_p), counts.ctypes.data_as(_c_int32_p),
+            status.ctypes.data_as(_c_int32_p), ctypes.byref(st), ctypes.byref(ms))
+        if rc != PINFER_OK:
+            raise PinferError(rc, "pinfer_b200_batch_generate_synthetic", self.lib.last_error())
+        return [out[i, :counts[i]].tolist() for i in range(n)], st, status.tolist(), ms.value
