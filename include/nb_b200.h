@@ -84,6 +84,10 @@ unsigned long long nb_argmax_key(float v, int row);
 typedef struct pinfer_b200_batch pinfer_b200_batch;
 pinfer_b200_batch *pinfer_b200_batch_create(pinfer_ctx *ctx, int slots, int max_ctx, int max_k, int *err);
 void pinfer_b200_batch_free(pinfer_b200_batch *b);
+/* The CUDA stream (cudaStream_t) the batch's work runs on, for timing with events. */
+void *pinfer_b200_batch_stream(pinfer_b200_batch *b);
+/* Verify rounds (passes over all the batch's sequences) the last generation ran. */
+int pinfer_b200_batch_rounds(const pinfer_b200_batch *b);
 /* Greedy speculative generation of n_seq (<= slots) independent sequences from fresh states,
  * with the synthetic drafter of pinfer_b200_generate_synthetic per sequence: prompts
  * concatenated (sequence i has prompt_lens[i] tokens), greedy [n_seq][n_max] and seeds [n_seq]

@@ -107,6 +107,8 @@ _OPTIONAL = {
     "pinfer_b200_batch_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                    _c_int_p]),
     "pinfer_b200_batch_free": (None, [ctypes.c_void_p]),
+    "pinfer_b200_batch_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "pinfer_b200_batch_rounds": (ctypes.c_int, [ctypes.c_void_p]),
     "pinfer_b200_batch_generate_synthetic": (ctypes.c_int, [
         ctypes.c_void_p, ctypes.c_int, _c_int32_p, _c_int32_p, ctypes.c_int, ctypes.c_int, _c_int32_p,
         ctypes.POINTER(ctypes.c_uint64), ctypes.c_float, _c_int32_p, _c_int32_p, _c_int32_p,

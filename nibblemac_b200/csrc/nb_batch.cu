@@ -64,6 +64,7 @@ struct pinfer_b200_batch {
 
     cudaGraphExec_t graph = nullptr;
     int graph_nseq = -1, graph_k = -1;
+    int last_rounds = 0;   // verify rounds (graph replays) of the last generation
     const int *graph_out = nullptr;
 
     template <class T>
@@ -315,6 +316,10 @@ pinfer_b200_batch *pinfer_b200_batch_create(pinfer_ctx *ctx, int slots, int max_
     return b;
 }
 
+void *pinfer_b200_batch_stream(pinfer_b200_batch *b) { return b ? (void *)b->stream : nullptr; }
+
+int pinfer_b200_batch_rounds(const pinfer_b200_batch *b) { return b ? b->last_rounds : -1; }
+
 void pinfer_b200_batch_free(pinfer_b200_batch *b) {
     if (!b) return;
     cudaSetDevice(b->device);
@@ -445,6 +450,7 @@ int pinfer_b200_batch_generate_synthetic(pinfer_b200_batch *b, int n_seq, const 
     }
     cudaEventRecord(ev1, s);
     cudaEventSynchronize(ev1);
+    b->last_rounds = rounds;
     float ms = 0.0f;
     cudaEventElapsedTime(&ms, ev0, ev1);
     cudaEventDestroy(ev0);

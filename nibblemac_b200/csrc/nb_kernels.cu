@@ -1729,6 +1729,157 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     cluster_wait();
 }
 
+// Grouped form of k_attn3 for multi-sequence passes: one cluster of kAttnCL CTAs per
+// (sequence, KV head g, chunk of kAttnQ / G rows), G = nq / nkv query heads per KV head, so the
+// cluster's up to kAttnQ queries (rows x heads of the group) share every K and V row it reads.
+// Per query the arithmetic is k_attn3's (scores with pf_dot's 16-lane order over this CTA's
+// positions, the full softmax in every CTA from the gathered scores: fmaxf max, pf_expf,
+// sum4_ref, one division, scaling; the P.V chain of this CTA's 32 columns in position order;
+// sigmoid gate; A8), so every output bit equals it. Positions are split over the CTAs by the
+// group's longest causal span; PV runs on all 8 warps, two queries per warp.
+constexpr int kAttnQ = 16;     // queries per cluster
+constexpr int kAttn4Ring = 8;  // V chunks in flight
+
+size_t attn4_smem(int max_ctx) {
+    const size_t per = ((size_t)max_ctx + kAttnCL - 1) / kAttnCL;
+    const size_t npad = ((size_t)max_ctx + 3) & ~(size_t)3;
+    return sizeof(float) * ((size_t)kAttnQ * kAttnHd + (size_t)kAttnQ * ((per + 3) & ~(size_t)3) +
+                            (size_t)kAttnQ * npad + (size_t)kAttn4Ring * kAttnChunk * kAttnSlice);
+}
+
+__global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
+    k_attn4(AttnLayer L, AttnDims d, const float *y, const float *qbuf, const Step *st, Act out) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int HD = kAttnHd;
+    const int G = d.nq / d.nkv, QR = kAttnQ / G;            // heads per group, rows per cluster
+    const int nch = (d.rps + QR - 1) / QR;
+    const int g = blockIdx.y / nch, rc = blockIdx.y % nch, seq = blockIdx.z, tid = threadIdx.x;
+    st += seq;
+    const int n = st->n, t0 = rc * QR;
+    if (t0 >= n) return;                                     // uniform over the cluster
+    const int nt = min(QR, n - t0), Q = nt * G;              // live queries: q = ti * G + hh
+    const int pos0 = st->pos0 + t0;
+    if (pos0 >= d.max_ctx) return;
+    const int np_max = min(pos0 + nt, d.max_ctx);            // longest causal span of the group
+    L.kc += seq * d.ss_kv;
+    L.vc += seq * d.ss_kv;
+    const uint32_t c = cluster_rank();
+    const int lane = tid & 31, warp = tid >> 5;
+    const int per_max = (d.max_ctx + kAttnCL - 1) / kAttnCL, perp = (per_max + 3) & ~3;
+    const int npad = (d.max_ctx + 3) & ~3;
+    extern __shared__ __align__(16) float asm4[];
+    float *qv = asm4;                                        // [kAttnQ][HD]
+    float *part = qv + kAttnQ * HD;                          // [kAttnQ][perp]: this CTA's scores
+    float *att = part + kAttnQ * perp;                       // [kAttnQ][npad]
+    float *vs = att + (size_t)kAttnQ * npad;                 // V ring [kAttn4Ring][kAttnChunk][32]
+    const int per = (np_max + kAttnCL - 1) / kAttnCL;        // positions per CTA (<= per_max)
+
+    const float *V = L.vc + (size_t)g * d.max_ctx * HD + c * kAttnSlice;
+    const int nvch = (np_max + kAttnChunk - 1) / kAttnChunk;
+    auto issue_chunk = [&](int ch) {
+        const int r = ch * kAttnChunk + (tid >> 3), k = tid & 7;
+        if (ch < nvch && r < np_max)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                         ::"r"(smem_u32(vs + ((size_t)(ch % kAttn4Ring) * kAttnChunk + (tid >> 3)) * kAttnSlice + 4 * k)),
+                         "l"(V + (size_t)r * HD + 4 * k) : "memory");
+        cp_async_commit();
+    };
+    for (int ch = 0; ch < kAttn4Ring - 1; ch++) issue_chunk(ch);
+    for (int i = tid; i < Q * HD; i += HD) {
+        const int q = i / HD, ti = q / G, h = g * G + q % G;
+        qv[i] = qbuf[((size_t)(st->row0 + t0 + ti) * d.nq + h) * HD + (i % HD)];
+    }
+    __syncthreads();
+
+    // 1. scores of this CTA's positions for every query of the group: the K row fragment is
+    // loaded once and used for all of them
+    const float scale = inv_sqrt_ref((float)HD);
+    const float *K = L.kc + (size_t)g * d.max_ctx * HD;
+    const int p0 = (int)c * per, p1 = min(np_max, p0 + per);
+    const int k4 = tid & 3;
+    for (int base = p0; base < p1; base += HD / 4) {
+        const int pp = base + (tid >> 2);
+        const bool act = pp < p1;
+        const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)(act ? pp : p0) * HD) + k4;
+        float4 kf[HD / 16];
+#pragma unroll
+        for (int i = 0; i < HD / 16; i++) kf[i] = __ldg(kr + 4 * i);
+        for (int q = 0; q < Q; q++) {
+            const float4 *q4 = reinterpret_cast<const float4 *>(qv + (size_t)q * HD);
+            float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < HD / 16; i++) {
+                const float4 qq = q4[4 * i + k4];
+                c0 = madd(c0, qq.x, kf[i].x);
+                c1 = madd(c1, qq.y, kf[i].y);
+                c2 = madd(c2, qq.z, kf[i].z);
+                c3 = madd(c3, qq.w, kf[i].w);
+            }
+            const float hh = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
+            const float pr = __fadd_rn(hh, __shfl_xor_sync(0xffffffffu, hh, 1));
+            const float sc = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 2));
+            if (act && k4 == 0) part[(size_t)q * perp + (pp - p0)] = __fmul_rn(__fadd_rn(sc, 0.0f), scale);
+        }
+    }
+    cluster_arrive();
+    cluster_wait();
+
+    // 2. every query's scores from their owners, then its softmax (one warp per query)
+    for (int i = tid; i < Q * np_max; i += HD) {
+        const int q = i / np_max, p = i % np_max;
+        const int np = pos0 + q / G + 1;
+        if (p < np) {
+            const int owner = p / per;
+            att[(size_t)q * npad + p] = ld_dsmem(part + (size_t)q * perp + (p - owner * per), (uint32_t)owner);
+        }
+    }
+    cluster_arrive();   // this CTA is done reading its peers; waited on before exit
+    __syncthreads();
+    for (int q = warp; q < Q; q += HD / 32) {
+        float *a = att + (size_t)q * npad;
+        const int np = pos0 + q / G + 1;
+        float m = -INFINITY;
+        for (int p = lane; p < np; p += 32) m = fmaxf(m, a[p]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        for (int p = lane; p < np; p += 32) a[p] = pf_expf(__fadd_rn(a[p], -m));
+        __syncwarp();
+        const float sum = sum4_ref(a, np);
+        const float inv = __fdiv_rn(1.0f, sum);
+        for (int p = lane; p < np; p += 32) a[p] = __fmul_rn(a[p], inv);
+    }
+
+    // 3. ordered PV chains of this CTA's 32 columns, two queries per warp, chunk by chunk
+    // through the V ring; gate and A8
+    const int qa = warp, qb = warp + HD / 32;
+    const int npa = qa < Q ? pos0 + qa / G + 1 : 0, npb = qb < Q ? pos0 + qb / G + 1 : 0;
+    const float *aa = att + (size_t)(qa < Q ? qa : 0) * npad, *ab = att + (size_t)(qb < Q ? qb : 0) * npad;
+    float oa = 0.0f, ob = 0.0f;
+    for (int ch = 0; ch < nvch; ch++) {
+        cp_async_wait<kAttn4Ring - 2>();
+        __syncthreads();
+        issue_chunk(ch + kAttn4Ring - 1);
+        const float *cv = vs + (size_t)(ch % kAttn4Ring) * kAttnChunk * kAttnSlice + lane;
+        const int pc = ch * kAttnChunk;
+        const int ra = min(kAttnChunk, npa - pc), rb = min(kAttnChunk, npb - pc);
+        for (int i = 0; i < ra; i++) oa = madd(oa, aa[pc + i], cv[(size_t)i * kAttnSlice]);
+        for (int i = 0; i < rb; i++) ob = madd(ob, ab[pc + i], cv[(size_t)i * kAttnSlice]);
+    }
+    cp_async_wait<0>();
+    const int nbo = out.cols >> 5;
+    for (int k = 0; k < 2; k++) {
+        const int q = k ? qb : qa;
+        if (q >= Q) continue;
+        const int h = g * G + q % G, row = st->row0 + t0 + q / G;
+        const float gate = y[(size_t)row * d.ldy + (size_t)2 * HD * h + HD + c * kAttnSlice + lane];
+        const float o = __fmul_rn(k ? ob : oa, pf_sigmoid(gate));
+        const int col = h * HD + (int)c * kAttnSlice;
+        quant_block_warp(o, lane, out.q + (size_t)row * out.cols + col, out.d + (size_t)row * nbo + (col >> 5),
+                         out.fs + (size_t)row * nbo + (col >> 5));
+    }
+    cluster_wait();
+}
+
 // Gated DeltaNet layer, latency-oriented form of k_deltanet with identical per-element
 // arithmetic (same citations). Differences are scheduling only:
 //  - one cp.async batch brings this key head's q / k / v / z / b / a rows of every token into
@@ -2555,12 +2706,23 @@ void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, flo
                       const Step *st, cudaStream_t s, int nseq) {
     launch_k(k_attn_prep, dim3(d.rps * nseq, d.nq + d.nkv), d.hd, (size_t)d.hd * sizeof(float), s, L, d, y, qbuf, st);
 }
+bool attn4_ok(const AttnDims &d) {
+    static const int attn4_lim = dyn_smem_limit(k_attn4);
+    const int G = d.nkv > 0 ? d.nq / d.nkv : 0;
+    return d.hd == kAttnHd && G > 0 && d.nq % d.nkv == 0 && G <= kAttnQ && kAttnQ % G == 0 &&
+           attn4_smem(d.max_ctx) <= (size_t)attn4_lim;
+}
 bool attn_batch_ok(const AttnDims &d) {
     static const int attn3_lim = dyn_smem_limit(k_attn3);
     return d.hd == kAttnHd && attn3_smem(d.max_ctx) <= (size_t)attn3_lim;
 }
 void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
                  const Step *st, Act out, cudaStream_t s, int nseq) {
+    if (nseq > 1 && attn4_ok(d)) {   // grouped queries share the K / V reads
+        const int QR = kAttnQ / (d.nq / d.nkv), nch = (d.rps + QR - 1) / QR;
+        launch_k(k_attn4, dim3(kAttnCL, d.nkv * nch, nseq), kAttnHd, attn4_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
+        return;
+    }
     if (attn_batch_ok(d)) {
         launch_k(k_attn3, dim3(kAttnCL, d.nq, d.rps * nseq), kAttnHd, attn3_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
         return;
@@ -2679,6 +2841,7 @@ int kernels_init(int max_ctx, int hd, int rep) {
         raise_smem(k_attn, ((size_t)hd + max_ctx) * sizeof(float));
         raise_smem(k_attn2, attn2_smem(max_ctx));
         raise_smem(k_attn3, attn3_smem(max_ctx));
+        raise_smem(k_attn4, attn4_smem(max_ctx));
     }
     if (gemm_init() != 0) return -1;
     return cudaGetLastError() == cudaSuccess ? 0 : -1;

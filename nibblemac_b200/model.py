@@ -222,6 +222,13 @@ class Batch:
         except Exception:
             pass
 
+    def stream(self) -> int:
+        return self.lib.pinfer_b200_batch_stream(self.h) or 0
+
+    def rounds(self) -> int:
+        """Verify rounds the last generation ran (passes over all sequences)."""
+        return self.lib.pinfer_b200_batch_rounds(self.h)
+
     def generate_synthetic(self, prompts, n_max: int, k: int = 0, greedy=None, seeds=None, p: float = 0.0):
         """(list of token lists, SpecStats, statuses, decode_ms) for the prompts (a list of
         token arrays); k > 0 drafts with the synthetic drafter from greedy[i] (n_max tokens
