@@ -1880,6 +1880,172 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     cluster_wait();
 }
 
+// Throughput form of the grouped attention for multi-sequence passes: one CTA (no cluster) per
+// (sequence, KV head g, chunk of kAttnQ / G rows), sized for many concurrent groups rather than
+// for the latency of one. Per query the arithmetic is k_attn3's: scores with pf_dot's 16-lane
+// order (4 threads per score; the K row fragment is loaded once into registers and used for all
+// the group's queries), the softmax (fmaxf max, pf_expf, sum4_ref's 4-lane sum order, one
+// division, scaling), P.V in position order from zero, sigmoid gate, A8. The probabilities are
+// kept position-major (att[p][q]), so the P.V loop reads a position's 16 values with four
+// 16-byte loads; thread j owns output column j of all the group's queries (16 independent
+// chains), with V read 8 positions ahead.
+size_t attn5_smem(int max_ctx) {
+    return sizeof(float) * ((size_t)kAttnQ * kAttnHd + (((size_t)max_ctx + 3) & ~(size_t)3) * kAttnQ);
+}
+
+// sum4_ref over a[i * stride], i < n (the same 4-lane order and final combination)
+__device__ float sum4_strided(const float *a, int stride, int n) {
+    const int lane = threadIdx.x & 31;
+    float c = 0.0f;
+    const int n4 = n & ~3;
+    if (lane < 4) {
+        for (int i = lane; i < n4; i += 4) c = __fadd_rn(c, a[(size_t)i * stride]);
+    } else if (lane == 4) {
+        for (int i = n4; i < n; i++) c = __fadd_rn(c, a[(size_t)i * stride]);
+    }
+    const float c1 = __shfl_sync(0xffffffffu, c, 1), c2 = __shfl_sync(0xffffffffu, c, 2);
+    const float c3 = __shfl_sync(0xffffffffu, c, 3), t = __shfl_sync(0xffffffffu, c, 4);
+    const float c0 = __shfl_sync(0xffffffffu, c, 0);
+    return __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), t);
+}
+
+__global__ void __launch_bounds__(kAttnHd)
+    k_attn5(AttnLayer L, AttnDims d, const float *y, const float *qbuf, const Step *st, Act out) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int HD = kAttnHd, QS = kAttnQ;   // att row stride: 16 queries
+    const int G = d.nq / d.nkv, QR = kAttnQ / G;
+    const int nch = (d.rps + QR - 1) / QR;
+    const int g = blockIdx.x / nch, rc = blockIdx.x % nch, seq = blockIdx.y, tid = threadIdx.x;
+    st += seq;
+    const int n = st->n, t0 = rc * QR;
+    if (t0 >= n) return;
+    const int nt = min(QR, n - t0), Q = nt * G;   // live queries: q = ti * G + hh
+    const int pos0 = st->pos0 + t0;
+    if (pos0 >= d.max_ctx) return;
+    const int np_max = min(pos0 + nt, d.max_ctx), np_min = pos0 + 1;
+    L.kc += seq * d.ss_kv;
+    L.vc += seq * d.ss_kv;
+    const int lane = tid & 31, warp = tid >> 5;
+    extern __shared__ __align__(16) float asm5[];
+    float *qv = asm5;               // [QS][HD]
+    float *att = qv + QS * HD;      // [np][QS]
+    for (int i = tid; i < QS * HD; i += HD) {
+        const int q = i / HD;
+        float v = 0.0f;
+        if (q < Q) {
+            const int ti = q / G, h = g * G + q % G;
+            v = qbuf[((size_t)(st->row0 + t0 + ti) * d.nq + h) * HD + (i % HD)];
+        }
+        qv[i] = v;
+    }
+    __syncthreads();
+
+    // 1. scores: 64 positions per pass, 4 threads per position, all queries per K fragment
+    const float scale = inv_sqrt_ref((float)HD);
+    const float *K = L.kc + (size_t)g * d.max_ctx * HD;
+    const int k4 = tid & 3;
+    for (int base = 0; base < np_max; base += HD / 4) {
+        const int pp = base + (tid >> 2);
+        const bool act = pp < np_max;
+        const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)(act ? pp : 0) * HD) + k4;
+        float4 kf[HD / 16];
+#pragma unroll
+        for (int i = 0; i < HD / 16; i++) kf[i] = __ldg(kr + 4 * i);
+        for (int q = 0; q < Q; q++) {
+            const float4 *q4 = reinterpret_cast<const float4 *>(qv + (size_t)q * HD);
+            float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < HD / 16; i++) {
+                const float4 qq = q4[4 * i + k4];
+                c0 = madd(c0, qq.x, kf[i].x);
+                c1 = madd(c1, qq.y, kf[i].y);
+                c2 = madd(c2, qq.z, kf[i].z);
+                c3 = madd(c3, qq.w, kf[i].w);
+            }
+            const float hh = __fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3));
+            const float pr = __fadd_rn(hh, __shfl_xor_sync(0xffffffffu, hh, 1));
+            const float sc = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, 2));
+            if (act && k4 == 0) att[(size_t)pp * QS + q] = __fmul_rn(__fadd_rn(sc, 0.0f), scale);
+        }
+    }
+    __syncthreads();
+
+    // 2. softmax of each query over its causal span (one warp per query)
+    for (int q = warp; q < Q; q += HD / 32) {
+        const int np = pos0 + q / G + 1;
+        float m = -INFINITY;
+        for (int p = lane; p < np; p += 32) m = fmaxf(m, att[(size_t)p * QS + q]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        for (int p = lane; p < np; p += 32) att[(size_t)p * QS + q] = pf_expf(__fadd_rn(att[(size_t)p * QS + q], -m));
+        __syncwarp();
+        const float sum = sum4_strided(att + q, QS, np);
+        const float inv = __fdiv_rn(1.0f, sum);
+        for (int p = lane; p < np; p += 32) att[(size_t)p * QS + q] = __fmul_rn(att[(size_t)p * QS + q], inv);
+    }
+    __syncthreads();
+
+    // 3. P.V: column tid of every query, positions in order; every query is live over
+    // [0, np_min), the group's later rows over their longer spans after that
+    const float *V = L.vc + (size_t)g * d.max_ctx * HD + tid;
+    float acc[QS];
+#pragma unroll
+    for (int q = 0; q < QS; q++) acc[q] = 0.0f;
+    constexpr int PF = 8;
+    float vn[PF];
+#pragma unroll
+    for (int i = 0; i < PF; i++) vn[i] = i < np_min ? __ldg(V + (size_t)i * HD) : 0.0f;
+    int p = 0;
+    for (; p + PF <= np_min; p += PF) {
+        float vc[PF];
+#pragma unroll
+        for (int i = 0; i < PF; i++) {
+            vc[i] = vn[i];
+            const int pn = p + PF + i;
+            vn[i] = pn < np_min ? __ldg(V + (size_t)pn * HD) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < PF; i++) {
+            const float4 *a4 = reinterpret_cast<const float4 *>(att + (size_t)(p + i) * QS);
+#pragma unroll
+            for (int j = 0; j < QS / 4; j++) {
+                const float4 a = a4[j];
+                acc[4 * j] = madd(acc[4 * j], a.x, vc[i]);
+                acc[4 * j + 1] = madd(acc[4 * j + 1], a.y, vc[i]);
+                acc[4 * j + 2] = madd(acc[4 * j + 2], a.z, vc[i]);
+                acc[4 * j + 3] = madd(acc[4 * j + 3], a.w, vc[i]);
+            }
+        }
+    }
+    for (; p < np_max; p++) {
+        const float v = __ldg(V + (size_t)p * HD);
+        const float4 *a4 = reinterpret_cast<const float4 *>(att + (size_t)p * QS);
+#pragma unroll
+        for (int j = 0; j < QS / 4; j++) {
+            const float4 a = a4[j];
+            const float aq[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const int q = 4 * j + r;
+                if (q < Q && p < pos0 + q / G + 1) acc[q] = madd(acc[q], aq[r], v);
+            }
+        }
+    }
+
+    // 4. gate and A8: warp w's 32 columns are one block of each query's output row
+    const int nbo = out.cols >> 5;
+#pragma unroll
+    for (int q = 0; q < QS; q++) {
+        if (q >= Q) break;
+        const int h = g * G + q % G, row = st->row0 + t0 + q / G;
+        const float gate = y[(size_t)row * d.ldy + (size_t)2 * HD * h + HD + tid];
+        const float o = __fmul_rn(acc[q], pf_sigmoid(gate));
+        const int col = h * HD + warp * 32;
+        quant_block_warp(o, lane, out.q + (size_t)row * out.cols + col, out.d + (size_t)row * nbo + (col >> 5),
+                         out.fs + (size_t)row * nbo + (col >> 5));
+    }
+}
+
 // Gated DeltaNet layer, latency-oriented form of k_deltanet with identical per-element
 // arithmetic (same citations). Differences are scheduling only:
 //  - one cp.async batch brings this key head's q / k / v / z / b / a rows of every token into
@@ -2712,12 +2878,23 @@ bool attn4_ok(const AttnDims &d) {
     return d.hd == kAttnHd && G > 0 && d.nq % d.nkv == 0 && G <= kAttnQ && kAttnQ % G == 0 &&
            attn4_smem(d.max_ctx) <= (size_t)attn4_lim;
 }
+bool attn5_ok(const AttnDims &d) {
+    static const int attn5_lim = dyn_smem_limit(k_attn5);
+    const int G = d.nkv > 0 ? d.nq / d.nkv : 0;
+    return d.hd == kAttnHd && G > 0 && d.nq % d.nkv == 0 && G <= kAttnQ && kAttnQ % G == 0 &&
+           attn5_smem(d.max_ctx) <= (size_t)attn5_lim;
+}
 bool attn_batch_ok(const AttnDims &d) {
     static const int attn3_lim = dyn_smem_limit(k_attn3);
     return d.hd == kAttnHd && attn3_smem(d.max_ctx) <= (size_t)attn3_lim;
 }
 void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
                  const Step *st, Act out, cudaStream_t s, int nseq) {
+    if (nseq > 1 && attn5_ok(d)) {   // one CTA per (sequence, KV group, rows): many in flight
+        const int QR = kAttnQ / (d.nq / d.nkv), nch = (d.rps + QR - 1) / QR;
+        launch_k(k_attn5, dim3(d.nkv * nch, nseq), kAttnHd, attn5_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
+        return;
+    }
     if (nseq > 1 && attn4_ok(d)) {   // grouped queries share the K / V reads
         const int QR = kAttnQ / (d.nq / d.nkv), nch = (d.rps + QR - 1) / QR;
         launch_k(k_attn4, dim3(kAttnCL, d.nkv * nch, nseq), kAttnHd, attn4_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
@@ -2842,6 +3019,7 @@ int kernels_init(int max_ctx, int hd, int rep) {
         raise_smem(k_attn2, attn2_smem(max_ctx));
         raise_smem(k_attn3, attn3_smem(max_ctx));
         raise_smem(k_attn4, attn4_smem(max_ctx));
+        raise_smem(k_attn5, attn5_smem(max_ctx));
     }
     if (gemm_init() != 0) return -1;
     return cudaGetLastError() == cudaSuccess ? 0 : -1;
