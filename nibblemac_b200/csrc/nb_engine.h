@@ -145,7 +145,7 @@ void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int 
 void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s);
 // nseq > 1 needs the fast kernel's shape (deltanet_batch_ok)
 void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
-                     Step *st, Act out, cudaStream_t s, int nseq = 1);
+                     Step *st, Act out, cudaStream_t s, int nseq = 1, int rps = kMaxRows);
 bool deltanet_batch_ok(const LinDims &d);
 // attention grids cover d.rps rows of each of nseq sequences; nseq > 1 needs the cluster kernel
 // (attn_batch_ok)

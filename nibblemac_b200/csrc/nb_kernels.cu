@@ -2152,7 +2152,9 @@ __device__ __forceinline__ void ld8(float (&v)[8], const float *p) {
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-template <int KC>
+// NR: the most rows a pass may have (the shared-memory row buffers; a 4-row variant serves
+// multi-sequence verify passes, where a smaller footprint fits three CTAs on an SM)
+template <int KC, int NR = kMaxRows>
 __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, const float *y, Step *st,
                                                       Act out) {
     constexpr int S = KC - 1;
@@ -2193,7 +2195,8 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     pdl_wait();
     pdl_trigger();
     const int n = st->n;
-    if (n <= 0) {   // nothing to do: let the state copy land before this CTA's shared memory goes
+    if (n <= 0 || n > NR) {   // nothing to do (or more rows than this variant holds: reported):
+        if (n > NR && j == 0) st->status = -92;   // let the state copy land before the CTA's smem goes
         mbar_wait(&sbar[1], 0);
         return;
     }
@@ -2203,9 +2206,9 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     conv_load_log(cq, L, C, pend_conv);
     conv_load_log(ck, L, C, pend_conv);
     conv_load_log(cv, L, C, pend_conv);
-    __shared__ __align__(16) float sq[kMaxRows][kDK], sk[kMaxRows][kDK], sv[kMaxRows][kDV];
-    __shared__ __align__(16) float sz[kMaxRows][kDV], so[kMaxRows][kDV];
-    __shared__ float sbeta[kMaxRows], sdec[kMaxRows], srn[kMaxRows];
+    __shared__ __align__(16) float sq[NR][kDK], sk[NR][kDK], sv[NR][kDV];
+    __shared__ __align__(16) float sz[NR][kDV], so[NR][kDV];
+    __shared__ float sbeta[NR], sdec[NR], srn[NR];
     __shared__ __align__(16) float skp[kMaxReplay][kDK];
     __shared__ float spd[kMaxReplay];
     const size_t logw = (size_t)kDK + kDV + 1;
@@ -2234,9 +2237,9 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     }
     float *rec = L.rec + (size_t)h * kDK * kDV + j;
     float *Sj = Ssm + j;   // column j: Sj[i * kDV]
-    // ---- gates of token t on thread kDV - kMaxRows + t (warp 3), while the state streams in
-    if (j >= kDV - kMaxRows && j - (kDV - kMaxRows) < n) {
-        const int t = j - (kDV - kMaxRows);
+    // ---- gates of token t on thread kDV - NR + t (warp 3), while the state streams in
+    if (j >= kDV - NR && j - (kDV - NR) < n) {
+        const int t = j - (kDV - NR);
         const float *yr = y + (size_t)(row0 + t) * d.ldy;
         const float b = yr[C + d.vd + h], a = yr[C + d.vd + d.nv + h];
         sbeta[t] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-b)));
@@ -2859,9 +2862,12 @@ bool deltanet_batch_ok(const LinDims &d) {
            d.ss_rec % 4 == 0;
 }
 void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
-                     Step *st, Act out, cudaStream_t s, int nseq) {
+                     Step *st, Act out, cudaStream_t s, int nseq, int rps) {
     if (deltanet_batch_ok(d) && ((uintptr_t)y & 15) == 0 && ((uintptr_t)L.rec & 15) == 0) {
-        launch_k(k_deltanet2<4>, dim3(d.nk, nseq), kDV, sizeof(float) * kDK * kDV, s, L, d, y, st, out);
+        if (nseq > 1 && rps <= 4)
+            launch_k(k_deltanet2<4, 4>, dim3(d.nk, nseq), kDV, sizeof(float) * kDK * kDV, s, L, d, y, st, out);
+        else
+            launch_k(k_deltanet2<4>, dim3(d.nk, nseq), kDV, sizeof(float) * kDK * kDV, s, L, d, y, st, out);
         return;
     }
     if (nseq != 1) return;   // callers check deltanet_batch_ok first
@@ -3014,6 +3020,7 @@ int kernels_init(int max_ctx, int hd, int rep) {
     raise_smem(k_mv_panel<4, 3, true>);
     if (max_ctx > 0) {
         raise_smem(k_deltanet2<4>, sizeof(float) * kDK * kDV);
+        raise_smem(k_deltanet2<4, 4>, sizeof(float) * kDK * kDV);
         raise_smem(k_deltanet, deltanet_smem(rep));
         raise_smem(k_attn, ((size_t)hd + max_ctx) * sizeof(float));
         raise_smem(k_attn2, attn2_smem(max_ctx));
