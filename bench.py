@@ -335,6 +335,54 @@ def run_config4(args, rank: int, world: int, local: int) -> None:
         dist.destroy_process_group()
 
 
+def run_profile_gemm(n: int) -> None:
+    """The tensor-core GEMM through the kernel ABI on the config-1 matrix shape, for ncu."""
+    import torch
+    from nibblemac_b200._lib import load_library
+    lib = load_library()
+    rows, cols = 3584, 1024
+    h = lib.nb_mv_create(rows, cols, n)
+    assert h, lib.last_error()
+    g = torch.Generator(device="cpu").manual_seed(1)
+    w = torch.randint(0, 255, (lib.nb_q4k_panel_bytes(rows, cols),), dtype=torch.uint8, generator=g).cuda()
+    x = torch.randn(n, cols, generator=g).cuda()
+    y = torch.zeros(n, rows, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.nb_mv_set_n(h, n, s) == 0 and lib.nb_mv_quant(h, x.data_ptr(), s) == 0
+    assert lib.nb_mv_prepare(h, w.data_ptr(), None, s) == 0
+    for _ in range(5):
+        assert lib.nb_mv_gemm(h, 0, y.data_ptr(), None, None, None, None, None, s) == 0
+    torch.cuda.synchronize()
+    assert lib.nb_mv_status(h) == 0
+    lib.nb_mv_destroy(h)
+
+
+def run_profile_batch(nseq: int, ntok: int) -> None:
+    """Config-4 style batch generation for ncu: plain and warm-up runs, then one k = 3 run
+    inside cudaProfilerStart/Stop."""
+    import torch
+    from nibblemac_b200.model import Model
+    path = model_path(0, None)
+    max_ctx = 1024 + GEN4 + 16
+    base = Model(path, max_ctx=max_ctx)
+    b = base.batch(nseq, max_ctx, max_k=K_DRAFT)
+    rng = np.random.default_rng(777)
+    lens = rng.integers(32, 1025, nseq)
+    prompts = [rng.integers(0, base.n_vocab, int(n)).astype(np.int32) for n in lens]
+    greedy, _, _, _ = b.generate_synthetic(prompts, ntok)
+    pad = [g + [0] * (ntok - len(g)) for g in greedy]
+    args = (prompts, ntok, K_DRAFT, pad, list(range(nseq)), P_MAIN)
+    b.generate_synthetic(*args)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    toks, _, status, _ = b.generate_synthetic(*args)
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    assert status == [0] * nseq and toks == greedy
+    b.close()
+    base.close()
+
+
 def run_config5(args, rank: int, world: int, local: int) -> None:
     """the 2B-shaped model, k = 3 at p = 0.8 on a 4096-token context, the
     LM head vocab-sharded over the `world` GPUs with the argmax merged by one NCCL all-reduce
@@ -420,7 +468,20 @@ def main() -> None:
     ap.add_argument("--profile", action="store_true",
                     help="setup, then exactly one generation inside cudaProfilerStart/Stop (for "
                          "ncu --profile-from-start off); prints nothing else")
+    ap.add_argument("--profile-gemm", type=int, default=0, metavar="N",
+                    help="the tensor-core GEMM on the config-1 matrix (3584 x 1024) over N activation "
+                         "rows through the kernel ABI: prepare once, then 5 launches (for ncu -k)")
+    ap.add_argument("--profile-batch", type=int, nargs=2, default=None, metavar=("SEQS", "TOKENS"),
+                    help="config-4 prompts (bench seed) for SEQS sequences: one plain and one warm-up "
+                         "batch generation of TOKENS tokens at k = 3, then one inside "
+                         "cudaProfilerStart/Stop")
     args = ap.parse_args()
+    if args.profile_gemm:
+        run_profile_gemm(args.profile_gemm)
+        return
+    if args.profile_batch:
+        run_profile_batch(*args.profile_batch)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
