@@ -98,9 +98,15 @@ struct pinfer_ctx {
     Mat mtp_head;                              // the head's first nv rows (draft vocabulary)
     cudaGraphExec_t round_graph_mtp[PINFER_SPEC_MAX_K + 1] = {};
     int graph_nv[PINFER_SPEC_MAX_K + 1] = {};
+    int graph_ng[PINFER_SPEC_MAX_K + 1] = {};   // n-gram draft limit the MTP graph was sized for
 
     // graphs of one verify round per draft depth k (index k), no graph = not captured yet
     cudaGraphExec_t round_graph[PINFER_SPEC_MAX_K + 1] = {};
+    cudaGraphExec_t round_graph_ng[PINFER_SPEC_MAX_K + 1] = {};   // n-gram drafts without MTP, by limit
+
+    // prompt lookup: the device history's length and indexed prefix after the last generation
+    int *ng_hist = nullptr, *ng_tab = nullptr;
+    int ng_cap = 0, ng_bits = 0, ng_n = 0, ng_idx = 0;
 
     // vocab-sharded LM head (pinfer_b200_shard_head): this GPU's rows [head_row0, +head_view.rows)
     int device = 0;

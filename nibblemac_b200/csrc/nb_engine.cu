@@ -320,6 +320,22 @@ int alloc_state(pinfer_ctx *c) {
         (rc = c->dalloc(&c->nan0, sizeof(int) * kMaxRows)) || (rc = c->dalloc(&c->step, sizeof(Step))))
         return rc;
     c->act_h.cols = c->H;
+    // prompt-lookup history and index (ngram.c pf_ngram_init: capacity max_ctx + 1, tables of
+    // 2^bits entries, 2^bits >= 2 x capacity, 10 <= bits <= 24)
+    c->ng_cap = c->max_ctx + 1;
+    c->ng_bits = 10;
+    while (c->ng_bits < 24 && (1 << c->ng_bits) < 2 * c->ng_cap) c->ng_bits++;
+    if ((rc = c->dalloc(&c->ng_hist, sizeof(int) * (size_t)c->ng_cap)) ||
+        (rc = c->dalloc(&c->ng_tab, sizeof(int) * ((size_t)3 << c->ng_bits))))
+        return rc;
+    {
+        const int dims[2] = {c->ng_cap, c->ng_bits};
+        int *const ptrs[2] = {c->ng_hist, c->ng_tab};
+        static_assert(offsetof(Step, ng_bits) == offsetof(Step, hist_cap) + sizeof(int), "adjacent fields");
+        static_assert(offsetof(Step, ng_tab) == offsetof(Step, hist) + sizeof(int *), "adjacent fields");
+        CUDA_OK(cudaMemcpy(&c->step->hist_cap, dims, sizeof dims, cudaMemcpyHostToDevice));
+        CUDA_OK(cudaMemcpy(&c->step->hist, ptrs, sizeof ptrs, cudaMemcpyHostToDevice));
+    }
     CUDA_OK(cudaMallocHost(&c->h_step, sizeof(Step)));
     memset(c->h_step, 0, sizeof(Step));
 
@@ -480,17 +496,21 @@ int ensure_out(pinfer_ctx *c, int n_max) {
     return PINFER_OK;
 }
 
-int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int nv = 0) {
-    if (drafter == 1 && c->round_graph_mtp[k] && c->graph_nv[k] != nv) {
+// The graph of one round at draft depth k (drafter 0: synthetic drafts or none, 1: the MTP
+// head) with n-gram drafts of up to `ngram` tokens: the verify pass holds max(k, ngram) + 1 rows.
+int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int nv = 0, int ngram = 0) {
+    if (drafter == 1 && c->round_graph_mtp[k] && (c->graph_nv[k] != nv || c->graph_ng[k] != ngram)) {
         cudaGraphExecDestroy(c->round_graph_mtp[k]);
         c->round_graph_mtp[k] = nullptr;
     }
-    cudaGraphExec_t &slot = drafter == 1 ? c->round_graph_mtp[k] : c->round_graph[k];
+    cudaGraphExec_t &slot = drafter == 1 ? c->round_graph_mtp[k]
+                                         : (ngram > 0 ? c->round_graph_ng[ngram] : c->round_graph[k]);
     if (slot) {
         *out = slot;
         return PINFER_OK;
     }
-    const int nmax = k + 1 <= 1 ? 1 : k + 1 <= 4 ? 4 : k + 1 <= 8 ? 8 : 16;
+    const int rows = std::max(k, ngram) + 1;
+    const int nmax = rows <= 1 ? 1 : rows <= 4 ? 4 : rows <= 8 ? 8 : 16;
     cudaStream_t s = c->stream;
     cudaGraph_t g;
     CUDA_OK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
@@ -518,8 +538,11 @@ int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int
     CUDA_OK(cudaGraphInstantiate(&ex, g, 0));
     cudaGraphDestroy(g);
     slot = ex;
-    if (drafter == 1) c->graph_nv[k] = nv;
-    c->round_nmax[k] = nmax;
+    if (drafter == 1) {
+        c->graph_nv[k] = nv;
+        c->graph_ng[k] = ngram;
+    }
+    if (drafter == 0 && ngram == 0) c->round_nmax[k] = nmax;
     *out = ex;
     return PINFER_OK;
 }
@@ -528,6 +551,8 @@ void drop_graphs(pinfer_ctx *c) {
     for (auto &g : c->round_graph)
         if (g) { cudaGraphExecDestroy(g); g = nullptr; }
     for (auto &g : c->round_graph_mtp)
+        if (g) { cudaGraphExecDestroy(g); g = nullptr; }
+    for (auto &g : c->round_graph_ng)
         if (g) { cudaGraphExecDestroy(g); g = nullptr; }
 }
 
@@ -582,7 +607,34 @@ struct GenRequest {
     float decode_ms;          // device time of the round loop (events on the context's stream)
     int drafter = 0;          // 0 synthetic drafts, 1 the MTP head
     int nv = 0;               // MTP draft vocabulary
+    int ngram = 0;            // longest n-gram (prompt-lookup) draft, 0 = none
+    long long ng_stats[3] = {0, 0, 0};
 };
+
+// The n-gram history before a prompt is fed (pf_spec_prefill, spec.c:163-171): the fed tokens
+// plus the last emitted one, which a continuation prompt leads with, so a continuation drops
+// that token and appends the prompt; any other context (a fresh start, pinfer_eval, a loaded
+// state) is not described by the history, which starts anew with the prompt.
+int ngram_prefill(pinfer_ctx *c, const int32_t *prompt, int n, int append, int base) {
+    if (!c->ng_hist) return PINFER_OK;
+    if (append && c->ng_n == base + 1) {
+        c->ng_n--;
+        c->ng_idx = std::min(c->ng_idx, c->ng_n);   // stale entries fail the checks
+    } else {
+        c->ng_n = c->ng_idx = 0;
+        CUDA_OK(cudaMemsetAsync(c->ng_tab, 0, sizeof(int) * ((size_t)3 << c->ng_bits), c->stream));
+    }
+    const int m = std::min(n, c->ng_cap - c->ng_n);
+    if (m > 0) {
+        CUDA_OK(cudaMemcpyAsync(c->ng_hist + c->ng_n, prompt, sizeof(int) * (size_t)m, cudaMemcpyHostToDevice,
+                                c->stream));
+        c->ng_n += m;
+    }
+    const int v[2] = {c->ng_n, c->ng_idx};
+    static_assert(offsetof(Step, hist_idx) == offsetof(Step, hist_n) + sizeof(int), "adjacent fields");
+    CUDA_OK(cudaMemcpyAsync(&c->step->hist_n, v, sizeof v, cudaMemcpyHostToDevice, c->stream));
+    return sync(c);   // v lives on this stack frame
+}
 
 // Generation (generate / pf_spec_prefill / pf_spec_decode, spec.c:153-416): prefill, then
 // rounds of [verify pass, argmax, greedy acceptance, commit, next drafts] replayed from one
@@ -613,7 +665,9 @@ int generate_impl(pinfer_ctx *c, GenRequest *r, int *status) {
     g.p24 = r->p24;
     g.seed = r->seed;
     g.drafter = r->drafter;
+    g.ngram = r->ngram;
     if (host_loop) g.eos = -1;   // the host decides when to stop (one token per round)
+    if ((rc = ngram_prefill(c, r->prompt, r->n_prompt, r->append, c->n_past))) return *status = rc;
     launch_set_gen(c->step, g, c->stream);
     if (r->drafter == 1) {
         set_mtp_head(c, r->nv);
@@ -623,7 +677,7 @@ int generate_impl(pinfer_ctx *c, GenRequest *r, int *status) {
     }
     launch_gen_start(c->step, c->d_greedy, c->d_out, c->stream);
     cudaGraphExec_t ex;
-    if ((rc = round_graph(c, r->k, &ex, r->drafter, r->nv))) return *status = rc;
+    if ((rc = round_graph(c, r->k, &ex, r->drafter, r->nv, r->ngram))) return *status = rc;
     int count = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     cudaEventCreate(&ev0);
@@ -671,6 +725,11 @@ int generate_impl(pinfer_ctx *c, GenRequest *r, int *status) {
     r->stats[0] = c->h_step->rounds;
     r->stats[1] = c->h_step->drafted;
     r->stats[2] = c->h_step->accepted;
+    r->ng_stats[0] = c->h_step->ng_rounds;
+    r->ng_stats[1] = c->h_step->ng_drafted;
+    r->ng_stats[2] = c->h_step->ng_accepted;
+    c->ng_n = c->h_step->hist_n;
+    c->ng_idx = c->h_step->hist_idx;
     *status = c->h_step->status;
     c->n_past = c->h_step->pos0;
     if (r->drafter == 1) c->mtp_rows = c->n_past;   // every committed row had its MTP pass
@@ -820,10 +879,10 @@ static int generate_api(pinfer_ctx *c, const int32_t *prompt, int n_prompt, int3
     if (sp && (sp->k < 0 || sp->k > PINFER_SPEC_MAX_K || sp->ngram < 0 || sp->ngram > PINFER_SPEC_MAX_K))
         return *status = PINFER_E_ARG;
     if (sp && sp->k > 0 && c && !(c->has_mtp && c->mtp_ok)) return *status = PINFER_E_FORMAT;
-    // k > 0: drafts from the MTP head, k per round (pf_spec_decode). Prompt-lookup (n-gram)
-    // drafts and the adaptive policy are not built: such requests draft with the MTP head at a
-    // fixed k, or decode plainly when k = 0; the tokens are the same either way (the output
-    // never depends on the drafts, pinfer.h:70-73), only the statistics differ.
+    // k > 0: drafts from the MTP head, k per round (pf_spec_decode); ngram > 0: prompt-lookup
+    // drafts of up to ngram tokens where the history's tail occurred before (with or without the
+    // MTP head). The adaptive policy is not built: such requests draft at the fixed k (the
+    // tokens are the same either way, pinfer.h:70-73; only the statistics can differ).
     GenRequest r{prompt, n_prompt, out, n_max, 0, nullptr, 0, 0, opts, append, {0, 0, 0}, 0.0f};
     if (sp && sp->k > 0) {
         r.k = sp->k;
@@ -831,11 +890,15 @@ static int generate_api(pinfer_ctx *c, const int32_t *prompt, int n_prompt, int3
         const int v = sp->draft_vocab;   // spec.c:88-91
         r.nv = v >= 4 && v < c->vocab ? (v & ~3) : c->vocab;
     }
+    if (sp) r.ngram = sp->ngram;
     const int n = generate_impl(c, &r, status);
-    if (stats && n >= 0 && r.k > 0) {   // accumulated, never reset (pinfer.h:110-116)
+    if (stats && n >= 0 && (r.k > 0 || r.ngram > 0)) {   // accumulated, never reset (pinfer.h:110-116)
         stats->rounds += r.stats[0];
         stats->drafted += r.stats[1];
         stats->accepted += r.stats[2];
+        stats->ngram_rounds += r.ng_stats[0];
+        stats->ngram_drafted += r.ng_stats[1];
+        stats->ngram_accepted += r.ng_stats[2];
     }
     return n;
 }

@@ -68,10 +68,18 @@ struct Step {
     int mtp_d1;
     int last_pos, last_e;
     int last_tok[kMaxRows];
+    // prompt lookup (n-gram drafts, engine/src/ngram.c): the history of fed and emitted tokens
+    // and its hash index, on the device
+    int ngram;             // longest n-gram draft (0: none)
+    int use_ng;            // the coming round drafts from the history
+    int hist_n, hist_idx;  // tokens in the history; n-grams ending before hist_idx are indexed
+    int hist_cap, ng_bits;
+    int *hist, *ng_tab;    // [hist_cap], [3][1 << ng_bits]: end position + 1, 0 = empty
+    long long ng_rounds, ng_drafted, ng_accepted;
 };
 
 struct GenArgs {
-    int n_max, k, eos, n_stop, max_ctx, vocab, drafter;
+    int n_max, k, eos, n_stop, max_ctx, vocab, drafter, ngram;
     int stop_ids[8];
     unsigned p24;
     unsigned long long seed;

@@ -1287,6 +1287,9 @@ __global__ void k_set_gen(Step *st, GenArgs g, const unsigned long long *seeds) 
     st->done = 0;
     st->status = 0;
     st->drafter = g.drafter;
+    st->ngram = g.ngram;
+    st->use_ng = 0;
+    st->ng_rounds = st->ng_drafted = st->ng_accepted = 0;
     st->last_e = 0;
 }
 
@@ -2516,7 +2519,7 @@ __global__ void k_mtp_chain_set(const Step *st, Step *ms, int s) {
     pdl_trigger();
     if (threadIdx.x != 0) return;
     const int n = st->n;
-    ms->n = (n > 0 && s < n - 1) ? 1 : 0;
+    ms->n = (n > 0 && !st->use_ng && s < n - 1) ? 1 : 0;
     ms->pos0 = st->pos0 - 1 + s;
     ms->tokens[0] = st->tokens[s];
     ms->logged = 0;
@@ -2540,6 +2543,8 @@ __global__ void k_mtp_pending_set(const Step *st, Step *ms) {
     for (int t = 0; t < e && t < kMaxRows; t++) ms->tokens[t] = st->last_tok[t];
     ms->logged = 0;
 }
+__device__ void plan_round(Step *st, const int *greedy);   // below, with the generation control
+
 // Its last row drafts the next round's first token; its m seeds the next chain.
 __global__ void k_mtp_pending_take(Step *st, const Step *ms, const float *mrows, float *mcur, int H) {
     pdl_wait();
@@ -2547,9 +2552,8 @@ __global__ void k_mtp_pending_take(Step *st, const Step *ms, const float *mrows,
     const int n = ms->n;
     if (n <= 0) return;
     if (threadIdx.x == 0) {
-        const int d1 = ms->argmax[n - 1];
-        st->mtp_d1 = d1;
-        if (st->n >= 2) st->tokens[1] = d1;
+        st->mtp_d1 = ms->argmax[n - 1];
+        if (!st->done && st->logged) plan_round(st, nullptr);   // verify rounds: the next round
     }
     for (int i = threadIdx.x; i < H; i += blockDim.x) mcur[i] = mrows[(size_t)(n - 1) * H + i];
 }
@@ -2586,8 +2590,63 @@ __device__ __forceinline__ int emit_tok(Step *st, int *out, int tok) {
     return stop;
 }
 
-// Shape of the next round (spec.c:285-293): never draft past n_max or the context.
-__device__ void prepare_round(Step *st, const int *greedy) {
+// ---- prompt lookup (engine/src/ngram.c, restated): one direct-mapped hash table per n-gram
+// length 2..4 maps an n-gram of the token history to the position where it most recently
+// ended (+1); new positions are indexed lazily by the next lookup; every hit is verified
+// against the history, so a collision can only lose a match. The hash (FNV-1 offset basis
+// mixed with the length, golden-ratio multiplier) and the table size (2^bits >= 2 x capacity,
+// 10 <= bits <= 24) are the reference's, so its drafts and ours coincide.
+constexpr int kNgMin = 2, kNgMax = 4, kNgExt = 32;
+constexpr int kNgTrust = 16, kNgAsk = 4, kNgShort = 3;   // spec.h PF_NG_TRUST / ASK / SHORT
+
+__device__ __forceinline__ uint32_t ng_hash(const int *t, int n, int bits) {
+    uint32_t h = 0x811C9DC5u ^ (uint32_t)n;
+    for (int i = 0; i < n; i++) h = (h ^ (uint32_t)t[i]) * 0x9E3779B1u;
+    return h >> (32 - bits);
+}
+// append a token (past the capacity it is dropped: drafting only gets weaker)
+__device__ __forceinline__ void ng_push(Step *st, int tok) {
+    if (st->hist && st->hist_n < st->hist_cap) st->hist[st->hist_n++] = tok;
+}
+// index the n-grams that end at positions [hist_idx, upto)
+__device__ void ng_index(Step *st, int upto) {
+    for (int q = st->hist_idx; q < upto; q++)
+        for (int n = kNgMin; n <= kNgMax && n <= q + 1; n++)
+            st->ng_tab[((size_t)(n - kNgMin) << st->ng_bits) + ng_hash(st->hist + q - n + 1, n, st->ng_bits)] = q + 1;
+    if (upto > st->hist_idx) st->hist_idx = upto;
+}
+// up to max tokens that followed the most recent earlier occurrence of the longest matching
+// tail n-gram; *match = how far back the two occurrences agree (n .. kNgExt)
+__device__ int ng_draft(Step *st, int *out, int max, int *match) {
+    const int n = st->hist_n;
+    *match = 0;
+    if (!st->hist || max <= 0 || n < kNgMin + 1) return 0;
+    ng_index(st, n - 1);   // earlier occurrences end before the tail's last token
+    for (int k = kNgMax; k >= kNgMin; k--) {
+        if (k > n - 1) continue;
+        const int *tail = st->hist + n - k;
+        const int q = st->ng_tab[((size_t)(k - kNgMin) << st->ng_bits) + ng_hash(tail, k, st->ng_bits)] - 1;
+        if (q < k - 1 || q >= n - 1) continue;
+        bool same = true;
+        for (int i = 0; i < k && same; i++) same = st->hist[q - k + 1 + i] == tail[i];
+        if (!same) continue;
+        const int m = n - 1 - q < max ? n - 1 - q : max;
+        for (int i = 0; i < m; i++) out[i] = st->hist[q + 1 + i];
+        int e = k;
+        while (e < kNgExt && q - e >= 0 && st->hist[q - e] == st->hist[n - 1 - e]) e++;
+        *match = e;
+        return m;
+    }
+    return 0;
+}
+
+// Shape and drafts of the next round (spec.c:280-321): never draft past n_max or the context;
+// the n-gram draft when the history's tail occurred before and the match is trusted
+// (ngram_pick, spec.c:138-151: a match of >= PF_NG_TRUST tokens in full; a shorter one only
+// without the MTP head, or when it extends >= PF_NG_ASK tokens and its first token is the MTP
+// head's d1, and then at most PF_NG_SHORT tokens); otherwise k drafts of the drafter. With the
+// MTP head this runs after the round's MTP pass, whose d1 it compares against.
+__device__ void plan_round(Step *st, const int *greedy) {
     int left = st->n_max - st->count - 1;
     const int room = st->max_ctx - st->pos0 - 1;
     if (left > room) left = room;
@@ -2597,9 +2656,25 @@ __device__ void prepare_round(Step *st, const int *greedy) {
         st->n = 0;
         return;
     }
-    const int ke = st->k < left ? st->k : left;
+    int d[kMaxRows];
+    int ke = 0, use_ng = 0;
+    if (st->ngram > 0 && left > 0) {
+        int match = 0;
+        const int mx = min(min(st->ngram, left), kMaxRows - 1);
+        const int nd = ng_draft(st, d, mx, &match);
+        if (nd > 0) {
+            if (match >= kNgTrust) ke = nd;
+            else if (st->k == 0) ke = nd < kNgShort ? nd : kNgShort;
+            else if (match >= kNgAsk && d[0] == st->mtp_d1) ke = nd < kNgShort ? nd : kNgShort;
+        }
+        use_ng = ke > 0;
+    }
+    if (!use_ng) ke = st->k < left ? st->k : left;
+    st->use_ng = use_ng;
     st->tokens[0] = st->cur;
-    if (st->drafter == 1) {
+    if (use_ng) {
+        for (int s = 1; s <= ke; s++) st->tokens[s] = d[s - 1];
+    } else if (st->drafter == 1) {
         // MTP drafts: d1 from the last MTP pass; drafts 2..ke come from this round's chain
         if (ke >= 1) st->tokens[1] = st->mtp_d1;
     } else {
@@ -2627,12 +2702,13 @@ __global__ void k_gen_start(Step *st, const int *greedy, int *out) {
     st->done = 0;
     st->status = 0;
     st->last_e = 0;
+    ng_push(st, st->cur);   // the history: fed tokens, then every emitted one
     if (emit_tok(st, out, st->cur)) {
         st->done = 1;
         st->n = 0;
         return;
     }
-    prepare_round(st, greedy);
+    plan_round(st, greedy);
 }
 
 // Greedy acceptance and commit of one verify pass (spec.c:337-351): the longest draft prefix
@@ -2670,15 +2746,22 @@ __global__ void k_accept(Step *st, const int *greedy, int *out) {
     st->wr ^= 1;
     st->pos0 += e;
     st->cur = vt[e];
+    for (int i = 1; i <= e; i++) ng_push(st, vt[i]);
     st->rounds++;
     st->drafted += ke;
     st->accepted += a;
+    if (st->use_ng) {
+        st->ng_rounds++;
+        st->ng_drafted += ke;
+        st->ng_accepted += a;
+    }
     if (done) {
         st->done = 1;
         st->n = 0;
         return;
     }
-    prepare_round(st, greedy);
+    // with the MTP head the next round is planned after this round's MTP pass (its d1)
+    if (st->drafter != 1) plan_round(st, greedy);
 }
 
 }  // namespace

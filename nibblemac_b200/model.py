@@ -89,13 +89,14 @@ class Model:
         return out
 
     def generate(self, prompt, n_max: int, k: int = 0, stop_ids=None, on_token=None,
-                 draft_vocab: int = 0, stats: SpecStats | None = None, append: bool = False
-                 ) -> tuple[list[int], int]:
+                 draft_vocab: int = 0, stats: SpecStats | None = None, append: bool = False,
+                 ngram: int = 0) -> tuple[list[int], int]:
         """pinfer_generate_greedy_ex (append: _cont): (tokens, status). k > 0 drafts with the
-        MTP head over the first draft_vocab ids (0: all); statistics accumulate into stats."""
+        MTP head over the first draft_vocab ids (0: all), ngram > 0 with prompt lookup;
+        statistics accumulate into stats."""
         t = _i32(prompt)
         out = np.zeros(n_max, np.int32)
-        sp = SpecParams(k, draft_vocab, 0, 0)
+        sp = SpecParams(k, draft_vocab, 0, ngram)
         st = stats if stats is not None else SpecStats()
         status = ctypes.c_int(0)
         opts = None

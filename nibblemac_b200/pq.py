@@ -205,20 +205,28 @@ def tensor_values(name: str, kind: str, shape: list[int], seed: int, std: float)
     return (rng.standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(np.float32)
 
 
-def synth_tensors(d: Dims, seed: int, std: float = 0.02):
-    """Yield (name, dtype, shape, bytes) in the converter's order (sorted HF names)."""
+OUT_PROJ_NAMES = ("o_proj.weight", "out_proj.weight", "down_proj.weight")
+
+
+def synth_tensors(d: Dims, seed: int, std: float = 0.02, out_scale: float = 1.0):
+    """Yield (name, dtype, shape, bytes) in the converter's order (sorted HF names).
+    out_scale multiplies the std of the projections that write into the residual stream
+    (o_proj, out_proj, down_proj): small values give a model whose next token depends mostly
+    on the current one, so greedy decoding falls into cycles (test models for prompt lookup)."""
     specs = sorted(tensor_specs(d), key=lambda s: hf_name(s[0]))
     for name, kind, shape in specs:
-        v = tensor_values(name, kind, shape, seed, std)
+        sd = std * out_scale if name.endswith(OUT_PROJ_NAMES) else std
+        v = tensor_values(name, kind, shape, seed, sd)
         if kind == "mat":
             yield name, Q4K, shape, quantize_q4k(v)
         else:
             yield name, F32, shape, v.astype("<f4").tobytes()
 
 
-def make_synthetic(path: str | os.PathLike, d: Dims, seed: int = 0, std: float = 0.02) -> Path:
+def make_synthetic(path: str | os.PathLike, d: Dims, seed: int = 0, std: float = 0.02,
+                   out_scale: float = 1.0) -> Path:
     """Write a random-init, Q4K-quantised Qwen3.5-shaped model to `path`."""
-    write_pq(path, d, list(synth_tensors(d, seed, std)))
+    write_pq(path, d, list(synth_tensors(d, seed, std, out_scale)))
     return Path(path)
 
 

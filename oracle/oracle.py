@@ -175,13 +175,15 @@ class RefEngine:
             raise RuntimeError(f"reference generate: {n}")
         return out[:n].tolist()
 
-    def generate_mtp(self, prompt, n_max: int, k: int, draft_vocab: int = 0, append: bool = False):
-        """The reference's own speculative decoding with its MTP head (pinfer_generate_greedy_ex
-        / _cont, fixed k, no prompt lookup, no adaptive policy): (tokens, [rounds, drafted,
-        accepted], status)."""
+    def generate_mtp(self, prompt, n_max: int, k: int, draft_vocab: int = 0, append: bool = False,
+                     ngram: int = 0, all_stats: bool = False):
+        """The reference's own speculative decoding (pinfer_generate_greedy_ex / _cont): MTP
+        drafts at a fixed k, prompt-lookup drafts of up to `ngram` tokens, no adaptive policy:
+        (tokens, [rounds, drafted, accepted] (+ the three n-gram counts with all_stats),
+        status)."""
         t = np.ascontiguousarray(prompt, np.int32)
         out = np.zeros(n_max, np.int32)
-        sp = _SpecParams(k, draft_vocab, 0, 0)
+        sp = _SpecParams(k, draft_vocab, 0, ngram)
         st = _SpecStats()
         status = ctypes.c_int(0)
         fn = self.lib.pinfer_generate_greedy_cont if append else self.lib.pinfer_generate_greedy_ex
@@ -189,7 +191,10 @@ class RefEngine:
                ctypes.byref(status))
         if n < 0:
             raise RuntimeError(f"reference generate: {n}")
-        return out[:n].tolist(), [st.rounds, st.drafted, st.accepted], status.value
+        stats = [st.rounds, st.drafted, st.accepted]
+        if all_stats:
+            stats += [st.ngram_rounds, st.ngram_drafted, st.ngram_accepted]
+        return out[:n].tolist(), stats, status.value
 
     def spec_generate(self, prompt, n_max: int, k: int, greedy, seed: int, p: float):
         t = np.ascontiguousarray(prompt, np.int32)

@@ -40,13 +40,21 @@ def q4k_oracle():
     return Q4KOracle()
 
 
-def _model(name: str, seed: int, std: float) -> Path:
+def _model(name: str, seed: int, std: float, out_scale: float = 1.0) -> Path:
     from nibblemac_b200 import pq
     root = Path(os.environ.get("NB_MODEL_CACHE", ROOT / "_models"))
-    path = root / f"test-{name}-s{seed}-std{std}.pq"
+    tag = "" if out_scale == 1.0 else f"-out{out_scale}"
+    path = root / f"test-{name}-s{seed}-std{std}{tag}.pq"
     if not path.exists():
-        pq.make_synthetic(path, pq.PRESETS[name], seed, std=std)
+        pq.make_synthetic(path, pq.PRESETS[name], seed, std=std, out_scale=out_scale)
     return path
+
+
+@pytest.fixture(scope="session")
+def looping_model() -> Path:
+    """TINY dims with the residual-stream projections scaled down: greedy decoding repeats
+    itself, so prompt lookup finds matches."""
+    return _model("tiny", 3, TEST_STD, out_scale=0.02)
 
 
 @pytest.fixture(scope="session")

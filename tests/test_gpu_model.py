@@ -231,3 +231,41 @@ def test_mtp_speculation_matches_reference(pair, k, nv):
     toks2, _ = dev.generate(q, 24, k=k, draft_vocab=nv, stats=st2, append=True)
     rtoks2, rst2, _ = ref.generate_mtp(q, 24, k, nv, append=True)
     assert toks2 == rtoks2 and [st2.rounds, st2.drafted, st2.accepted] == rst2
+
+
+@pytest.fixture(scope="module")
+def looping_pair(looping_model):
+    from nibblemac_b200.model import Model
+    from oracle import RefEngine
+    dev = Model(looping_model, max_ctx=512)
+    ref = RefEngine(looping_model, max_ctx=512)
+    yield dev, ref
+    dev.close()
+    ref.close()
+
+
+@pytest.mark.parametrize("k,ngram", [(0, 3), (0, 7), (3, 4), (2, 7)])
+def test_ngram_drafts_match_reference(looping_pair, k, ngram):
+    """Prompt-lookup drafts (spec.c ngram_pick with ngram.c's index, alone at k = 0 or beside
+    the MTP head) on a model whose greedy output repeats itself: the plain greedy tokens and
+    exactly the reference's six statistics (n-gram rounds among them), then a continuation
+    (the history drops its last token and appends the new prompt)."""
+    from nibblemac_b200._lib import SpecStats
+    dev, ref = looping_pair
+    p = prompt(dev.n_vocab, 30, 90 + k + ngram)
+    dev.reset()
+    plain, _ = dev.generate(p, 48)
+    st = SpecStats()
+    toks, status = dev.generate(p, 48, k=k, stats=st, ngram=ngram)
+    rtoks, rst, rstatus = ref.generate_mtp(p, 48, k, ngram=ngram, all_stats=True)
+    assert status == rstatus == 0
+    assert toks == plain == rtoks
+    got = [st.rounds, st.drafted, st.accepted, st.ngram_rounds, st.ngram_drafted, st.ngram_accepted]
+    assert got == rst, f"k={k} ngram={ngram}: {got} vs {rst}"
+    assert rst[3] > 0, "the looping model should give n-gram rounds"
+    q = np.concatenate([[toks[-1]], p[5:20]]).astype(np.int32)
+    st2 = SpecStats()
+    toks2, _ = dev.generate(q, 40, k=k, stats=st2, append=True, ngram=ngram)
+    rtoks2, rst2, _ = ref.generate_mtp(q, 40, k, append=True, ngram=ngram, all_stats=True)
+    got2 = [st2.rounds, st2.drafted, st2.accepted, st2.ngram_rounds, st2.ngram_drafted, st2.ngram_accepted]
+    assert toks2 == rtoks2 and got2 == rst2, f"continuation: {got2} vs {rst2}"
