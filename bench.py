@@ -452,6 +452,82 @@ def run_config5(args, rank: int, world: int, local: int) -> None:
         dist.destroy_process_group()
 
 
+def run_config5_batch(args, rank: int, world: int, local: int) -> None:
+    """BASELINE configs[4] as configured: the 2B-shaped model, k = 3 at p = 0.8, 8 sequences of
+    a 4096-token context each in one multi-sequence batch (pinfer_b200_batch), the LM head
+    vocab-sharded over the `world` GPUs: every verify round of the 8 x 4 rows ends with one
+    NCCL all-reduce (max) of the per-row argmax keys. The same batch on every rank (the layers
+    are replicated), so the total work is fixed: strong scaling. A step is one batch generation
+    of N_GEN tokens per sequence; value = 8 x (N_GEN - 1) tokens / the device time of its verify
+    rounds (the prompts' prefill is outside it), max over ranks."""
+    import datetime
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=1800))
+    from nibblemac_b200.model import Model
+    path = model_path(rank, dist, "2b")
+    max_ctx = CTX5 + N_GEN + 16
+    m = Model(path, max_ctx=max_ctx)
+    if world > 1:
+        obj = [m.nccl_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        m.shard_head(rank, world, obj[0])
+    nseq = args.batch5
+    b = m.batch(nseq, max_ctx, max_k=K_DRAFT)
+    rng = np.random.default_rng(4321)   # the same contexts on every rank
+    prompts = [rng.integers(0, m.n_vocab, CTX5).astype(np.int32) for _ in range(nseq)]
+    greedy, _, status, _ = b.generate_synthetic(prompts, N_GEN)
+    assert status == [0] * nseq
+    pad = [g + [0] * (N_GEN - len(g)) for g in greedy]
+    tokens_per_step = sum(len(g) - 1 for g in greedy)
+
+    def step(i: int):
+        toks, st, status, ms = b.generate_synthetic(prompts, N_GEN, K_DRAFT, pad,
+                                                    [600 + 97 * i + j for j in range(nseq)], P_MAIN)
+        assert status == [0] * nseq and toks == greedy, "speculative output differs from plain greedy"
+        return ms, st
+
+    for i in range(args.warmup):
+        step(i)
+    if dist is not None:
+        dist.barrier()
+    ms_all, rounds = [], 0
+    with Clocks(local) as clk:
+        for i in range(args.steps):
+            ms, st = step(100 + i)
+            ms_all.append(ms)
+            rounds += b.rounds()
+    t_dev = sum(ms_all) / 1000.0
+    if dist is not None:
+        t = torch.tensor([t_dev], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_dev = float(t.item())
+    b.close()
+    m.close()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "greedy spec-decode tok/s (k=3), 2B shape, LM head vocab-sharded",
+            "value": round(tokens_per_step * args.steps / t_dev, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_dev * 1000.0 / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "q4k x int8 -> fp32",
+            "data": "synthetic (random-init 2B-shaped weights, uniform-random contexts, synthetic drafter)",
+            "config": {"workload": f"configs[4]: Qwen3.5-2B-shaped Q4K, k=3, p={P_MAIN}, {CTX5}-token "
+                                   f"contexts, {N_GEN} generated each, batch {nseq} (multi-sequence batch)",
+                       "head_rows_per_gpu": 248320 // world,
+                       "collective": (f"ncclAllReduce max of the per-row argmax keys per verify round"
+                                      if world > 1 else None),
+                       "verify_rounds_per_step": rounds // max(args.steps, 1)},
+            "clocks": clk.summary()}), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -462,6 +538,8 @@ def main() -> None:
     ap.add_argument("--config4", action="store_true",
                     help="BASELINE configs[3]: 256 requests per GPU in one multi-sequence batch "
                          "(one JSON line)")
+    ap.add_argument("--batch5", type=int, default=8,
+                    help="sequences of the --config5 batch (1: one context, the earlier form)")
     ap.add_argument("--config5", action="store_true",
                     help="BASELINE configs[4]: 2B shape, 4096-token context, LM head vocab-sharded "
                          "over the torchrun ranks (one JSON line, strong scaling)")
@@ -490,7 +568,10 @@ def main() -> None:
         run_reference(args, rank, world)
         return
     if args.config5:
-        run_config5(args, rank, world, local)
+        if args.batch5 > 1:
+            run_config5_batch(args, rank, world, local)
+        else:
+            run_config5(args, rank, world, local)
         return
     if args.config4:
         run_config4(args, rank, world, local)

@@ -53,6 +53,9 @@ struct pinfer_b200_batch {
     GemmMaps maps_h, maps_ol, maps_oa, maps_f;
     unsigned long long *partial = nullptr;
     int *nan0 = nullptr;
+    unsigned long long *keys = nullptr;   // vocab-sharded head: [2][rmax] per-row keys, merged by NCCL
+    bool sharded = false;
+    int row_base = 0;
     int *status = nullptr;
     Step *steps = nullptr, *h_steps = nullptr;
     SeqPass *d_pass = nullptr, *h_pass = nullptr;
@@ -108,6 +111,7 @@ void gemm(pinfer_b200_batch *b, int epi, const GemmMaps &maps, const GemmW &W, i
     g.ldy = ldy;
     g.partial = b->partial;
     g.nan0 = b->nan0;
+    g.row_base = epi == 4 ? b->row_base : 0;
     g.status = b->status;
     launch_gemm(epi, maps, g, b->stream);
 }
@@ -148,7 +152,16 @@ void enqueue_forward(pinfer_b200_batch *b, int R, int nseq, int rps, bool head) 
     if (head) {
         launch_norm_quant(b->x, c->norm, c->H, c->eps, b->steps, b->act_h, s, nseq, rps);
         gemm(b, 4, b->maps_h, b->head, R, nullptr, 0);
-        launch_argmax_final(b->partial, b->nan0, b->head.npanels, b->steps, s, nseq, rps);
+        if (!b->sharded) {
+            launch_argmax_final(b->partial, b->nan0, b->head.npanels, b->steps, s, nseq, rps);
+        } else {
+            // this GPU's vocabulary rows only: per-row best keys (global row indices), one
+            // all-reduce (max) across the shards, then tokens exactly as the unsharded path
+            launch_argmax_keys(b->partial, b->nan0, b->head.npanels, b->steps, b->keys, s, b->rmax, nseq, rps);
+            nccl_api(nullptr, 0)->all_reduce(b->keys, b->keys, 2 * (size_t)b->rmax, ncclUint64, ncclMax,
+                                             c->nccl, s);
+            launch_keys_argmax(b->keys, b->steps, s, b->rmax, nseq, rps);
+        }
     }
     launch_pass_end(b->steps, s, nseq);
 }
@@ -171,7 +184,9 @@ int batch_alloc(pinfer_b200_batch *b) {
             (rc = tile_mat(b, D.gate, D.up, &T.gu)) || (rc = tile_mat(b, D.down, none, &T.down)))
             return rc;
     }
-    if ((rc = tile_mat(b, c->head, Mat(), &b->head))) return rc;
+    b->sharded = c->shard_world > 1;
+    b->row_base = b->sharded ? c->head_row0 : 0;
+    if ((rc = tile_mat(b, b->sharded ? c->head_view : c->head, Mat(), &b->head))) return rc;
 
     // per-sequence states, strided by sequence
     const int cap = b->kmax + 1;
@@ -218,6 +233,7 @@ int batch_alloc(pinfer_b200_batch *b) {
         (rc = b->dalloc(&b->act_mid.fs, sizeof(float) * R * (mid / 32))) ||
         (rc = b->dalloc(&b->partial, sizeof(unsigned long long) * R * b->head.npanels)) ||
         (rc = b->dalloc(&b->nan0, sizeof(int) * R)) || (rc = b->dalloc(&b->status, sizeof(int))) ||
+        (rc = b->dalloc(&b->keys, sizeof(unsigned long long) * 2 * R)) ||
         (rc = b->dalloc(&b->steps, sizeof(Step) * S)) || (rc = b->dalloc(&b->d_seeds, sizeof(unsigned long long) * S)) ||
         (rc = b->dalloc(&b->d_ndone, sizeof(int))))
         return rc;
@@ -231,6 +247,7 @@ int batch_alloc(pinfer_b200_batch *b) {
     NB_CUDA_OK(cudaMemsetAsync(b->act_mid.q, 0, R * mid, b->stream));
     NB_CUDA_OK(cudaMemsetAsync(b->act_mid.d, 0, sizeof(float) * R * (mid / 32), b->stream));
     NB_CUDA_OK(cudaMemsetAsync(b->act_mid.fs, 0, sizeof(float) * R * (mid / 32), b->stream));
+    NB_CUDA_OK(cudaMemsetAsync(b->nan0, 0, sizeof(int) * R, b->stream));   // only vocabulary row 0's shard sets it
     if (gemm_maps(b->act_h, (int)R, &b->maps_h) || gemm_maps(with_cols(b->act_mid, c->vd), (int)R, &b->maps_ol) ||
         gemm_maps(with_cols(b->act_mid, c->nq * c->hd), (int)R, &b->maps_oa) ||
         gemm_maps(with_cols(b->act_mid, c->ffn), (int)R, &b->maps_f))
@@ -289,7 +306,7 @@ pinfer_b200_batch *pinfer_b200_batch_create(pinfer_ctx *ctx, int slots, int max_
     if (!err) err = &dummy;
     *err = PINFER_E_ARG;
     if (!ctx || slots < 1 || slots > 2048 || max_k < 0 || max_k >= kMaxRows || max_ctx < 2 ||
-        max_ctx > ctx->max_ctx || ctx->shard_world > 1)
+        max_ctx > ctx->max_ctx)
         return nullptr;
     if (cudaSetDevice(ctx->device) != cudaSuccess) {
         *err = PINFER_E_NOMEM;

@@ -149,8 +149,10 @@ void launch_argmax_final(const unsigned long long *partial, const int *nan0, int
 // vocab-sharded head: per-row best keys and NaN flags into keys [2][kMaxRows] (to be merged by
 // an all-reduce max across the shards), then the merged keys into Step::argmax
 void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int npanels, const Step *st,
-                        unsigned long long *keys, cudaStream_t s);
-void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s);
+                        unsigned long long *keys, cudaStream_t s, int kstride = kMaxRows, int nseq = 1,
+                        int rps = kMaxRows);
+void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s, int kstride = kMaxRows,
+                        int nseq = 1, int rps = kMaxRows);
 // nseq > 1 needs the fast kernel's shape (deltanet_batch_ok)
 void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
                      Step *st, Act out, cudaStream_t s, int nseq = 1, int rps = kMaxRows);

@@ -737,16 +737,20 @@ size_t panel_smem(int nw, int cols, int nmat, int nmax, bool norm) {
 // Vocab-sharded head: this GPU's best key per verify row and its row-0 NaN flag, for the
 // all-reduce (max) across the shards; k_keys_argmax turns the merged keys into tokens exactly
 // as k_argmax_final does.
+// keys: [best key of row r][NaN flag of row r] with the flags kstride after the keys; blockIdx.y
+// = the sequence of a multi-sequence pass (row r = its row0 + v)
 __global__ void k_argmax_keys(const unsigned long long *partial, const int *nan0, int npanels,
-                              const Step *st, unsigned long long *keys) {
+                              const Step *st, unsigned long long *keys, int kstride) {
     pdl_wait();
     pdl_trigger();
+    st += blockIdx.y;
     const int v = blockIdx.x;
     if (v >= st->n) return;
+    const int row = st->row0 + v;
     __shared__ unsigned long long red[32];
     unsigned long long best = 0ull;
     for (int i = threadIdx.x; i < npanels; i += blockDim.x) {
-        const unsigned long long k = partial[(size_t)v * npanels + i];
+        const unsigned long long k = partial[(size_t)row * npanels + i];
         best = k > best ? k : best;
     }
     best = warp_max_u64(best);
@@ -756,17 +760,19 @@ __global__ void k_argmax_keys(const unsigned long long *partial, const int *nan0
         unsigned long long b = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
         b = warp_max_u64(b);
         if (threadIdx.x == 0) {
-            keys[v] = b;
-            keys[kMaxRows + v] = nan0[v] ? 1ull : 0ull;
+            keys[row] = b;
+            keys[kstride + row] = nan0[row] ? 1ull : 0ull;
         }
     }
 }
-__global__ void k_keys_argmax(const unsigned long long *keys, Step *st) {
+__global__ void k_keys_argmax(const unsigned long long *keys, Step *st, int kstride) {
     pdl_wait();
     pdl_trigger();
+    st += blockIdx.x;   // the sequence of a multi-sequence pass
     const int v = threadIdx.x;
     if (v >= st->n) return;
-    st->argmax[v] = keys[kMaxRows + v] ? 0 : (int)(0xffffffffu - (uint32_t)(keys[v] & 0xffffffffu));
+    const int row = st->row0 + v;
+    st->argmax[v] = keys[kstride + row] ? 0 : (int)(0xffffffffu - (uint32_t)(keys[row] & 0xffffffffu));
 }
 
 __global__ void k_argmax_final(const unsigned long long *partial, const int *nan0, int npanels,
@@ -3015,11 +3021,11 @@ void launch_flush(const LinLayer *layers, int n_lin, const LinDims &d, Step *st,
     launch_k(k_clear_pending, nseq, 1, 0, s, st);
 }
 void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int npanels, const Step *st,
-                        unsigned long long *keys, cudaStream_t s) {
-    launch_k(k_argmax_keys, kMaxRows, 256, 0, s, partial, nan0, npanels, st, keys);
+                        unsigned long long *keys, cudaStream_t s, int kstride, int nseq, int rps) {
+    launch_k(k_argmax_keys, dim3(rps, nseq), 256, 0, s, partial, nan0, npanels, st, keys, kstride);
 }
-void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s) {
-    launch_k(k_keys_argmax, 1, kMaxRows, 0, s, keys, st);
+void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s, int kstride, int nseq, int rps) {
+    launch_k(k_keys_argmax, nseq, rps, 0, s, keys, st, kstride);
 }
 void launch_norm_rows(const float *x, const float *w, int H, float eps, const Step *st, float *out,
                       cudaStream_t s) {
