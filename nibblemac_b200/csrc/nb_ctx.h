@@ -99,6 +99,8 @@ struct pinfer_ctx {
     cudaGraphExec_t round_graph_mtp[PINFER_SPEC_MAX_K + 1] = {};
     int graph_nv[PINFER_SPEC_MAX_K + 1] = {};
     int graph_ng[PINFER_SPEC_MAX_K + 1] = {};   // n-gram draft limit the MTP graph was sized for
+    int graph_ad[PINFER_SPEC_MAX_K + 1] = {};   // the MTP graph holds the adaptive policy's kernels
+    int graph_ng_ad[PINFER_SPEC_MAX_K + 1] = {};
 
     // graphs of one verify round per draft depth k (index k), no graph = not captured yet
     cudaGraphExec_t round_graph[PINFER_SPEC_MAX_K + 1] = {};

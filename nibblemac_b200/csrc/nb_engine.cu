@@ -412,7 +412,7 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = fal
 // rows, ms->tokens the tokens that follow them, positions ms->pos0..; writes the MTP KV rows,
 // the normed outputs m (c->mrows) and, with head, the argmax over the draft vocabulary
 // (ms->argmax). Uses the main pass's scratch buffers, so it runs between main passes.
-void enqueue_mtp(pinfer_ctx *c, Step *ms, const float *h, int nmax, bool head) {
+void enqueue_mtp(pinfer_ctx *c, Step *ms, const float *h, int nmax, bool head, bool conf = false) {
     cudaStream_t s = c->stream;
     const auto &D = c->mtp_layer;
     launch_mtp_input(c->embed, h, ms, c->mtp_norm_emb, c->mtp_norm_hid, c->H, c->eps, c->act_cat, s);
@@ -428,13 +428,16 @@ void enqueue_mtp(pinfer_ctx *c, Step *ms, const float *h, int nmax, bool head) {
     launch_norm_rows(c->x, c->mtp_norm_out, c->H, c->eps, ms, c->mrows, s);   // m = mtp.norm(u)
     if (head) {
         if (nmax <= 4) {
-            launch_matvec_head_norm(c->mtp_head, c->x, c->mtp_norm_out, c->eps, ms, nullptr, c->vocab,
+            launch_matvec_head_norm(c->mtp_head, c->x, c->mtp_norm_out, c->eps, ms, conf ? c->logits : nullptr, c->vocab,
                                     c->partial, c->nan0, nmax, s);
         } else {
             launch_norm_quant(c->x, c->mtp_norm_out, c->H, c->eps, ms, c->act_h, s);
-            launch_matvec_head(c->mtp_head, c->act_h, ms, nullptr, c->vocab, c->partial, c->nan0, nmax, s);
+            launch_matvec_head(c->mtp_head, c->act_h, ms, conf ? c->logits : nullptr, c->vocab, c->partial, c->nan0,
+                               nmax, s);
         }
         launch_argmax_final(c->partial, c->nan0, c->mtp_head.npanels, ms, s);
+        // adaptive: the top-1 probability of the pass's newest draft (its last row)
+        if (conf) launch_conf(c->logits, c->vocab, c->mtp_head.rows, ms, c->step, s);
     }
 }
 
@@ -498,10 +501,16 @@ int ensure_out(pinfer_ctx *c, int n_max) {
 
 // The graph of one round at draft depth k (drafter 0: synthetic drafts or none, 1: the MTP
 // head) with n-gram drafts of up to `ngram` tokens: the verify pass holds max(k, ngram) + 1 rows.
-int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int nv = 0, int ngram = 0) {
-    if (drafter == 1 && c->round_graph_mtp[k] && (c->graph_nv[k] != nv || c->graph_ng[k] != ngram)) {
+int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int nv = 0, int ngram = 0,
+                int adaptive = 0) {
+    if (drafter == 1 && c->round_graph_mtp[k] &&
+        (c->graph_nv[k] != nv || c->graph_ng[k] != ngram || c->graph_ad[k] != adaptive)) {
         cudaGraphExecDestroy(c->round_graph_mtp[k]);
         c->round_graph_mtp[k] = nullptr;
+    }
+    if (drafter == 0 && ngram > 0 && c->round_graph_ng[ngram] && c->graph_ng_ad[ngram] != adaptive) {
+        cudaGraphExecDestroy(c->round_graph_ng[ngram]);
+        c->round_graph_ng[ngram] = nullptr;
     }
     cudaGraphExec_t &slot = drafter == 1 ? c->round_graph_mtp[k]
                                          : (ngram > 0 ? c->round_graph_ng[ngram] : c->round_graph[k]);
@@ -518,19 +527,29 @@ int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int
         // pf_spec_decode with MTP drafts (spec.c:300-374): the chain drafts 2..ke, the verify
         // pass (with its normed rows), acceptance, then the MTP pass over the committed rows,
         // which drafts the next round's first token
+        // adaptive (spec_adapt.c): timestamps of the round's phases, and the top-1 probability
+        // of every MTP draft for the chain rule
         set_mtp_head(c, nv);
+        if (adaptive) launch_stamp(c->step, 0, s);
         for (int i = 1; i < k; i++) {
             launch_mtp_chain_set(c->step, c->msteps + i, i, s);
-            enqueue_mtp(c, c->msteps + i, c->mcur, 1, true);
+            enqueue_mtp(c, c->msteps + i, c->mcur, 1, true, adaptive != 0);
             launch_mtp_chain_take(c->step, c->msteps + i, i, c->mrows, c->mcur, c->H, s);
         }
+        if (adaptive) launch_stamp(c->step, 1, s);
         enqueue_forward(c, nmax, 2, true);
+        if (adaptive) launch_stamp(c->step, 2, s);
         launch_accept(c->step, c->d_greedy, c->d_out, s);
         launch_mtp_pending_set(c->step, c->msteps, s);
-        enqueue_mtp(c, c->msteps, c->hn, nmax, true);
+        enqueue_mtp(c, c->msteps, c->hn, nmax, true, adaptive != 0);
         launch_mtp_pending_take(c->step, c->msteps, c->mrows, c->mcur, c->H, s);
     } else {
+        if (adaptive) {
+            launch_stamp(c->step, 0, s);
+            launch_stamp(c->step, 1, s);
+        }
         enqueue_forward(c, nmax, 2);
+        if (adaptive) launch_stamp(c->step, 2, s);
         launch_accept(c->step, c->d_greedy, c->d_out, s);
     }
     CUDA_OK(cudaStreamEndCapture(s, &g));
@@ -541,7 +560,9 @@ int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int
     if (drafter == 1) {
         c->graph_nv[k] = nv;
         c->graph_ng[k] = ngram;
+        c->graph_ad[k] = adaptive;
     }
+    if (drafter == 0 && ngram > 0) c->graph_ng_ad[ngram] = adaptive;
     if (drafter == 0 && ngram == 0) c->round_nmax[k] = nmax;
     *out = ex;
     return PINFER_OK;
@@ -608,6 +629,7 @@ struct GenRequest {
     int drafter = 0;          // 0 synthetic drafts, 1 the MTP head
     int nv = 0;               // MTP draft vocabulary
     int ngram = 0;            // longest n-gram (prompt-lookup) draft, 0 = none
+    int adaptive = 0;         // the adaptive speculation policy
     long long ng_stats[3] = {0, 0, 0};
 };
 
@@ -666,6 +688,7 @@ int generate_impl(pinfer_ctx *c, GenRequest *r, int *status) {
     g.seed = r->seed;
     g.drafter = r->drafter;
     g.ngram = r->ngram;
+    g.adaptive = r->adaptive;
     if (host_loop) g.eos = -1;   // the host decides when to stop (one token per round)
     if ((rc = ngram_prefill(c, r->prompt, r->n_prompt, r->append, c->n_past))) return *status = rc;
     launch_set_gen(c->step, g, c->stream);
@@ -677,7 +700,7 @@ int generate_impl(pinfer_ctx *c, GenRequest *r, int *status) {
     }
     launch_gen_start(c->step, c->d_greedy, c->d_out, c->stream);
     cudaGraphExec_t ex;
-    if ((rc = round_graph(c, r->k, &ex, r->drafter, r->nv, r->ngram))) return *status = rc;
+    if ((rc = round_graph(c, r->k, &ex, r->drafter, r->nv, r->ngram, r->adaptive))) return *status = rc;
     int count = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     cudaEventCreate(&ev0);
@@ -881,8 +904,9 @@ static int generate_api(pinfer_ctx *c, const int32_t *prompt, int n_prompt, int3
     if (sp && sp->k > 0 && c && !(c->has_mtp && c->mtp_ok)) return *status = PINFER_E_FORMAT;
     // k > 0: drafts from the MTP head, k per round (pf_spec_decode); ngram > 0: prompt-lookup
     // drafts of up to ngram tokens where the history's tail occurred before (with or without the
-    // MTP head). The adaptive policy is not built: such requests draft at the fixed k (the
-    // tokens are the same either way, pinfer.h:70-73; only the statistics can differ).
+    // MTP head); adaptive: k becomes an upper bound (the chain runs while the newest draft's
+    // top-1 probability is >= 0.6) and plain steps replace speculation while it measures slower
+    // (spec_adapt.c). The tokens never depend on any of this (pinfer.h:70-73).
     GenRequest r{prompt, n_prompt, out, n_max, 0, nullptr, 0, 0, opts, append, {0, 0, 0}, 0.0f};
     if (sp && sp->k > 0) {
         r.k = sp->k;
@@ -890,7 +914,10 @@ static int generate_api(pinfer_ctx *c, const int32_t *prompt, int n_prompt, int3
         const int v = sp->draft_vocab;   // spec.c:88-91
         r.nv = v >= 4 && v < c->vocab ? (v & ~3) : c->vocab;
     }
-    if (sp) r.ngram = sp->ngram;
+    if (sp) {
+        r.ngram = sp->ngram;
+        r.adaptive = (r.k > 0 || r.ngram > 0) && sp->adaptive ? 1 : 0;
+    }
     const int n = generate_impl(c, &r, status);
     if (stats && n >= 0 && (r.k > 0 || r.ngram > 0)) {   // accumulated, never reset (pinfer.h:110-116)
         stats->rounds += r.stats[0];

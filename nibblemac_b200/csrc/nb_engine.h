@@ -76,10 +76,20 @@ struct Step {
     int hist_cap, ng_bits;
     int *hist, *ng_tab;    // [hist_cap], [3][1 << ng_bits]: end position + 1, 0 = empty
     long long ng_rounds, ng_drafted, ng_accepted;
+    // adaptive speculation (engine/src/spec_adapt.c): the chain runs on while the newest
+    // draft's top-1 probability is high enough; plain steps while speculation measures slower
+    int adaptive;
+    int chain_stop;                   // this round's chain stopped early
+    int last_n;                       // rows of the round just committed
+    float conf;                       // top-1 probability of the newest MTP draft
+    unsigned long long t_stamp[3];    // %globaltimer: round start, verify start, verify end
+    double ad_tv[kMaxRows + 1];       // EMA seconds of a verify pass of n rows
+    double ad_t_plain, ad_r_tok, ad_r_sec;
+    int ad_n_spec, ad_plain_mode, ad_plain_run, ad_probe_after, ad_probing;
 };
 
 struct GenArgs {
-    int n_max, k, eos, n_stop, max_ctx, vocab, drafter, ngram;
+    int n_max, k, eos, n_stop, max_ctx, vocab, drafter, ngram, adaptive;
     int stop_ids[8];
     unsigned p24;
     unsigned long long seed;
@@ -173,12 +183,16 @@ void launch_norm_rows(const float *x, const float *w, int H, float eps, const St
                       cudaStream_t s);
 void launch_mtp_input(const Mat &E, const float *h, const Step *ms, const float *w_emb, const float *w_hid,
                       int H, float eps, Act out, cudaStream_t s);
-void launch_mtp_chain_set(const Step *st, Step *ms, int step, cudaStream_t s);
+void launch_mtp_chain_set(Step *st, Step *ms, int step, cudaStream_t s);
 void launch_mtp_chain_take(Step *st, const Step *ms, int step, const float *mrows, float *mcur, int H,
                            cudaStream_t s);
 void launch_mtp_pending_set(const Step *st, Step *ms, cudaStream_t s);
 void launch_mtp_pending_take(Step *st, const Step *ms, const float *mrows, float *mcur, int H, cudaStream_t s);
 void launch_mtp_prefill_fix(const Step *st, Step *ms, cudaStream_t s);
+// adaptive speculation: a %globaltimer stamp into st->t_stamp[idx]; the top-1 probability of
+// the last row of an MTP head pass (logits [rows][ld], draft vocabulary nv) into st->conf
+void launch_stamp(Step *st, int idx, cudaStream_t s);
+void launch_conf(const float *logits, int ld, int nv, const Step *ms, Step *st, cudaStream_t s);
 size_t deltanet_smem(int rep);
 void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, cudaStream_t s);
 void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s, int nseq = 1,

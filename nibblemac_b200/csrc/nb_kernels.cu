@@ -1296,6 +1296,13 @@ __global__ void k_set_gen(Step *st, GenArgs g, const unsigned long long *seeds) 
     st->ngram = g.ngram;
     st->use_ng = 0;
     st->ng_rounds = st->ng_drafted = st->ng_accepted = 0;
+    st->adaptive = g.adaptive;   // pf_adapt_init (spec_adapt.c): measurements cleared
+    st->chain_stop = 0;
+    st->conf = 0.0f;
+    for (int i = 0; i <= kMaxRows; i++) st->ad_tv[i] = 0.0;
+    st->ad_t_plain = st->ad_r_tok = st->ad_r_sec = 0.0;
+    st->ad_n_spec = st->ad_plain_mode = st->ad_plain_run = st->ad_probing = 0;
+    st->ad_probe_after = 8;
     st->last_e = 0;
 }
 
@@ -2520,12 +2527,21 @@ __global__ void k_mtp_input(Mat E, const float *h, const Step *ms, const float *
 
 // Chain step s of a verify round (spec.c:300-321): draft s + 1 from (m of draft s, draft s) at
 // position P - 1 + s; runs only while s < ke (verify rows - 1).
-__global__ void k_mtp_chain_set(const Step *st, Step *ms, int s) {
+__global__ void k_mtp_chain_set(Step *st, Step *ms, int s) {
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x != 0) return;
     const int n = st->n;
-    ms->n = (n > 0 && !st->use_ng && s < n - 1) ? 1 : 0;
+    int run = (n > 0 && !st->use_ng && s < n - 1) ? 1 : 0;
+    // adaptive (spec.c:310): draft s + 1 only while draft s's top-1 probability >= 0.6
+    if (run && st->adaptive && (st->chain_stop || !(st->conf >= 0.6f))) {
+        run = 0;
+        if (!st->chain_stop) {
+            st->chain_stop = 1;
+            st->n = s + 1;   // verify cur and drafts 1..s
+        }
+    }
+    ms->n = run;
     ms->pos0 = st->pos0 - 1 + s;
     ms->tokens[0] = st->tokens[s];
     ms->logged = 0;
@@ -2550,6 +2566,7 @@ __global__ void k_mtp_pending_set(const Step *st, Step *ms) {
     ms->logged = 0;
 }
 __device__ void plan_round(Step *st, const int *greedy);   // below, with the generation control
+__device__ void ad_record(Step *st, int n, int e);
 
 // Its last row drafts the next round's first token; its m seeds the next chain.
 __global__ void k_mtp_pending_take(Step *st, const Step *ms, const float *mrows, float *mcur, int H) {
@@ -2559,10 +2576,60 @@ __global__ void k_mtp_pending_take(Step *st, const Step *ms, const float *mrows,
     if (n <= 0) return;
     if (threadIdx.x == 0) {
         st->mtp_d1 = ms->argmax[n - 1];
-        if (!st->done && st->logged) plan_round(st, nullptr);   // verify rounds: the next round
+        if (!st->done && st->logged) {   // verify rounds: the next round
+            if (st->adaptive) ad_record(st, st->last_n, st->last_e);
+            plan_round(st, nullptr);
+        }
     }
     for (int i = threadIdx.x; i < H; i += blockDim.x) mcur[i] = mrows[(size_t)(n - 1) * H + i];
 }
+// Adaptive speculation: timestamps of the round's phases (%globaltimer, nanoseconds).
+__global__ void k_stamp(Step *st, int idx) {
+    pdl_wait();
+    pdl_trigger();
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    st->t_stamp[idx] = t;
+}
+// Top-1 probability of the newest MTP draft (top1_prob, spec.c:89-92): 1 / sum exp(l - max)
+// over the draft vocabulary, for the chain rule of the adaptive policy. The max is exact; the
+// sum is a parallel tree (the reference's 4-lane order would take ~60 K dependent adds), so a
+// decision can differ from the reference's only where the probability lies within rounding
+// of the 0.6 threshold.
+__global__ void __launch_bounds__(1024) k_conf(const float *logits, int ld, int nv, const Step *ms, Step *st) {
+    pdl_wait();
+    pdl_trigger();
+    const int n = ms->n;
+    if (n <= 0) return;
+    const float *l = logits + (size_t)(n - 1) * ld;
+    __shared__ float red[32];
+    __shared__ float s_m;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) m = fmaxf(m, l[i]);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (warp == 0) {
+        float v = lane < (int)(blockDim.x >> 5) ? red[lane] : -INFINITY;
+        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) s_m = v;
+    }
+    __syncthreads();
+    const float mx = s_m;
+    float sum = 0.0f;
+    for (int i = threadIdx.x; i < nv; i += blockDim.x) sum = __fadd_rn(sum, pf_expf(__fadd_rn(l[i], -mx)));
+    for (int o = 16; o; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    __syncthreads();
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    if (warp == 0) {
+        float v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+        for (int o = 16; o; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) st->conf = v > 0.0f ? __fdiv_rn(1.0f, v) : 0.0f;
+    }
+}
+
 // Prefill: the prompt's last row pairs with the first generated token (spec.c:186-190).
 __global__ void k_mtp_prefill_fix(const Step *st, Step *ms) {
     pdl_wait();
@@ -2646,6 +2713,71 @@ __device__ int ng_draft(Step *st, int *out, int max, int *match) {
     return 0;
 }
 
+// ---- adaptive policy (engine/src/spec_adapt.c, restated): EMA of verify-pass times per width,
+// decayed tokens and seconds of the speculative rounds, plain mode when speculation measures
+// >= 5 % slower than plain steps (or than any verify pass, the sure case), probes out of plain
+// mode after 8, 16, .. 64 plain steps, each probe judged on its own 2 rounds.
+__device__ __forceinline__ double ad_ema(double old, double x) { return old <= 0.0 ? x : old + 0.25 * (x - old); }
+
+__device__ bool ad_plain_now(Step *st) {
+    if (!st->ad_plain_mode) return false;
+    if (st->ad_plain_run < st->ad_probe_after) return true;
+    if (!st->ad_probing) {   // a probe starts
+        st->ad_probing = 1;
+        st->ad_n_spec = 0;
+        st->ad_r_tok = st->ad_r_sec = 0.0;
+    }
+    return false;
+}
+__device__ void ad_plain(Step *st, double sec) {
+    st->ad_t_plain = ad_ema(st->ad_t_plain, sec);
+    if (st->ad_plain_mode) st->ad_plain_run++;
+}
+__device__ void ad_round(Step *st, int n, int emitted, double sec, double t_verify) {
+    if (n < 2 || n > kMaxRows) return;
+    st->ad_tv[n] = ad_ema(st->ad_tv[n], t_verify);
+    st->ad_r_tok = 0.95 * st->ad_r_tok + emitted;
+    st->ad_r_sec = 0.95 * st->ad_r_sec + sec;
+    st->ad_n_spec++;
+    double tv_min = 0.0;
+    for (int i = 2; i <= kMaxRows; i++)
+        if (st->ad_tv[i] > 0.0 && (tv_min <= 0.0 || st->ad_tv[i] < tv_min)) tv_min = st->ad_tv[i];
+    double ts = 0.0;   // a plain step's seconds: measured, else extrapolated from widths 2 and 3
+    if (st->ad_t_plain > 0.0) ts = st->ad_t_plain;
+    else if (st->ad_tv[2] > 0.0 && st->ad_tv[3] > 0.0) {
+        const double t = 2.0 * st->ad_tv[2] - st->ad_tv[3];
+        ts = t > 0.5 * st->ad_tv[2] ? t : 0.5 * st->ad_tv[2];
+    }
+    const bool slow = st->ad_r_tok * tv_min < 0.95 * st->ad_r_sec ||
+                      (ts > 0.0 && st->ad_r_tok * ts < 0.95 * st->ad_r_sec);
+    if (st->ad_plain_mode) {   // a probe round
+        if (st->ad_n_spec < 2) return;
+        st->ad_probing = 0;
+        st->ad_plain_mode = slow;
+        st->ad_probe_after = !slow ? 8 : (st->ad_probe_after * 2 < 64 ? st->ad_probe_after * 2 : 64);
+        st->ad_plain_run = 0;
+        st->ad_n_spec = 0;
+        if (slow) st->ad_r_tok = st->ad_r_sec = 0.0;
+    } else if (slow && (st->ad_n_spec >= 8 || (ts > 0.0 && st->ad_tv[2] >= 1.5 * ts && st->ad_n_spec >= 2))) {
+        st->ad_plain_mode = 1;
+        st->ad_plain_run = 0;
+        st->ad_probe_after = 8;
+    }
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// the measurements of the round that just committed (n rows verified, e tokens emitted)
+__device__ void ad_record(Step *st, int n, int e) {
+    const unsigned long long t_end = globaltimer();
+    const double sec = (double)(t_end - st->t_stamp[0]) * 1e-9;
+    const double tv = (double)(st->t_stamp[2] - st->t_stamp[1]) * 1e-9;
+    if (n <= 1) ad_plain(st, tv);   // a plain step: its forward pass
+    else ad_round(st, n, e, sec, tv);
+}
+
 // Shape and drafts of the next round (spec.c:280-321): never draft past n_max or the context;
 // the n-gram draft when the history's tail occurred before and the match is trusted
 // (ngram_pick, spec.c:138-151: a match of >= PF_NG_TRUST tokens in full; a shorter one only
@@ -2664,7 +2796,9 @@ __device__ void plan_round(Step *st, const int *greedy) {
     }
     int d[kMaxRows];
     int ke = 0, use_ng = 0;
-    if (st->ngram > 0 && left > 0) {
+    st->chain_stop = 0;
+    const bool plain = st->adaptive && ad_plain_now(st);   // spec.c:288
+    if (!plain && st->ngram > 0 && left > 0) {
         int match = 0;
         const int mx = min(min(st->ngram, left), kMaxRows - 1);
         const int nd = ng_draft(st, d, mx, &match);
@@ -2675,7 +2809,7 @@ __device__ void plan_round(Step *st, const int *greedy) {
         }
         use_ng = ke > 0;
     }
-    if (!use_ng) ke = st->k < left ? st->k : left;
+    if (!use_ng) ke = plain ? 0 : (st->k < left ? st->k : left);
     st->use_ng = use_ng;
     st->tokens[0] = st->cur;
     if (use_ng) {
@@ -2746,6 +2880,7 @@ __global__ void k_accept(Step *st, const int *greedy, int *out) {
     while (e <= a && !done) done = emit_tok(st, out, vt[++e]);
     st->last_pos = st->pos0;   // for the MTP pass over the committed rows
     st->last_e = e;
+    st->last_n = n;
     for (int i = 0; i < e; i++) st->last_tok[i] = vt[i + 1];
     st->pend_keep = e - 1;   // pf_lin_commit (forward_lin.c:413-432)
     st->pend_conv = e;
@@ -2767,7 +2902,10 @@ __global__ void k_accept(Step *st, const int *greedy, int *out) {
         return;
     }
     // with the MTP head the next round is planned after this round's MTP pass (its d1)
-    if (st->drafter != 1) plan_round(st, greedy);
+    if (st->drafter != 1) {
+        if (st->adaptive) ad_record(st, n, e);
+        plan_round(st, greedy);
+    }
 }
 
 }  // namespace
@@ -3035,7 +3173,7 @@ void launch_mtp_input(const Mat &E, const float *h, const Step *ms, const float 
                       int H, float eps, Act out, cudaStream_t s) {
     launch_k(k_mtp_input, kMaxRows, 256, 2 * (size_t)H * sizeof(float), s, E, h, ms, w_emb, w_hid, H, eps, out);
 }
-void launch_mtp_chain_set(const Step *st, Step *ms, int step, cudaStream_t s) {
+void launch_mtp_chain_set(Step *st, Step *ms, int step, cudaStream_t s) {
     launch_k(k_mtp_chain_set, 1, 32, 0, s, st, ms, step);
 }
 void launch_mtp_chain_take(Step *st, const Step *ms, int step, const float *mrows, float *mcur, int H,
@@ -3062,6 +3200,10 @@ void launch_set_pass(Step *st, int n, int pos0, int logged, const int *tokens, c
 }
 void launch_set_gen(Step *st, const GenArgs &g, cudaStream_t s, int nseq, const unsigned long long *seeds) {
     launch_k(k_set_gen, nseq, 1, 0, s, st, g, seeds);
+}
+void launch_stamp(Step *st, int idx, cudaStream_t s) { launch_k(k_stamp, 1, 1, 0, s, st, idx); }
+void launch_conf(const float *logits, int ld, int nv, const Step *ms, Step *st, cudaStream_t s) {
+    launch_k(k_conf, 1, 1024, 0, s, logits, ld, nv, ms, st);
 }
 void launch_set_pass_seqs(Step *st, const SeqPass *dev_passes, int nseq, cudaStream_t s) {
     launch_k(k_set_pass_seqs, nseq, 32, 0, s, st, dev_passes);

@@ -269,3 +269,32 @@ def test_ngram_drafts_match_reference(looping_pair, k, ngram):
     rtoks2, rst2, _ = ref.generate_mtp(q, 40, k, append=True, ngram=ngram, all_stats=True)
     got2 = [st2.rounds, st2.drafted, st2.accepted, st2.ngram_rounds, st2.ngram_drafted, st2.ngram_accepted]
     assert toks2 == rtoks2 and got2 == rst2, f"continuation: {got2} vs {rst2}"
+
+
+@pytest.mark.parametrize("k,ngram", [(2, 0), (4, 0), (4, 5)])
+def test_adaptive_speculation_keeps_tokens(pair, k, ngram):
+    """pinfer_spec_params.adaptive (spec_adapt.c): k becomes an upper bound, the MTP chain runs
+    on only while the newest draft's top-1 probability is >= 0.6, and plain steps replace
+    speculation while it measures slower. The tokens stay the plain greedy ones (and the
+    reference's); on a random model the drafts' confidence is far below 0.6, so the chain stops
+    after the first draft: fewer than k drafts per speculative round. (The statistics depend on
+    measured times on both sides and are not compared.)"""
+    from nibblemac_b200._lib import SpecStats, SpecParams
+    import ctypes
+    name, dev, ref = pair
+    p = prompt(dev.n_vocab, 33, 70 + k)
+    dev.reset()
+    plain, _ = dev.generate(p, 40)
+    st = SpecStats()
+    t = np.ascontiguousarray(p, np.int32)
+    out = np.zeros(40, np.int32)
+    sp = SpecParams(k, 0, 1, ngram)
+    status = ctypes.c_int(0)
+    n = dev.lib.pinfer_generate_greedy_ex(dev.ctx, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(t),
+                                          out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), 40,
+                                          ctypes.byref(sp), None, ctypes.byref(st), ctypes.byref(status))
+    assert n == len(plain) and status.value == 0
+    assert out[:n].tolist() == plain
+    rtoks, _, _ = ref.generate_mtp(p, 40, k, ngram=ngram)
+    assert rtoks == plain
+    assert st.rounds > 0 and st.drafted < k * st.rounds, (st.rounds, st.drafted)
