@@ -2072,7 +2072,6 @@ __global__ void __launch_bounds__(kAttnHd)
 //    (S += k delta; o += S q) runs in the same loop as token t+1's first sweep (S *= decay;
 //    kv += S k), two independent add chains per iteration.
 // rep == 1 only (one value head per key head, every Qwen3.5 size); KC taps.
-constexpr int kMaxReplay = 8;   // a verify pass holds at most PINFER_SPEC_MAX_K + 1 rows
 
 // One conv channel of k_deltanet2 held in registers (every array index a constant): the state
 // rows, the taps, and the conv-log rows a pending commit shifts in (pf_lin_commit's conv part,
@@ -2222,11 +2221,15 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     conv_load_log(cq, L, C, pend_conv);
     conv_load_log(ck, L, C, pend_conv);
     conv_load_log(cv, L, C, pend_conv);
+    constexpr int RP = NR - 1;   // replayed rows of the last commit (it committed <= NR rows)
     __shared__ __align__(16) float sq[NR][kDK], sk[NR][kDK], sv[NR][kDV];
-    __shared__ __align__(16) float sz[NR][kDV], so[NR][kDV];
+    __shared__ __align__(16) float sz[NR][kDV];
+    // token t's output row reuses its v row: thread j reads v[t][j] at the start of token t and
+    // writes o[t][j] at its end, and no other thread reads column j of either
+    float (*so)[kDV] = sv;
     __shared__ float sbeta[NR], sdec[NR], srn[NR];
-    __shared__ __align__(16) float skp[kMaxReplay][kDK];
-    __shared__ float spd[kMaxReplay];
+    __shared__ __align__(16) float skp[RP][kDK];
+    __shared__ float spd[RP];
     const size_t logw = (size_t)kDK + kDV + 1;
 
     if (j == 0) {
@@ -2239,10 +2242,10 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             bulk_g2s(sz[t], yr + C + h * kDV, kDV * 4, &sbar[0]);
         }
     }
-    const int keep = pend_keep < kMaxReplay ? pend_keep : kMaxReplay;
-    float dl[kMaxReplay];
+    const int keep = pend_keep < RP ? pend_keep : RP;
+    float dl[RP];
 #pragma unroll
-    for (int tp = 0; tp < kMaxReplay; tp++) {   // deferred commit: rows 1..keep of half wr^1
+    for (int tp = 0; tp < RP; tp++) {   // deferred commit: rows 1..keep of half wr^1
         dl[tp] = 0.0f;
         if (tp < keep) {
             const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp + 1) * d.nv + h) * logw;
@@ -2344,7 +2347,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             ld8col(sn, Sj, i0 + 8 < kDK ? i0 + 8 : i0);
             ld8(k8, k0 + i0);
 #pragma unroll
-            for (int tp = 0; tp < kMaxReplay; tp++) {
+            for (int tp = 0; tp < RP; tp++) {
                 if (tp < keep) {
                     float kp[8];
                     ld8(kp, skp[tp] + i0);
@@ -3128,7 +3131,8 @@ void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const fl
         launch_k(k_attn5, dim3(d.nkv * nch, nseq), kAttnHd, attn5_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
         return;
     }
-    if (nseq > 1 && attn4_ok(d)) {   // grouped queries share the K / V reads
+    if (nseq > 1 && attn4_ok(d)) {   // grouped queries share the K / V reads (one context: the
+                                     // per-query clusters below have the shorter critical path)
         const int QR = kAttnQ / (d.nq / d.nkv), nch = (d.rps + QR - 1) / QR;
         launch_k(k_attn4, dim3(kAttnCL, d.nkv * nch, nseq), kAttnHd, attn4_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
         return;

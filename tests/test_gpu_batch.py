@@ -52,6 +52,28 @@ def test_batch_equals_single_sequences(small, k, p):
         b.close()
 
 
+@pytest.mark.parametrize("k,p", [(12, 1.0), (15, 1.0), (15, 0.7)])
+def test_batch_deep_drafts(small, k, p):
+    """Draft depths beyond a context's PINFER_SPEC_MAX_K (the batch takes up to 15): 16-row
+    passes whose commits of up to 16 tokens the next pass's DeltaNet replays from the update
+    log. Tokens equal plain greedy; at p = 1 every draft is accepted."""
+    lens = [3, 20, 47]
+    ps = prompts_of(small.n_vocab, lens, 300 + k)
+    n_max = 50
+    greedy = [small.generate(pr, n_max)[0] for pr in ps]
+    b = small.batch(len(ps), 256, max_k=k)
+    try:
+        got, st, status, _ = b.generate_synthetic(ps, n_max, k, greedy=[g + [0] * (n_max - len(g)) for g in greedy],
+                                                  seeds=[5 + i for i in range(len(ps))], p=p)
+        assert status == [0] * len(ps)
+        assert got == greedy
+        assert st.drafted > 0
+        if p == 1.0:
+            assert st.accepted == st.drafted
+    finally:
+        b.close()
+
+
 def test_batch_reuse_and_partial_slots(small):
     """A batch object runs several generations (fresh states each time), with fewer sequences
     than slots, and the same sequence gives the same tokens at any slot."""
