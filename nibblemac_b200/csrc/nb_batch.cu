@@ -141,7 +141,7 @@ void enqueue_forward(pinfer_b200_batch *b, int R, int nseq, int rps, bool head) 
         } else {
             gemm(b, 0, b->maps_h, T.win, R, b->y, c->lind.ldy);
             const Act o = with_cols(b->act_mid, c->vd);
-            launch_deltanet(b->lin[D.lin], b->lind, b->y, b->steps, o, s, nseq, rps);
+            launch_deltanet(b->lin[D.lin], b->lind, b->y, b->steps, o, s, nseq, rps, b->kmax);
             gemm(b, 1, b->maps_ol, T.out, R, b->x, c->H);
         }
         launch_norm_quant(b->x, D.post_norm, c->H, c->eps, b->steps, b->act_h, s, nseq, rps);

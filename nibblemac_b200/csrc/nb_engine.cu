@@ -365,7 +365,7 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = fal
         } else {
             const Act o = mid_act(c, c->vd);
             launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->lind.ldy, nmax, c->act_h, s);
-            launch_deltanet(c->lin[D.lin], c->lind, c->y, c->step, o, s);
+            launch_deltanet(c->lin[D.lin], c->lind, c->y, c->step, o, s, 1, nmax);
             launch_matvec(D.out, o, c->step, c->x, c->H, 1, nmax, s);
         }
         const Act h = mid_act(c, c->ffn);

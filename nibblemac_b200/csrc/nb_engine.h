@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include "nb_math.cuh"
+#include "pinfer.h"
 
 namespace nb {
 
@@ -163,9 +164,11 @@ void launch_argmax_keys(const unsigned long long *partial, const int *nan0, int 
                         int rps = kMaxRows);
 void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s, int kstride = kMaxRows,
                         int nseq = 1, int rps = kMaxRows);
-// nseq > 1 needs the fast kernel's shape (deltanet_batch_ok)
+// nseq > 1 needs the fast kernel's shape (deltanet_batch_ok); keep_max: the most deferred
+// updates a pass may replay (a context: PINFER_SPEC_MAX_K; a batch: its draft depth)
 void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
-                     Step *st, Act out, cudaStream_t s, int nseq = 1, int rps = kMaxRows);
+                     Step *st, Act out, cudaStream_t s, int nseq = 1, int rps = kMaxRows,
+                     int keep_max = PINFER_SPEC_MAX_K);
 bool deltanet_batch_ok(const LinDims &d);
 // attention grids cover d.rps rows of each of nseq sequences; nseq > 1 needs the cluster kernel
 // (attn_batch_ok)

@@ -2168,8 +2168,11 @@ __device__ __forceinline__ void ld8(float (&v)[8], const float *p) {
 }
 
 // NR: the most rows a pass may have (the shared-memory row buffers; a 4-row variant serves
-// multi-sequence verify passes, where a smaller footprint fits three CTAs on an SM)
-template <int KC, int NR = kMaxRows>
+// multi-sequence verify passes, where a smaller footprint fits three CTAs on an SM). RP: the
+// most deferred updates a pass may replay (the last commit's rows after its first: up to
+// PINFER_SPEC_MAX_K on a context, the batch's draft depth on a batch); the replay is unrolled
+// over RP, so each launch takes the smallest variant that holds its bound.
+template <int KC, int NR = kMaxRows, int RP = NR - 1>
 __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, const float *y, Step *st,
                                                       Act out) {
     constexpr int S = KC - 1;
@@ -2210,8 +2213,9 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     pdl_wait();
     pdl_trigger();
     const int n = st->n;
-    if (n <= 0 || n > NR) {   // nothing to do (or more rows than this variant holds: reported):
-        if (n > NR && j == 0) st->status = -92;   // let the state copy land before the CTA's smem goes
+    if (n <= 0 || n > NR || st->pend_keep > RP) {   // nothing to do (or more rows / replayed
+        // updates than this variant holds: reported); the state copy lands before smem goes
+        if ((n > NR || st->pend_keep > RP) && j == 0) st->status = -92;
         mbar_wait(&sbar[1], 0);
         return;
     }
@@ -2221,7 +2225,6 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
     conv_load_log(cq, L, C, pend_conv);
     conv_load_log(ck, L, C, pend_conv);
     conv_load_log(cv, L, C, pend_conv);
-    constexpr int RP = NR - 1;   // replayed rows of the last commit (it committed <= NR rows)
     __shared__ __align__(16) float sq[NR][kDK], sk[NR][kDK], sv[NR][kDV];
     __shared__ __align__(16) float sz[NR][kDV];
     // token t's output row reuses its v row: thread j reads v[t][j] at the start of token t and
@@ -2242,7 +2245,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             bulk_g2s(sz[t], yr + C + h * kDV, kDV * 4, &sbar[0]);
         }
     }
-    const int keep = pend_keep < RP ? pend_keep : RP;
+    const int keep = pend_keep;   // <= RP (checked above)
     float dl[RP];
 #pragma unroll
     for (int tp = 0; tp < RP; tp++) {   // deferred commit: rows 1..keep of half wr^1
@@ -2448,6 +2451,322 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             quant_block_warp(v, lane, out.q + (size_t)(row0 + t) * out.cols + (col & ~31),
                              out.d + (size_t)(row0 + t) * nbo + (col >> 5), out.fs + (size_t)(row0 + t) * nbo + (col >> 5));
             (void)warp;
+        }
+    }
+}
+
+
+// Gated DeltaNet layer of a single context's pass, spread over a 4-CTA cluster per key head:
+// the same per-element arithmetic as k_deltanet2 (same citations), scheduled for latency.
+// k_deltanet2 gives each state column one thread, which then does every state update of that
+// column and both of its ordered add chains: one warp per SM sub-partition, issue-bound. Here
+// CTA c of the cluster owns state columns 32c..32c+31 and its warp p owns state rows
+// 32p..32p+31, the state itself in registers, so every element update and product of a token
+// runs on 16 warps of 4 SMs in parallel; only the adds of the ordered chains (kv and o run over
+// the rows i = 0..127 in order, kern_lin.c) pass from warp to warp: warp p adds the products of
+// its 32 rows to the partial sum warp p - 1 hands it through shared memory and a named barrier.
+// Each CTA computes the whole q and k vectors of every token (conv, L2 norm), the gates and the
+// v / z columns it owns; the gated RMSNorm runs over the head's 128 outputs, which the CTAs
+// exchange through distributed shared memory; each CTA quantises its own 32-column A8 block.
+// Conv states, logs and state rows are written by the CTA that owns them.
+constexpr int kDnCl = 4;                    // CTAs per key head (cluster)
+constexpr int kDnCols = kDV / kDnCl;        // state columns per CTA
+constexpr int kDnParts = 4;                 // warps per CTA
+constexpr int kDnPart = kDK / kDnParts;     // state rows per warp
+
+__device__ __forceinline__ void bar_sync_n(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_arrive_n(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// a float into CTA `rank`'s shared memory at the offset of `local` in this CTA's
+__device__ __forceinline__ void st_dsmem(float *local, uint32_t rank, float v) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
+// pre: the rows the pass may have; rows 0..pre-1 of this head are loaded right after pdl_wait,
+// beside the Step block (the pass must start at row 0 and have at most pre rows: checked).
+template <int KC, int NR, int RP>
+__global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1)
+    k_deltanet3(LinLayer L, LinDims d, const float *y, Step *st, Act out, int pre) {
+    static_assert(kDnParts * 32 == kDK && kDnCols == 32 && NR <= kDnParts * 32 && RP >= 1, "shape");
+    constexpr int S = KC - 1;
+    constexpr int NT = (NR + kDnParts - 1) / kDnParts;   // output rows per warp (epilogue)
+    const int h = blockIdx.x / kDnCl, c = (int)cluster_rank();
+    const int j = threadIdx.x, w = j >> 5, lane = j & 31;
+    const int col = c * kDnCols + lane;   // this thread's state column (within the head)
+    const int i0 = w * kDnPart;           // its first state row
+    const int C = d.C;
+    // conv taps and state rows: q and k channel j (every CTA needs the whole q and k vectors),
+    // v channel col (warp 0); this thread's 32 state elements. All independent of the step and
+    // written only by this kernel, so requested before pdl_wait.
+    ConvCh<KC> cq, ck, cv;
+    conv_load(cq, L, C, h * kDK + j);
+    conv_load(ck, L, C, d.kd + h * kDK + j);
+    if (w == 0) conv_load(cv, L, C, 2 * d.kd + h * kDV + col);
+    float *rec = L.rec + (size_t)h * kDK * kDV + col;   // rec[i * kDV]: row i of this column
+    float Sr[kDnPart];
+#pragma unroll
+    for (int r = 0; r < kDnPart; r++) Sr[r] = ld_early(rec + (size_t)r * kDV + (size_t)i0 * kDV);
+    pdl_wait();
+    pdl_trigger();
+    // rows 0..pre-1: the conv inputs of this thread's channels, its z column for the output rows
+    // it gates, the gate inputs (thread kDK - NR + t); requested together with the Step block
+    float xq[NR], xk[NR], xv[NR], zt[NT], gb = 0.0f, ga = 0.0f;
+#pragma unroll
+    for (int t = 0; t < NR; t++) {
+        xq[t] = xk[t] = xv[t] = 0.0f;
+        if (t < pre) {
+            const float *yr = y + (size_t)t * d.ldy;
+            xq[t] = ld_early(yr + h * kDK + j);
+            xk[t] = ld_early(yr + d.kd + h * kDK + j);
+            if (w == 0) xv[t] = ld_early(yr + 2 * d.kd + h * kDV + col);
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < NT; q++) {
+        const int t = w + q * kDnParts;
+        zt[q] = t < pre ? ld_early(y + (size_t)t * d.ldy + C + h * kDV + col) : 0.0f;
+    }
+    const int tg = j - (kDK - NR);   // this thread's gate row
+    if (tg >= 0 && tg < pre) {
+        const float *yr = y + (size_t)tg * d.ldy;
+        gb = ld_early(yr + C + d.vd + h);
+        ga = ld_early(yr + C + d.vd + d.nv + h);
+    }
+    const int n = st->n;
+    if (n <= 0 || n > NR || n > pre || st->row0 != 0 || st->pend_keep > RP) {   // nothing to do, or
+        // a pass this variant does not hold (reported); the same for every CTA of the cluster
+        if (n > 0 && j == 0 && c == 0) st->status = -92;
+        return;
+    }
+    const int logged = st->logged, keep = st->pend_keep, pend_conv = st->pend_conv, wr = st->wr;
+    conv_load_log(cq, L, C, pend_conv);
+    conv_load_log(ck, L, C, pend_conv);
+    if (w == 0) conv_load_log(cv, L, C, pend_conv);
+    __shared__ __align__(16) float sq[NR][kDK], sk[NR][kDK];
+    __shared__ __align__(16) float sv[NR][kDnCols];
+    __shared__ __align__(16) float so[NR][kDV];   // the head's output rows
+    __shared__ float sbeta[NR], sdec[NR], srn[NR];
+    __shared__ __align__(16) float skp[RP][kDK];
+    __shared__ float spd[RP];
+    __shared__ float sdelta[kDnCols], xo[kDnParts][kDnCols], xk_[kDnParts][kDnCols];
+    const size_t logw = (size_t)kDK + kDV + 1;
+    // deferred commit: rows 1..keep of half wr^1, held in registers until the first sweep
+    float dl[RP], kpr[RP], pdr[RP];
+#pragma unroll
+    for (int tp = 0; tp < RP; tp++) {
+        dl[tp] = kpr[tp] = pdr[tp] = 0.0f;
+        if (tp < keep) {
+            const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp + 1) * d.nv + h) * logw;
+            kpr[tp] = ld_early(u + j);
+            dl[tp] = ld_early(u + kDK + col);
+            if (j == 0) pdr[tp] = ld_early(u + kDK + kDV);
+        }
+    }
+    // ---- gates of token tg
+    if (tg >= 0 && tg < n) {
+        sbeta[tg] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-gb)));
+        const float xs = __fadd_rn(ga, L.dt_bias[h]);
+        const float sp = xs > 20.0f ? xs : glibc_log1pf(glibc_expf(xs));
+        sdec[tg] = glibc_expf(__fmul_rn(L.A[h], sp));
+    }
+    // ---- pending conv commit, then conv + SiLU (q / k channel j; v channel col on warp 0)
+    const bool own_qk = w == c;   // q / k channel j is this CTA's to store and log
+    conv_commit(cq, pend_conv);
+    conv_commit(ck, pend_conv);
+    if (w == 0) conv_commit(cv, pend_conv);
+    {
+        float lq[S > 0 ? S : 1], lk[S > 0 ? S : 1], lv[S > 0 ? S : 1];
+#pragma unroll
+        for (int r = 0; r < S; r++) lq[r] = lk[r] = lv[r] = 0.0f;
+#pragma unroll
+        for (int t = 0; t < NR; t++) {
+            if (t < n) {
+                sq[t][j] = conv_step(cq, xq[t]);
+                sk[t][j] = conv_step(ck, xk[t]);
+                if (w == 0) sv[t][lane] = conv_step(cv, xv[t]);
+                if (logged) {
+                    if (t == 0) {
+#pragma unroll
+                        for (int r = 0; r < S; r++) {
+                            lq[r] = cq.st[r];
+                            lk[r] = ck.st[r];
+                            lv[r] = cv.st[r];
+                        }
+                    } else {
+                        if (own_qk) {
+                            L.xin[(size_t)t * C + cq.c] = xq[t];
+                            L.xin[(size_t)t * C + ck.c] = xk[t];
+                        }
+                        if (w == 0) L.xin[(size_t)t * C + cv.c] = xv[t];
+                    }
+                }
+            }
+        }
+        if (own_qk) {
+            conv_store(cq, L, C, lq, logged);
+            conv_store(ck, L, C, lk, logged);
+        }
+        if (w == 0) conv_store(cv, L, C, lv, logged);
+    }
+    __syncthreads();
+    // ---- L2 norm of q and k: 4 lanes per (token, vector)
+    {
+        const float qscale = inv_sqrt_ref((float)kDK);
+        for (int u0 = w * 8; u0 < 2 * n; u0 += kDnParts * 8) {
+            const int u = u0 + (lane >> 2), l = lane & 3;
+            const bool act = u < 2 * n;
+            float *vec = act ? ((u & 1) ? sk[u >> 1] : sq[u >> 1]) : sq[0];
+            float cs = 0.0f;
+            if (act) {
+#pragma unroll 8
+                for (int i = l; i < kDK; i += 4) cs = madd(cs, vec[i], vec[i]);
+            }
+            const int base = lane & ~3;
+            const float c0 = __shfl_sync(0xffffffffu, cs, base), c1 = __shfl_sync(0xffffffffu, cs, base + 1);
+            const float c2 = __shfl_sync(0xffffffffu, cs, base + 2), c3 = __shfl_sync(0xffffffffu, cs, base + 3);
+            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+            const float r = inv_sqrt_ref(__fadd_rn(ss, 1e-6f));
+            __syncwarp();
+            if (act) {
+                const float sc = (u & 1) ? 1.0f : qscale;
+                for (int i = l; i < kDK; i += 4) vec[i] = __fmul_rn(__fmul_rn(vec[i], r), sc);
+            }
+        }
+    }
+#pragma unroll
+    for (int tp = 0; tp < RP; tp++) {
+        if (tp < keep) {
+            skp[tp][j] = kpr[tp];
+            if (j == 0) spd[tp] = pdr[tp];
+        }
+    }
+    __syncthreads();
+
+    // ---- recurrence. Named barriers: 1 (all warps) publishes a token's delta; 1 + p hands
+    // the partial sums of rows 0..32p-1 from warp p - 1 to warp p.
+    float pk[kDnPart];
+    {   // replay of the deferred commit (per element in commit order) and token 0's decay,
+        // then kv over the rows in order
+#pragma unroll
+        for (int tp = 0; tp < RP; tp++) {
+            if (tp < keep) {
+                const float pd = spd[tp], dt = dl[tp];
+                const float *kp = skp[tp] + i0;
+#pragma unroll
+                for (int r = 0; r < kDnPart; r++) Sr[r] = __fadd_rn(__fmul_rn(Sr[r], pd), __fmul_rn(kp[r], dt));
+            }
+        }
+        const float dec = sdec[0];
+        const float *k0 = sk[0] + i0;
+#pragma unroll
+        for (int r = 0; r < kDnPart; r++) {
+            Sr[r] = __fmul_rn(Sr[r], dec);
+            pk[r] = __fmul_rn(Sr[r], k0[r]);
+        }
+        float kv = 0.0f;
+        if (w > 0) {
+            bar_sync_n(1 + w, 64);
+            kv = xk_[w][lane];
+        }
+#pragma unroll
+        for (int r = 0; r < kDnPart; r++) kv = __fadd_rn(kv, pk[r]);
+        if (w < kDnParts - 1) {
+            xk_[w + 1][lane] = kv;
+            bar_arrive_n(2 + w, 64);
+        } else {
+            sdelta[lane] = __fmul_rn(__fadd_rn(sv[0][lane], -kv), sbeta[0]);
+        }
+    }
+    for (int t = 0; t < n; t++) {
+        bar_sync_n(1, kDnParts * 32);   // delta of token t
+        const float delta = sdelta[lane];
+        const bool next = t + 1 < n;
+        const float decn = next ? sdec[t + 1] : 0.0f;
+        const float *kt = sk[t] + i0, *qt = sq[t] + i0, *kn = sk[next ? t + 1 : t] + i0;
+        const bool store_live = logged && t == 0;
+        const bool store_rec = store_live || (!next && !logged);
+        float po[kDnPart];
+#pragma unroll
+        for (int r = 0; r < kDnPart; r++) {
+            float sv_ = __fadd_rn(Sr[r], __fmul_rn(kt[r], delta));
+            po[r] = __fmul_rn(sv_, qt[r]);
+            if (store_rec) rec[(size_t)(i0 + r) * kDV] = sv_;
+            if (next) {
+                sv_ = __fmul_rn(sv_, decn);
+                pk[r] = __fmul_rn(sv_, kn[r]);
+            }
+            Sr[r] = sv_;
+        }
+        float o = 0.0f, kvn = 0.0f;
+        if (w > 0) {
+            bar_sync_n(1 + w, 64);
+            o = xo[w][lane];
+            kvn = xk_[w][lane];
+        }
+        if (next) {
+#pragma unroll
+            for (int r = 0; r < kDnPart; r++) {
+                o = __fadd_rn(o, po[r]);
+                kvn = __fadd_rn(kvn, pk[r]);
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < kDnPart; r++) o = __fadd_rn(o, po[r]);
+        }
+        if (w < kDnParts - 1) {
+            xo[w + 1][lane] = o;
+            xk_[w + 1][lane] = kvn;
+            bar_arrive_n(2 + w, 64);
+        } else {
+            if (next) sdelta[lane] = __fmul_rn(__fadd_rn(sv[t + 1][lane], -kvn), sbeta[t + 1]);
+#pragma unroll
+            for (int r = 0; r < kDnCl; r++) st_dsmem(&so[t][col], (uint32_t)r, o);   // to every CTA
+        }
+        if (logged && t > 0 && w == 0) {   // log row t: k, delta per column, decay
+            float *u = L.upd + (((size_t)wr * d.cap + t) * d.nv + h) * logw;
+            u[kDK + col] = delta;
+            u[col] = sk[t][col];
+            if (col == 0) u[kDK + kDV] = sdec[t];
+        }
+    }
+    // every CTA's output columns in every CTA (no shared memory of a peer is touched after this)
+    cluster_arrive();
+    cluster_wait();
+    // ---- gated RMSNorm over the 128 outputs, then A8 of this CTA's 32-column block
+    for (int u0 = w * 8; u0 < n; u0 += kDnParts * 8) {
+        const int u = u0 + (lane >> 2), l = lane & 3;
+        const bool act = u < n;
+        const float *vec = so[act ? u : 0];
+        float cs = 0.0f;
+        if (act) {
+#pragma unroll 8
+            for (int i = l; i < kDV; i += 4) cs = madd(cs, vec[i], vec[i]);
+        }
+        const int base = lane & ~3;
+        const float c0 = __shfl_sync(0xffffffffu, cs, base), c1 = __shfl_sync(0xffffffffu, cs, base + 1);
+        const float c2 = __shfl_sync(0xffffffffu, cs, base + 2), c3 = __shfl_sync(0xffffffffu, cs, base + 3);
+        const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+        if (act && l == 0) srn[u] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)kDV), d.eps));
+    }
+    __syncthreads();
+    {
+        const int nbo = out.cols >> 5, gcol = h * kDV + col;
+        const float nw = L.norm_w[col];
+#pragma unroll
+        for (int q = 0; q < NT; q++) {
+            const int t = w + q * kDnParts;
+            if (t < n) {
+                float v = __fmul_rn(__fmul_rn(so[t][col], srn[t]), nw);
+                v = __fmul_rn(v, pf_silu(zt[q]));
+                quant_block_warp(v, lane, out.q + (size_t)t * out.cols + (gcol & ~31), out.d + (size_t)t * nbo + (gcol >> 5),
+                                 out.fs + (size_t)t * nbo + (gcol >> 5));
+            }
         }
     }
 }
@@ -3092,12 +3411,26 @@ bool deltanet_batch_ok(const LinDims &d) {
            d.ss_rec % 4 == 0;
 }
 void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
-                     Step *st, Act out, cudaStream_t s, int nseq, int rps) {
+                     Step *st, Act out, cudaStream_t s, int nseq, int rps, int keep_max) {
     if (deltanet_batch_ok(d) && ((uintptr_t)y & 15) == 0 && ((uintptr_t)L.rec & 15) == 0) {
+        const size_t sm = sizeof(float) * kDK * kDV;
+        // a pass of rps rows follows a commit of at most rps rows of the same generation
+        if (nseq == 1 && keep_max <= PINFER_SPEC_MAX_K) {   // one sequence: the 4-CTA cluster form
+            const int pre = rps < kMaxRows ? rps : kMaxRows;
+            if (pre <= 4)
+                launch_k(k_deltanet3<4, 4, PINFER_SPEC_MAX_K>, dim3(d.nk * kDnCl, 1), kDnParts * 32, 0, s, L, d, y,
+                         st, out, pre);
+            else
+                launch_k(k_deltanet3<4, kMaxRows, PINFER_SPEC_MAX_K>, dim3(d.nk * kDnCl, 1), kDnParts * 32, 0, s, L,
+                         d, y, st, out, pre);
+            return;
+        }
         if (nseq > 1 && rps <= 4)
-            launch_k(k_deltanet2<4, 4>, dim3(d.nk, nseq), kDV, sizeof(float) * kDK * kDV, s, L, d, y, st, out);
+            launch_k(k_deltanet2<4, 4, 3>, dim3(d.nk, nseq), kDV, sm, s, L, d, y, st, out);
+        else if (keep_max <= PINFER_SPEC_MAX_K)
+            launch_k(k_deltanet2<4, kMaxRows, PINFER_SPEC_MAX_K>, dim3(d.nk, nseq), kDV, sm, s, L, d, y, st, out);
         else
-            launch_k(k_deltanet2<4>, dim3(d.nk, nseq), kDV, sizeof(float) * kDK * kDV, s, L, d, y, st, out);
+            launch_k(k_deltanet2<4>, dim3(d.nk, nseq), kDV, sm, s, L, d, y, st, out);
         return;
     }
     if (nseq != 1) return;   // callers check deltanet_batch_ok first
@@ -3255,7 +3588,8 @@ int kernels_init(int max_ctx, int hd, int rep) {
     raise_smem(k_mv_panel<4, 3, true>);
     if (max_ctx > 0) {
         raise_smem(k_deltanet2<4>, sizeof(float) * kDK * kDV);
-        raise_smem(k_deltanet2<4, 4>, sizeof(float) * kDK * kDV);
+        raise_smem(k_deltanet2<4, kMaxRows, PINFER_SPEC_MAX_K>, sizeof(float) * kDK * kDV);
+        raise_smem(k_deltanet2<4, 4, 3>, sizeof(float) * kDK * kDV);
         raise_smem(k_deltanet, deltanet_smem(rep));
         raise_smem(k_attn, ((size_t)hd + max_ctx) * sizeof(float));
         raise_smem(k_attn2, attn2_smem(max_ctx));
