@@ -236,7 +236,7 @@ __device__ __forceinline__ void norm_quant_smem(const float *sx, const float *sw
         float c = 0.0f;
         if (v < n) {
             const float *x = sx + (size_t)v * cols;
-#pragma unroll 8
+#pragma unroll 32
             for (int i = l; i < cols; i += 4) c = madd(c, x[i], x[i]);
         }
         const int base = lane & ~3;
@@ -246,19 +246,53 @@ __device__ __forceinline__ void norm_quant_smem(const float *sx, const float *sw
         if (v < n && l == 0) srr[v] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)cols), eps));
     }
     __syncthreads();
-    const int nb = cols >> 5, sub = lane & 7;
-    // four blocks per warp per step; every lane of the warp takes part in the shuffles
-    for (int u0 = warp * 4; u0 < n * nb; u0 += nw * 4) {
-        const int u = u0 + (lane >> 3);
-        const bool act = u < n * nb;
-        const int v = act ? u / nb : 0, b = act ? u % nb : 0, i = b * 32 + 4 * sub;
-        const float4 xv = *reinterpret_cast<const float4 *>(sx + (size_t)v * cols + i);
-        const float4 wv = *reinterpret_cast<const float4 *>(sw + i);
+    // A8: one thread per 32-column block (kern_quant_act: max, division, rounding and code sum
+    // are order-independent, so the bits equal the warp-wide form). Thread t starts at 16-byte
+    // chunk t % 8 of its block, so the 8 threads of a shared-memory phase read 8 distinct
+    // bank groups although their blocks are 128 bytes apart.
+    const int nb = cols >> 5;
+    (void)lane;
+    (void)warp;
+    (void)nw;
+    for (int u = tid; u < n * nb; u += blockDim.x) {
+        const int v = u / nb, b = u % nb;
         const float r = srr[v];
-        const float x4[4] = {__fmul_rn(__fmul_rn(xv.x, r), wv.x), __fmul_rn(__fmul_rn(xv.y, r), wv.y),
-                             __fmul_rn(__fmul_rn(xv.z, r), wv.z), __fmul_rn(__fmul_rn(xv.w, r), wv.w)};
-        quant_block_oct(x4, sub, act, sq + (size_t)v * qstride + b * 32, sd + (size_t)v * nb + b,
-                        sfs + (size_t)v * nb + b);
+        const float *xb = sx + (size_t)v * cols + b * 32, *wb = sw + b * 32;
+        float xn[32];
+        float a = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int ch = (k + tid) & 7;
+            const float4 xv = *reinterpret_cast<const float4 *>(xb + 4 * ch);
+            const float4 wv = *reinterpret_cast<const float4 *>(wb + 4 * ch);
+            xn[4 * k + 0] = __fmul_rn(__fmul_rn(xv.x, r), wv.x);
+            xn[4 * k + 1] = __fmul_rn(__fmul_rn(xv.y, r), wv.y);
+            xn[4 * k + 2] = __fmul_rn(__fmul_rn(xv.z, r), wv.z);
+            xn[4 * k + 3] = __fmul_rn(__fmul_rn(xv.w, r), wv.w);
+            // fmaxf keeps the non-NaN operand: the max of the block's non-NaN |x|, NaN if all
+            // are NaN, in any order (no seed value, as in the warp-wide form)
+            const float m4 = fmaxf(fmaxf(fabsf(xn[4 * k]), fabsf(xn[4 * k + 1])),
+                                   fmaxf(fabsf(xn[4 * k + 2]), fabsf(xn[4 * k + 3])));
+            a = k == 0 ? m4 : fmaxf(a, m4);
+        }
+        const float id = a > 0.0f ? __fdiv_rn(127.0f, a) : 0.0f;
+        int sum = 0;
+        int8_t *qb = sq + (size_t)v * qstride + b * 32;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int ch = (k + tid) & 7;
+            uint32_t packed = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int q = __float2int_rn(__fmul_rn(xn[4 * k + i], id));
+                sum += q;
+                packed |= (uint32_t)(uint8_t)(int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q)) << (8 * i);
+            }
+            *reinterpret_cast<uint32_t *>(qb + 4 * ch) = packed;
+        }
+        const float d = __fdiv_rn(a, 127.0f);
+        sd[(size_t)v * nb + b] = d;
+        sfs[(size_t)v * nb + b] = __fmul_rn(d, (float)sum);
     }
 }
 
@@ -332,6 +366,42 @@ __device__ __forceinline__ bool stage_act(uint64_t *abar, int n, int cols, const
     }
     __syncthreads();
     return mbar_wait(abar, 0);
+}
+
+// An int loaded where it is written (volatile asm keeps its place among the other volatile asm),
+// waited for only where it is used.
+__device__ __forceinline__ int ld_early_s32(const int *p) {
+    int v;
+    asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// The residual rows x [NMAX][cols] of a NORM panel kernel into shared memory with 16-byte loads
+// by every thread, rows 0..NMAX-1 whatever the pass's row count (the residual buffer holds
+// kMaxRows rows; rows the pass does not have are staged but never used), so the copy is
+// requested together with the Step block instead of after it. Needs rows_ld_ok.
+__device__ __forceinline__ bool rows_ld_ok(int cols, const NormIn &nin) {
+    return ((uintptr_t)nin.x & 15) == 0 && ((uintptr_t)nin.w & 15) == 0 && cols % 4 == 0;
+}
+template <int NMAX>
+__device__ __forceinline__ void stage_rows(int cols, const NormIn &nin, float *sx) {
+    const int tid = threadIdx.x, bd = blockDim.x;
+    const int total = NMAX * cols / 4;
+    const float4 *src = reinterpret_cast<const float4 *>(nin.x);
+    float4 *dst = reinterpret_cast<float4 *>(sx);
+    for (int base = 0; base < total; base += 8 * bd) {
+        float4 r[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = base + k * bd + tid;
+            if (i < total) r[k] = src[i];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int i = base + k * bd + tid;
+            if (i < total) dst[i] = r[k];
+        }
+    }
 }
 
 size_t tall_smem(int cols, int nmax, bool norm) {
@@ -632,16 +702,23 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
                         (m ? W1 : W0).w + ((size_t)panel * nsb + sb) * kUnitBytes, kUnitBytes, bars + warp);
         }
     }
+    const bool fast = NORM && rows_ld_ok(cols, nin);
+    if (fast) {   // the norm weight (constant: safe before pdl_wait)
+        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
+            reinterpret_cast<float4 *>(sw)[i] = reinterpret_cast<const float4 *>(nin.w)[i];
+    }
     pdl_wait();
     pdl_trigger();
-    const int n = st->n;
+    const int n = fast ? ld_early_s32(&st->n) : st->n;
+    if (fast) stage_rows<NMAX>(cols, nin, sx);   // beside the Step block
     if (n <= 0) {   // nothing to do: let the weight copy land before this CTA's shared memory goes
         __syncwarp();
         if (warp < nunit) mbar_wait(bars + warp, 0);
         return;
     }
     // activations into shared memory while the weights are in flight
-    if (!stage_act<NORM>(abar, n, cols, in, nin, sx, sw, sq, sd, sfs) && threadIdx.x == 0)
+    if (fast) __syncthreads();
+    else if (!stage_act<NORM>(abar, n, cols, in, nin, sx, sw, sq, sd, sfs) && threadIdx.x == 0)
         st->status = -90;   // device wait timed out: reported, no hang
     if (NORM) norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sd, sfs, srr);
     __syncthreads();
