@@ -915,7 +915,7 @@ __device__ float sumsq_ref(const float *x, int n) {
     float c = 0.0f;
     const int n4 = n & ~3;
     if (lane < 4) {
-#pragma unroll 8
+#pragma unroll 32
         for (int i = lane; i < n4; i += 4) c = madd(c, x[i], x[i]);
     } else if (lane == 4) {
         for (int i = n4; i < n; i++) c = madd(c, x[i], x[i]);
@@ -933,7 +933,7 @@ __device__ float sum4_ref(const float *a, int n) {
     float c = 0.0f;
     const int n4 = n & ~3;
     if (lane < 4) {
-#pragma unroll 8
+#pragma unroll 32
         for (int i = lane; i < n4; i += 4) c = __fadd_rn(c, a[i]);
     } else if (lane == 4) {
         for (int i = n4; i < n; i++) c = __fadd_rn(c, a[i]);
@@ -1117,7 +1117,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet(LinLayer L, LinDims d, cons
             float *vec = act ? ((u & 1) ? s.ck : s.cq) + (u >> 1) * kDK : s.cq;
             float c = 0.0f;
             if (act) {
-#pragma unroll 8
+#pragma unroll 32
                 for (int i = l; i < kDK; i += 4) c = madd(c, vec[i], vec[i]);
             }
             const int base = lane & ~3;
@@ -1711,21 +1711,27 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     __shared__ float red[32];
     __shared__ float s_mx, s_inv;
 
-    // V columns c*32 .. c*32+31 stream through a ring of kAttnRing chunks of kAttnChunk rows
-    // (8 x 16 bytes per row, one copy per thread per chunk, one cp.async group per chunk); the
-    // first kAttnRing - 1 chunks start now, behind the scores
+    // V columns c*32 .. c*32+31 stream through a ring of kAttnRing chunks of kAttnChunk rows,
+    // all of it warp 0's: lane l copies row l of a chunk (8 x 16 bytes), one cp.async group per
+    // chunk, so the P.V chain below waits on its own copies and a warp barrier only. The first
+    // kAttnRing - 1 chunks start now, behind the scores.
     const float *V = L.vc + (size_t)g * d.max_ctx * HD + c * kAttnSlice;
     const int nch = (np + kAttnChunk - 1) / kAttnChunk;
+    const int lane = tid & 31, warp = tid >> 5, nw = HD >> 5;
     auto issue_chunk = [&](int ch) {
-        const int r = ch * kAttnChunk + (tid >> 3), k = tid & 7;
-        if (ch < nch && r < np)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
-                         ::"r"(smem_u32(vs + ((size_t)(ch % kAttnRing) * kAttnChunk + (tid >> 3)) * kAttnSlice + 4 * k)),
-                         "l"(V + (size_t)r * HD + 4 * k) : "memory");
+        const int r = ch * kAttnChunk + lane;
+        if (ch < nch && r < np) {
+            const uint32_t dst = smem_u32(vs + ((size_t)(ch % kAttnRing) * kAttnChunk + lane) * kAttnSlice);
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16 * k), "l"(V + (size_t)r * HD + 4 * k)
+                             : "memory");
+        }
         cp_async_commit();   // one group per chunk, empty past the end
     };
-    static_assert(kAttnChunk * 8 == kAttnHd, "one 16-byte copy per thread per chunk");
-    for (int ch = 0; ch < kAttnRing - 1; ch++) issue_chunk(ch);
+    static_assert(kAttnChunk == 32, "one row per lane per chunk");
+    if (warp == 0)
+        for (int ch = 0; ch < kAttnRing - 1; ch++) issue_chunk(ch);
     q[tid] = qbuf[((size_t)row * d.nq + h) * HD + tid];
     const float gate = tid < kAttnSlice ? y[(size_t)row * d.ldy + (size_t)2 * HD * h + HD + c * kAttnSlice + tid] : 0.0f;
     __syncthreads();
@@ -1764,7 +1770,6 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     }
     cluster_arrive();   // this CTA is done reading its peers; waited on before exit
     __syncthreads();
-    const int lane = tid & 31, warp = tid >> 5, nw = HD >> 5;
     float m = -INFINITY;
     for (int p = tid; p < np; p += HD) m = fmaxf(m, att[p]);
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -1786,16 +1791,17 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     __syncthreads();
     const float inv = s_inv;
     for (int p = tid; p < np; p += HD) att[p] = __fmul_rn(att[p], inv);
+    __syncthreads();
 
-    // 3. ordered PV chain for this CTA's 32 columns (warp 0, chunk by chunk through the ring;
-    // every thread waits for its copy of chunk ch, refills the slot chunk ch - 1 used), gate, A8
+    // 3. ordered PV chain for this CTA's 32 columns (warp 0, chunk by chunk through the ring:
+    // its lanes wait for their copies of chunk ch, then refill the slot chunk ch - 1 used), gate, A8
     float o = 0.0f;
     const float *vp = vs + lane;
-    for (int ch = 0; ch < nch; ch++) {
+    for (int ch = 0; ch < nch && warp == 0; ch++) {
         cp_async_wait<kAttnRing - 2>();
-        __syncthreads();
+        __syncwarp();   // every lane's rows of chunk ch landed; every lane is done with chunk ch - 1
         issue_chunk(ch + kAttnRing - 1);
-        if (warp == 0) {
+        {
             const float *cv = vp + (size_t)(ch % kAttnRing) * kAttnChunk * kAttnSlice;
             const int p0c = ch * kAttnChunk, rows = min(kAttnChunk, np - p0c);
             int i = 0;
@@ -2393,7 +2399,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             float *vec = act ? ((u & 1) ? sk[u >> 1] : sq[u >> 1]) : sq[0];
             float c = 0.0f;
             if (act) {
-#pragma unroll 8
+#pragma unroll 32
                 for (int i = l; i < kDK; i += 4) c = madd(c, vec[i], vec[i]);
             }
             const int base = lane & ~3;
@@ -2507,7 +2513,7 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             const float *vec = so[act ? u : 0];
             float c = 0.0f;
             if (act) {
-#pragma unroll 8
+#pragma unroll 32
                 for (int i = l; i < kDV; i += 4) c = madd(c, vec[i], vec[i]);
             }
             const int base = lane & ~3;
@@ -2701,7 +2707,7 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
             float *vec = act ? ((u & 1) ? sk[u >> 1] : sq[u >> 1]) : sq[0];
             float cs = 0.0f;
             if (act) {
-#pragma unroll 8
+#pragma unroll 32
                 for (int i = l; i < kDK; i += 4) cs = madd(cs, vec[i], vec[i]);
             }
             const int base = lane & ~3;
@@ -2822,7 +2828,7 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
         const float *vec = so[act ? u : 0];
         float cs = 0.0f;
         if (act) {
-#pragma unroll 8
+#pragma unroll 32
             for (int i = l; i < kDV; i += 4) cs = madd(cs, vec[i], vec[i]);
         }
         const int base = lane & ~3;
