@@ -1711,13 +1711,23 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     __shared__ float red[32];
     __shared__ float s_mx, s_inv;
 
-    // V columns c*32 .. c*32+31 stream through a ring of kAttnRing chunks of kAttnChunk rows,
-    // all of it warp 0's: lane l copies row l of a chunk (8 x 16 bytes), one cp.async group per
-    // chunk, so the P.V chain below waits on its own copies and a warp barrier only. The first
-    // kAttnRing - 1 chunks start now, behind the scores.
+    // V columns c*32 .. c*32+31 stream through a ring of kAttnRing chunks of kAttnChunk rows
+    // (8 x 16 bytes per row). The first kAttnRing - 1 chunks start now, behind the scores, one
+    // copy per thread per chunk; the CTA waits for them once, before the P.V chain. The chain
+    // and the later chunks are warp 0's: lane l copies row l of a chunk, one cp.async group per
+    // chunk, so the chain waits on its own copies and a warp barrier only.
     const float *V = L.vc + (size_t)g * d.max_ctx * HD + c * kAttnSlice;
     const int nch = (np + kAttnChunk - 1) / kAttnChunk;
     const int lane = tid & 31, warp = tid >> 5, nw = HD >> 5;
+    static_assert(kAttnChunk * 8 == kAttnHd, "one 16-byte copy per thread per chunk");
+    for (int ch = 0; ch < kAttnRing - 1 && ch < nch; ch++) {
+        const int r = ch * kAttnChunk + (tid >> 3), k = tid & 7;
+        if (r < np)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+                         ::"r"(smem_u32(vs + ((size_t)ch * kAttnChunk + (tid >> 3)) * kAttnSlice + 4 * k)),
+                         "l"(V + (size_t)r * HD + 4 * k) : "memory");
+    }
+    cp_async_commit();
     auto issue_chunk = [&](int ch) {
         const int r = ch * kAttnChunk + lane;
         if (ch < nch && r < np) {
@@ -1730,8 +1740,6 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
         cp_async_commit();   // one group per chunk, empty past the end
     };
     static_assert(kAttnChunk == 32, "one row per lane per chunk");
-    if (warp == 0)
-        for (int ch = 0; ch < kAttnRing - 1; ch++) issue_chunk(ch);
     q[tid] = qbuf[((size_t)row * d.nq + h) * HD + tid];
     const float gate = tid < kAttnSlice ? y[(size_t)row * d.ldy + (size_t)2 * HD * h + HD + c * kAttnSlice + tid] : 0.0f;
     __syncthreads();
@@ -1791,6 +1799,7 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     __syncthreads();
     const float inv = s_inv;
     for (int p = tid; p < np; p += HD) att[p] = __fmul_rn(att[p], inv);
+    cp_async_wait<0>();   // the first kAttnRing - 1 chunks, every thread's copies
     __syncthreads();
 
     // 3. ordered PV chain for this CTA's 32 columns (warp 0, chunk by chunk through the ring:
@@ -1798,8 +1807,10 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
     float o = 0.0f;
     const float *vp = vs + lane;
     for (int ch = 0; ch < nch && warp == 0; ch++) {
-        cp_async_wait<kAttnRing - 2>();
-        __syncwarp();   // every lane's rows of chunk ch landed; every lane is done with chunk ch - 1
+        if (ch > 0) {   // chunk ch (>= kAttnRing - 1: this warp's copies) landed, ch - 1 consumed
+            cp_async_wait<kAttnRing - 2>();
+            __syncwarp();
+        }
         issue_chunk(ch + kAttnRing - 1);
         {
             const float *cv = vp + (size_t)(ch % kAttnRing) * kAttnChunk * kAttnSlice;
