@@ -375,6 +375,11 @@ __device__ __forceinline__ int ld_early_s32(const int *p) {
     asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p));
     return v;
 }
+__device__ __forceinline__ float ld_early_f32(const float *p) {
+    float v;
+    asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
 
 // The residual rows x [NMAX][cols] of a NORM panel kernel into shared memory with 16-byte loads
 // by every thread, rows 0..NMAX-1 whatever the pass's row count (the residual buffer holds
@@ -773,6 +778,9 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
     __syncthreads();
     const int row = panel * kPanelRows + lane;
     for (int v = warp; v < n; v += nw) {
+        // EPI 1: the residual this thread's chain adds to (its own element), requested before
+        // the chain so the read overlaps it
+        const float y_old = (EPI == 1 && row < W0.rows) ? ld_early_f32(y + (size_t)v * ldy + row) : 0.0f;
         float acc[2] = {0.0f, 0.0f};
 #pragma unroll
         for (int m = 0; m < 2; m++) {
@@ -781,7 +789,7 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
             const int32_t *is = isum + ((size_t)m * nb * NMAX + v) * 32 + lane;
             const float *dsp = ds + (size_t)m * nb * 32 + lane, *osp = os + (size_t)m * nb * 32 + lane;
             const float *dv = sd + (size_t)v * nb, *fv = sfs + (size_t)v * nb;
-#pragma unroll 4
+#pragma unroll 8
             for (int b = 0; b < nb; b++) {
                 const float s = (float)is[(size_t)b * NMAX * 32];
                 a = __fmaf_rn(s, __fmul_rn(dsp[b * 32], dv[b]), a);
@@ -796,7 +804,7 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
                              out.d + (size_t)v * nbo + panel, out.fs + (size_t)v * nbo + panel);
         } else if (row < W0.rows) {
             float *p = y + (size_t)v * ldy + row;
-            *p = EPI == 0 ? acc[0] : __fadd_rn(*p, acc[0]);
+            *p = EPI == 0 ? acc[0] : __fadd_rn(y_old, acc[0]);
         }
     }
 }
