@@ -354,13 +354,15 @@ Act mid_act(pinfer_ctx *c, int cols) {
 void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = false) {
     cudaStream_t s = c->stream;
     launch_embed(c->embed, c->step, c->x, c->H, s);
+    AttnDims ad = c->attd;
+    ad.rps = std::min(nmax, kMaxRows);   // attention grids cover the pass's rows only
     for (int l = 0; l < c->n_layers; l++) {
         auto &D = c->layers[l];
         if (D.is_full) {
             const Act o = mid_act(c, c->nq * c->hd);
             launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->attd.ldy, nmax, c->act_h, s);
-            launch_attn_prep(c->att[l], c->attd, c->y, c->qbuf, c->step, s);
-            launch_attn(c->att[l], c->attd, c->y, c->qbuf, c->step, o, s);
+            launch_attn_prep(c->att[l], ad, c->y, c->qbuf, c->step, s);
+            launch_attn(c->att[l], ad, c->y, c->qbuf, c->step, o, s);
             launch_matvec(D.out, o, c->step, c->x, c->H, 1, nmax, s);
         } else {
             const Act o = mid_act(c, c->vd);
@@ -419,8 +421,10 @@ void enqueue_mtp(pinfer_ctx *c, Step *ms, const float *h, int nmax, bool head, b
     launch_matvec(c->mtp_fc, c->act_cat, ms, c->x, c->H, 0, nmax, s);   // u = fc [e | h]
     const Act o = mid_act(c, c->nq * c->hd);
     launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, ms, c->y, c->attd.ldy, nmax, c->act_h, s);
-    launch_attn_prep(c->mtp_att, c->attd, c->y, c->qbuf, ms, s);
-    launch_attn(c->mtp_att, c->attd, c->y, c->qbuf, ms, o, s);
+    AttnDims ad = c->attd;
+    ad.rps = std::min(nmax, kMaxRows);   // attention grids cover the pass's rows only
+    launch_attn_prep(c->mtp_att, ad, c->y, c->qbuf, ms, s);
+    launch_attn(c->mtp_att, ad, c->y, c->qbuf, ms, o, s);
     launch_matvec(D.out, o, ms, c->x, c->H, 1, nmax, s);
     const Act hm = mid_act(c, c->ffn);
     launch_matvec_swiglu_norm(D.gate, D.up, c->x, D.post_norm, c->eps, ms, hm, nmax, c->act_h, s);
