@@ -3140,7 +3140,7 @@ __device__ int ng_draft(Step *st, int *out, int max, int *match) {
 // ---- adaptive policy (engine/src/spec_adapt.c, restated): EMA of verify-pass times per width,
 // decayed tokens and seconds of the speculative rounds, plain mode when speculation measures
 // >= 5 % slower than plain steps (or than any verify pass, the sure case), probes out of plain
-// mode after 8, 16, .. 64 plain steps, each probe judged on its own 2 rounds.
+// mode after 8, 16, .. 64 plain steps, each probe decided by its own 2 rounds.
 __device__ __forceinline__ double ad_ema(double old, double x) { return old <= 0.0 ? x : old + 0.25 * (x - old); }
 
 __device__ bool ad_plain_now(Step *st) {
