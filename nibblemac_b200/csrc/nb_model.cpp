@@ -38,8 +38,6 @@ const PqEntry *PqFile::find(const char *name) const {
     return nullptr;
 }
 
-static size_t q4k_bytes(uint64_t rows, uint64_t cols) { return rows / 4 * (cols / 256) * 576; }
-
 // entry_bytes (model.c:31-55): the size the dtype and shape imply, built against the file size
 static int entry_bytes(const PqEntry *e, uint64_t limit, uint64_t *bytes) {
     const uint64_t es = e->dtype == kPqF32 ? 4 : e->dtype == kPqBF16 ? 2 : 0;
