@@ -7,7 +7,7 @@ import os
 
 import numpy as np
 
-from ._lib import (GenOpts, Lib, PINFER_OK, Params, SpecParams, SpecStats, load_library,
+from ._lib import (GenOpts, Lib, PINFER_OK, SpecParams, SpecStats, load_library,
                    _c_float_p, _c_int32_p)
 
 
