@@ -102,14 +102,15 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def model_path(rank: int, dist, preset: str = "0.8b") -> Path:
+def model_path(rank: int, dist, preset: str = "0.8b", native: bool = True) -> Path:
     """The synthetic model of `preset`, written once by rank 0 (to a temporary name, then
-    renamed, so no rank opens a partial file)."""
+    renamed, so no rank opens a partial file). native=False writes it with numpy only (the
+    same bytes), for a process that must not load this package's libraries."""
     from nibblemac_b200 import pq
     path = ROOT / "_models" / f"bench-{preset}-s{SEED_MODEL}.pq"
     if rank == 0 and not path.exists():
         tmp = path.with_suffix(".tmp")
-        pq.make_synthetic(tmp, pq.PRESETS[preset], SEED_MODEL, std=0.02)
+        pq.make_synthetic(tmp, pq.PRESETS[preset], SEED_MODEL, std=0.02, native=native)
         os.replace(tmp, path)
     if dist is not None:
         dist.barrier()
@@ -202,51 +203,108 @@ def traffic_from_profiles() -> float | None:
     return None
 
 
-def cpu_baseline_sample(path: Path) -> dict:
-    """The reference's CPU path (oracle/_ref: the reference engine's own scalar C, one thread)
-    on a bounded sample of the same workload: 32-token context, 16 tokens, k = 3, p = 0.8;
-    tokens / seconds of the decode loop."""
-    from oracle import RefEngine
-    ref = RefEngine(path, max_ctx=256)
-    ctx = context_tokens(0, ref.n_vocab)[:32]
-    greedy = ref.generate(ctx, 16)
-    toks, st = ref.spec_generate(ctx, 16, K_DRAFT, greedy, 11, P_MAIN)
-    assert toks == greedy
-    sec = ref.last_decode_s
-    ref.close()
-    return {"value": round((len(toks) - 1) / sec, 3), "unit": UNIT, "cores": 1, "kind": "reference",
-            "sample": "reference engine (scalar C, oracle/_ref) on the 0.8B model: 32-token "
-                      "context, 16 tokens at k=3 p=0.8, decode loop timed"}
+REF_TOKENS = 16   # tokens per step of the reference CPU path: a bounded sample of the N_GEN
+
+
+class RefContext:
+    """The reference engine (oracle/_ref: its own scalar C sources, one thread) holding the
+    benchmark context, prefilled once and checkpointed; each step rewinds to it
+    (pinfer_checkpoint / pinfer_rewind, engine/include/pinfer.h:170-175) and runs the
+    synthetic-drafter verify loop for REF_TOKENS tokens at k = 3 continuing the context, the
+    same workload as the device's steps cut to a bounded sample."""
+
+    def __init__(self, path: Path) -> None:
+        from oracle import RefEngine
+        self.ref = RefEngine(path, max_ctx=CTX + N_GEN + 16)
+        self.ctx = context_tokens(0, self.ref.n_vocab)
+        t0 = time.perf_counter()
+        self.ref.reset()
+        self.ref.eval(self.ctx[:-1])
+        self.prefill_s = time.perf_counter() - t0
+        self.blob = self.ref.save_state()
+        self.ref.checkpoint()
+        self.greedy, _, st = self.ref.generate_mtp(self.ctx[-1:], REF_TOKENS, 0, append=True)
+        assert st == 0 and len(self.greedy) == REF_TOKENS
+
+    def step(self, seed: int, p: float = P_MAIN) -> tuple[int, float]:
+        """(decode-loop tokens, decode-loop seconds) of one sample."""
+        self.ref.rewind()
+        toks, _ = self.ref.spec_generate(self.ctx[-1:], REF_TOKENS, K_DRAFT, self.greedy, seed, p,
+                                         append=True)
+        assert toks == self.greedy, "reference speculative tokens differ from its greedy tokens"
+        return len(toks) - 1, self.ref.last_decode_s   # the first token comes from the prefill
+
+    def close(self) -> None:
+        self.ref.close()
+
+
+def ref_sample_text(steps: int) -> str:
+    return (f"reference engine (scalar C, oracle/_ref, 1 thread) on the same 0.8B-shaped model: "
+            f"the {CTX}-token context prefilled once and restored by pinfer_rewind before each "
+            f"step, then {REF_TOKENS} of the {N_GEN} generated tokens at k={K_DRAFT} p={P_MAIN} "
+            f"per step, {steps} steps, decode loop timed")
+
+
+def cpu_baseline_sample(path: Path, dev_blob: bytes, dev_greedy: list[int]) -> dict:
+    """The reference's CPU path on a bounded sample of the bench workload (RefContext), after
+    two checks against the device run on the same context: the reference's state blob after
+    the context equals the device's byte for byte, and its greedy tokens continuing it equal
+    the device's first REF_TOKENS tokens."""
+    rc = RefContext(path)
+    try:
+        assert rc.blob == dev_blob, "reference state after the bench context differs from the device's"
+        assert rc.greedy == dev_greedy[:REF_TOKENS], "reference greedy tokens differ from the device's"
+        steps = 2
+        toks = secs = 0.0
+        for i in range(steps):
+            n, t = rc.step(1000 + i)
+            toks += n
+            secs += t
+    finally:
+        rc.close()
+    return {"value": round(toks / secs, 3), "unit": UNIT, "cores": 1, "kind": "reference",
+            "sample": ref_sample_text(steps), "tokens_match_device": True, "state_matches_device": True}
+
+
+def bench_config(world: int) -> dict:
+    return {"workload": "configs[2]: Qwen3.5-0.8B-shaped Q4K, k=3 speculation, "
+                        f"p={P_MAIN}, {CTX}-token context, {N_GEN} generated",
+            "k": K_DRAFT, "p": P_MAIN, "context": CTX, "generated": N_GEN,
+            "parallelism": f"replicas x{world}" if world > 1 else "single replica",
+            "l2": "inputs larger than L2 (425 MB of weights streamed per round)"}
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """--impl reference: the reference's own CPU implementation of the path (oracle/_ref,
+    built from its sources; scalar C, whose thread pool is a stub, so one host thread) on this
+    arm's workload. Each step is a bounded sample (RefContext). Loads no library of this
+    package: the model file, if missing, is written by the numpy-only writer."""
     if rank != 0:
         return
-    from oracle import RefEngine
-    path = model_path(0, None)
-    ref = RefEngine(path, max_ctx=256)
-    ctx = context_tokens(0, ref.n_vocab)[:32]
-    n_gen = 12
-    greedy = ref.generate(ctx, n_gen)
+    path = model_path(0, None, native=False)
+    rc = RefContext(path)
     secs, toks = [], 0
     for i in range(args.warmup + args.steps):
-        out, st = ref.spec_generate(ctx, n_gen, K_DRAFT, greedy, 11 + i, P_MAIN)
-        assert out == greedy
+        n, t = rc.step(11 + i)
         if i >= args.warmup:
-            secs.append(ref.last_decode_s)
-            toks += len(out) - 1   # the decode loop's tokens (the first comes from the prefill)
-    ref.close()
+            secs.append(t)
+            toks += n
+    rc.close()
     total = sum(secs)
     value = toks / total
+    cfg = bench_config(1)
+    if world > 1:
+        cfg["parallelism"] = f"single process (rank 0 of {world})"
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(total * 1000 / args.steps, 1), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "q4k x int8 -> fp32", "data": "synthetic",
-            "config": {"workload": "configs[2] sample: 0.8B-shaped Q4K model, k=3, p=0.8, "
-                                   f"32-token context, {n_gen} tokens per step (CPU-bounded)",
-                       "parallelism": "single process"},
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4k x int8 -> fp32",
+            "data": "synthetic (random-init 0.8B-shaped weights, uniform-random context, "
+                    "synthetic drafter)",
+            "config": cfg,
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": 1, "kind": "reference",
-                             "sample": f"reference engine scalar C, {n_gen} tokens per step"},
+                             "sample": ref_sample_text(args.steps),
+                             "prefill_s": round(rc.prefill_s, 1)},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -256,32 +314,23 @@ CTX5 = 4096
 N_SEQ4, GEN4 = 256, 256
 
 
-def run_config4(args, rank: int, world: int, local: int) -> None:
-    """BASELINE configs[3]: 256 independent requests per GPU (uniform-random prompts of length
-    U[32, 1024], 256 generated tokens each, k = 3 at p = 0.8) on the 0.8B-shaped model, all in
-    one multi-sequence batch (pinfer_b200_batch): the prompts' prefill and every verify round run
-    the 256 sequences in merged passes, so each projection is one tcgen05 tensor-core GEMM over
-    up to 4096 prefill rows or 1024 verify rows; replicas across GPUs (weak scaling). The greedy
-    streams the drafter needs come from an untimed plain (k = 0) batch run, whose tokens equal
-    single-sequence greedy decoding. value = generated tokens / device time of the whole batched
-    generation (prefill included; CUDA events on the batch's stream), max over ranks; e2e = the
-    same over the host wall time of the API call (prompts in, tokens out)."""
-    import datetime
+def measure_config4(m, rank: int, world: int, local: int, dist, dev_tensors: bool) -> dict | None:
+    """configs[3]: 256 independent requests per GPU (uniform-random prompts of length
+    U[32, 1024], 256 generated tokens each, k = 3 at p = 0.8) on the 0.8B-shaped model `m`, all
+    in one multi-sequence batch (pinfer_b200_batch on m's weights): the prompts' prefill and every
+    verify round run the 256 sequences in merged passes, so each projection is one tcgen05
+    tensor-core GEMM over up to 4096 prefill rows or 1024 verify rows; one replica per GPU (weak
+    scaling). The greedy streams the drafter needs come from an untimed plain (k = 0) batch run,
+    whose tokens equal single-sequence greedy decoding. value = generated tokens of all ranks /
+    max over ranks of the device time of the whole batched generation (prefill included; CUDA
+    events on the batch's stream); e2e = the same over the host wall time of the API call
+    (prompts in, tokens out). Returns the record on rank 0."""
     import torch
-    sys.path.insert(0, str(ROOT / "oracle"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=1800))
-    from nibblemac_b200.model import Model
-    path = model_path(rank, dist)
     max_ctx = 1024 + GEN4 + 16
-    base = Model(path, max_ctx=max_ctx)
-    batch = base.batch(N_SEQ4, max_ctx, max_k=K_DRAFT)
+    batch = m.batch(N_SEQ4, max_ctx, max_k=K_DRAFT)
     rng = np.random.default_rng(777 + rank)
     lens = rng.integers(32, 1025, N_SEQ4)
-    prompts = [rng.integers(0, base.n_vocab, int(n)).astype(np.int32) for n in lens]
+    prompts = [rng.integers(0, m.n_vocab, int(n)).astype(np.int32) for n in lens]
     seeds = [9000 + j for j in range(N_SEQ4)]
     # untimed: the greedy streams (shorter where the random model emits EOS), then a short run
     # that captures the k = 3 round graph
@@ -306,30 +355,55 @@ def run_config4(args, rank: int, world: int, local: int) -> None:
     t = ev0.elapsed_time(ev1) / 1000.0
     wall = w1 - w0
     if dist is not None:
-        tt = torch.tensor([t, wall], dtype=torch.float64)
+        tt = torch.tensor([t, wall], dtype=torch.float64, device="cuda" if dev_tensors else "cpu")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t, wall = float(tt[0].item()), float(tt[1].item())
+        t, wall = tt.tolist()
     batch.close()
+    if rank != 0:
+        return None
+    tokens = sum(len(g) for g in greedy) * world
+    h2d = int(lens.sum()) * 4 + N_SEQ4 * GEN4 * 4 + N_SEQ4 * 12
+    return {
+        "metric": "greedy spec-decode tok/s (k=3), multi-stream, whole job", "value": round(tokens / t, 1),
+        "unit": UNIT, "n_gpus": world, "ms": round(t * 1000.0, 1), "scaling": "weak",
+        "workload": f"configs[3]: {N_SEQ4} requests per GPU, prompts U[32,1024], {GEN4} generated "
+                    f"each, k=3, p={P_MAIN}; prefill inside the timed span",
+        "batching": f"{N_SEQ4} sequences in merged passes (verify rows {N_SEQ4 * (K_DRAFT + 1)})",
+        "parallelism": f"replicas x{world}" if world > 1 else "single replica",
+        "batch_rounds": batch_rounds, "rounds_per_gpu": int(st.rounds), "accepted_per_gpu": int(st.accepted),
+        "decode_ms": round(decode_ms, 1), "prefill_and_setup_ms": round(t * 1000.0 - decode_ms, 1),
+        "mean_prompt": float(lens.mean()), "l2": "inputs larger than L2 (weights 425 MB, states 4.8 GB)",
+        "e2e": {"value": round(tokens / wall, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": N_SEQ4 * GEN4 * 4 + N_SEQ4 * 8},
+        "clocks": clk.summary()}
+
+
+def run_config4(args, rank: int, world: int, local: int) -> None:
+    """--config4: the configs[3] record (measure_config4) as its own JSON line."""
+    import datetime
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=1800))
+    from nibblemac_b200.model import Model
+    path = model_path(rank, dist)
+    base = Model(path, max_ctx=256)
+    rec = measure_config4(base, rank, world, local, dist, False)
     base.close()
     if rank == 0:
-        tokens = sum(len(g) for g in greedy) * world
-        h2d = int(lens.sum()) * 4 + N_SEQ4 * GEN4 * 4 + N_SEQ4 * 12
-        print(json.dumps({
-            "metric": "greedy spec-decode tok/s (k=3), multi-stream, per job", "value": round(tokens / t, 1),
-            "unit": UNIT, "n_gpus": world, "steps": 1, "warmup": 1, "ms_per_step": round(t * 1000.0, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4k x int8 -> fp32",
-            "data": "synthetic (random-init 0.8B-shaped weights, uniform-random prompts, synthetic drafter)",
-            "config": {"workload": f"configs[3]: {N_SEQ4} requests per GPU, prompts U[32,1024], {GEN4} "
-                                   f"generated each, k=3, p={P_MAIN}; prefill inside the timed span",
-                       "batching": f"{N_SEQ4} sequences in merged passes (verify rows {N_SEQ4 * (K_DRAFT + 1)})",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single replica",
-                       "batch_rounds": batch_rounds, "rounds_per_gpu": int(st.rounds),
-                       "accepted_per_gpu": int(st.accepted),
-                       "decode_ms": round(decode_ms, 1), "prefill_and_setup_ms": round(t * 1000.0 - decode_ms, 1),
-                       "mean_prompt": float(lens.mean()), "l2_flush": "inputs larger than L2 (weights 425 MB)"},
-            "e2e": {"value": round(tokens / wall, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": N_SEQ4 * GEN4 * 4 + N_SEQ4 * 8},
-            "clocks": clk.summary()}), flush=True)
+        line = {k: rec[k] for k in ("metric", "value", "unit", "n_gpus")}
+        line.update({"steps": 1, "warmup": 1, "ms_per_step": rec["ms"], "higher_is_better": True,
+                     "scaling": "weak", "vs_baseline": None, "dtype": "q4k x int8 -> fp32",
+                     "data": "synthetic (random-init 0.8B-shaped weights, uniform-random prompts, "
+                             "synthetic drafter)",
+                     "config": {k: rec[k] for k in ("workload", "batching", "parallelism", "batch_rounds",
+                                                    "rounds_per_gpu", "accepted_per_gpu", "decode_ms",
+                                                    "prefill_and_setup_ms", "mean_prompt", "l2")},
+                     "e2e": rec["e2e"], "clocks": rec["clocks"]})
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -535,6 +609,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="leave the configs[3] multi-stream record out of the default line")
     ap.add_argument("--config4", action="store_true",
                     help="BASELINE configs[3]: 256 requests per GPU in one multi-sequence batch "
                          "(one JSON line)")
@@ -594,6 +670,7 @@ def main() -> None:
     ctx = context_tokens(rank, m.n_vocab)
     m.reset()
     m.eval(ctx[:-1], logits=False)
+    dev_blob = m.save_state() if rank == 0 else b""
     m.checkpoint()
     greedy, _, st0, _ = m.generate_synthetic_ex(ctx[-1:], N_GEN, 0, np.zeros(N_GEN, np.int32), 0, 0.0,
                                                 append=True)
@@ -665,6 +742,8 @@ def main() -> None:
     config2 = {"tok_s": round((N_GEN - 1) / (statistics.median(c2) / 1000.0), 1), "prompt": 64,
                "generated": N_GEN, "k": 0, "ms": round(statistics.median(c2), 3)}
 
+    config4 = None if args.no_config4 else measure_config4(m, rank, world, local, dist, True)
+
     roof = None
     extra = {}
     if rank == 0:
@@ -683,19 +762,16 @@ def main() -> None:
                 "scaling": "weak", "vs_baseline": None, "dtype": "q4k x int8 -> fp32",
                 "data": "synthetic (random-init 0.8B-shaped weights, uniform-random context, "
                         "synthetic drafter)",
-                "config": {"workload": "configs[2]: Qwen3.5-0.8B-shaped Q4K, k=3 speculation, "
-                                       f"p={P_MAIN}, {CTX}-token context, {N_GEN} generated",
-                           "k": K_DRAFT, "p": P_MAIN, "context": CTX, "generated": N_GEN,
-                           "parallelism": f"replicas x{world}" if world > 1 else "single replica",
-                           "l2": "inputs larger than L2 (425 MB of weights streamed per round)"},
+                "config": bench_config(world),
                 "e2e": {"value": round(e2e, 2), "unit": UNIT,
                         "h2d_bytes_per_step": 4 * (1 + N_GEN), "d2h_bytes_per_step": 4 * N_GEN},
                 "gpu_launches": int(rounds * kernels_per_round * world),
                 "kernels_per_round": kernels_per_round, "rounds": rounds,
-                "sweep": sweep, "config2_plain": config2, "roofline": roof, "clocks": clk.summary()}
+                "sweep": sweep, "config2_plain": config2, "roofline": roof, "clocks": clk.summary(),
+                "config4": config4}
         line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_sample(path)
+            line["cpu_baseline"] = cpu_baseline_sample(path, dev_blob, greedy)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

@@ -163,6 +163,11 @@ int nb_libm_selftest(int threads, long long stride, long long *mismatches);
 int nb_libm_eval_host(int fn, const float *x, float *y, long long n);
 int nb_libm_eval_device(int fn, const float *x, float *y, long long n, void *stream);
 
+/* Test hook of the bounded device waits: a one-warp kernel waits on an mbarrier whose expected
+ * bytes never arrive, gives up after spin_limit polls (1 .. 2^22), records -90 in a status word
+ * and returns; *status_out receives that word. 0, -4 (arguments), -3 (CUDA error). */
+int nb_test_bounded_wait(unsigned spin_limit, int *status_out);
+
 /* Allocation-free Q4K x A8 matmul. No counterpart in the reference (its CPU pf_matmul takes
  * caller buffers and needs no scratch).
  * Y [n][rows] = W (device panel layout) x A8(X [n][cols]), the same kernels and the same
@@ -176,9 +181,14 @@ int nb_libm_eval_device(int fn, const float *x, float *y, long long n, void *str
  * device address with that device current and sets the kernels' shared-memory limits) and
  * should come before any stream capture. One scratch per device: calls that overlap in time on
  * one device (other streams or threads) race on it and must be serialised by the caller.
- * 0, -4 (arguments), -3 (CUDA error). */
+ * The call returns once Y is written (it waits for `stream`), after reading the status word of
+ * the kernels' bounded device waits: -3 with pinfer_b200_last_error set if one gave up.
+ * The scratch takes NB_MV_STATIC_BYTES of every device that loads the library, until exit.
+ * 0, -4 (arguments), -3 (CUDA error or a device wait that gave up). */
 #define NB_MV_STATIC_MAX_N 16
 #define NB_MV_STATIC_MAX_COLS 8192
+#define NB_MV_STATIC_STEP_BYTES 768       /* the control block, padded to 256 B */
+#define NB_MV_STATIC_BYTES 164608         /* 768 + 16 x 8192 + 2 x 16 x 256 x 4 */
 int nb_mv_run_static(const void *W, int rows, int cols, const float *X, int n, float *Y,
                      void *stream);
 

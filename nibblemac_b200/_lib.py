@@ -139,6 +139,7 @@ _OPTIONAL = {
     "nb_mv_run_static": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "nb_argmax_key": (ctypes.c_ulonglong, [ctypes.c_float, ctypes.c_int]),
+    "nb_test_bounded_wait": (ctypes.c_int, [ctypes.c_uint, ctypes.POINTER(ctypes.c_int)]),
     "nb_libm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_longlong, ctypes.POINTER(ctypes.c_longlong)]),
     "nb_libm_eval_host": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong]),
     "nb_libm_eval_device": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,

@@ -8,14 +8,16 @@
 #include <new>
 
 #include "nb_b200.h"
+#include "nb_dev.cuh"
 #include "nb_engine.h"
 
 using namespace nb;
 
 // ------------------------------------------------------------------ allocation-free scratch
 // nb_mv_run_static keeps its scratch in this array of the library's own device image instead of
-// cudaMalloc'd buffers. Layout: [Step control block, padded to 256 B][A8 codes q: 16 x 8192
-// int8][block scales d: 16 x 256 fp32][block sums fsum: 16 x 256 fp32], 164,096 bytes per device.
+// cudaMalloc'd buffers. Layout: [Step control block, padded to a multiple of 256 B][A8 codes q:
+// 16 x 8192 int8][block scales d: 16 x 256 fp32][block sums fsum: 16 x 256 fp32]; kStaticBytes
+// per device (pinned below).
 namespace {
 constexpr int kStaticMaxCols = NB_MV_STATIC_MAX_COLS;
 constexpr int kStaticMaxN = NB_MV_STATIC_MAX_N;
@@ -28,6 +30,9 @@ constexpr size_t kStaticDBytes = sizeof(float) * kStaticMaxN * (kStaticMaxCols /
 constexpr size_t kStaticFsOff = kStaticDOff + kStaticDBytes;
 constexpr size_t kStaticBytes = kStaticFsOff + kStaticDBytes;
 constexpr int kStaticMaxDevices = 64;
+// The documented size (include/nb_b200.h): a change of the control block's size shows here.
+static_assert(kStaticQOff == NB_MV_STATIC_STEP_BYTES, "static scratch: control block size changed");
+static_assert(kStaticBytes == NB_MV_STATIC_BYTES, "static scratch: total size changed");
 
 std::mutex g_static_mu;
 std::atomic<unsigned char *> g_static_addr[kStaticMaxDevices];
@@ -36,20 +41,17 @@ std::atomic<unsigned char *> g_static_addr[kStaticMaxDevices];
 static __device__ __align__(256) unsigned char g_mv_static_scratch[kStaticBytes];
 
 namespace {
-// The scratch's address on the current device. The first call on a device looks the symbol up
-// (which makes the runtime load this library's device image there if it has not yet) and raises
-// the matvec kernels' shared-memory limits on that device; later calls read the cached pointer.
+// The scratch's address on the current device, looked up on every call with that device current
+// (a cheap table read once the runtime has loaded this library's device image there; the first
+// lookup loads it). When the address differs from the one cached for the device (the first call,
+// or a primary context torn down by cudaDeviceReset and made anew, which also drops the kernels'
+// shared-memory limits), the matvec kernels' shared-memory limits are raised again before use.
 unsigned char *static_scratch() {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kStaticMaxDevices) {
         set_last_error("nb_mv_run_static: no current CUDA device (or device index >= 64)");
         return nullptr;
     }
-    unsigned char *p = g_static_addr[dev].load(std::memory_order_acquire);
-    if (p) return p;
-    std::lock_guard<std::mutex> lock(g_static_mu);
-    p = g_static_addr[dev].load(std::memory_order_relaxed);
-    if (p) return p;
     void *addr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&addr, g_mv_static_scratch);
     if (e != cudaSuccess || !addr) {
@@ -59,11 +61,14 @@ unsigned char *static_scratch() {
         set_last_error(b);
         return nullptr;
     }
+    unsigned char *p = static_cast<unsigned char *>(addr);
+    if (g_static_addr[dev].load(std::memory_order_acquire) == p) return p;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (g_static_addr[dev].load(std::memory_order_relaxed) == p) return p;
     if (kernels_init(0, 0, 0) != 0) {
         set_last_error("nb_mv_run_static: raising the kernels' shared-memory limits failed");
         return nullptr;
     }
-    p = static_cast<unsigned char *>(addr);
     g_static_addr[dev].store(p, std::memory_order_release);
     return p;
 }
@@ -336,7 +341,58 @@ int nb_mv_run_static(const void *W, int rows, int cols, const float *X, int n, f
     m.npanels = (rows + kPanelRows - 1) / kPanelRows;
     m.nsb = cols / 256;
     launch_matvec(m, act, step, Y, rows, 0, n, s);
-    return cudaGetLastError() == cudaSuccess ? PINFER_OK : PINFER_E_NOMEM;
+    if (cudaGetLastError() != cudaSuccess) {
+        set_last_error("nb_mv_run_static: kernel launch failed");
+        return PINFER_E_NOMEM;
+    }
+    // the status word after the launches: a bounded device wait that gave up leaves -90 there
+    // and Y incomplete, so the call waits for its stream and reports it
+    int status = 0;
+    if (cudaMemcpyAsync(&status, &step->status, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        set_last_error("nb_mv_run_static: reading the status word failed");
+        return PINFER_E_NOMEM;
+    }
+    if (status != 0) {
+        char b[160];
+        snprintf(b, sizeof b, "nb_mv_run_static: a device wait gave up (status %d); Y is not valid", status);
+        set_last_error(b);
+        return PINFER_E_NOMEM;
+    }
+    return PINFER_OK;
+}
+
+// Test hook: one warp waits on an mbarrier that expects transaction bytes no copy will ever
+// bring, with `spin_limit` polls per wait, as every bounded wait of the kernels above does. The
+// wait gives up, the warp records -90 in the status word, waits once more (bounded) as the
+// kernels do for their copies in flight, and returns; nothing is copied, so nothing is left in
+// flight. *status_out receives the status word. 0, or -4 / -3.
+static __global__ void k_wait_timeout_probe(int *status, unsigned spin_limit) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect(&bar, 1024u);   // the one arrival, 1024 bytes that never come
+    }
+    __syncwarp();
+    if (!mbar_wait(&bar, 0, spin_limit)) {
+        if (threadIdx.x == 0) *status = -90;
+        mbar_wait(&bar, 0, spin_limit);
+    }
+}
+
+int nb_test_bounded_wait(unsigned spin_limit, int *status_out) {
+    if (!status_out || spin_limit == 0 || spin_limit > (1u << 22)) return PINFER_E_ARG;
+    int *d = nullptr;
+    if (cudaMalloc(&d, sizeof(int)) != cudaSuccess) return PINFER_E_NOMEM;
+    bool ok = cudaMemset(d, 0, sizeof(int)) == cudaSuccess;
+    if (ok) {
+        k_wait_timeout_probe<<<1, 32>>>(d, spin_limit);
+        ok = cudaGetLastError() == cudaSuccess &&
+             cudaMemcpy(status_out, d, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess;
+    }
+    cudaFree(d);
+    return ok ? PINFER_OK : PINFER_E_NOMEM;
 }
 
 }  // extern "C"

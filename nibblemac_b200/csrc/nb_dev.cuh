@@ -142,11 +142,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
-// wait for phase `parity` of the barrier; false after kSpinLimit polls (the caller reports
+// wait for phase `parity` of the barrier; false after `limit` polls (the caller reports
 // the timeout instead of hanging)
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned limit = kSpinLimit) {
     const uint32_t a = smem_u32(bar);
-    for (unsigned i = 0; i < kSpinLimit; i++) {
+    for (unsigned i = 0; i < limit; i++) {
         uint32_t ok;
         asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
                      "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(a), "r"(parity) : "memory");

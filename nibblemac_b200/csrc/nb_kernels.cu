@@ -365,7 +365,9 @@ __device__ __forceinline__ bool stage_act(uint64_t *abar, int n, int cols, const
         }
     }
     __syncthreads();
-    return mbar_wait(abar, 0);
+    if (mbar_wait(abar, 0)) return true;
+    mbar_wait(abar, 0);   // timed out: a second bounded wait lets the copies in flight land
+    return false;
 }
 
 // An int loaded where it is written (volatile asm keeps its place among the other volatile asm),
@@ -407,6 +409,13 @@ __device__ __forceinline__ void stage_rows(int cols, const NormIn &nin, float *s
             if (i < total) dst[i] = r[k];
         }
     }
+}
+
+// After a timed-out wait on unit u of a warp's kRing-deep ring: units u .. u + kRing - 1 may
+// still be in flight into this CTA's shared memory, so wait for each once more (bounded) before
+// the warp returns.
+__device__ __forceinline__ void drain_ring(uint64_t *bars, int u, int total) {
+    for (int j = u; j < u + kRing && j < total; j++) mbar_wait(bars + j % kRing, (uint32_t)(j / kRing) & 1u);
 }
 
 size_t tall_smem(int cols, int nmax, bool norm) {
@@ -469,6 +478,7 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head(Mat W0, Act in, Nor
         const int slot = u % kRing;
         if (!mbar_wait(bars + slot, (uint32_t)(u / kRing) & 1u)) {
             if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
+            drain_ring(bars, u, total);
             return;
         }
         const uint8_t *sp = ring + (size_t)slot * kUnitBytes + lane * 16;
@@ -591,6 +601,7 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in,
         const int slot = u % kRing;
         if (!mbar_wait(bars + slot, (uint32_t)(u / kRing) & 1u)) {
             if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
+            drain_ring(bars, u, total);
             return;
         }
         const uint8_t *sp = ring + (size_t)slot * kUnitBytes;
@@ -736,6 +747,7 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
         }
         if (!mbar_wait(bars + warp, (uint32_t)it & 1u)) {
             if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
+            mbar_wait(bars + warp, (uint32_t)it & 1u);   // the unit in flight lands before the warp goes
             return;
         }
         const uint8_t *sp = slot + lane * 16;
@@ -2371,7 +2383,10 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
         const float sp = xs > 20.0f ? xs : glibc_log1pf(glibc_expf(xs));
         sdec[t] = glibc_expf(__fmul_rn(L.A[h], sp));
     }
-    if (!mbar_wait(&sbar[0], 0) && j == 0) st->status = -90;   // timed out: reported, no hang
+    if (!mbar_wait(&sbar[0], 0)) {   // the rows: timed out, reported, no hang; a second
+        if (j == 0) st->status = -90;   // bounded wait lets the copies in flight land
+        mbar_wait(&sbar[0], 0);
+    }
     __syncthreads();
     // ---- pending conv commit, then conv + SiLU for the three channels
     // (the three channels advance together: three independent chains per token)
@@ -2433,7 +2448,10 @@ __global__ void __launch_bounds__(128, 1) k_deltanet2(LinLayer L, LinDims d, con
             }
         }
     }
-    if (!mbar_wait(&sbar[1], 0) && j == 0) st->status = -90;   // the state
+    if (!mbar_wait(&sbar[1], 0)) {   // the state: timed out, reported, no hang; a second
+        if (j == 0) st->status = -90;   // bounded wait lets the copies in flight land
+        mbar_wait(&sbar[1], 0);
+    }
     __syncthreads();
 
     // ---- recurrence: replay + token 0 first sweep, then fused sweeps (column j in smem).

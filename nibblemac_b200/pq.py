@@ -78,7 +78,13 @@ TINY = Dims(hidden=256, ffn=512, n_layers=4, vocab=2048, n_heads=1, n_kv_heads=1
 SMALL = Dims(hidden=512, ffn=1024, n_layers=8, vocab=8192, n_heads=4, n_kv_heads=2,
              head_dim=256, rot_dim=64, lin_k_heads=4, lin_v_heads=4, lin_k_dim=128,
              lin_v_dim=128, eos_id=8191)
-PRESETS = {"0.8b": QWEN35_08B, "2b": QWEN35_2B, "tiny": TINY, "small": SMALL}
+# The two configured shapes at reduced depth (one 3:1 group: 3 DeltaNet layers, then full
+# attention) with every width and the full vocabulary kept: what the reference engine, run on
+# the host, can check bit for bit within a test's time.
+QWEN35_08B_4L = Dims(**{**asdict(QWEN35_08B), "n_layers": 4})
+QWEN35_2B_4L = Dims(**{**asdict(QWEN35_2B), "n_layers": 4})
+PRESETS = {"0.8b": QWEN35_08B, "2b": QWEN35_2B, "tiny": TINY, "small": SMALL,
+           "0.8b-4l": QWEN35_08B_4L, "2b-4l": QWEN35_2B_4L}
 
 
 def _quant_lib() -> ctypes.CDLL:
@@ -109,6 +115,97 @@ def quantize_q4k(w: np.ndarray, threads: int | None = None) -> bytes:
     if rc != 0:
         raise ValueError("quantisation failed")
     return out.tobytes()
+
+
+_F = np.float32
+
+
+def _clip(v: np.ndarray, hi: float) -> np.ndarray:
+    """np.clip(v, 0, hi) in float32 (NaN passes through)."""
+    return np.clip(v, _F(0.0), _F(hi))
+
+
+def _posmax(v: np.ndarray) -> np.ndarray:
+    """max(v, 0) with NaN passed through, float32."""
+    return np.maximum(v, _F(0.0))
+
+
+def _fit(x: np.ndarray, q: np.ndarray, d: np.ndarray, m: np.ndarray, sign: float):
+    """One least-squares refit of (scale, offset) over groups of 32 (last axis) from codes q:
+    n = 32; den = n sqq - sq^2; d' = (n sqx - sq sx) / den; m' = sign (sx - d' sq) / n where
+    den > 0, else the old (d, m). Group sums are numpy float32 sums over a contiguous axis of 32,
+    the summation order of the reference quantiser."""
+    n = _F(32.0)
+    sq, sx = q.sum(-1), x.sum(-1)
+    sqq, sqx = (q * q).sum(-1), (q * x).sum(-1)
+    den = n * sqq - sq * sq
+    ok = den > _F(0.0)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        dn = np.where(ok, (n * sqx - sq * sx) / np.where(ok, den, _F(1.0)), d)
+        mn = np.where(ok, (sx - dn * sq) / n, m)
+    return dn.astype(_F), (mn if sign > 0 else np.where(ok, -mn, m)).astype(_F)
+
+
+def _q4k_rows_numpy(w: np.ndarray) -> bytes:
+    """Q4K_G32 of whole 4-row tiles, vectorised over every group: the same float32 steps as the
+    C quantiser (csrc/pq_quant.c, which restates tools/quant.py quant_asym4 :78-105, quant_q4k
+    :108-141, _pack6 :210-217 and pack_q4k :220-244)."""
+    rows, cols = w.shape
+    nsb = cols // 256
+    x = w.reshape(rows, nsb, 8, 32)
+    f16 = lambda v: v.astype(np.float16).astype(_F)
+    # asym4 per group of 32: 4 refits of (d, m) with codes against the fp16-rounded fit
+    lo, hi = x.min(-1), x.max(-1)
+    d, m = ((hi - lo) / _F(15.0)).astype(_F), lo
+    with np.errstate(divide="ignore", invalid="ignore"):
+        for it in range(5):
+            d16, m16 = f16(d), f16(m)
+            safe = np.where(d16 == _F(0.0), _F(1.0), d16)
+            q = _clip(np.rint((x - m16[..., None]) / safe[..., None]), 15.0)
+            if it == 4:
+                break
+            d, m = _fit(x, q, d, m, 1.0)
+        dg, mn = d16, _posmax(-m16)
+        # superblock scales: 6-bit multiples of fp16 D = max d / 63 and M = max m / 63
+        D, M = f16(dg.max(-1) / _F(63.0)), f16(mn.max(-1) / _F(63.0))
+        Ds = np.where(D == _F(0.0), _F(1.0), D)[..., None]
+        Ms = np.where(M == _F(0.0), _F(1.0), M)[..., None]
+        sq, mq = _clip(np.rint(dg / Ds), 63.0), _clip(np.rint(mn / Ms), 63.0)
+        for it in range(3):
+            d_eff, m_eff = D[..., None] * sq, M[..., None] * mq
+            safe = np.where(d_eff == _F(0.0), _F(1.0), d_eff)
+            q = _clip(np.rint((x + m_eff[..., None]) / safe[..., None]), 15.0)
+            if it == 2:
+                break
+            dn, mm = _fit(x, q, d_eff, m_eff, -1.0)
+            sq, mq = _clip(np.rint(dn / Ds), 63.0), _clip(np.rint(_posmax(mm) / Ms), 63.0)
+    # pack: per (tile, superblock) D[4] | M[4] fp16, 6-bit s and m of [group][row], then codes
+    t = rows // 4
+    out = np.empty((t, nsb, 576), np.uint8)
+    Dt = D.astype(np.float16).view(np.uint16).reshape(t, 4, nsb).transpose(0, 2, 1)
+    Mt = M.astype(np.float16).view(np.uint16).reshape(t, 4, nsb).transpose(0, 2, 1)
+    out[:, :, 0:8] = np.ascontiguousarray(Dt).view(np.uint8).reshape(t, nsb, 8)
+    out[:, :, 8:16] = np.ascontiguousarray(Mt).view(np.uint8).reshape(t, nsb, 8)
+    for off, v in ((16, sq), (40, mq)):
+        s6 = v.astype(np.uint8).reshape(t, 4, nsb, 8).transpose(0, 2, 3, 1).reshape(t, nsb, 32)
+        out[:, :, off:off + 16] = (s6[..., :16] & 15) | ((s6[..., 16:] & 15) << 4)
+        out[:, :, off + 16:off + 24] = ((s6[..., 0:8] >> 4) | ((s6[..., 8:16] >> 4) << 2) |
+                                        ((s6[..., 16:24] >> 4) << 4) | ((s6[..., 24:32] >> 4) << 6))
+    c = q.astype(np.uint8).reshape(t, 4, nsb, 8, 32).transpose(0, 2, 3, 1, 4)   # [t][sb][g][row][32]
+    out[:, :, 64:] = (c[..., :16] | (c[..., 16:] << 4)).reshape(t, nsb, 512)
+    return out.tobytes()
+
+
+def quantize_q4k_numpy(w: np.ndarray, chunk_rows: int = 2048) -> bytes:
+    """quantize_q4k without native code: numpy float32 arithmetic only, the same bytes (tested
+    against the C quantiser and the reference's fixtures). Used where a process must not load
+    this package's libraries (the benchmark's reference arm)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, cols = w.shape
+    if rows % 4 or cols % 256:
+        raise ValueError(f"Q4K needs rows % 4 == 0 and cols % 256 == 0, got {rows}x{cols}")
+    step = max(4, chunk_rows // 4 * 4)
+    return b"".join(_q4k_rows_numpy(w[r:r + step]) for r in range(0, rows, step))
 
 
 def header_bytes(d: Dims, n_tensors: int, dir_off: int, data_off: int) -> bytes:
@@ -208,25 +305,46 @@ def tensor_values(name: str, kind: str, shape: list[int], seed: int, std: float)
 OUT_PROJ_NAMES = ("o_proj.weight", "out_proj.weight", "down_proj.weight")
 
 
+def _tensor_bytes(args) -> tuple[str, int, list[int], bytes]:
+    """One synthetic tensor as (name, dtype, shape, bytes); native=False quantises with numpy
+    only (a worker of make_synthetic's process pool)."""
+    name, kind, shape, seed, sd, native = args
+    v = tensor_values(name, kind, shape, seed, sd)
+    if kind == "mat":
+        return name, Q4K, shape, quantize_q4k(v) if native else quantize_q4k_numpy(v)
+    return name, F32, shape, v.astype("<f4").tobytes()
+
+
+def _synth_args(d: Dims, seed: int, std: float, out_scale: float, native: bool):
+    specs = sorted(tensor_specs(d), key=lambda s: hf_name(s[0]))
+    return [(name, kind, shape, seed, std * out_scale if name.endswith(OUT_PROJ_NAMES) else std, native)
+            for name, kind, shape in specs]
+
+
 def synth_tensors(d: Dims, seed: int, std: float = 0.02, out_scale: float = 1.0):
     """Yield (name, dtype, shape, bytes) in the converter's order (sorted HF names).
     out_scale multiplies the std of the projections that write into the residual stream
     (o_proj, out_proj, down_proj): small values give a model whose next token depends mostly
     on the current one, so greedy decoding falls into cycles (test models for prompt lookup)."""
-    specs = sorted(tensor_specs(d), key=lambda s: hf_name(s[0]))
-    for name, kind, shape in specs:
-        sd = std * out_scale if name.endswith(OUT_PROJ_NAMES) else std
-        v = tensor_values(name, kind, shape, seed, sd)
-        if kind == "mat":
-            yield name, Q4K, shape, quantize_q4k(v)
-        else:
-            yield name, F32, shape, v.astype("<f4").tobytes()
+    for a in _synth_args(d, seed, std, out_scale, True):
+        yield _tensor_bytes(a)
 
 
 def make_synthetic(path: str | os.PathLike, d: Dims, seed: int = 0, std: float = 0.02,
-                   out_scale: float = 1.0) -> Path:
-    """Write a random-init, Q4K-quantised Qwen3.5-shaped model to `path`."""
-    write_pq(path, d, list(synth_tensors(d, seed, std, out_scale)))
+                   out_scale: float = 1.0, native: bool = True) -> Path:
+    """Write a random-init, Q4K-quantised Qwen3.5-shaped model to `path`. native=False loads no
+    native library: the matrices are quantised with numpy in a pool of spawned processes (the
+    same bytes)."""
+    args = _synth_args(d, seed, std, out_scale, native)
+    if native:
+        tensors = [_tensor_bytes(a) for a in args]
+    else:
+        import concurrent.futures as cf
+        import multiprocessing as mp
+        workers = max(1, min(16, os.cpu_count() or 1))
+        with cf.ProcessPoolExecutor(workers, mp_context=mp.get_context("spawn")) as ex:
+            tensors = list(ex.map(_tensor_bytes, args))
+    write_pq(path, d, tensors)
     return Path(path)
 
 

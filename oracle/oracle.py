@@ -107,6 +107,7 @@ class RefEngine:
         L.pinfer_n_vocab.argtypes = [_P]
         L.ref_spec_generate.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, ctypes.c_int, _P,
                                         ctypes.c_uint64, ctypes.c_uint32, _P]
+        L.ref_spec_generate_cont.argtypes = L.ref_spec_generate.argtypes
         L.ref_forward_all.argtypes = [_P, _P, ctypes.c_int, _P]
         L.pinfer_generate_greedy_ex.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, _P, _P, _P, _P]
         L.pinfer_generate_greedy_cont.argtypes = [_P, _P, ctypes.c_int, _P, ctypes.c_int, _P, _P, _P, _P]
@@ -114,6 +115,9 @@ class RefEngine:
         L.pinfer_state_size.argtypes = [_P]
         L.pinfer_state_save.argtypes = [_P, _P, ctypes.c_size_t]
         L.pinfer_state_load.argtypes = [_P, _P, ctypes.c_size_t]
+        L.pinfer_checkpoint.argtypes = [_P]
+        L.pinfer_rewind.argtypes = [_P]
+        L.pinfer_n_past.argtypes = [_P]
         L.nb_synth_draft.restype = ctypes.c_int32
         L.nb_synth_draft.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_uint32, ctypes.c_int32,
                                      ctypes.c_int32]
@@ -159,6 +163,20 @@ class RefEngine:
     def load_state(self, data: bytes) -> int:
         return self.lib.pinfer_state_load(self.ctx, data, len(data))
 
+    def checkpoint(self) -> None:
+        rc = self.lib.pinfer_checkpoint(self.ctx)
+        if rc:
+            raise RuntimeError(f"reference pinfer_checkpoint: {rc}")
+
+    def rewind(self) -> None:
+        rc = self.lib.pinfer_rewind(self.ctx)
+        if rc:
+            raise RuntimeError(f"reference pinfer_rewind: {rc}")
+
+    @property
+    def n_past(self) -> int:
+        return self.lib.pinfer_n_past(self.ctx)
+
     def forward_all(self, tokens) -> np.ndarray:
         t = np.ascontiguousarray(tokens, np.int32)
         out = np.zeros((len(t), self.n_vocab), np.float32)
@@ -196,14 +214,17 @@ class RefEngine:
             stats += [st.ngram_rounds, st.ngram_drafted, st.ngram_accepted]
         return out[:n].tolist(), stats, status.value
 
-    def spec_generate(self, prompt, n_max: int, k: int, greedy, seed: int, p: float):
+    def spec_generate(self, prompt, n_max: int, k: int, greedy, seed: int, p: float,
+                      append: bool = False):
+        """Synthetic-drafter speculation on the reference's verify/accept/commit steps;
+        append keeps the context and feeds the prompt on top of it."""
         t = np.ascontiguousarray(prompt, np.int32)
         g = np.ascontiguousarray(greedy, np.int32)
         out = np.zeros(n_max, np.int32)
         st = np.zeros(4, np.int64)
         p24 = min(1 << 24, int(np.floor(p * (1 << 24) + 0.5)))
-        n = self.lib.ref_spec_generate(self.ctx, _ptr(t), len(t), _ptr(out), n_max, k, _ptr(g),
-                                       seed, p24, _ptr(st))
+        fn = self.lib.ref_spec_generate_cont if append else self.lib.ref_spec_generate
+        n = fn(self.ctx, _ptr(t), len(t), _ptr(out), n_max, k, _ptr(g), seed, p24, _ptr(st))
         if n < 0:
             raise RuntimeError(f"reference spec generate: {n}")
         self.last_decode_s = st[3] * 1e-9

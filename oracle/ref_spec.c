@@ -43,17 +43,19 @@ static int64_t now_ns(void) {
 
 /* stats (may be NULL): [0] rounds, [1] drafted, [2] accepted, [3] ns spent after the prompt
  * (the decode loop, for the benchmark's CPU baseline). greedy: the plain greedy
- * output of the same prompt, n_max entries. Returns tokens written or a negative code. */
-int ref_spec_generate(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt, int32_t *out,
-                      int n_max, int k, const int32_t *greedy, uint64_t seed, uint32_t p24,
-                      int64_t *stats) {
+ * output of the same prompt, n_max entries. append: keep the context and feed the prompt on
+ * top of it (pinfer_generate_greedy_cont's rule), else start from a reset context. Returns
+ * tokens written or a negative code. */
+static int spec_generate(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt, int32_t *out,
+                         int n_max, int k, const int32_t *greedy, uint64_t seed, uint32_t p24,
+                         int64_t *stats, int append) {
     if (!ctx || !prompt || n_prompt <= 0 || !out || n_max <= 0 || k < 0 ||
         k > PINFER_SPEC_MAX_K || !greedy)
         return PINFER_E_ARG;
     const int V = ctx->vocab;
     float *logits = malloc((size_t)(k + 1) * V * sizeof(float));
     if (!logits) return PINFER_E_NOMEM;
-    pinfer_reset(ctx);
+    if (!append) pinfer_reset(ctx);
     int rc = k > 0 ? pf_lin_log_alloc(ctx, k + 1) : PINFER_OK;
     if (rc == PINFER_OK) rc = pf_forward(ctx, prompt, n_prompt, logits, NULL, NULL);
     if (rc != PINFER_OK) {
@@ -107,6 +109,18 @@ int ref_spec_generate(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt, int3
     if (stats) stats[3] += now_ns() - t0;
     free(logits);
     return rc == PINFER_OK || count > 0 ? count : rc;
+}
+
+int ref_spec_generate(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt, int32_t *out,
+                      int n_max, int k, const int32_t *greedy, uint64_t seed, uint32_t p24,
+                      int64_t *stats) {
+    return spec_generate(ctx, prompt, n_prompt, out, n_max, k, greedy, seed, p24, stats, 0);
+}
+
+int ref_spec_generate_cont(pinfer_ctx *ctx, const int32_t *prompt, int n_prompt, int32_t *out,
+                           int n_max, int k, const int32_t *greedy, uint64_t seed, uint32_t p24,
+                           int64_t *stats) {
+    return spec_generate(ctx, prompt, n_prompt, out, n_max, k, greedy, seed, p24, stats, 1);
 }
 
 /* Logits of every row of one forward pass (pf_forward's logits_all) for tests. */

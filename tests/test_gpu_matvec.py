@@ -142,3 +142,16 @@ def test_head_kernel_bit_exact_and_argmax(lib, torch, q4k_oracle, rows, cols, n)
         assert not nan0.cpu().numpy()[:n].any()
     finally:
         dev.close()
+
+
+def test_bounded_wait_gives_up_and_reports(lib, torch):
+    """A device wait whose data never comes (an mbarrier expecting bytes no copy brings, with a
+    short poll limit) ends with status -90 instead of hanging, and the context stays usable."""
+    import ctypes
+    for limit in (64, 1024):
+        st = ctypes.c_int(0)
+        assert lib.nb_test_bounded_wait(limit, ctypes.byref(st)) == 0
+        assert st.value == -90
+    x = torch.ones(1024, device="cuda")
+    assert float((x * 2).sum().item()) == 2048.0     # the context still works
+    assert lib.nb_test_bounded_wait(0, ctypes.byref(ctypes.c_int())) == -4

@@ -56,6 +56,30 @@ def test_static_matches_handle_api(lib, torch, q4k_oracle, rows, cols, ns):
         lib.nb_mv_destroy(h)
 
 
+def test_static_allocates_nothing(lib, torch, q4k_oracle):
+    """After a first call (which does the per-device setup), further calls at different sizes
+    change neither the device's free memory nor what torch's allocator has reserved."""
+    rows, cols = 1024, 2048
+    w = q4k_oracle.kb_matrix(rows, cols, 5)
+    panels = np.zeros(lib.nb_q4k_panel_bytes(rows, cols), np.uint8)
+    assert lib.nb_q4k_repack(w.ctypes.data, rows, cols, panels.ctypes.data) == 0
+    dW = torch.from_numpy(panels).cuda()
+    dX = torch.from_numpy(np.random.default_rng(1).standard_normal((16, cols)).astype(np.float32)).cuda()
+    dY = torch.zeros((16, rows), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.nb_mv_run_static(dW.data_ptr(), rows, cols, dX.data_ptr(), 1, dY.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    free0, reserved0 = torch.cuda.mem_get_info()[0], torch.cuda.memory_reserved()
+    for n in (16, 3, 8, 1):
+        rc = lib.nb_mv_run_static(dW.data_ptr(), rows, cols, dX.data_ptr(), n, dY.data_ptr(), stream)
+        assert rc == 0, lib.last_error()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert torch.cuda.memory_reserved() == reserved0
+    want = q4k_oracle.matmul(w, rows, cols, dX[:1].cpu().numpy())
+    assert np.array_equal(_bits(dY[:1].cpu().numpy()), _bits(want))
+
+
 def test_static_rejects_sizes_beyond_scratch(lib, torch):
     buf = torch.zeros(16, dtype=torch.float32, device="cuda")
     p = buf.data_ptr()
