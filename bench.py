@@ -1,11 +1,11 @@
-"""Benchmark of the speculative verify path (BASELINE.json metric: greedy spec-decode tok/s/GPU
-at k = 3, and Q4K matvec HBM GB/s).
+"""Benchmark of the speculative verify path (metric: greedy spec-decode tok/s/GPU at k = 3, and
+Q4K matvec HBM GB/s).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N ...
 
-Workload (BASELINE.json configs[2]): the Qwen3.5-0.8B-shaped model, random init (std 0.02,
+Workload (configs[2]): the Qwen3.5-0.8B-shaped model, random init (std 0.02,
 norms 1), Q4K-quantised; a 512-token uniform-random context; 128 greedy tokens with draft
 depth k = 3 and the synthetic drafter at acceptance p = 0.8 (the sweep p in {0, 0.5, 0.8, 1}
 is reported beside it). A step is one generation of 128 tokens continuing the prefilled
@@ -390,7 +390,7 @@ def run_config4(args, rank: int, world: int, local: int) -> None:
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=1800))
     from nibblemac_b200.model import Model
     path = model_path(rank, dist)
-    base = Model(path, max_ctx=256)
+    base = Model(path, max_ctx=1024 + GEN4 + 16)
     rec = measure_config4(base, rank, world, local, dist, False)
     base.close()
     if rank == 0:
@@ -458,7 +458,7 @@ def run_profile_batch(nseq: int, ntok: int) -> None:
 
 
 def run_config5(args, rank: int, world: int, local: int) -> None:
-    """BASELINE configs[4]: the 2B-shaped model, k = 3 at p = 0.8 on a 4096-token context, the
+    """configs[4]: the 2B-shaped model, k = 3 at p = 0.8 on a 4096-token context, the
     LM head vocab-sharded over the `world` GPUs with the argmax merged by one NCCL all-reduce
     per verify pass (pinfer_b200_shard_head). Every rank runs the same single stream (batch 1;
     the configured batch of 8 sequences needs multi-stream batching, not built), so the total
@@ -527,7 +527,7 @@ def run_config5(args, rank: int, world: int, local: int) -> None:
 
 
 def run_config5_batch(args, rank: int, world: int, local: int) -> None:
-    """BASELINE configs[4] as configured: the 2B-shaped model, k = 3 at p = 0.8, 8 sequences of
+    """configs[4] as configured: the 2B-shaped model, k = 3 at p = 0.8, 8 sequences of
     a 4096-token context each in one multi-sequence batch (pinfer_b200_batch), the LM head
     vocab-sharded over the `world` GPUs: every verify round of the 8 x 4 rows ends with one
     NCCL all-reduce (max) of the per-row argmax keys. The same batch on every rank (the layers
@@ -612,12 +612,12 @@ def main() -> None:
     ap.add_argument("--no-config4", action="store_true",
                     help="leave the configs[3] multi-stream record out of the default line")
     ap.add_argument("--config4", action="store_true",
-                    help="BASELINE configs[3]: 256 requests per GPU in one multi-sequence batch "
+                    help="configs[3]: 256 requests per GPU in one multi-sequence batch "
                          "(one JSON line)")
     ap.add_argument("--batch5", type=int, default=8,
                     help="sequences of the --config5 batch (1: one context, the earlier form)")
     ap.add_argument("--config5", action="store_true",
-                    help="BASELINE configs[4]: 2B shape, 4096-token context, LM head vocab-sharded "
+                    help="configs[4]: 2B shape, 4096-token context, LM head vocab-sharded "
                          "over the torchrun ranks (one JSON line, strong scaling)")
     ap.add_argument("--profile", action="store_true",
                     help="setup, then exactly one generation inside cudaProfilerStart/Stop (for "
@@ -666,7 +666,8 @@ def main() -> None:
     from nibblemac_b200.model import Model
     lib = load_library()
     path = model_path(rank, dist)
-    m = Model(path, max_ctx=CTX + N_GEN + 16)
+    # a batch's contexts cannot be longer than the context whose weights it shares
+    m = Model(path, max_ctx=max(CTX + N_GEN + 16, 1024 + GEN4 + 16))
     ctx = context_tokens(rank, m.n_vocab)
     m.reset()
     m.eval(ctx[:-1], logits=False)

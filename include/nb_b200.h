@@ -57,7 +57,7 @@ void *pinfer_b200_stream(pinfer_ctx *ctx);
  * per context. NULL on failure with *err set. */
 pinfer_ctx *pinfer_b200_clone(const pinfer_ctx *src, int max_ctx, int *err);
 
-/* ---- vocab-sharded LM head ------------------------------------------
+/* ---- vocab-sharded LM head (the 2B benchmark config) ------------------------------------------
  * No reference counterpart (the reference runs on one device). One context per GPU, each with
  * the same model and fed the same tokens: every GPU runs the layers, and its LM head covers only
  * vocabulary rows [rank * V / world, (rank + 1) * V / world); the greedy argmax of each verify

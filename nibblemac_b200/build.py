@@ -77,10 +77,20 @@ def build_engine() -> Path:
     return out
 
 
+def reference_checkout() -> Path | None:
+    """The reference's source checkout: $NB_REFERENCE, else a `reference` directory beside this
+    repository; None when neither holds the engine sources."""
+    env = os.environ.get("NB_REFERENCE")
+    for cand in ([Path(env)] if env else []) + [ROOT.parent / "reference"]:
+        if (cand / "engine" / "src" / "forward.c").exists():
+            return cand
+    return None
+
+
 def build_oracle() -> None:
     run(["make", "-s", "-C", ROOT / "oracle", "all"])
-    ref = Path(os.environ.get("NB_REFERENCE", "/root/reference"))
-    if (ref / "engine" / "src" / "forward.c").exists():
+    ref = reference_checkout()
+    if ref is not None:
         run(["make", "-s", "-C", ROOT / "oracle", "ref", f"REF={ref}"])
 
 

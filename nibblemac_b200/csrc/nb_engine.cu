@@ -358,15 +358,23 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = fal
     ad.rps = std::min(nmax, kMaxRows);   // attention grids cover the pass's rows only
     for (int l = 0; l < c->n_layers; l++) {
         auto &D = c->layers[l];
+        // the next layer's matrices into L2 while this layer runs, so the weight copies its
+        // kernels issue before their griddepcontrol.wait are L2 hits
+        L2Prefetch pf;
+        if (l + 1 < c->n_layers) {
+            const auto &N = c->layers[l + 1];
+            for (const Mat *m : {&N.win, &N.out, &N.gate, &N.up, &N.down})
+                pf.add(m->w, (size_t)m->npanels * m->nsb * kUnitBytes);
+        }
         if (D.is_full) {
             const Act o = mid_act(c, c->nq * c->hd);
-            launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->attd.ldy, nmax, c->act_h, s);
+            launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->attd.ldy, nmax, c->act_h, s, pf);
             launch_attn_prep(c->att[l], ad, c->y, c->qbuf, c->step, s);
             launch_attn(c->att[l], ad, c->y, c->qbuf, c->step, o, s);
             launch_matvec(D.out, o, c->step, c->x, c->H, 1, nmax, s);
         } else {
             const Act o = mid_act(c, c->vd);
-            launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->lind.ldy, nmax, c->act_h, s);
+            launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->lind.ldy, nmax, c->act_h, s, pf);
             launch_deltanet(c->lin[D.lin], c->lind, c->y, c->step, o, s, 1, nmax);
             launch_matvec(D.out, o, c->step, c->x, c->H, 1, nmax, s);
         }
@@ -959,8 +967,9 @@ int pinfer_generate_greedy(pinfer_ctx *c, const int32_t *prompt, int n_prompt, i
 //                   mask, pf_model_fingerprint of the file
 //   per linear-attention layer (layer order): conv state [(K-1)][C], recurrent state [nv][dk][dv]
 //   per full-attention layer: K rows [n_kv][n_past][hd], then V rows (fp32 storage)
-// This build keeps no MTP cache, so the MTP row count is 0. Every generation ends with its
-// deferred DeltaNet commit flushed, so the device state is complete whenever the API returns.
+//   MTP rows (mtp_rows of them): the MTP head's K and V rows, as the reference writes them
+// Every generation ends with its deferred DeltaNet commit flushed, so the device state is
+// complete whenever the API returns.
 namespace {
 struct StateHdr {
     char magic[8];

@@ -139,10 +139,26 @@ void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int 
                    cudaStream_t s);
 void launch_matvec_chunked(const Mat &W, Act in, const Step *st, float *y, int ldy, int mode,
                            int nmax, cudaStream_t s);
+// Byte ranges (16-byte aligned, sizes multiples of 16) a kernel asks the L2 to fetch ahead of
+// the kernels that will read them (cp.async.bulk.prefetch.L2), split over the kernel's CTAs.
+constexpr int kMaxPrefetch = 8;
+struct L2Prefetch {
+    const void *p[kMaxPrefetch] = {};
+    unsigned bytes[kMaxPrefetch] = {};
+    int n = 0;
+    void add(const void *ptr, size_t nbytes) {
+        if (n < kMaxPrefetch && ptr && nbytes >= 16) {
+            p[n] = ptr;
+            bytes[n] = (unsigned)(nbytes & ~(size_t)15);
+            n++;
+        }
+    }
+};
 // The same with the RMSNorm + A8 of the residual rows x fused into the kernel (scratch: the A8
-// buffer a fallback path may use for large passes)
+// buffer a fallback path may use for large passes); pf: ranges to prefetch into L2
 void launch_matvec_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
-                        float *y, int ldy, int nmax, Act scratch, cudaStream_t s);
+                        float *y, int ldy, int nmax, Act scratch, cudaStream_t s,
+                        const L2Prefetch &pf = L2Prefetch());
 void launch_matvec_swiglu_norm(const Mat &G, const Mat &U, const float *x, const float *w, float eps,
                                const Step *st, Act out, int nmax, Act scratch, cudaStream_t s);
 void launch_matvec_head_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,

@@ -383,34 +383,6 @@ __device__ __forceinline__ float ld_early_f32(const float *p) {
     return v;
 }
 
-// The residual rows x [NMAX][cols] of a NORM panel kernel into shared memory with 16-byte loads
-// by every thread, rows 0..NMAX-1 whatever the pass's row count (the residual buffer holds
-// kMaxRows rows; rows the pass does not have are staged but never used), so the copy is
-// requested together with the Step block instead of after it. Needs rows_ld_ok.
-__device__ __forceinline__ bool rows_ld_ok(int cols, const NormIn &nin) {
-    return ((uintptr_t)nin.x & 15) == 0 && ((uintptr_t)nin.w & 15) == 0 && cols % 4 == 0;
-}
-template <int NMAX>
-__device__ __forceinline__ void stage_rows(int cols, const NormIn &nin, float *sx) {
-    const int tid = threadIdx.x, bd = blockDim.x;
-    const int total = NMAX * cols / 4;
-    const float4 *src = reinterpret_cast<const float4 *>(nin.x);
-    float4 *dst = reinterpret_cast<float4 *>(sx);
-    for (int base = 0; base < total; base += 8 * bd) {
-        float4 r[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int i = base + k * bd + tid;
-            if (i < total) r[k] = src[i];
-        }
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int i = base + k * bd + tid;
-            if (i < total) dst[i] = r[k];
-        }
-    }
-}
-
 // After a timed-out wait on unit u of a warp's kRing-deep ring: units u .. u + kRing - 1 may
 // still be in flight into this CTA's shared memory, so wait for each once more (bounded) before
 // the warp returns.
@@ -677,157 +649,452 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in,
     }
 }
 
-// Every matrix except the LM head: one CTA per 32-row panel, one warp per superblock unit
-// (up to kPanelWarps), every unit of the panel requested at once with a TMA bulk copy. While
-// the units are in flight the CTA stages its activations in shared memory: the A8 input of the
-// previous kernel, or (NORM) the RMSNorm of the residual rows x [n][cols] quantised right here
-// (pf_rmsnorm + kern_quant_act: every CTA computes the same bits). Warps write their integer
-// block dots and decoded scales to shared memory; after a barrier the ordered fused chains run
-// with lane = row, vectors spread over warps, and the epilogue writes
-//   EPI 0: y[v][row] = acc        (projections feeding DeltaNet / attention)
-//   EPI 1: y[v][row] += acc       (out_proj / o_proj / down_proj into the residual stream)
-//   EPI 3: SwiGLU over (W0 = gate, W1 = up) and A8 of the product for down_proj.
-// nmax <= 4.
+// Every matrix except the LM head: one CTA per 32-row panel, laid out for latency (a verify
+// pass reads each 1-5 MB matrix once; the kernel's time is its chain of dependent steps, not
+// the weight stream):
+//   before pdl_wait  every superblock unit of the panel is requested with one TMA bulk copy
+//                    into a slot of its own (weights are constants), and NORM stages the norm
+//                    multiplier;
+//   after pdl_wait   the pass's input rows are loaded with 16-byte loads by every thread beside
+//                    the Step block (rows 0..NMAX-1 whatever the pass's row count: the buffers
+//                    hold kMaxRows rows, rows past n are never used): the A8 input of the
+//                    previous kernel, or (NORM) the residual rows, normalised and quantised here
+//                    (pf_rmsnorm + kern_quant_act; every CTA computes the same bits);
+//   units            each unit is split over 1, 2 or 4 warps by blocks; a warp decodes the
+//                    scales of its blocks and forms the exact int32 block dots of every vector
+//                    with no branch on the row count (the dp4a terms of a block are summed as two
+//                    4-deep chains: integer addition is exact in any order);
+//   chain            one warp per (matrix, vector) with lane = row runs the ordered fused chain
+//                    acc = fmaf((float)isum, (D s6) d, acc); acc = fmaf(-(M m6), fsum, acc)
+//                    over the blocks in column order, its operands loaded eight blocks ahead;
+//   epilogue         EPI 0: y[v][row] = acc (projections feeding DeltaNet / attention)
+//                    EPI 1: y[v][row] += acc (out_proj / o_proj / down_proj into the residual)
+//                    EPI 3: SwiGLU over (W0 = gate, W1 = up), the up accumulators handed to
+//                    the gate warps through shared memory, then A8 of the product for down_proj.
+// nmax <= 4. Block: 8 warps (16 when the panel has more than 8 units).
 constexpr int kPanelWarps = 16;
+constexpr int kPanelPad = 4;   // fp32 row padding of the staged residual rows (bank spread)
 
-template <int NMAX, int EPI, bool NORM>
-__global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, Act in, NormIn nin,
-                                                               Step *st, float *y, int ldy, Act out) {
-    extern __shared__ __align__(128) uint8_t wsm[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int nsb = W0.nsb, cols = W0.cols, nb = cols >> 5, panel = blockIdx.x;
-    const int nmat = EPI == 3 ? 2 : 1, nunit = nsb * nmat;
-    uint8_t *units = wsm;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(wsm + (size_t)nw * kUnitBytes);
-    uint64_t *abar = bars + nw;   // the activations
-    int32_t *isum = reinterpret_cast<int32_t *>(wsm + (size_t)nw * kUnitBytes + (((size_t)nw * 8 + 8 + 15) & ~(size_t)15));
-    float *ds = reinterpret_cast<float *>(isum + (size_t)nmat * nb * NMAX * 32);   // [nmat][nb][32]
-    float *os = ds + (size_t)nmat * nb * 32;
-    float *sd = os + (size_t)nmat * nb * 32;                                     // [NMAX][nb]
-    float *sfs = sd + (size_t)NMAX * nb;                                          // [NMAX][nb]
-    int8_t *sq = reinterpret_cast<int8_t *>(sfs + (size_t)NMAX * nb);          // [NMAX][cols]
-    float *sx = reinterpret_cast<float *>(sq + (size_t)NMAX * cols);           // NORM: [NMAX][cols]
-    float *sw = sx + (size_t)NMAX * cols;                                       // NORM: [cols]
-    __shared__ float srr[NMAX];
-    if (lane == 0) {
-        mbar_init(bars + warp, 1);
-        fence_mbar_init();
-        if (warp < nunit) {   // first unit of every warp (weights: safe before pdl_wait)
-            const int m = warp / nsb, sb = warp % nsb;
-            tma_load_1d(units + (size_t)warp * kUnitBytes,
-                        (m ? W1 : W0).w + ((size_t)panel * nsb + sb) * kUnitBytes, kUnitBytes, bars + warp);
-        }
+struct PanelSmem {             // byte offsets into the dynamic shared memory
+    size_t bars, isum, ds, os, sd, sfs, sq, sx, sw, sg, total;
+};
+__host__ __device__ inline PanelSmem panel_layout(int nunit, int cols, int nmat, int nmax, bool norm) {
+    PanelSmem L;
+    const size_t nb = cols / 32;
+    size_t o = (size_t)nunit * kUnitBytes;
+    L.bars = o;
+    o += (((size_t)nunit + 1) * 8 + 15) & ~(size_t)15;
+    L.isum = o;
+    o += (size_t)nmat * nb * nmax * 32 * 4;
+    L.ds = o;
+    o += (size_t)nmat * nb * 32 * 4;
+    L.os = o;
+    o += (size_t)nmat * nb * 32 * 4;
+    L.sd = o;
+    o += (size_t)nmax * nb * 4;
+    L.sfs = o;
+    o += (size_t)nmax * nb * 4;
+    L.sq = o;
+    o += (size_t)nmax * cols;
+    o = (o + 15) & ~(size_t)15;
+    L.sx = o;
+    if (norm) o += (size_t)nmax * (cols + kPanelPad) * 4;
+    L.sw = o;
+    if (norm) o += (size_t)cols * 4;
+    L.sg = o;
+    o += (size_t)nmax * 32 * 4;
+    L.total = o;
+    return L;
+}
+
+// RMSNorm + A8 of the staged rows (pf_rmsnorm, forward_ops.c:191-200, then kern_quant_act):
+// sx [NMAX][cols + kPanelPad] fp32, sw [cols]; writes sq [NMAX][cols], sd / sfs [NMAX][cols/32].
+// The sum of squares keeps the reference's four interleaved lane sums (lane l adds x[l], x[l+4],
+// ... in order): lanes 4v..4v+3 of warp 0 (the padded row stride puts the 16 lanes on distinct
+// banks). The A8 takes four threads per
+// 32-column block, eight columns each: max, division, rounding and code sum are
+// order-independent, so the bits equal the warp-wide quantiser's.
+template <int NMAX>
+__device__ __forceinline__ void panel_norm_quant(const float *sx, const float *sw, int cols, float eps,
+                                                 int8_t *sq, float *sd, float *sfs, float *srr) {
+    const int tid = threadIdx.x, xs = cols + kPanelPad;
+    if (tid < 4 * NMAX) {
+        const int v = tid >> 2, l = tid & 3;
+        const float *x = sx + (size_t)v * xs + l;
+        float c = 0.0f;
+#pragma unroll 32
+        for (int i = 0; i < cols; i += 4) c = madd(c, x[i], x[i]);
+        const int base = tid & ~3;
+        const unsigned m = (4 * NMAX >= 32) ? 0xffffffffu : ((1u << (4 * NMAX)) - 1u);
+        const float c0 = __shfl_sync(m, c, base), c1 = __shfl_sync(m, c, base + 1);
+        const float c2 = __shfl_sync(m, c, base + 2), c3 = __shfl_sync(m, c, base + 3);
+        const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+        if (l == 0) srr[v] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)cols), eps));
     }
-    const bool fast = NORM && rows_ld_ok(cols, nin);
-    if (fast) {   // the norm weight (constant: safe before pdl_wait)
-        for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
+    __syncthreads();
+    // A8: one thread per 32-column block, starting at 16-byte chunk t % 8 of its block so the 8
+    // threads of a shared-memory phase read 8 distinct bank groups
+    const int nb = cols >> 5;
+    for (int u = tid; u < NMAX * nb; u += blockDim.x) {
+        const int v = u / nb, b = u - v * nb;
+        const float r = srr[v];
+        const float *xb = sx + (size_t)v * xs + b * 32, *wb = sw + b * 32;
+        float xn[32];
+        float a = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int ch = (k + tid) & 7;
+            const float4 xv = *reinterpret_cast<const float4 *>(xb + 4 * ch);
+            const float4 wv = *reinterpret_cast<const float4 *>(wb + 4 * ch);
+            xn[4 * k + 0] = __fmul_rn(__fmul_rn(xv.x, r), wv.x);
+            xn[4 * k + 1] = __fmul_rn(__fmul_rn(xv.y, r), wv.y);
+            xn[4 * k + 2] = __fmul_rn(__fmul_rn(xv.z, r), wv.z);
+            xn[4 * k + 3] = __fmul_rn(__fmul_rn(xv.w, r), wv.w);
+            // fmaxf keeps the non-NaN operand: the max of the block's non-NaN |x|, NaN if all
+            // are NaN, in any order (as the warp-wide form)
+            const float m4 = fmaxf(fmaxf(fabsf(xn[4 * k]), fabsf(xn[4 * k + 1])),
+                                   fmaxf(fabsf(xn[4 * k + 2]), fabsf(xn[4 * k + 3])));
+            a = k == 0 ? m4 : fmaxf(a, m4);
+        }
+        const float id = a > 0.0f ? __fdiv_rn(127.0f, a) : 0.0f;
+        int sum = 0;
+        int8_t *qb = sq + (size_t)v * cols + b * 32;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const int ch = (k + tid) & 7;
+            uint32_t packed = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int q = __float2int_rn(__fmul_rn(xn[4 * k + i], id));
+                sum += q;
+                packed |= (uint32_t)(uint8_t)(int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q)) << (8 * i);
+            }
+            *reinterpret_cast<uint32_t *>(qb + 4 * ch) = packed;
+        }
+        const float d = __fdiv_rn(a, 127.0f);
+        sd[(size_t)v * nb + b] = d;
+        sfs[(size_t)v * nb + b] = __fmul_rn(d, (float)sum);
+    }
+}
+
+// This CTA's share of the L2 prefetch ranges: the concatenated ranges split evenly (16-byte
+// granules) over the grid, one bulk prefetch per range piece.
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch &pf) {
+    if (pf.n == 0 || threadIdx.x != 0) return;
+    unsigned long long total = 0;
+    for (int i = 0; i < pf.n; i++) total += pf.bytes[i];
+    const unsigned long long g = total >> 4, G = gridDim.x, c = blockIdx.x;
+    unsigned long long lo = (g * c / G) << 4, hi = (g * (c + 1) / G) << 4, base = 0;
+    for (int i = 0; i < pf.n && lo < hi; i++) {
+        const unsigned long long e = base + pf.bytes[i];
+        if (lo < e) {
+            const unsigned long long a = lo, b = hi < e ? hi : e;
+            const char *src = static_cast<const char *>(pf.p[i]) + (a - base);
+            for (unsigned long long o = 0; o < b - a; o += 65536) {
+                const unsigned sz = (unsigned)((b - a - o) < 65536 ? (b - a - o) : 65536);
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src + o), "r"(sz) : "memory");
+            }
+            lo = b;
+        }
+        base = e;
+    }
+}
+
+// PPC: panels per CTA for EPI 0 (2 when the matrix has more panels than the GPU has SMs, so
+// the CTAs fit beside the previous kernel's); EPI 1 / 3 take one.
+template <int NMAX, int EPI, bool NORM, int PPC = 1>
+__global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, Act in, NormIn nin,
+                                                               Step *st, float *y, int ldy, Act out,
+                                                               L2Prefetch pf) {
+    static_assert(PPC == 1 || (PPC == 2 && EPI == 0), "two panels per CTA for EPI 0 only");
+    extern __shared__ __align__(128) uint8_t wsm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    const int nsb = W0.nsb, cols = W0.cols, nb = cols >> 5, panel = blockIdx.x * PPC;
+    constexpr int nmat = EPI == 3 ? 2 : PPC;   // unit groups: gate / up, or this CTA's panels
+    // the panel of unit group m, and whether it exists (a last CTA may have one panel of two)
+    auto gpanel = [&](int m) { return PPC == 2 ? panel + m : panel; };
+    auto gmat = [&](int m) -> const Mat & { return (EPI == 3 && m) ? W1 : W0; };
+    const int nunit = nsb * nmat;
+    const PanelSmem PL = panel_layout(nunit, cols, nmat, NMAX, NORM);
+    uint8_t *units = wsm;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(wsm + PL.bars);
+    int32_t *isum = reinterpret_cast<int32_t *>(wsm + PL.isum);   // [nmat][nb][NMAX][32]
+    float *ds = reinterpret_cast<float *>(wsm + PL.ds);           // [nmat][nb][32]
+    float *os = reinterpret_cast<float *>(wsm + PL.os);
+    float *sd = reinterpret_cast<float *>(wsm + PL.sd);           // [NMAX][nb]
+    float *sfs = reinterpret_cast<float *>(wsm + PL.sfs);
+    int8_t *sq = reinterpret_cast<int8_t *>(wsm + PL.sq);          // [NMAX][cols]
+    float *sx = reinterpret_cast<float *>(wsm + PL.sx);           // NORM: [NMAX][cols + pad]
+    float *sw = reinterpret_cast<float *>(wsm + PL.sw);           // NORM: [cols]
+    float *sg = reinterpret_cast<float *>(wsm + PL.sg);           // EPI 3: [NMAX][32]
+    __shared__ float srr[NMAX];
+    // thread u requests unit u (weights: safe before pdl_wait)
+    if (tid < nunit && gpanel(tid / nsb) < W0.npanels) {
+        const int m = tid / nsb, sb = tid % nsb;
+        mbar_init(bars + tid, 1);
+        fence_mbar_init();
+        tma_load_1d(units + (size_t)tid * kUnitBytes, gmat(m).w + ((size_t)gpanel(m) * nsb + sb) * kUnitBytes,
+                    kUnitBytes, bars + tid);
+    }
+    if (NORM) {   // the norm multiplier (constant: safe before pdl_wait)
+        for (int i = tid; i < cols / 4; i += blockDim.x)
             reinterpret_cast<float4 *>(sw)[i] = reinterpret_cast<const float4 *>(nin.w)[i];
     }
+    l2_prefetch_share(pf);   // weights of kernels further ahead (constants)
     pdl_wait();
     pdl_trigger();
-    const int n = fast ? ld_early_s32(&st->n) : st->n;
-    if (fast) stage_rows<NMAX>(cols, nin, sx);   // beside the Step block
-    if (n <= 0) {   // nothing to do: let the weight copy land before this CTA's shared memory goes
-        __syncwarp();
-        if (warp < nunit) mbar_wait(bars + warp, 0);
+    const int n = ld_early_s32(&st->n);
+    if (NORM) {   // the residual rows beside the Step block
+        const int per = cols / 4, total = NMAX * per;
+        for (int i = tid; i < total; i += blockDim.x) {
+            const int v = i / per, c4 = i - v * per;
+            reinterpret_cast<float4 *>(sx + (size_t)v * (cols + kPanelPad))[c4] =
+                reinterpret_cast<const float4 *>(nin.x + (size_t)v * cols)[c4];
+        }
+    } else {      // the A8 rows of the previous kernel beside the Step block
+        const int per = cols / 16, nbi = in.cols >> 5;
+        for (int i = tid; i < NMAX * per; i += blockDim.x) {
+            const int v = i / per, c16 = i - v * per;
+            reinterpret_cast<int4 *>(sq + (size_t)v * cols)[c16] =
+                reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols)[c16];
+        }
+        const int per4 = nb / 4;
+        for (int i = tid; i < NMAX * per4; i += blockDim.x) {
+            const int v = i / per4, b4 = i - v * per4;
+            reinterpret_cast<float4 *>(sd + (size_t)v * nb)[b4] = reinterpret_cast<const float4 *>(in.d + (size_t)v * nbi)[b4];
+            reinterpret_cast<float4 *>(sfs + (size_t)v * nb)[b4] = reinterpret_cast<const float4 *>(in.fs + (size_t)v * nbi)[b4];
+        }
+    }
+    __syncthreads();
+    if (n <= 0) {   // nothing to do: the weight copies land before this CTA's shared memory goes
+        if (tid < nunit && gpanel(tid / nsb) < W0.npanels) mbar_wait(bars + tid, 0);
         return;
     }
-    // activations into shared memory while the weights are in flight
-    if (fast) __syncthreads();
-    else if (!stage_act<NORM>(abar, n, cols, in, nin, sx, sw, sq, sd, sfs) && threadIdx.x == 0)
-        st->status = -90;   // device wait timed out: reported, no hang
-    if (NORM) norm_quant_smem(sx, sw, n, cols, nin.eps, sq, sd, sfs, srr);
-    __syncthreads();
-    for (int u = warp, it = 0; u < nunit; u += nw, it++) {
-        const int m = u / nsb, sb = u % nsb;
-        uint8_t *slot = units + (size_t)warp * kUnitBytes;
-        if (it > 0 && lane == 0) {
-            fence_proxy_async();
-            tma_load_1d(slot, (m ? W1 : W0).w + ((size_t)panel * nsb + sb) * kUnitBytes, kUnitBytes, bars + warp);
-        }
-        if (!mbar_wait(bars + warp, (uint32_t)it & 1u)) {
+    if (NORM) {
+        panel_norm_quant<NMAX>(sx, sw, cols, nin.eps, sq, sd, sfs, srr);
+        __syncthreads();
+    }
+    // ---- units: task = (unit, part), part = a run of 8 / sp blocks
+    const int sp = nunit * 4 <= nw ? 4 : (nunit * 2 <= nw ? 2 : 1), kb = 8 / sp;
+    for (int task = warp; task < nunit * sp; task += nw) {
+        const int u = task / sp, part = task - u * sp, m = u / nsb, sb = u - m * nsb;
+        if (gpanel(m) >= W0.npanels) continue;
+        if (!mbar_wait(bars + u, 0)) {
             if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
-            mbar_wait(bars + warp, (uint32_t)it & 1u);   // the unit in flight lands before the warp goes
-            return;
+            mbar_wait(bars + u, 0);            // the unit in flight lands before the warp goes
+            continue;
         }
-        const uint8_t *sp = slot + lane * 16;
-        const uint4 sc = lds128(sp);
-        uint4 cd[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) cd[k] = lds128(sp + 512 * (k + 1));
-        __syncwarp();
+        const uint8_t *sp_ = units + (size_t)u * kUnitBytes + lane * 16;
+        const uint4 sc = lds128(sp_);
         const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
         const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
         const float D = half_bits_to_float((uint32_t)(A >> 48));
         const float M = half_bits_to_float((uint32_t)(B >> 48));
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int b = sb * 8 + k;
+        for (int kk = 0; kk < kb; kk++) {
+            const int k = part * kb + kk, b = sb * 8 + k;
+            const uint4 cd = lds128(sp_ + 512 * (k + 1));
             ds[((size_t)m * nb + b) * 32 + lane] = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
             os[((size_t)m * nb + b) * 32 + lane] = __fmul_rn(M, (float)(uint32_t)((B >> (6 * k)) & 63u));
-            const int lo0 = (int)(cd[k].x & 0x0f0f0f0fu), lo1 = (int)(cd[k].y & 0x0f0f0f0fu);
-            const int lo2 = (int)(cd[k].z & 0x0f0f0f0fu), lo3 = (int)(cd[k].w & 0x0f0f0f0fu);
-            const int hi0 = (int)((cd[k].x >> 4) & 0x0f0f0f0fu), hi1 = (int)((cd[k].y >> 4) & 0x0f0f0f0fu);
-            const int hi2 = (int)((cd[k].z >> 4) & 0x0f0f0f0fu), hi3 = (int)((cd[k].w >> 4) & 0x0f0f0f0fu);
+            const int lo0 = (int)(cd.x & 0x0f0f0f0fu), lo1 = (int)(cd.y & 0x0f0f0f0fu);
+            const int lo2 = (int)(cd.z & 0x0f0f0f0fu), lo3 = (int)(cd.w & 0x0f0f0f0fu);
+            const int hi0 = (int)((cd.x >> 4) & 0x0f0f0f0fu), hi1 = (int)((cd.y >> 4) & 0x0f0f0f0fu);
+            const int hi2 = (int)((cd.z >> 4) & 0x0f0f0f0fu), hi3 = (int)((cd.w >> 4) & 0x0f0f0f0fu);
+            int32_t *is = isum + ((size_t)m * nb + b) * NMAX * 32 + lane;
 #pragma unroll
-            for (int v = 0; v < NMAX; v++) {
-                if (v < n) {
-                    const int4 *xq = reinterpret_cast<const int4 *>(sq + (size_t)v * cols + b * 32);
-                    const int4 x0 = xq[0], x1 = xq[1];
-                    int sacc = __dp4a(lo0, x0.x, 0);
-                    sacc = __dp4a(lo1, x0.y, sacc);
-                    sacc = __dp4a(lo2, x0.z, sacc);
-                    sacc = __dp4a(lo3, x0.w, sacc);
-                    sacc = __dp4a(hi0, x1.x, sacc);
-                    sacc = __dp4a(hi1, x1.y, sacc);
-                    sacc = __dp4a(hi2, x1.z, sacc);
-                    sacc = __dp4a(hi3, x1.w, sacc);
-                    isum[(((size_t)m * nb + b) * NMAX + v) * 32 + lane] = sacc;
-                }
+            for (int v = 0; v < NMAX; v++) {   // every vector: rows past n give unused sums
+                const int4 *xq = reinterpret_cast<const int4 *>(sq + (size_t)v * cols + b * 32);
+                const int4 x0 = xq[0], x1 = xq[1];
+                int sl = __dp4a(lo0, x0.x, 0);
+                int sh = __dp4a(hi0, x1.x, 0);
+                sl = __dp4a(lo1, x0.y, sl);
+                sh = __dp4a(hi1, x1.y, sh);
+                sl = __dp4a(lo2, x0.z, sl);
+                sh = __dp4a(hi2, x1.z, sh);
+                sl = __dp4a(lo3, x0.w, sl);
+                sh = __dp4a(hi3, x1.w, sh);
+                is[v * 32] = sl + sh;
             }
         }
     }
     __syncthreads();
-    const int row = panel * kPanelRows + lane;
-    for (int v = warp; v < n; v += nw) {
-        // EPI 1: the residual this thread's chain adds to (its own element), requested before
-        // the chain so the read overlaps it
+    // ---- chains: warp (m, v), lane = row
+    const int m = warp / NMAX, v = warp - m * NMAX;
+    const int row = gpanel(m) * kPanelRows + lane;
+    const bool chain = warp < nmat * NMAX && v < n && gpanel(m) < W0.npanels;
+    float acc = 0.0f;
+    if (chain) {
         const float y_old = (EPI == 1 && row < W0.rows) ? ld_early_f32(y + (size_t)v * ldy + row) : 0.0f;
-        float acc[2] = {0.0f, 0.0f};
-#pragma unroll
-        for (int m = 0; m < 2; m++) {
-            if (m >= nmat) break;
-            float a = 0.0f;
-            const int32_t *is = isum + ((size_t)m * nb * NMAX + v) * 32 + lane;
-            const float *dsp = ds + (size_t)m * nb * 32 + lane, *osp = os + (size_t)m * nb * 32 + lane;
-            const float *dv = sd + (size_t)v * nb, *fv = sfs + (size_t)v * nb;
-#pragma unroll 8
-            for (int b = 0; b < nb; b++) {
-                const float s = (float)is[(size_t)b * NMAX * 32];
-                a = __fmaf_rn(s, __fmul_rn(dsp[b * 32], dv[b]), a);
-                a = __fmaf_rn(-osp[b * 32], fv[b], a);
-            }
-            acc[m] = a;
+        const int32_t *is = isum + ((size_t)m * nb * NMAX + v) * 32 + lane;
+        const float *dsp = ds + (size_t)m * nb * 32 + lane, *osp = os + (size_t)m * nb * 32 + lane;
+        const float *dv = sd + (size_t)v * nb, *fv = sfs + (size_t)v * nb;
+        float PA[8], QA[8], OA[8], FA[8], PB[8], QB[8], OB[8], FB[8];
+#define NB_CHAIN_LOAD(P, Q, O, F, b0)                                                         \
+        _Pragma("unroll") for (int j = 0; j < 8; j++) {                                      \
+            P[j] = (float)is[(size_t)((b0) + j) * NMAX * 32];                                \
+            Q[j] = __fmul_rn(dsp[((b0) + j) * 32], dv[(b0) + j]);                              \
+            O[j] = osp[((b0) + j) * 32];                                                      \
+            F[j] = fv[(b0) + j];                                                              \
         }
-        if (EPI == 3) {
-            const float h = __fmul_rn(pf_silu(acc[0]), acc[1]);
+#define NB_CHAIN_RUN(P, Q, O, F)                                                              \
+        _Pragma("unroll") for (int j = 0; j < 8; j++) {                                      \
+            acc = __fmaf_rn(P[j], Q[j], acc);                                                 \
+            acc = __fmaf_rn(-O[j], F[j], acc);                                                \
+        }
+        NB_CHAIN_LOAD(PA, QA, OA, FA, 0)
+        for (int b0 = 0; b0 < nb; b0 += 16) {   // nb is a multiple of 8
+            if (b0 + 8 < nb) { NB_CHAIN_LOAD(PB, QB, OB, FB, b0 + 8) }
+            NB_CHAIN_RUN(PA, QA, OA, FA)
+            if (b0 + 16 < nb) { NB_CHAIN_LOAD(PA, QA, OA, FA, b0 + 16) }
+            if (b0 + 8 < nb) { NB_CHAIN_RUN(PB, QB, OB, FB) }
+        }
+#undef NB_CHAIN_LOAD
+#undef NB_CHAIN_RUN
+        if (EPI == 0 && row < W0.rows) y[(size_t)v * ldy + row] = acc;
+        if (EPI == 1 && row < W0.rows) y[(size_t)v * ldy + row] = __fadd_rn(y_old, acc);
+        if (EPI == 3 && m == 1) sg[v * 32 + lane] = acc;   // up, for the gate warp of vector v
+    }
+    if (EPI == 3) {
+        __syncthreads();
+        if (chain && m == 0) {
+            const float h = __fmul_rn(pf_silu(acc), sg[v * 32 + lane]);
             const int nbo = out.cols >> 5;
             quant_block_warp(h, lane, out.q + (size_t)v * out.cols + panel * 32,
                              out.d + (size_t)v * nbo + panel, out.fs + (size_t)v * nbo + panel);
-        } else if (row < W0.rows) {
-            float *p = y + (size_t)v * ldy + row;
-            *p = EPI == 0 ? acc[0] : __fadd_rn(y_old, acc[0]);
         }
     }
 }
 
-size_t panel_smem(int nw, int cols, int nmat, int nmax, bool norm) {
+
+// The same matvec for matrices with long chains (out_proj / o_proj / down_proj: 1024 rows, 64 to
+// 112 blocks per row), one CTA per 8-row slice of a panel (four CTAs share a panel), laid out so
+// that every phase but the ordered chain runs on all 16 warps:
+//   before pdl_wait  this slice of every unit (the 8 rows' scale entries and code entries: nine
+//                    128-byte bulk copies per unit);
+//   after pdl_wait   the A8 rows of the previous kernel, 16-byte loads spread over the CTA;
+//   operands         (block, lane) items over all warps, lane = (vector v = lane / 8, row r =
+//                    lane % 8): the exact int32 block dot and the four operands of the block's
+//                    two chain steps, {(float)isum, (D s6) d, -(M m6), fsum}, one float4 per item;
+//   chain            warp 0 runs the 32 ordered chains of the slice, one 16-byte shared-memory
+//                    load and two dependent fmaf per block (the result is independent of where
+//                    the operands were formed: the same roundings in the same order).
+// EPI 0 / 1 as k_mv_panel; NMAX = 4.
+constexpr int kSliceRows = 8;
+constexpr int kSliceBytes = 9 * 128;   // per unit: scale entries + 8 blocks of code entries
+constexpr int kSliceWarps = 16;
+constexpr int kSlicePad = 16;          // bytes between the staged A8 rows (bank spread)
+
+struct SliceSmem {
+    size_t bars, ops, sd, sfs, sq, total;
+};
+__host__ __device__ inline SliceSmem slice_layout(int nunit, int cols) {
+    SliceSmem L;
     const size_t nb = cols / 32;
-    size_t b = (size_t)nw * kUnitBytes + (((size_t)nw * 8 + 8 + 15) & ~(size_t)15) + (size_t)nmat * nb * nmax * 32 * 4 +
-               (size_t)nmat * nb * 32 * 8 + (size_t)nmax * nb * 8 + (size_t)nmax * cols;
-    b = (b + 15) & ~(size_t)15;
-    if (norm) b += (size_t)nmax * cols * 4 + (size_t)cols * 4;
-    return b;
+    size_t o = (size_t)nunit * kSliceBytes;
+    L.bars = o;
+    o += (((size_t)nunit) * 8 + 15) & ~(size_t)15;
+    L.ops = o;
+    o += nb * 32 * 16;
+    L.sd = o;
+    o += 4 * (nb + 4) * 4;
+    L.sfs = o;
+    o += 4 * (nb + 4) * 4;
+    L.sq = o;
+    o += 4 * ((size_t)cols + kSlicePad);
+    L.total = (o + 15) & ~(size_t)15;
+    return L;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kSliceWarps * 32) k_mv_slice(Mat W0, Act in, Step *st, float *y, int ldy) {
+    extern __shared__ __align__(128) uint8_t ssm[];
+    constexpr int NMAX = 4;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nsb = W0.nsb, cols = W0.cols, nb = cols >> 5, nunit = nsb, nbp = nb + 4, qs = cols + kSlicePad;
+    const int panel = blockIdx.x >> 2, r0 = (blockIdx.x & 3) * kSliceRows;
+    const SliceSmem SL = slice_layout(nunit, cols);
+    uint8_t *units = ssm;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ssm + SL.bars);
+    float4 *ops = reinterpret_cast<float4 *>(ssm + SL.ops);       // [nb][32 lanes]
+    float *sd = reinterpret_cast<float *>(ssm + SL.sd);           // [NMAX][nb + 4]
+    float *sfs = reinterpret_cast<float *>(ssm + SL.sfs);
+    int8_t *sq = reinterpret_cast<int8_t *>(ssm + SL.sq);          // [NMAX][cols + pad]
+    // thread u copies its slice of unit u (weights: safe before pdl_wait)
+    if (tid < nunit) {
+        const uint8_t *src = W0.w + ((size_t)panel * nsb + tid) * kUnitBytes + r0 * 16;
+        uint8_t *dst = units + (size_t)tid * kSliceBytes;
+        mbar_init(bars + tid, 1);
+        fence_mbar_init();
+        mbar_arrive_expect(bars + tid, kSliceBytes);
+        for (int p = 0; p < 9; p++) bulk_g2s(dst + p * 128, src + p * 512, 128, bars + tid);
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int n = ld_early_s32(&st->n);
+    {   // the A8 rows of the previous kernel beside the Step block
+        const int per = cols / 16, nbi = in.cols >> 5, per4 = nb / 4;
+        for (int i = tid; i < NMAX * per; i += blockDim.x) {
+            const int v = i / per, c16 = i - v * per;
+            reinterpret_cast<int4 *>(sq + (size_t)v * qs)[c16] = reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols)[c16];
+        }
+        for (int i = tid; i < 2 * NMAX * per4; i += blockDim.x) {
+            const int which = i / (NMAX * per4), j = i - which * NMAX * per4, v = j / per4, b4 = j - v * per4;
+            const float *src = (which ? in.fs : in.d) + (size_t)v * nbi;
+            float *dst = (which ? sfs : sd) + (size_t)v * nbp;
+            reinterpret_cast<float4 *>(dst)[b4] = reinterpret_cast<const float4 *>(src)[b4];
+        }
+    }
+    if (tid < nunit && !mbar_wait(bars + tid, 0)) {   // every unit in shared memory
+        st->status = -90;                                // device wait timed out: reported, no hang
+        mbar_wait(bars + tid, 0);                        // the copies in flight land before the CTA goes
+    }
+    __syncthreads();
+    if (n <= 0) return;
+    // ---- operands: item (block b, lane)
+    const int v = lane >> 3, r = lane & 7;
+    for (int b = warp; b < nb; b += kSliceWarps) {
+        const int u = b >> 3, k = b & 7;
+        const uint8_t *up = units + (size_t)u * kSliceBytes;
+        const uint4 sc = lds128(up + r * 16);
+        const uint4 cd = lds128(up + 128 * (k + 1) + r * 16);
+        const int4 *xq = reinterpret_cast<const int4 *>(sq + (size_t)v * qs + b * 32);
+        const int4 x0 = xq[0], x1 = xq[1];
+        int sl = __dp4a((int)(cd.x & 0x0f0f0f0fu), x0.x, 0);
+        int sh = __dp4a((int)((cd.x >> 4) & 0x0f0f0f0fu), x1.x, 0);
+        sl = __dp4a((int)(cd.y & 0x0f0f0f0fu), x0.y, sl);
+        sh = __dp4a((int)((cd.y >> 4) & 0x0f0f0f0fu), x1.y, sh);
+        sl = __dp4a((int)(cd.z & 0x0f0f0f0fu), x0.z, sl);
+        sh = __dp4a((int)((cd.z >> 4) & 0x0f0f0f0fu), x1.z, sh);
+        sl = __dp4a((int)(cd.w & 0x0f0f0f0fu), x0.w, sl);
+        sh = __dp4a((int)((cd.w >> 4) & 0x0f0f0f0fu), x1.w, sh);
+        const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
+        const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
+        const float D = half_bits_to_float((uint32_t)(A >> 48));
+        const float M = half_bits_to_float((uint32_t)(B >> 48));
+        const float dsc = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
+        const float osc = __fmul_rn(M, (float)(uint32_t)((B >> (6 * k)) & 63u));
+        ops[b * 32 + lane] = make_float4((float)(sl + sh), __fmul_rn(dsc, sd[v * nbp + b]), -osc, sfs[v * nbp + b]);
+    }
+    __syncthreads();
+    // ---- the ordered chains: warp 0, lane (v, r)
+    if (warp != 0) return;
+    const int row = panel * kPanelRows + r0 + r;
+    const bool live = v < n && row < W0.rows;
+    const float y_old = (EPI == 1 && live) ? ld_early_f32(y + (size_t)v * ldy + row) : 0.0f;
+    const float4 *op = ops + lane;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int b = 0; b < nb; b++) {
+        const float4 f = op[b * 32];
+        acc = __fmaf_rn(f.x, f.y, acc);
+        acc = __fmaf_rn(f.z, f.w, acc);
+    }
+    if (live) y[(size_t)v * ldy + row] = EPI == 1 ? __fadd_rn(y_old, acc) : acc;
+}
+
+size_t slice_smem(int nunit, int cols) { return slice_layout(nunit, cols).total; }
+
+size_t panel_smem(int nunit, int cols, int nmat, int nmax, bool norm) {
+    return panel_layout(nunit, cols, nmat, nmax, norm).total;
 }
 
 // ------------------------------------------------------------------ argmax over the panels
@@ -3408,11 +3675,20 @@ int dyn_smem_limit(K kern) {
 
 // Allow the kernel the whole opt-in limit: the attribute only bounds what a launch may request,
 // and contexts with different sizes (max_ctx) share the kernels, so it is never lowered.
+// Every kernel also prefers the largest shared-memory carveout: the kernels of a round follow
+// one another on the same SMs with programmatic dependent launch, and an SM whose carveout a
+// starting kernel would have to change cannot take that kernel's CTAs until it drains, which
+// defeats the early launch the weight prefetch relies on.
+template <class K>
+void max_carveout(K kern) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+}
 template <class K>
 void raise_smem(K kern, size_t want = 0) {
     (void)want;
     const int lim = dyn_smem_limit(kern);
     if (lim > 0) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    max_carveout(kern);
 }
 
 template <int NMAX, bool NORM>
@@ -3431,16 +3707,28 @@ void head_mma_t(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int 
              const_cast<Step *>(st), y, ldy, partial, nan0, row_base);
 }
 
-template <int NMAX, int EPI, bool NORM>
+template <int NMAX, int EPI, bool NORM, int PPC = 1>
 bool panel_t(const Mat &W0, const Mat &W1, Act in, NormIn nin, const Step *st, float *y, int ldy,
-             Act out, cudaStream_t s) {
-    const int nmat = EPI == 3 ? 2 : 1;
-    const int nw = std::min(W0.nsb * nmat, kPanelWarps);
-    const size_t sm = panel_smem(nw, W0.cols, nmat, NMAX, NORM);
-    static const int lim = dyn_smem_limit(k_mv_panel<NMAX, EPI, NORM>);
+             Act out, cudaStream_t s, const L2Prefetch &pf = L2Prefetch()) {
+    const int nmat = EPI == 3 ? 2 : PPC;
+    const int nunit = W0.nsb * nmat, nw = nunit > 8 ? kPanelWarps : 8;
+    const size_t sm = panel_smem(nunit, W0.cols, nmat, NMAX, NORM);
+    // 16-byte row loads of the inputs (every engine buffer is 256-byte aligned, cols % 256 == 0)
+    if (((uintptr_t)nin.x | (uintptr_t)nin.w | (uintptr_t)in.q | (uintptr_t)in.d | (uintptr_t)in.fs) & 15) return false;
+    static const int lim = dyn_smem_limit(k_mv_panel<NMAX, EPI, NORM, PPC>);
     if (sm > (size_t)lim) return false;
-    launch_k(k_mv_panel<NMAX, EPI, NORM>, W0.npanels, nw * 32, sm, s, W0, W1, in, nin, const_cast<Step *>(st),
-                                                                y, ldy, out);
+    launch_k(k_mv_panel<NMAX, EPI, NORM, PPC>, (W0.npanels + PPC - 1) / PPC, nw * 32, sm, s, W0, W1, in, nin,
+             const_cast<Step *>(st), y, ldy, out, pf);
+    return true;
+}
+
+template <int EPI>
+bool slice_t(const Mat &W, Act in, const Step *st, float *y, int ldy, cudaStream_t s) {
+    const size_t sm = slice_smem(W.nsb, W.cols);
+    static const int lim = dyn_smem_limit(k_mv_slice<EPI>);
+    if (sm > (size_t)lim || (((uintptr_t)in.q | (uintptr_t)in.d | (uintptr_t)in.fs) & 15)) return false;
+    launch_k(k_mv_slice<EPI>, W.npanels * (kPanelRows / kSliceRows), kSliceWarps * 32, sm, s, W, in,
+             const_cast<Step *>(st), y, ldy);
     return true;
 }
 
@@ -3449,18 +3737,24 @@ void launch_matvec(const Mat &W, Act in, const Step *st, float *y, int ldy, int 
     Act none;
     NormIn nn{};
     bool done = false;
+    // long chains (64 or more blocks per row) on 8-row slices
+    if (nmax > 1 && nmax <= 4 && W.cols >= 2048)
+        done = mode ? slice_t<1>(W, in, st, y, ldy, s) : slice_t<0>(W, in, st, y, ldy, s);
+    if (done) return;
     if (nmax <= 1) done = mode ? panel_t<1, 1, false>(W, W, in, nn, st, y, ldy, none, s) : panel_t<1, 0, false>(W, W, in, nn, st, y, ldy, none, s);
     else if (nmax <= 4) done = mode ? panel_t<4, 1, false>(W, W, in, nn, st, y, ldy, none, s) : panel_t<4, 0, false>(W, W, in, nn, st, y, ldy, none, s);
     if (!done) launch_matvec_chunked(W, in, st, y, ldy, mode, nmax, s);
 }
 
 void launch_matvec_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
-                        float *y, int ldy, int nmax, Act scratch, cudaStream_t s) {
+                        float *y, int ldy, int nmax, Act scratch, cudaStream_t s, const L2Prefetch &pf) {
     Act none;
     const NormIn nin{x, w, eps};
     bool done = false;
-    if (nmax <= 1) done = panel_t<1, 0, true>(W, W, none, nin, st, y, ldy, none, s);
-    else if (nmax <= 4) done = panel_t<4, 0, true>(W, W, none, nin, st, y, ldy, none, s);
+    if (nmax <= 1) done = panel_t<1, 0, true>(W, W, none, nin, st, y, ldy, none, s, pf);
+    else if (nmax <= 4 && W.npanels > num_sms())   // two panels per CTA: one CTA per SM
+        done = panel_t<4, 0, true, 2>(W, W, none, nin, st, y, ldy, none, s, pf);
+    else if (nmax <= 4) done = panel_t<4, 0, true>(W, W, none, nin, st, y, ldy, none, s, pf);
     if (done) return;
     launch_norm_quant(x, w, W.cols, eps, st, scratch, s);
     launch_matvec_chunked(W, scratch, st, y, ldy, 0, nmax, s);
@@ -3669,6 +3963,18 @@ void launch_count_done(const Step *st, int nseq, int *ndone, cudaStream_t s) {
     launch_k(k_count_done, 1, 256, 0, s, st, nseq, ndone);
 }
 int kernels_init(int max_ctx, int hd, int rep) {
+    // the largest carveout for the kernels of a verify round that take no dynamic shared memory
+    max_carveout(k_embed);
+    max_carveout(k_attn_prep);
+    max_carveout(k_argmax_final);
+    max_carveout(k_argmax_keys);
+    max_carveout(k_keys_argmax);
+    max_carveout(k_pass_end);
+    max_carveout(k_accept);
+    max_carveout(k_norm_rows);
+    max_carveout(k_norm_quant);
+    max_carveout(k_deltanet3<4, 4, PINFER_SPEC_MAX_K>);
+    max_carveout(k_deltanet3<4, kMaxRows, PINFER_SPEC_MAX_K>);
     // raise the dynamic shared memory limits once, outside any stream capture
     raise_smem(k_matvec<1, 0>, mv_smem<1>());
     raise_smem(k_matvec<1, 1>, mv_smem<1>());
@@ -3706,6 +4012,9 @@ int kernels_init(int max_ctx, int hd, int rep) {
     raise_smem(k_mv_panel<4, 3, false>);
     raise_smem(k_mv_panel<4, 0, true>);
     raise_smem(k_mv_panel<4, 3, true>);
+    raise_smem(k_mv_panel<4, 0, true, 2>);
+    raise_smem(k_mv_slice<0>);
+    raise_smem(k_mv_slice<1>);
     if (max_ctx > 0) {
         raise_smem(k_deltanet2<4>, sizeof(float) * kDK * kDV);
         raise_smem(k_deltanet2<4, kMaxRows, PINFER_SPEC_MAX_K>, sizeof(float) * kDK * kDV);

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import glob
 import json
+import os
 import sys
 from collections import defaultdict
 from pathlib import Path
@@ -53,7 +54,9 @@ def collect(ref: Path) -> dict:
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference checkout: argument, $NB_REFERENCE, else `reference` beside this repository
+    ref = Path(sys.argv[1] if len(sys.argv) > 1 else
+               os.environ.get("NB_REFERENCE", Path(__file__).resolve().parents[3] / "reference"))
     out = Path(__file__).with_name("kbench_yhash.json")
     out.write_text(json.dumps(collect(ref), indent=1) + "\n")
     print(f"wrote {out}")

@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import hashlib
 import json
+import os
 import struct
 import subprocess
 import sys
@@ -84,7 +85,9 @@ def write_hf_checkpoint(d: pq.Dims, seed: int, out: Path) -> None:
 
 
 def main() -> None:
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference checkout: argument, $NB_REFERENCE, else `reference` beside this repository
+    ref = Path(sys.argv[1] if len(sys.argv) > 1 else
+               os.environ.get("NB_REFERENCE", Path(__file__).resolve().parents[3] / "reference"))
     sys.path.insert(0, str(ref / "tools"))
     import quant  # the reference's quantiser
 

@@ -33,7 +33,7 @@ def test_kbench_yhash(q4k_oracle, case):
 
 
 def test_fixture_covers_the_config1_shape():
-    """BASELINE config 1 is the 3584 x 1024 shape at n = 1, 2, 4."""
+    """Config 1 of the benchmark is the 3584 x 1024 shape at n = 1, 2, 4."""
     got = {(c["rows"], c["cols"], c["n"]) for c in GOLD["cases"]}
     for n in (1, 2, 4):
         assert (3584, 1024, n) in got
