@@ -3403,7 +3403,8 @@ __device__ int ng_draft(Step *st, int *out, int max, int *match) {
     const int n = st->hist_n;
     *match = 0;
     if (!st->hist || max <= 0 || n < kNgMin + 1) return 0;
-    ng_index(st, n - 1);   // earlier occurrences end before the tail's last token
+    // index every position but the newest: a match for the tail must lie strictly earlier
+    ng_index(st, n - 1);
     for (int k = kNgMax; k >= kNgMin; k--) {
         if (k > n - 1) continue;
         const int *tail = st->hist + n - k;
