@@ -78,6 +78,8 @@ struct pinfer_ctx {
     Act act_h, act_mid;
     unsigned long long *partial = nullptr;
     int *nan0 = nullptr;
+    unsigned long long *head_best = nullptr;   // [4][grid] per-CTA keys of the fused head argmax
+    int *head_ctr = nullptr;                   // its grid counter (zero between launches)
     Step *step = nullptr;
     Step *h_step = nullptr;   // pinned mirror for reads
     int *d_out = nullptr, *d_greedy = nullptr;

@@ -317,7 +317,9 @@ int alloc_state(pinfer_ctx *c) {
         (rc = c->dalloc(&c->act_mid.d, sizeof(float) * kMaxRows * (mid / 32))) ||
         (rc = c->dalloc(&c->act_mid.fs, sizeof(float) * kMaxRows * (mid / 32))) ||
         (rc = c->dalloc(&c->partial, sizeof(unsigned long long) * kMaxRows * c->head.npanels)) ||
-        (rc = c->dalloc(&c->nan0, sizeof(int) * kMaxRows)) || (rc = c->dalloc(&c->step, sizeof(Step))))
+        (rc = c->dalloc(&c->nan0, sizeof(int) * kMaxRows)) || (rc = c->dalloc(&c->step, sizeof(Step))) ||
+        (rc = c->dalloc(&c->head_best, sizeof(unsigned long long) * kHeadFuseSlots)) ||
+        (rc = c->dalloc(&c->head_ctr, sizeof(int))))
         return rc;
     c->act_h.cols = c->H;
     // prompt-lookup history and index (ngram.c pf_ngram_init: capacity max_ctx + 1, tables of
@@ -351,7 +353,9 @@ Act mid_act(pinfer_ctx *c, int cols) {
 
 // One forward pass over the rows described by the Step block (<= nmax rows).
 // head: 0 none, 1 logits + argmax, 2 argmax only (no logits written)
-void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = false) {
+// accept_follows: k_accept runs right after the pass (verify rounds); it sets the deferred
+// commit itself, so the pass's own k_pass_end is left out.
+void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = false, bool accept_follows = false) {
     cudaStream_t s = c->stream;
     launch_embed(c->embed, c->step, c->x, c->H, s);
     AttnDims ad = c->attd;
@@ -388,16 +392,17 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = fal
         const bool sharded = c->shard_world > 1;
         const Mat &HW = sharded ? c->head_view : c->head;
         float *lg = head == 1 ? c->logits + c->head_row0 : nullptr;
-        if (nmax <= 4) {
+        if (nmax <= 4) {   // unsharded: the head kernel finishes the argmax itself
             launch_matvec_head_norm(HW, c->x, c->norm, c->eps, c->step, lg, c->vocab, c->partial, c->nan0,
-                                    nmax, s, c->head_row0);
+                                    nmax, s, c->head_row0, sharded ? nullptr : c->head_best,
+                                    sharded ? nullptr : c->head_ctr);
         } else {
             launch_norm_quant(c->x, c->norm, c->H, c->eps, c->step, c->act_h, s);
             launch_matvec_head(HW, c->act_h, c->step, lg, c->vocab, c->partial, c->nan0, nmax, s,
                                c->head_row0);
         }
         if (!sharded) {
-            launch_argmax_final(c->partial, c->nan0, c->head.npanels, c->step, s);
+            if (nmax > 4) launch_argmax_final(c->partial, c->nan0, c->head.npanels, c->step, s);
         } else {
             // one all-reduce (max) of the (value, first index) keys across the shards: the
             // tie and NaN rules of pf_argmax hold because the keys order exactly as they do
@@ -415,7 +420,7 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = fal
             }
         }
     }
-    launch_pass_end(c->step, s);
+    if (!accept_follows) launch_pass_end(c->step, s);
 }
 
 // One MTP pass (pf_mtp_forward, mtp.c:62-100) over the rows of step block ms: h [n][H] hidden
@@ -439,15 +444,15 @@ void enqueue_mtp(pinfer_ctx *c, Step *ms, const float *h, int nmax, bool head, b
     launch_matvec(D.down, hm, ms, c->x, c->H, 1, nmax, s);
     launch_norm_rows(c->x, c->mtp_norm_out, c->H, c->eps, ms, c->mrows, s);   // m = mtp.norm(u)
     if (head) {
-        if (nmax <= 4) {
+        if (nmax <= 4) {   // the head kernel finishes the argmax itself
             launch_matvec_head_norm(c->mtp_head, c->x, c->mtp_norm_out, c->eps, ms, conf ? c->logits : nullptr, c->vocab,
-                                    c->partial, c->nan0, nmax, s);
+                                    c->partial, c->nan0, nmax, s, 0, c->head_best, c->head_ctr);
         } else {
             launch_norm_quant(c->x, c->mtp_norm_out, c->H, c->eps, ms, c->act_h, s);
             launch_matvec_head(c->mtp_head, c->act_h, ms, conf ? c->logits : nullptr, c->vocab, c->partial, c->nan0,
                                nmax, s);
         }
-        launch_argmax_final(c->partial, c->nan0, c->mtp_head.npanels, ms, s);
+        if (nmax > 4) launch_argmax_final(c->partial, c->nan0, c->mtp_head.npanels, ms, s);
         // adaptive: the top-1 probability of the pass's newest draft (its last row)
         if (conf) launch_conf(c->logits, c->vocab, c->mtp_head.rows, ms, c->step, s);
     }
@@ -549,7 +554,7 @@ int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int
             launch_mtp_chain_take(c->step, c->msteps + i, i, c->mrows, c->mcur, c->H, s);
         }
         if (adaptive) launch_stamp(c->step, 1, s);
-        enqueue_forward(c, nmax, 2, true);
+        enqueue_forward(c, nmax, 2, true, !adaptive);
         if (adaptive) launch_stamp(c->step, 2, s);
         launch_accept(c->step, c->d_greedy, c->d_out, s);
         launch_mtp_pending_set(c->step, c->msteps, s);
@@ -560,7 +565,7 @@ int round_graph(pinfer_ctx *c, int k, cudaGraphExec_t *out, int drafter = 0, int
             launch_stamp(c->step, 0, s);
             launch_stamp(c->step, 1, s);
         }
-        enqueue_forward(c, nmax, 2);
+        enqueue_forward(c, nmax, 2, false, !adaptive);
         if (adaptive) launch_stamp(c->step, 2, s);
         launch_accept(c->step, c->d_greedy, c->d_out, s);
     }
@@ -1182,7 +1187,7 @@ int pinfer_b200_round_kernels(pinfer_ctx *c, int k) {
     // the graph is only instantiated; count its kernel nodes from a fresh capture
     cudaGraph_t g;
     if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return PINFER_E_NOMEM;
-    enqueue_forward(c, c->round_nmax[k], 2);
+    enqueue_forward(c, c->round_nmax[k], 2, false, true);
     launch_accept(c->step, c->d_greedy, c->d_out, c->stream);
     if (cudaStreamEndCapture(c->stream, &g) != cudaSuccess) return PINFER_E_NOMEM;
     size_t n = 0;

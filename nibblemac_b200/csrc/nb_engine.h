@@ -161,9 +161,13 @@ void launch_matvec_norm(const Mat &W, const float *x, const float *w, float eps,
                         const L2Prefetch &pf = L2Prefetch());
 void launch_matvec_swiglu_norm(const Mat &G, const Mat &U, const float *x, const float *w, float eps,
                                const Step *st, Act out, int nmax, Act scratch, cudaStream_t s);
+// With fbest / fctr (nmax <= 4, one context, unsharded) the kernel also finishes the argmax into
+// Step::argmax (no launch_argmax_final): fbest [4][grid] keys, fctr a zeroed counter it resets.
+constexpr int kHeadFuseSlots = 4 * 1024;
 void launch_matvec_head_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
                              float *logits, int ld, unsigned long long *partial, int *nan0, int nmax,
-                             cudaStream_t s, int row_base = 0);
+                             cudaStream_t s, int row_base = 0, unsigned long long *fbest = nullptr,
+                             int *fctr = nullptr);
 // gate / up with SwiGLU and A8 quantisation of the product
 void launch_matvec_swiglu(const Mat &G, const Mat &U, Act in, const Step *st, Act out, int nmax,
                           cudaStream_t s);

@@ -517,11 +517,17 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
 }
 
+// fctr != nullptr (one context, unsharded head): the argmax is finished here as well. Each CTA
+// folds its warps' running best keys per vector into fbest[v][cta]; the CTA whose increment of
+// *fctr completes the grid reduces fbest and writes Step::argmax with pf_argmax's NaN rule (the
+// keys order like pf_argmax: value, then lowest index), then resets the counter for the next
+// launch.
 template <bool NORM>
 __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in, NormIn nin, Step *st,
                                                                  float *y, int ldy,
                                                                  unsigned long long *partial, int *nan0,
-                                                                 int row_base) {
+                                                                 int row_base, unsigned long long *fbest,
+                                                                 int *fctr) {
     extern __shared__ __align__(128) uint8_t hsm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3, tv = t & 1;   // MMA group / thread in group; vector pair
@@ -569,12 +575,13 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in,
     const int8_t *bq = sq + (size_t)(g & 3) * qs + 4 * t;   // B fragment base of this lane
     const int r0 = (t < 2 ? 0 : 8) + g;                     // this lane's row in each 16-row half
     float acc[2][2];                                         // [half][vector of the pair]
+    unsigned long long run[2] = {0ull, 0ull};               // best key so far of vector 2 tv + j
     for (int u = 0; u < total; u++) {
         const int slot = u % kRing;
         if (!mbar_wait(bars + slot, (uint32_t)(u / kRing) & 1u)) {
             if (lane == 0) st->status = -90;   // device wait timed out: reported, no hang
             drain_ring(bars, u, total);
-            return;
+            break;                             // (the fused argmax below still meets every CTA)
         }
         const uint8_t *sp = ring + (size_t)slot * kUnitBytes;
         const int sb = u % nsb;
@@ -645,8 +652,40 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in,
             }
             if (live && lane == tv) partial[(size_t)v * W0.npanels + panel] = best;
             if (live && panel == 0 && lane == tv && row_base == 0) nan0[v] = acc[0][j] != acc[0][j];
+            run[j] = best > run[j] ? best : run[j];
         }
     }
+    if (fctr == nullptr) return;
+    __shared__ unsigned long long s_best[kTallWarps][4];
+    __shared__ int s_last;
+    if (lane < 2) {   // lane tv holds vectors 2 tv and 2 tv + 1
+        s_best[warp][2 * lane] = run[0];
+        s_best[warp][2 * lane + 1] = run[1];
+    }
+    __syncthreads();
+    if (threadIdx.x < 4) {
+        unsigned long long b = 0ull;
+        for (int w = 0; w < kTallWarps; w++) b = s_best[w][threadIdx.x] > b ? s_best[w][threadIdx.x] : b;
+        fbest[(size_t)threadIdx.x * gridDim.x + blockIdx.x] = b;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(fctr, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (warp < n) {   // warp v finishes vector v
+        unsigned long long b = 0ull;
+        for (int i = lane; i < (int)gridDim.x; i += 32) {
+            const unsigned long long k = __ldcg(fbest + (size_t)warp * gridDim.x + i);
+            b = k > b ? k : b;
+        }
+        b = warp_max_u64(b);
+        if (lane == 0) st->argmax[warp] = __ldcg(nan0 + warp) ? 0 : (int)(0xffffffffu - (uint32_t)(b & 0xffffffffu));
+    }
+    if (threadIdx.x == 0) *fctr = 0;
 }
 
 // Every matrix except the LM head: one CTA per 32-row panel, laid out for latency (a verify
@@ -3702,10 +3741,11 @@ void head_t2(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int ldy
 
 template <bool NORM>
 void head_mma_t(const Mat &W, Act in, NormIn nin, const Step *st, float *y, int ldy,
-                unsigned long long *partial, int *nan0, int row_base, cudaStream_t s) {
+                unsigned long long *partial, int *nan0, int row_base, cudaStream_t s,
+                unsigned long long *fbest = nullptr, int *fctr = nullptr) {
     const int grid = std::min(2 * num_sms(), (W.npanels + kTallWarps - 1) / kTallWarps);
     launch_k(k_mv_head_mma<NORM>, std::max(grid, 1), kTallWarps * 32, head_mma_smem(W.cols, NORM), s, W, in, nin,
-             const_cast<Step *>(st), y, ldy, partial, nan0, row_base);
+             const_cast<Step *>(st), y, ldy, partial, nan0, row_base, fbest, fctr);
 }
 
 template <int NMAX, int EPI, bool NORM, int PPC = 1>
@@ -3786,10 +3826,10 @@ void launch_matvec_head(const Mat &W, Act in, const Step *st, float *logits, int
 
 void launch_matvec_head_norm(const Mat &W, const float *x, const float *w, float eps, const Step *st,
                              float *logits, int ld, unsigned long long *partial, int *nan0, int nmax,
-                             cudaStream_t s, int row_base) {
+                             cudaStream_t s, int row_base, unsigned long long *fbest, int *fctr) {
     const NormIn nin{x, w, eps};
     const Act none;
-    if (nmax <= 4) head_mma_t<true>(W, none, nin, st, logits, ld, partial, nan0, row_base, s);
+    if (nmax <= 4) head_mma_t<true>(W, none, nin, st, logits, ld, partial, nan0, row_base, s, fbest, fctr);
     else if (nmax <= 8) head_t2<8, true>(W, none, nin, st, logits, ld, partial, nan0, row_base, s);
     else head_t2<16, true>(W, none, nin, st, logits, ld, partial, nan0, row_base, s);
 }
