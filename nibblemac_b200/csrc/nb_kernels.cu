@@ -2938,6 +2938,29 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
     float Sr[kDnPart];
 #pragma unroll
     for (int r = 0; r < kDnPart; r++) Sr[r] = ld_early(rec + (size_t)r * kDV + (size_t)i0 * kDV);
+    // The pass's Step block is written only between passes (set_pass / k_accept, never by this
+    // kernel's predecessor, the W_in matvec), and the conv-input log and the deferred-commit rows
+    // only by this layer's own DeltaNet in an earlier pass, so all of them are read before
+    // pdl_wait as well; the W_in rows are not.
+    const int n = ld_early_s32(&st->n), row0 = ld_early_s32(&st->row0);
+    const int logged = ld_early_s32(&st->logged), keep = ld_early_s32(&st->pend_keep);
+    const int pend_conv = ld_early_s32(&st->pend_conv), wr = ld_early_s32(&st->wr);
+    conv_load_log(cq, L, C, pend_conv);
+    conv_load_log(ck, L, C, pend_conv);
+    if (w == 0) conv_load_log(cv, L, C, pend_conv);
+    const size_t logw = (size_t)kDK + kDV + 1;
+    // deferred commit: rows 1..keep of half wr^1, held in registers until the first sweep
+    float dl[RP], kpr[RP], pdr[RP];
+#pragma unroll
+    for (int tp = 0; tp < RP; tp++) {
+        dl[tp] = kpr[tp] = pdr[tp] = 0.0f;
+        if (tp < keep) {
+            const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp + 1) * d.nv + h) * logw;
+            kpr[tp] = ld_early(u + j);
+            dl[tp] = ld_early(u + kDK + col);
+            if (j == 0) pdr[tp] = ld_early(u + kDK + kDV);
+        }
+    }
     pdl_wait();
     pdl_trigger();
     // rows 0..pre-1: the conv inputs of this thread's channels, its z column for the output rows
@@ -2964,16 +2987,11 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
         gb = ld_early(yr + C + d.vd + h);
         ga = ld_early(yr + C + d.vd + d.nv + h);
     }
-    const int n = st->n;
-    if (n <= 0 || n > NR || n > pre || st->row0 != 0 || st->pend_keep > RP) {   // nothing to do, or
-        // a pass this variant does not hold (reported); the same for every CTA of the cluster
+    if (n <= 0 || n > NR || n > pre || row0 != 0 || keep > RP) {   // nothing to do, or a pass
+        // this variant does not hold (reported); the same for every CTA of the cluster
         if (n > 0 && j == 0 && c == 0) st->status = -92;
         return;
     }
-    const int logged = st->logged, keep = st->pend_keep, pend_conv = st->pend_conv, wr = st->wr;
-    conv_load_log(cq, L, C, pend_conv);
-    conv_load_log(ck, L, C, pend_conv);
-    if (w == 0) conv_load_log(cv, L, C, pend_conv);
     __shared__ __align__(16) float sq[NR][kDK], sk[NR][kDK];
     __shared__ __align__(16) float sv[NR][kDnCols];
     __shared__ __align__(16) float so[NR][kDV];   // the head's output rows
@@ -2981,19 +2999,6 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
     __shared__ __align__(16) float skp[RP][kDK];
     __shared__ float spd[RP];
     __shared__ float sdelta[kDnCols], xo[kDnParts][kDnCols], xk_[kDnParts][kDnCols];
-    const size_t logw = (size_t)kDK + kDV + 1;
-    // deferred commit: rows 1..keep of half wr^1, held in registers until the first sweep
-    float dl[RP], kpr[RP], pdr[RP];
-#pragma unroll
-    for (int tp = 0; tp < RP; tp++) {
-        dl[tp] = kpr[tp] = pdr[tp] = 0.0f;
-        if (tp < keep) {
-            const float *u = L.upd + (((size_t)(wr ^ 1) * d.cap + tp + 1) * d.nv + h) * logw;
-            kpr[tp] = ld_early(u + j);
-            dl[tp] = ld_early(u + kDK + col);
-            if (j == 0) pdr[tp] = ld_early(u + kDK + kDV);
-        }
-    }
     // ---- gates of token tg
     if (tg >= 0 && tg < n) {
         sbeta[tg] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-gb)));
