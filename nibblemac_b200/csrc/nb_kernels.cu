@@ -710,7 +710,7 @@ __global__ void __launch_bounds__(kTallWarps * 32) k_mv_head_mma(Mat W0, Act in,
 //                    EPI 1: y[v][row] += acc (out_proj / o_proj / down_proj into the residual)
 //                    EPI 3: SwiGLU over (W0 = gate, W1 = up), the up accumulators handed to
 //                    the gate warps through shared memory, then A8 of the product for down_proj.
-// nmax <= 4. Block: 8 warps (16 when the panel has more than 8 units).
+// nmax <= 4. Block: 16 warps (8 for one-row passes of up to 8 units).
 constexpr int kPanelWarps = 16;
 constexpr int kPanelPad = 4;   // fp32 row padding of the staged residual rows (bank spread)
 
@@ -3757,7 +3757,10 @@ template <int NMAX, int EPI, bool NORM, int PPC = 1>
 bool panel_t(const Mat &W0, const Mat &W1, Act in, NormIn nin, const Step *st, float *y, int ldy,
              Act out, cudaStream_t s, const L2Prefetch &pf = L2Prefetch()) {
     const int nmat = EPI == 3 ? 2 : PPC;
-    const int nunit = W0.nsb * nmat, nw = nunit > 8 ? kPanelWarps : 8;
+    // passes of several rows: 16 warps, since the units phase is latency-bound and splits into
+    // as many short per-warp sequences as the block allows (a unit's blocks over 2 or 4 warps);
+    // one-row passes: 8 warps (16 for more than 8 units)
+    const int nunit = W0.nsb * nmat, nw = (NMAX > 1 || nunit > 8) ? kPanelWarps : 8;
     const size_t sm = panel_smem(nunit, W0.cols, nmat, NMAX, NORM);
     // 16-byte row loads of the inputs (every engine buffer is 256-byte aligned, cols % 256 == 0)
     if (((uintptr_t)nin.x | (uintptr_t)nin.w | (uintptr_t)in.q | (uintptr_t)in.d | (uintptr_t)in.fs) & 15) return false;
