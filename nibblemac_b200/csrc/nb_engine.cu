@@ -371,6 +371,12 @@ void enqueue_forward(pinfer_ctx *c, int nmax, int head, bool export_normed = fal
                 pf.add(m->w, (size_t)m->npanels * m->nsb * kUnitBytes);
         }
         if (D.is_full) {
+            // and this layer's K / V rows of the positions the pass attends to
+            const size_t kvb = (size_t)ad.max_ctx * c->hd * sizeof(float);
+            for (int g = 0; g < c->nkv; g++) {
+                pf.add(c->att[l].kc + (size_t)g * ad.max_ctx * c->hd, kvb, (unsigned)(c->hd * sizeof(float)));
+                pf.add(c->att[l].vc + (size_t)g * ad.max_ctx * c->hd, kvb, (unsigned)(c->hd * sizeof(float)));
+            }
             const Act o = mid_act(c, c->nq * c->hd);
             launch_matvec_norm(D.win, c->x, D.in_norm, c->eps, c->step, c->y, c->attd.ldy, nmax, c->act_h, s, pf);
             launch_attn_prep(c->att[l], ad, c->y, c->qbuf, c->step, s);

@@ -141,15 +141,20 @@ void launch_matvec_chunked(const Mat &W, Act in, const Step *st, float *y, int l
                            int nmax, cudaStream_t s);
 // Byte ranges (16-byte aligned, sizes multiples of 16) a kernel asks the L2 to fetch ahead of
 // the kernels that will read them (cp.async.bulk.prefetch.L2), split over the kernel's CTAs.
-constexpr int kMaxPrefetch = 8;
+// A range with row_bytes > 0 is a KV cache: only its first (Step::pos0 + Step::n) rows of
+// row_bytes are fetched (the positions the pass attends to), read from the Step block when the
+// kernel starts.
+constexpr int kMaxPrefetch = 12;
 struct L2Prefetch {
     const void *p[kMaxPrefetch] = {};
     unsigned bytes[kMaxPrefetch] = {};
+    unsigned row_bytes[kMaxPrefetch] = {};
     int n = 0;
-    void add(const void *ptr, size_t nbytes) {
+    void add(const void *ptr, size_t nbytes, unsigned rowb = 0) {
         if (n < kMaxPrefetch && ptr && nbytes >= 16) {
             p[n] = ptr;
             bytes[n] = (unsigned)(nbytes & ~(size_t)15);
+            row_bytes[n] = rowb;
             n++;
         }
     }

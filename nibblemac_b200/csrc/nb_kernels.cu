@@ -818,14 +818,24 @@ __device__ __forceinline__ void panel_norm_quant(const float *sx, const float *s
 
 // This CTA's share of the L2 prefetch ranges: the concatenated ranges split evenly (16-byte
 // granules) over the grid, one bulk prefetch per range piece.
-__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch &pf) {
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch &pf, const Step *st) {
     if (pf.n == 0 || threadIdx.x != 0) return;
+    unsigned len[kMaxPrefetch];
     unsigned long long total = 0;
-    for (int i = 0; i < pf.n; i++) total += pf.bytes[i];
+    int rows = -1;
+    for (int i = 0; i < pf.n; i++) {
+        len[i] = pf.bytes[i];
+        if (pf.row_bytes[i]) {   // a KV cache: the rows up to the pass's last position
+            if (rows < 0) rows = st->pos0 + st->n;
+            const unsigned long long want = (unsigned long long)(rows > 0 ? rows : 0) * pf.row_bytes[i];
+            len[i] = (unsigned)((want < len[i] ? want : len[i]) & ~15ull);
+        }
+        total += len[i];
+    }
     const unsigned long long g = total >> 4, G = gridDim.x, c = blockIdx.x;
     unsigned long long lo = (g * c / G) << 4, hi = (g * (c + 1) / G) << 4, base = 0;
     for (int i = 0; i < pf.n && lo < hi; i++) {
-        const unsigned long long e = base + pf.bytes[i];
+        const unsigned long long e = base + len[i];
         if (lo < e) {
             const unsigned long long a = lo, b = hi < e ? hi : e;
             const char *src = static_cast<const char *>(pf.p[i]) + (a - base);
@@ -879,7 +889,7 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
         for (int i = tid; i < cols / 4; i += blockDim.x)
             reinterpret_cast<float4 *>(sw)[i] = reinterpret_cast<const float4 *>(nin.w)[i];
     }
-    l2_prefetch_share(pf);   // weights of kernels further ahead (constants)
+    l2_prefetch_share(pf, st);   // weights and KV rows of kernels further ahead
     pdl_wait();
     pdl_trigger();
     const int n = ld_early_s32(&st->n);
