@@ -176,9 +176,19 @@ def matvec_roofline(torch, lib, peak_gbs: float) -> dict:
         return us, alg, exact
 
     us, alg, exact = run(248320, 1024, 4, 2, 20, head=True)
-    achieved = alg / (us * 1e-6) / 1e9
     out["head"] = {"rows": 248320, "cols": 1024, "n": 4, "us": round(us, 2),
-                   "bytes": alg, "gbs": round(achieved, 1), "bit_exact": exact}
+                   "bytes": alg, "gbs": round(alg / (us * 1e-6) / 1e9, 1), "bit_exact": exact}
+    # the dominant kernel of a verify round: the 8-row slice matvec of the out / o / down
+    # projections (1024 rows x 2048 / 3584 columns, the pass's 4 rows)
+    sl, tb, tt = {}, 0, 0.0
+    for rows, cols in ((1024, 2048), (1024, 3584)):
+        us1, alg1, ex1 = run(rows, cols, 4, 256, 512)
+        sl[f"{rows}x{cols}"] = {"us": round(us1, 2), "bytes": alg1, "gbs": round(alg1 / (us1 * 1e-6) / 1e9, 1),
+                                "bit_exact": ex1}
+        tb += alg1
+        tt += us1
+    out["slice_out_down"] = sl
+    achieved = tb / (tt * 1e-6) / 1e9
     cfg1 = {}
     for n in (1, 2, 4):
         us1, alg1, ex1 = run(3584, 1024, n, 128, 256)
@@ -189,9 +199,38 @@ def matvec_roofline(torch, lib, peak_gbs: float) -> dict:
     return out
 
 
-def traffic_from_profiles() -> float | None:
-    """dram bytes per launch of the head-shaped matvec from the committed ncu summary."""
-    p = ROOT / "profiles" / "q4k_matvec_head_n4.md"
+def round_bytes(path: Path, ctx_avg: int, k: int) -> int:
+    """Algorithmic bytes of one verify round of the model at `path`: every tensor of the forward
+    (the layers, the tied head and the norms; not the MTP head) read once, the DeltaNet
+    recurrent states read and written, the conv states read and written, the K/V rows of
+    ctx_avg positions read, and the k rows of the update log written."""
+    import struct
+    from nibblemac_b200 import pq
+    with open(path, "rb") as f:
+        hdr = f.read(pq.HEADER_BYTES)
+        fields = struct.unpack_from(pq.HEADER_FMT, hdr)
+        n_tensors, dir_off = fields[2], fields[3]
+        f.seek(dir_off)
+        d = f.read(128 * n_tensors)
+    wbytes = 0
+    for i in range(n_tensors):
+        name, dt, nd, s0, s1, s2, s3, off, nb = struct.unpack_from(pq.ENTRY_FMT, d, 128 * i)
+        if not name.split(b"\0", 1)[0].startswith(b"mtp."):
+            wbytes += nb
+    (_, _, _, _, _, _, H, L, V, ffn, nq, nkv, hd, rot, lkh, lvh, lkd, lvd, K, mask, *_rest) = fields
+    n_full = bin(mask).count("1")
+    n_lin = L - n_full
+    C = 2 * lkh * lkd + lvh * lvd
+    state = 2 * n_lin * lvh * lkd * lvd * 4
+    conv = 2 * n_lin * (K - 1) * C * 4
+    kv = n_full * 2 * nkv * hd * 4 * ctx_avg
+    log = k * n_lin * lvh * (lkd + lvd + 1) * 4
+    return int(wbytes + state + conv + kv + log)
+
+
+def traffic_from_profiles(name: str = "q4k_slice_out_down_n4.md") -> float | None:
+    """dram bytes per launch of the dominant kernel from its committed ncu summary."""
+    p = ROOT / "profiles" / name
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -431,6 +470,33 @@ def run_profile_gemm(n: int) -> None:
     lib.nb_mv_destroy(h)
 
 
+def run_profile_matvec(rows: int, cols: int, n: int) -> None:
+    """The Q4K x A8 matmul through the kernel ABI (nb_mv_matmul: the slice kernel for 2048 or more
+    columns and 2-4 vectors, else the panel kernel), 4 launches on the kbench-seeded matrix,
+    checked bit for bit against the oracle; for ncu -k."""
+    import torch
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from nibblemac_b200._lib import load_library
+    from oracle import Q4KOracle
+    lib, orc = load_library(), Q4KOracle()
+    s = torch.cuda.current_stream().cuda_stream
+    w = orc.kb_matrix(rows, cols, 42)
+    panels = np.zeros(lib.nb_q4k_panel_bytes(rows, cols), np.uint8)
+    assert lib.nb_q4k_repack(w.ctypes.data, rows, cols, panels.ctypes.data) == 0
+    dW = torch.from_numpy(panels).cuda()
+    x = torch.from_numpy(orc.kb_vec(n * cols, 7).reshape(n, cols)).cuda()
+    y = torch.empty((n, rows), dtype=torch.float32, device="cuda")
+    h = lib.nb_mv_create(rows, cols, max(n, 4))
+    assert h, lib.last_error()
+    assert lib.nb_mv_set_n(h, n, s) == 0 and lib.nb_mv_quant(h, x.data_ptr(), s) == 0
+    for _ in range(4):
+        assert lib.nb_mv_matmul(h, dW.data_ptr(), y.data_ptr(), s) == 0
+    torch.cuda.synchronize()
+    lib.nb_mv_destroy(h)
+    ref = orc.matmul(w, rows, cols, x.cpu().numpy())
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32)), "matvec != oracle"
+
+
 def run_profile_batch(nseq: int, ntok: int) -> None:
     """Config-4 style batch generation for ncu: plain and warm-up runs, then one k = 3 run
     inside cudaProfilerStart/Stop."""
@@ -625,6 +691,9 @@ def main() -> None:
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="N",
                     help="the tensor-core GEMM on the config-1 matrix (3584 x 1024) over N activation "
                          "rows through the kernel ABI: prepare once, then 5 launches (for ncu -k)")
+    ap.add_argument("--profile-matvec", type=int, nargs=3, default=None, metavar=("ROWS", "COLS", "N"),
+                    help="the Q4K x A8 matmul through the kernel ABI on the kbench matrix: 4 launches, "
+                         "checked against the oracle (for ncu -k)")
     ap.add_argument("--profile-batch", type=int, nargs=2, default=None, metavar=("SEQS", "TOKENS"),
                     help="config-4 prompts (bench seed) for SEQS sequences: one plain and one warm-up "
                          "batch generation of TOKENS tokens at k = 3, then one inside "
@@ -635,6 +704,9 @@ def main() -> None:
         return
     if args.profile_batch:
         run_profile_batch(*args.profile_batch)
+        return
+    if args.profile_matvec:
+        run_profile_matvec(*args.profile_matvec)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -750,10 +822,19 @@ def main() -> None:
     if rank == 0:
         peak, kind = peaks()
         mv = matvec_roofline(torch, lib, peak)
+        rb = round_bytes(path, CTX + N_GEN // 2, K_DRAFT)
+        round_s = t_dev / max(rounds, 1)
         roof = {"bound": "hbm", "achieved": round(mv["_achieved"], 1), "peak": peak, "unit": "GB/s",
                 "frac": round(mv["_achieved"] / peak, 4), "traffic": traffic_from_profiles(),
                 "peak_kind": kind,
-                "kernel": "q4k x a8 matvec, LM-head shape 248320x1024, n=4 (verify rows)"}
+                "kernel": "k_mv_slice: q4k x a8 matvec of the out / o / down projections (1024 x 2048 and "
+                          "1024 x 3584, n=4 verify rows), timed alone over a rotating arena of weight copies; "
+                          "the largest share of a verify round (profiles/verify_round_launches_config3.md)",
+                "round": {"bytes": rb, "us": round(round_s * 1e6, 1),
+                          "gbs": round(rb / round_s / 1e9, 1), "frac": round(rb / round_s / 1e9 / peak, 4),
+                          "what": "algorithmic bytes of one verify round (weights, DeltaNet and conv "
+                                  "states read and written, K/V rows read, logs written) / device time "
+                                  "per round"}}
         extra["matvec"] = {k: v for k, v in mv.items() if not k.startswith("_")}
     m.close()
     if rank == 0:
