@@ -816,6 +816,45 @@ __device__ __forceinline__ void panel_norm_quant(const float *sx, const float *s
     }
 }
 
+// ---- staging of a pass's input rows into shared memory, after pdl_wait
+// A segment is `rows` rows of `per` 16-byte chunks. Each row gets blockDim / rows threads (rows
+// divides the block), and thread t of a row takes chunks t, t + TPR, ...: no division per chunk.
+// Every load of a thread (up to 4 chunks of the first segment and one of each of the others) is
+// issued, volatile and so in program order, before its first store, so the rows arrive in one
+// round trip to L2 (the compiler cannot tell the shared destination from the global source).
+struct StageSeg {
+    uint8_t *dst;
+    const uint8_t *src;
+    int dstride, sstride;   // bytes between rows
+    int per, rows;          // 16-byte chunks per row, rows
+};
+__device__ __forceinline__ uint4 ld_early_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+// a: the main segment; b, c: small segments of the same row count with per <= blockDim / rows
+// (b.rows == 0: none)
+__device__ __forceinline__ void stage_rows3(const StageSeg &a, const StageSeg &b, const StageSeg &c) {
+    const int tpr = (int)blockDim.x / a.rows, v = (int)threadIdx.x / tpr, c0 = (int)threadIdx.x - v * tpr;
+    uint4 ra[4], rb, rc;
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        if (c0 + j * tpr < a.per) ra[j] = ld_early_v4(a.src + (size_t)v * a.sstride + 16 * (c0 + j * tpr));
+    const bool hb = b.rows > 0 && c0 < b.per, hc = c.rows > 0 && c0 < c.per;
+    if (hb) rb = ld_early_v4(b.src + (size_t)v * b.sstride + 16 * c0);
+    if (hc) rc = ld_early_v4(c.src + (size_t)v * c.sstride + 16 * c0);
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+        if (c0 + j * tpr < a.per)
+            *reinterpret_cast<uint4 *>(a.dst + (size_t)v * a.dstride + 16 * (c0 + j * tpr)) = ra[j];
+    if (hb) *reinterpret_cast<uint4 *>(b.dst + (size_t)v * b.dstride + 16 * c0) = rb;
+    if (hc) *reinterpret_cast<uint4 *>(c.dst + (size_t)v * c.dstride + 16 * c0) = rc;
+    for (int k = c0 + 4 * tpr; k < a.per; k += tpr)   // rows longer than 4 chunks per thread
+        *reinterpret_cast<uint4 *>(a.dst + (size_t)v * a.dstride + 16 * k) =
+            ld_early_v4(a.src + (size_t)v * a.sstride + 16 * k);
+}
+
 // This CTA's share of the L2 prefetch ranges: the concatenated ranges split evenly (16-byte
 // granules) over the grid, one bulk prefetch per range piece.
 __device__ __forceinline__ void l2_prefetch_share(const L2Prefetch &pf, const Step *st) {
@@ -894,24 +933,38 @@ __global__ void __launch_bounds__(kPanelWarps * 32) k_mv_panel(Mat W0, Mat W1, A
     pdl_trigger();
     const int n = ld_early_s32(&st->n);
     if (NORM) {   // the residual rows beside the Step block
-        const int per = cols / 4, total = NMAX * per;
-        for (int i = tid; i < total; i += blockDim.x) {
-            const int v = i / per, c4 = i - v * per;
-            reinterpret_cast<float4 *>(sx + (size_t)v * (cols + kPanelPad))[c4] =
-                reinterpret_cast<const float4 *>(nin.x + (size_t)v * cols)[c4];
+        if (NMAX == 1) {   // one row: all of it at once (measured faster for one-row passes)
+            const StageSeg none{};
+            stage_rows3({reinterpret_cast<uint8_t *>(sx), reinterpret_cast<const uint8_t *>(nin.x),
+                         (cols + kPanelPad) * 4, cols * 4, cols / 4, NMAX}, none, none);
+        } else {   // several rows, which 100+ CTAs read at once: one chunk after another per thread,
+                   // which spreads the requests for the same lines (measured faster than a burst)
+            const int per = cols / 4, total = NMAX * per;
+            for (int i = tid; i < total; i += blockDim.x) {
+                const int v = i / per, c4 = i - v * per;
+                reinterpret_cast<float4 *>(sx + (size_t)v * (cols + kPanelPad))[c4] =
+                    reinterpret_cast<const float4 *>(nin.x + (size_t)v * cols)[c4];
+            }
         }
     } else {      // the A8 rows of the previous kernel beside the Step block
-        const int per = cols / 16, nbi = in.cols >> 5;
-        for (int i = tid; i < NMAX * per; i += blockDim.x) {
-            const int v = i / per, c16 = i - v * per;
-            reinterpret_cast<int4 *>(sq + (size_t)v * cols)[c16] =
-                reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols)[c16];
-        }
-        const int per4 = nb / 4;
-        for (int i = tid; i < NMAX * per4; i += blockDim.x) {
-            const int v = i / per4, b4 = i - v * per4;
-            reinterpret_cast<float4 *>(sd + (size_t)v * nb)[b4] = reinterpret_cast<const float4 *>(in.d + (size_t)v * nbi)[b4];
-            reinterpret_cast<float4 *>(sfs + (size_t)v * nb)[b4] = reinterpret_cast<const float4 *>(in.fs + (size_t)v * nbi)[b4];
+        const int nbi = in.cols >> 5;
+        if (NMAX == 1) {
+            stage_rows3({reinterpret_cast<uint8_t *>(sq), reinterpret_cast<const uint8_t *>(in.q), cols, in.cols, cols / 16, NMAX},
+                        {reinterpret_cast<uint8_t *>(sd), reinterpret_cast<const uint8_t *>(in.d), nb * 4, nbi * 4, nb / 4, NMAX},
+                        {reinterpret_cast<uint8_t *>(sfs), reinterpret_cast<const uint8_t *>(in.fs), nb * 4, nbi * 4, nb / 4, NMAX});
+        } else {
+            const int per = cols / 16;
+            for (int i = tid; i < NMAX * per; i += blockDim.x) {
+                const int v = i / per, c16 = i - v * per;
+                reinterpret_cast<int4 *>(sq + (size_t)v * cols)[c16] =
+                    reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols)[c16];
+            }
+            const int per4 = nb / 4;
+            for (int i = tid; i < NMAX * per4; i += blockDim.x) {
+                const int v = i / per4, b4 = i - v * per4;
+                reinterpret_cast<float4 *>(sd + (size_t)v * nb)[b4] = reinterpret_cast<const float4 *>(in.d + (size_t)v * nbi)[b4];
+                reinterpret_cast<float4 *>(sfs + (size_t)v * nb)[b4] = reinterpret_cast<const float4 *>(in.fs + (size_t)v * nbi)[b4];
+            }
         }
     }
     __syncthreads();
@@ -1080,7 +1133,10 @@ __global__ void __launch_bounds__(kSliceWarps * 32) k_mv_slice(Mat W0, Act in, S
     pdl_trigger();
     const int n = ld_early_s32(&st->n);
     {   // the A8 rows of the previous kernel beside the Step block
-        const int per = cols / 16, nbi = in.cols >> 5, per4 = nb / 4;
+        const int nbi = in.cols >> 5;
+        // one chunk after another per thread: 128 CTAs read the same rows at once, and spreading
+        // the requests measured faster than issuing them in one burst
+        const int per = cols / 16, per4 = nb / 4;
         for (int i = tid; i < NMAX * per; i += blockDim.x) {
             const int v = i / per, c16 = i - v * per;
             reinterpret_cast<int4 *>(sq + (size_t)v * qs)[c16] = reinterpret_cast<const int4 *>(in.q + (size_t)v * in.cols)[c16];
