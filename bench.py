@@ -14,6 +14,8 @@ context (restored with pinfer_rewind before every step, outside the timed region
          weights, states and context already in HBM)
   e2e    tokens / wall time of the public API call (pinfer_b200_generate_synthetic_ex: prompt
          and greedy stream copied in, 1-token prefill, decode, tokens copied out)
+  prefill  pinfer_eval of the 511 context tokens from an empty state (tensor-core chunks of up
+         to 64 rows), and at N=1 of configs[4]'s 4095 tokens on the 2B shape: device and wall ms
 Multi-GPU: one independent replica per GPU (replicas only, no collective on the data path),
 weak scaling; value = all tokens / max over ranks of the device time.
 --impl reference: the reference engine's own CPU path (oracle/_ref, scalar C) on the host
@@ -121,6 +123,42 @@ def model_path(rank: int, dist, preset: str = "0.8b", native: bool = True) -> Pa
 
 def context_tokens(rank: int, vocab: int) -> np.ndarray:
     return np.random.default_rng(1234 + rank).integers(0, vocab, CTX).astype(np.int32)
+
+
+def measure_prefill(m, torch, tokens: np.ndarray, reps: int = 3) -> dict:
+    """pinfer_eval of a context's tokens from an empty state (tensor-core prefill chunks of up
+    to 64 rows): device time from CUDA events on the context's stream, and the call's wall time
+    (tokens copied in, launches, the final synchronisation). One untimed call first; leaves
+    the context filled with the tokens."""
+    stream = torch.cuda.ExternalStream(m.stream())
+    dev, wall = [], []
+    for i in range(reps + 1):
+        m.reset()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        t0 = time.perf_counter()
+        m.eval(tokens, logits=False)
+        t1 = time.perf_counter()
+        e1.record(stream)
+        e1.synchronize()
+        if i:
+            dev.append(e0.elapsed_time(e1))
+            wall.append((t1 - t0) * 1000.0)
+    d = statistics.median(dev)
+    return {"tokens": int(len(tokens)), "device_ms": round(d, 3), "wall_ms": round(statistics.median(wall), 3),
+            "tok_s": round(len(tokens) / (d / 1000.0), 1)}
+
+
+def measure_prefill5(torch, rank: int) -> dict:
+    """configs[4]'s context on one GPU: the 2B-shaped model, 4095 tokens prefilled."""
+    from nibblemac_b200.model import Model
+    path = model_path(rank, None, "2b")
+    m = Model(path, max_ctx=CTX5 + 16)
+    try:
+        ctx = np.random.default_rng(4321).integers(0, m.n_vocab, CTX5).astype(np.int32)
+        return {"model": "2b", **measure_prefill(m, torch, ctx[:-1], reps=2)}
+    finally:
+        m.close()
 
 
 def matvec_roofline(torch, lib, peak_gbs: float) -> dict:
@@ -677,6 +715,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config4", action="store_true",
                     help="leave the configs[3] multi-stream record out of the default line")
+    ap.add_argument("--no-prefill5", action="store_true",
+                    help="leave the configs[4] (2B, 4095-token) prefill time out of the default line")
     ap.add_argument("--config4", action="store_true",
                     help="configs[3]: 256 requests per GPU in one multi-sequence batch "
                          "(one JSON line)")
@@ -741,8 +781,7 @@ def main() -> None:
     # a batch's contexts cannot be longer than the context whose weights it shares
     m = Model(path, max_ctx=max(CTX + N_GEN + 16, 1024 + GEN4 + 16))
     ctx = context_tokens(rank, m.n_vocab)
-    m.reset()
-    m.eval(ctx[:-1], logits=False)
+    prefill = {"config3": measure_prefill(m, torch, ctx[:-1])}   # leaves the context filled
     dev_blob = m.save_state() if rank == 0 else b""
     m.checkpoint()
     greedy, _, st0, _ = m.generate_synthetic_ex(ctx[-1:], N_GEN, 0, np.zeros(N_GEN, np.int32), 0, 0.0,
@@ -837,6 +876,8 @@ def main() -> None:
                                   "per round"}}
         extra["matvec"] = {k: v for k, v in mv.items() if not k.startswith("_")}
     m.close()
+    if rank == 0 and world == 1 and not args.no_prefill5:
+        prefill["config5"] = measure_prefill5(torch, rank)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup,
@@ -850,7 +891,7 @@ def main() -> None:
                 "gpu_launches": int(rounds * kernels_per_round * world),
                 "kernels_per_round": kernels_per_round, "rounds": rounds,
                 "sweep": sweep, "config2_plain": config2, "roofline": roof, "clocks": clk.summary(),
-                "config4": config4}
+                "config4": config4, "prefill": prefill}
         line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(path, dev_blob, greedy)

@@ -55,7 +55,7 @@ def build_quant() -> Path:
 
 def build_engine() -> Path:
     out = LIB / "libpinfer.so"
-    cu = ["nb_kernels.cu", "nb_gemm.cu", "nb_engine.cu", "nb_batch.cu", "nb_capi.cu"]
+    cu = ["nb_kernels.cu", "nb_gemm.cu", "nb_engine.cu", "nb_prefill.cu", "nb_batch.cu", "nb_capi.cu"]
     cpp = ["nb_model.cpp", "nb_libm.cpp", "nb_nccl.cpp"]
     headers = sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
     BUILD.mkdir(exist_ok=True)

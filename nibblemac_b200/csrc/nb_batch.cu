@@ -175,14 +175,12 @@ int batch_alloc(pinfer_b200_batch *b) {
         set_last_error("pinfer_b200_batch_create: kernel setup failed");
         return PINFER_E_NOMEM;
     }
-    // tile images of every projection and of the head
+    // tile images of every projection (shared with the context's prefill and its clones) and
+    // of this batch's head rows
+    if ((rc = ensure_gemm_tiles(b->src, false))) return rc;
     for (int l = 0; l < c->n_layers; l++) {
-        const auto &D = c->layers[l];
-        auto &T = b->layers[l];
-        const Mat none;
-        if ((rc = tile_mat(b, D.win, none, &T.win)) || (rc = tile_mat(b, D.out, none, &T.out)) ||
-            (rc = tile_mat(b, D.gate, D.up, &T.gu)) || (rc = tile_mat(b, D.down, none, &T.down)))
-            return rc;
+        const auto &W = b->weights->tiles[l];
+        b->layers[l] = {W.win, W.out, W.gu, W.down};
     }
     b->sharded = c->shard_world > 1;
     b->row_base = b->sharded ? c->head_row0 : 0;

@@ -3,6 +3,7 @@
 #pragma once
 #include <cstdio>
 #include <memory>
+#include <mutex>
 #include <vector>
 
 #include "nb_engine.h"
@@ -34,15 +35,44 @@ using nb::AttnLayer;
 using nb::AttnDims;
 using nb::kMaxLayers;
 using nb::kMaxRows;
+using nb::GemmMaps;
+using nb::SeqPass;
 
 // ---------------------------------------------------------------- the context
 // Device buffers of the model parameters (weights, norms, RoPE tables), shared by a context and
 // its clones (pinfer_b200_clone) and freed with the last of them.
 struct WeightStore {
     std::vector<void *> ptrs;
+    // tensor-core tile images of the projections (nb_gemm.cu), made on the first prefill or
+    // batch that needs them (ensure_gemm_tiles) and shared like the weights
+    std::mutex tile_mu;
+    bool tiles_ok = false, head_tile_ok = false;
+    struct TileLayer {
+        GemmW win, out, gu, down;   // gu: gate ++ up
+    } tiles[kMaxLayers];
+    GemmW head_tile;                // the whole LM head (logits of every prefill row)
     ~WeightStore() {
         for (void *p : ptrs) cudaFree(p);
     }
+};
+
+// Rows of one prefill chunk through the tensor-core GEMMs (nb_prefill.cu), as the reference's
+// batched prefill (engine/src/forward.c:154-165: chunks of ctx->batch <= 64 rows).
+constexpr int kPrefillRows = 64;
+constexpr int kPrefillSub = kPrefillRows / kMaxRows;   // 16-row sub-passes (Step blocks) per chunk
+
+// A context's buffers for prefill chunks, allocated on first use.
+struct PrefillScratch {
+    bool ready = false;
+    int ldy = 0;                              // y: W_in rows, or gate ++ up rows
+    float *x = nullptr, *y = nullptr, *qbuf = nullptr;
+    Act act_h, act_mid;
+    GemmMaps maps_h, maps_ol, maps_oa, maps_f;
+    Step *steps = nullptr;                    // [kPrefillSub]
+    SeqPass *d_pass = nullptr;                // [chunks of max_ctx][kPrefillSub]
+    float *logits = nullptr;                  // [kPrefillRows][vocab] (forward_all), on first use
+    unsigned long long *partial = nullptr;
+    int *nan0 = nullptr;
 };
 
 struct pinfer_ctx {
@@ -120,6 +150,8 @@ struct pinfer_ctx {
     unsigned long long *d_keys = nullptr;   // [2][kMaxRows]: best key, row-0 NaN flag
     int round_nmax[PINFER_SPEC_MAX_K + 1] = {};
 
+    PrefillScratch pf;
+
     // checkpoint slot (pinfer_checkpoint)
     float *ck_buf = nullptr;
     size_t ck_floats = 0;
@@ -139,3 +171,10 @@ struct pinfer_ctx {
     }
 };
 
+// nb_prefill.cu
+int ensure_gemm_tiles(pinfer_ctx *c, bool head);   // the shared tile images (head: the LM head's too)
+bool prefill_gemm_ok(const pinfer_ctx *c);          // the model shape has the prefill kernels
+// n rows (> kMaxRows worth it) at positions n_past.. in chunks of up to kPrefillRows rows;
+// logits_all (host, [n][vocab], unsharded heads only) receives every row's logits. Advances
+// n_past; asynchronous on the context's stream unless logits are copied out.
+int prefill_gemm(pinfer_ctx *c, const int32_t *tokens, int n, float *logits_all);

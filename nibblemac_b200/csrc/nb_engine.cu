@@ -486,10 +486,19 @@ int flush_pending(pinfer_ctx *c) {
     return PINFER_OK;
 }
 
-// Feed tokens through the model in chunks of kMaxRows (pf_forward_h, forward.c:149-165: the
-// rows of a chunk give the same results whatever the chunk size). want: 0 nothing,
-// 1 logits + argmax of the last chunk, 2 argmax only.
+// Feed tokens through the model (pf_forward_h, forward.c:149-165: the rows of a chunk give the
+// same results whatever the chunk size). The rows before the last pass go through the tensor-
+// core GEMMs in chunks of up to kPrefillRows when there are more than one pass's worth of them;
+// the last (n - 1) % kMaxRows + 1 rows, whose logits or argmax are wanted, take one CUDA-core
+// pass. want: 0 nothing, 1 logits + argmax of the last pass, 2 argmax only.
 int forward_tokens(pinfer_ctx *c, const int32_t *tokens, int n, int want) {
+    const int tail = want ? (n - 1) % kMaxRows + 1 : 0;
+    if (n - tail > kMaxRows && prefill_gemm_ok(c)) {
+        const int rc = prefill_gemm(c, tokens, n - tail, nullptr);
+        if (rc) return rc;
+        tokens += n - tail;
+        n = tail;
+    }
     for (int t0 = 0; t0 < n; t0 += kMaxRows) {
         const int nb = std::min(kMaxRows, n - t0);
         const bool last = t0 + nb == n;
@@ -509,16 +518,25 @@ int validate_tokens(const pinfer_ctx *c, const int32_t *tokens, int n) {
     return PINFER_OK;
 }
 
+void drop_graphs(pinfer_ctx *c);
+
+// Output and target-token buffers of a generation of n_max tokens. Captured round graphs hold
+// the buffers' addresses, so growing them drops the graphs (recaptured on next use); they grow
+// at least twofold to keep that rare.
 int ensure_out(pinfer_ctx *c, int n_max) {
     if (c->out_cap >= n_max) return PINFER_OK;
+    const int cap = std::max(n_max, std::max(2 * c->out_cap, 256));
+    CUDA_OK(cudaStreamSynchronize(c->stream));   // no round in flight uses the old buffers
+    drop_graphs(c);
     cudaFree(c->d_out);
     cudaFree(c->d_greedy);
     c->d_out = nullptr;
     c->d_greedy = nullptr;
-    CUDA_OK(cudaMalloc(&c->d_out, sizeof(int) * (size_t)n_max));
-    CUDA_OK(cudaMalloc(&c->d_greedy, sizeof(int) * (size_t)n_max));
-    CUDA_OK(cudaMemset(c->d_greedy, 0, sizeof(int) * (size_t)n_max));
-    c->out_cap = n_max;
+    c->out_cap = 0;
+    CUDA_OK(cudaMalloc(&c->d_out, sizeof(int) * (size_t)cap));
+    CUDA_OK(cudaMalloc(&c->d_greedy, sizeof(int) * (size_t)cap));
+    CUDA_OK(cudaMemset(c->d_greedy, 0, sizeof(int) * (size_t)cap));
+    c->out_cap = cap;
     return PINFER_OK;
 }
 
@@ -1205,6 +1223,11 @@ int pinfer_b200_round_kernels(pinfer_ctx *c, int k) {
 int pinfer_b200_forward_all(pinfer_ctx *c, const int32_t *tokens, int n, float *logits_all) {
     int rc = validate_tokens(c, tokens, n);
     if (rc) return rc;
+    if (!logits_all) return PINFER_E_ARG;
+    if (n > kMaxRows && c->shard_world == 1 && prefill_gemm_ok(c)) {   // chunks of up to 64 rows
+        if ((rc = prefill_gemm(c, tokens, n, logits_all))) return rc;
+        return sync(c);
+    }
     for (int t0 = 0; t0 < n; t0 += kMaxRows) {
         const int nb = std::min(kMaxRows, n - t0);
         launch_set_pass(c->step, nb, c->n_past, 0, tokens + t0, c->stream);

@@ -3268,6 +3268,224 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
     }
 }
 
+// Gated DeltaNet layer of a prefill chunk: rows 0..n-1 of y (any n), with no deferred commit to
+// replay and nothing logged (the caller flushes a pending commit first). The layout and the
+// arithmetic are k_deltanet3's (4-CTA cluster per key head, state columns per CTA, state rows
+// per warp, the ordered kv / o chains handed warp to warp); the state stays in registers over
+// the whole chunk, which arrives in blocks of kDnBlk rows: a block's conv inputs, z columns and
+// gate inputs are loaded, convolved and normalised, its tokens run through the recurrence, its
+// outputs are normed and quantised, and a cluster barrier frees the block buffers (peers write
+// this CTA's output rows) before the next block. The decay of a block's first token is applied
+// in its own first sweep instead of inside the previous token's sweep: per element the same
+// operations in the same order (kern_lin.c: S *= decay, kv = S.k, delta, S += k delta, o = S.q).
+constexpr int kDnBlk = 16;
+
+template <int KC>
+__global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1)
+    k_deltanet_rows(LinLayer L, LinDims d, const float *y, int n, Act out) {
+    constexpr int S = KC - 1;
+    constexpr int NR = kDnBlk;
+    constexpr int NT = (NR + kDnParts - 1) / kDnParts;   // output rows per warp per block
+    const int h = blockIdx.x / kDnCl, c = (int)cluster_rank();
+    const int j = threadIdx.x, w = j >> 5, lane = j & 31;
+    const int col = c * kDnCols + lane;
+    const int i0 = w * kDnPart;
+    const int C = d.C;
+    // conv taps and states, the state elements: written only by this layer's DeltaNet, which
+    // ran before this kernel's predecessor, so requested before pdl_wait
+    ConvCh<KC> cq, ck, cv;
+    conv_load(cq, L, C, h * kDK + j);
+    conv_load(ck, L, C, d.kd + h * kDK + j);
+    if (w == 0) conv_load(cv, L, C, 2 * d.kd + h * kDV + col);
+    float *rec = L.rec + (size_t)h * kDK * kDV + col;
+    float Sr[kDnPart];
+#pragma unroll
+    for (int r = 0; r < kDnPart; r++) Sr[r] = ld_early(rec + (size_t)(i0 + r) * kDV);
+    const float nw = L.norm_w[col];
+    pdl_wait();
+    pdl_trigger();
+    __shared__ __align__(16) float sq[NR][kDK], sk[NR][kDK];
+    __shared__ __align__(16) float sv[NR][kDnCols];
+    __shared__ __align__(16) float so[NR][kDV];
+    __shared__ float sbeta[NR], sdec[NR], srn[NR];
+    __shared__ float sdelta[kDnCols], xo[kDnParts][kDnCols], xk_[kDnParts][kDnCols];
+    const bool own_qk = w == c;
+    const int tg = j - (kDK - NR);   // this thread's gate row within a block
+    const int nbo = out.cols >> 5, gcol = h * kDV + col;
+    for (int b0 = 0; b0 < n; b0 += NR) {
+        const int nb = n - b0 < NR ? n - b0 : NR;
+        const float *yb = y + (size_t)b0 * d.ldy;
+        float xq[NR], xk[NR], xv[NR], zt[NT];
+#pragma unroll
+        for (int t = 0; t < NR; t++) {
+            xq[t] = xk[t] = xv[t] = 0.0f;
+            if (t < nb) {
+                const float *yr = yb + (size_t)t * d.ldy;
+                xq[t] = ld_early(yr + h * kDK + j);
+                xk[t] = ld_early(yr + d.kd + h * kDK + j);
+                if (w == 0) xv[t] = ld_early(yr + 2 * d.kd + h * kDV + col);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < NT; q++) {
+            const int t = w + q * kDnParts;
+            zt[q] = t < nb ? ld_early(yb + (size_t)t * d.ldy + C + h * kDV + col) : 0.0f;
+        }
+        if (tg >= 0 && tg < nb) {   // gates of row tg
+            const float *yr = yb + (size_t)tg * d.ldy;
+            const float gb = yr[C + d.vd + h], ga = yr[C + d.vd + d.nv + h];
+            sbeta[tg] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-gb)));
+            const float xs = __fadd_rn(ga, L.dt_bias[h]);
+            const float sp = xs > 20.0f ? xs : glibc_log1pf(glibc_expf(xs));
+            sdec[tg] = glibc_expf(__fmul_rn(L.A[h], sp));
+        }
+        // ---- conv + SiLU (q / k channel j; v channel col on warp 0)
+#pragma unroll
+        for (int t = 0; t < NR; t++) {
+            if (t < nb) {
+                sq[t][j] = conv_step(cq, xq[t]);
+                sk[t][j] = conv_step(ck, xk[t]);
+                if (w == 0) sv[t][lane] = conv_step(cv, xv[t]);
+            }
+        }
+        __syncthreads();
+        // ---- L2 norm of q and k: 4 lanes per (token, vector)
+        {
+            const float qscale = inv_sqrt_ref((float)kDK);
+            for (int u0 = w * 8; u0 < 2 * nb; u0 += kDnParts * 8) {
+                const int u = u0 + (lane >> 2), l = lane & 3;
+                const bool act = u < 2 * nb;
+                float *vec = act ? ((u & 1) ? sk[u >> 1] : sq[u >> 1]) : sq[0];
+                float cs = 0.0f;
+                if (act) {
+#pragma unroll 32
+                    for (int i = l; i < kDK; i += 4) cs = madd(cs, vec[i], vec[i]);
+                }
+                const int base = lane & ~3;
+                const float c0 = __shfl_sync(0xffffffffu, cs, base), c1 = __shfl_sync(0xffffffffu, cs, base + 1);
+                const float c2 = __shfl_sync(0xffffffffu, cs, base + 2), c3 = __shfl_sync(0xffffffffu, cs, base + 3);
+                const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+                const float r = inv_sqrt_ref(__fadd_rn(ss, 1e-6f));
+                __syncwarp();
+                if (act) {
+                    const float sc = (u & 1) ? 1.0f : qscale;
+                    for (int i = l; i < kDK; i += 4) vec[i] = __fmul_rn(__fmul_rn(vec[i], r), sc);
+                }
+            }
+        }
+        __syncthreads();
+        // ---- recurrence (named barriers as in k_deltanet3): the block's first decay and kv
+        float pk[kDnPart];
+        {
+            const float dec = sdec[0];
+            const float *k0 = sk[0] + i0;
+#pragma unroll
+            for (int r = 0; r < kDnPart; r++) {
+                Sr[r] = __fmul_rn(Sr[r], dec);
+                pk[r] = __fmul_rn(Sr[r], k0[r]);
+            }
+            float kv = 0.0f;
+            if (w > 0) {
+                bar_sync_n(1 + w, 64);
+                kv = xk_[w][lane];
+            }
+#pragma unroll
+            for (int r = 0; r < kDnPart; r++) kv = __fadd_rn(kv, pk[r]);
+            if (w < kDnParts - 1) {
+                xk_[w + 1][lane] = kv;
+                bar_arrive_n(2 + w, 64);
+            } else {
+                sdelta[lane] = __fmul_rn(__fadd_rn(sv[0][lane], -kv), sbeta[0]);
+            }
+        }
+        const bool last_block = b0 + nb == n;
+        for (int t = 0; t < nb; t++) {
+            bar_sync_n(1, kDnParts * 32);   // delta of token t
+            const float delta = sdelta[lane];
+            const bool next = t + 1 < nb;
+            const float decn = next ? sdec[t + 1] : 0.0f;
+            const float *kt = sk[t] + i0, *qt = sq[t] + i0, *kn = sk[next ? t + 1 : t] + i0;
+            const bool store_rec = !next && last_block;
+            float po[kDnPart];
+#pragma unroll
+            for (int r = 0; r < kDnPart; r++) {
+                float sv_ = __fadd_rn(Sr[r], __fmul_rn(kt[r], delta));
+                po[r] = __fmul_rn(sv_, qt[r]);
+                if (store_rec) rec[(size_t)(i0 + r) * kDV] = sv_;
+                if (next) {
+                    sv_ = __fmul_rn(sv_, decn);
+                    pk[r] = __fmul_rn(sv_, kn[r]);
+                }
+                Sr[r] = sv_;
+            }
+            float o = 0.0f, kvn = 0.0f;
+            if (w > 0) {
+                bar_sync_n(1 + w, 64);
+                o = xo[w][lane];
+                kvn = xk_[w][lane];
+            }
+            if (next) {
+#pragma unroll
+                for (int r = 0; r < kDnPart; r++) {
+                    o = __fadd_rn(o, po[r]);
+                    kvn = __fadd_rn(kvn, pk[r]);
+                }
+            } else {
+#pragma unroll
+                for (int r = 0; r < kDnPart; r++) o = __fadd_rn(o, po[r]);
+            }
+            if (w < kDnParts - 1) {
+                xo[w + 1][lane] = o;
+                xk_[w + 1][lane] = kvn;
+                bar_arrive_n(2 + w, 64);
+            } else {
+                if (next) sdelta[lane] = __fmul_rn(__fadd_rn(sv[t + 1][lane], -kvn), sbeta[t + 1]);
+#pragma unroll
+                for (int r = 0; r < kDnCl; r++) st_dsmem(&so[t][col], (uint32_t)r, o);   // to every CTA
+            }
+        }
+        cluster_arrive();   // every CTA's output columns of the block in every CTA
+        cluster_wait();
+        // ---- gated RMSNorm over the 128 outputs, then A8 of this CTA's 32-column block
+        for (int u0 = w * 8; u0 < nb; u0 += kDnParts * 8) {
+            const int u = u0 + (lane >> 2), l = lane & 3;
+            const bool act = u < nb;
+            const float *vec = so[act ? u : 0];
+            float cs = 0.0f;
+            if (act) {
+#pragma unroll 32
+                for (int i = l; i < kDV; i += 4) cs = madd(cs, vec[i], vec[i]);
+            }
+            const int base = lane & ~3;
+            const float c0 = __shfl_sync(0xffffffffu, cs, base), c1 = __shfl_sync(0xffffffffu, cs, base + 1);
+            const float c2 = __shfl_sync(0xffffffffu, cs, base + 2), c3 = __shfl_sync(0xffffffffu, cs, base + 3);
+            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+            if (act && l == 0) srn[u] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)kDV), d.eps));
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < NT; q++) {
+            const int t = w + q * kDnParts;
+            if (t < nb) {
+                float v = __fmul_rn(__fmul_rn(so[t][col], srn[t]), nw);
+                v = __fmul_rn(v, pf_silu(zt[q]));
+                const size_t row = (size_t)(b0 + t);
+                quant_block_warp(v, lane, out.q + row * out.cols + (gcol & ~31), out.d + row * nbo + (gcol >> 5),
+                                 out.fs + row * nbo + (gcol >> 5));
+            }
+        }
+        // the block's buffers (this CTA's, and the output rows its peers write) are free again
+        cluster_arrive();
+        cluster_wait();
+    }
+    const float none[S > 0 ? S : 1] = {};
+    if (own_qk) {
+        conv_store(cq, L, C, none, 0);
+        conv_store(ck, L, C, none, 0);
+    }
+    if (w == 0) conv_store(cv, L, C, none, 0);
+}
+
 
 // ------------------------------------------------------------------ MTP draft head
 // The Qwen3.5 MTP head (engine/src/mtp.c:60-100, semantics engine/src/mtp.h): row t at position
@@ -3966,6 +4184,9 @@ void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
     const size_t sm = deltanet_smem(d.rep);
     launch_k(k_deltanet, d.nk, kDV, sm, s, L, d, y, st, out);
 }
+void launch_deltanet_rows(const LinLayer &L, const LinDims &d, const float *y, int n, Act out, cudaStream_t s) {
+    launch_k(k_deltanet_rows<4>, dim3(d.nk * kDnCl, 1), kDnParts * 32, 0, s, L, d, y, n, out);
+}
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
                       const Step *st, cudaStream_t s, int nseq) {
     launch_k(k_attn_prep, dim3(d.rps * nseq, d.nq + d.nkv), d.hd, (size_t)d.hd * sizeof(float), s, L, d, y, qbuf, st);
@@ -4090,6 +4311,7 @@ int kernels_init(int max_ctx, int hd, int rep) {
     max_carveout(k_norm_quant);
     max_carveout(k_deltanet3<4, 4, PINFER_SPEC_MAX_K>);
     max_carveout(k_deltanet3<4, kMaxRows, PINFER_SPEC_MAX_K>);
+    max_carveout(k_deltanet_rows<4>);
     // raise the dynamic shared memory limits once, outside any stream capture
     raise_smem(k_matvec<1, 0>, mv_smem<1>());
     raise_smem(k_matvec<1, 1>, mv_smem<1>());

@@ -8,7 +8,7 @@ DeltaNet layers, then gated full attention) so the scalar reference finishes in 
         group of 4), rot 64;
   2B:   H 2048, ffn 6144, the same DeltaNet, attention 16 Q / 2 KV heads (a query group of 8).
 Weights are the configured random init (std 0.02, norms 1). Each preset fills a context of
-`CTX` uniform-random tokens, then checks the logits of every row of the context's last 40
+`CTX` uniform-random tokens, then checks the logits of every row of the context's last 130
 positions, the state blob after the context, plain greedy tokens continuing it, and synthetic
 k = 3 speculation continuing it (tokens, and rounds / drafted / accepted equal to the
 reference's own verify / accept / commit loop, engine/src/spec.c:323-351)."""
@@ -21,7 +21,7 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not ref_available(), reason="oracle/_ref not built")]
 
 CTX = {"0.8b-4l": 512, "2b-4l": 320}
-TAIL = 40          # rows of the context's end compared with the logits of every row
+TAIL = 130         # rows of the context's end compared with the logits of every row
 GEN = 32           # tokens generated after the context
 SPEC_P = {"0.8b-4l": (0.0, 0.8), "2b-4l": (0.8,)}
 
@@ -61,8 +61,9 @@ def shaped(request):
 
 
 def test_context_logits_every_row_bit_exact(shaped):
-    """The last-token logits after the first part of the context, then the logits of every row
-    of its last 40 positions (chunks of 16, 16 and 8 rows on the device), over all 248,320
+    """The last-token logits after the first part of the context (tensor-core prefill chunks of
+    64 rows, then one 16-row pass with the head), then the logits of every row of its last 130
+    positions (prefill chunks of 64, 64 and 2 rows with the head's logits), over all 248,320
     vocabulary rows."""
     s = shaped
     assert np.array_equal(bits(s["dlast"]), bits(s["rlast"])), f"{s['name']}: prefill logits differ"

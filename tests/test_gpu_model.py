@@ -33,15 +33,34 @@ def bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
 
 
-def test_logits_all_rows_bit_exact(pair):
+@pytest.mark.parametrize("n", [40, 64, 130])
+def test_logits_all_rows_bit_exact(pair, n):
+    """The logits of every row of a prompt. `small` runs it as tensor-core prefill chunks of up
+    to 64 rows (40: one chunk of three 16-row sub-passes; 130: 64 + 64 + 2), `tiny` (a DeltaNet
+    shape without the chunk kernels) as 16-row CUDA-core passes."""
     name, dev, ref = pair
-    toks = prompt(dev.n_vocab, 40, 1)            # 40 rows: chunks of 16, 16, 8 on the device
+    toks = prompt(dev.n_vocab, n, 1)
     dev.reset()
     ref.reset()
     got = dev.forward_all(toks)
     want = ref.forward_all(toks)
     bad = np.nonzero((bits(got) != bits(want)).any(axis=1))[0]
     assert len(bad) == 0, f"{name}: rows {bad[:8]} differ; max |d| {np.abs(got - want).max()}"
+
+
+@pytest.mark.parametrize("lens", [(64,), (130, 70), (17, 200)])
+def test_long_prompts_continue_exactly(pair, lens):
+    """Evals of long prompts in a row: the rows before the last pass go through the prefill
+    chunks (positions continuing across chunks and calls), the last-token logits and the whole
+    state blob after each equal the reference's."""
+    name, dev, ref = pair
+    dev.reset()
+    ref.reset()
+    for i, n in enumerate(lens):
+        toks = prompt(dev.n_vocab, n, 40 + i)
+        assert np.array_equal(bits(dev.eval(toks)), bits(ref.eval(toks))), f"{name}: eval {i} ({n} rows)"
+        assert dev.save_state() == ref.save_state(), f"{name}: state after eval {i} ({n} rows)"
+    assert dev.n_past == sum(lens)
 
 
 def test_eval_continues_exactly(pair):
