@@ -535,6 +535,24 @@ def run_profile_matvec(rows: int, cols: int, n: int) -> None:
     assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32)), "matvec != oracle"
 
 
+def run_profile_prefill(preset: str, ntok: int) -> None:
+    """One untimed pinfer_eval of ntok uniform-random tokens on the bench model of `preset`,
+    then the same prefill inside cudaProfilerStart/Stop (for ncu --profile-from-start off)."""
+    import torch
+    from nibblemac_b200.model import Model
+    path = model_path(0, None, preset)
+    m = Model(path, max_ctx=ntok + 16)
+    toks = np.random.default_rng(4321).integers(0, m.n_vocab, ntok).astype(np.int32)
+    m.eval(toks, logits=False)
+    m.reset()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    m.eval(toks, logits=False)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    m.close()
+
+
 def run_profile_batch(nseq: int, ntok: int) -> None:
     """Config-4 style batch generation for ncu: plain and warm-up runs, then one k = 3 run
     inside cudaProfilerStart/Stop."""
@@ -738,7 +756,13 @@ def main() -> None:
                     help="config-4 prompts (bench seed) for SEQS sequences: one plain and one warm-up "
                          "batch generation of TOKENS tokens at k = 3, then one inside "
                          "cudaProfilerStart/Stop")
+    ap.add_argument("--profile-prefill", nargs=2, default=None, metavar=("PRESET", "TOKENS"),
+                    help="one untimed prefill of TOKENS tokens on the PRESET bench model (0.8b, 2b), "
+                         "then one inside cudaProfilerStart/Stop")
     args = ap.parse_args()
+    if args.profile_prefill:
+        run_profile_prefill(args.profile_prefill[0], int(args.profile_prefill[1]))
+        return
     if args.profile_gemm:
         run_profile_gemm(args.profile_gemm)
         return

@@ -246,7 +246,7 @@ void launch_quant_act(const float *x, int n, int cols, Act out, cudaStream_t s);
 // ---- tensor-core GEMM for passes of many rows (nb_gemm.cu) --------------------------------
 // TMA descriptors of an A8 activation buffer of `rows` rows (codes, block scales, block sums).
 struct GemmMaps {
-    CUtensorMap q, d, fs;
+    CUtensorMap q[3], d[3], fs[3];   // boxes of 16, 32 and 64 rows (the GEMM's activation tile heights)
     int rows = 0, cols = 0;
 };
 // A matrix (or the row concatenation of two) in the tensor-core tile image: per tile of 128

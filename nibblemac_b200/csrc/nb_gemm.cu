@@ -19,16 +19,18 @@
 // the 4 panels' scale entries (2 KB). One bulk copy per stage brings it in; nothing is unpacked
 // on the hot path. (The CUDA-core matvec kernels keep reading the packed panels.)
 //
-// Persistent CTAs, one per SM, walk tiles of 128 weight rows x 64 activation rows (activation
-// tiles fastest, so concurrent CTAs share weight tiles in L2):
+// Persistent CTAs, one per SM, walk tiles of 128 weight rows x N activation rows (activation
+// tiles fastest, so concurrent CTAs share weight tiles in L2). N is 64, or 32 / 16 when a pass
+// has too few tiles of 64 rows to occupy half the SMs (a 64-row prefill chunk through a 1024-row
+// projection has 8): each CTA then runs a quarter of the chains, which bound it.
 //   warp 16      producer: per stage (one superblock of one tile) the tile-image chunk by bulk
 //                copy, the A8 codes (two 128-column boxes, 128-byte swizzle) and the block
 //                scales d / fsum by TMA tensor copies, into a ring of 3 stages.
 //   warp 17      TMEM owner and MMA issuer: pairs (d, fsum) per block for the chains, then 8 MMAs
-//                (M 128, N 64, K 32) per stage into a ring of 8 TMEM slots of 64 columns, each
+//                (M 128, N, K 32) per stage into a ring of 8 TMEM slots of N columns, each
 //                completion signalled by tcgen05.commit.
 //   warps 0..15  the chains: warp w reads TMEM lanes 32 (w % 4) .. (its 32 weight rows) and
-//                activation rows 16 (w / 4) .. of the tile, frees a TMEM slot as soon as its
+//                activation rows (N / 4) (w / 4) .. of the tile, frees a TMEM slot as soon as its
 //                dots are in registers, and writes the tile's outputs after the last stage.
 // Every wait is bounded: a timeout sets the status word, lets the copies and MMAs in flight
 // finish, frees TMEM and returns.
@@ -46,37 +48,43 @@ namespace nb {
 namespace {
 
 constexpr int kGmM = 128;            // weight rows per tile (4 panels = TMEM lanes)
-constexpr int kGmN = 64;             // activation rows per tile
-constexpr int kGmSlots = 8;          // TMEM ring: one slot of kGmN columns per block
+constexpr int kGmSlots = 8;          // TMEM ring: one slot of N columns per block
 constexpr int kGmStages = 3;         // shared-memory ring
-constexpr int kGmEpiWarps = 16;      // 4 warpgroups; warpgroup g takes activation rows 16 g ..
+constexpr int kGmEpiWarps = 16;      // 4 warpgroups; warpgroup g takes activation rows g N / 4 ..
 constexpr int kGmWg = kGmEpiWarps / 4;
-constexpr int kGmTpt = kGmN / kGmWg;  // activation rows per epilogue thread
 constexpr int kGmProducer = kGmEpiWarps, kGmMma = kGmEpiWarps + 1;
 constexpr int kGmThreads = (kGmEpiWarps + 2) * 32;
-constexpr uint32_t kGmTmemCols = kGmSlots * kGmN;   // 512: the whole TMEM of the SM
-
-// one stage of shared memory (1024-byte aligned: the swizzled operand tiles need it)
 constexpr uint32_t kGmACodes = 2 * kGmM * 128;                 // int8 codes [2 halves][128 rows][128 B]
 constexpr uint32_t kGmTileBytes = kGmACodes + 4 * 512;         // + 4 panels' scale entries
-constexpr uint32_t kGmBStage = 2 * kGmN * 128;                 // A8 codes [2 halves][64 rows][128 B]
-constexpr uint32_t kGmQStage = kGmN * 8 * 4;                   // d or fsum [64 rows][8 blocks] fp32
-constexpr uint32_t kGmDfStage = 8 * kGmN * 2 * 4;              // [8 blocks][32] (d_t, d_t+1, fs_t, fs_t+1)
-constexpr uint32_t kGmOffB = kGmTileBytes;
-constexpr uint32_t kGmOffDq = kGmOffB + kGmBStage;
-constexpr uint32_t kGmOffFq = kGmOffDq + kGmQStage;
-constexpr uint32_t kGmOffDf = kGmOffFq + kGmQStage;
-constexpr uint32_t kGmStageBytes = kGmOffDf + kGmDfStage;
-constexpr uint32_t kGmBar = kGmStages * kGmStageBytes;
-constexpr uint32_t kGmMisc = kGmBar + 32 * 8;
-constexpr uint32_t kGmSmem = kGmMisc + 64 + 1024;              // + alignment slack
-static_assert(kGmSmem <= 227 * 1024, "shared memory of one CTA");
-static_assert(kGmStageBytes % 1024 == 0 && kGmOffB % 1024 == 0 && kGmACodes % 2048 == 0, "swizzle atoms");
 
-// instruction descriptor of tcgen05.mma kind::i8: D s32 (bits 4-5 = 2), A and B s8 (bits 7-9,
-// 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
-constexpr uint32_t kGmIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGmN >> 3) << 17) |
-                              ((uint32_t)(kGmM >> 4) << 24);
+// The activation tile height N (16, 32 or 64 rows) sets everything else: a pass with few weight
+// tiles takes a smaller N so that more CTAs share the work (the FMA chains, one per weight row
+// and activation row, are what bounds a CTA).
+template <int N>
+struct GmCfg {
+    static_assert(N == 16 || N == 32 || N == 64, "activation tile height");
+    static constexpr int kTpt = N / kGmWg;                            // activation rows per epilogue thread
+    static constexpr uint32_t kTmemCols = kGmSlots * N;              // a power of two >= 32
+    // one stage of shared memory (1024-byte aligned: the swizzled operand tiles need it)
+    static constexpr uint32_t kBStage = 2 * N * 128;                 // A8 codes [2 halves][N rows][128 B]
+    static constexpr uint32_t kQStage = N * 8 * 4;                   // d or fsum [N rows][8 blocks] fp32
+    static constexpr uint32_t kDfStage = 8 * N * 2 * 4;              // [8 blocks][N / 2] (d_t, d_t+1, fs_t, fs_t+1)
+    static constexpr uint32_t kOffB = kGmTileBytes;
+    static constexpr uint32_t kOffDq = kOffB + kBStage;
+    static constexpr uint32_t kOffFq = kOffDq + kQStage;
+    static constexpr uint32_t kOffDf = kOffFq + kQStage;
+    static constexpr uint32_t kStageBytes = kOffDf + kDfStage;
+    static constexpr uint32_t kBar = kGmStages * kStageBytes;
+    static constexpr uint32_t kMisc = kBar + 32 * 8;
+    static constexpr uint32_t kSmem = kMisc + 64 + 1024;              // + alignment slack
+    static_assert(kSmem <= 227 * 1024, "shared memory of one CTA");
+    static_assert(kStageBytes % 1024 == 0 && kOffB % 1024 == 0 && kGmACodes % 2048 == 0, "swizzle atoms");
+    // instruction descriptor of tcgen05.mma kind::i8: D s32 (bits 4-5 = 2), A and B s8 (bits 7-9,
+    // 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
+    static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+                                       ((uint32_t)(kGmM >> 4) << 24);
+};
+constexpr int gm_index(int N) { return N == 16 ? 0 : N == 32 ? 1 : 2; }
 
 // shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart
 // (start >> 4 in bits 0-13, leading offset 16 B, stride offset 1024 B at bit 32, version 1 at
@@ -132,10 +140,22 @@ __device__ __forceinline__ void tm_ld16(uint32_t taddr, uint32_t (&r)[16]) {
                    "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
                  : "r"(taddr));
 }
+__device__ __forceinline__ void tm_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tm_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+}
 template <int N>
 __device__ __forceinline__ void tm_ld(uint32_t taddr, uint32_t (&r)[N]) {
     if constexpr (N == 32) tm_ld32(taddr, r);
-    else tm_ld16(taddr, r);
+    else if constexpr (N == 16) tm_ld16(taddr, r);
+    else if constexpr (N == 8) tm_ld8(taddr, r);
+    else tm_ld4(taddr, r);
 }
 // (float)v for |v| < 2^22, exactly, without the conversion unit: the bits of 1.5 * 2^23 + v
 // read as a float are 12582912 + v, and subtracting 12582912 is exact
@@ -195,23 +215,24 @@ __global__ void k_swiglu_quant(const float *y, int ldy, int ffn, int n, Act out)
 
 // EPI 0: y[v][row] = acc; 1: y[v][row] += acc (the residual stream); 4: LM head, logits into y
 // (may be null) and per-panel argmax keys.
-template <int EPI>
+template <int EPI, int N>
 __global__ void __launch_bounds__(kGmThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap td,
            const __grid_constant__ CUtensorMap tf, GemmArgs g) {
+    using Cfg = GmCfg<N>;
     extern __shared__ uint8_t gsm_raw[];
     const uint32_t raw_u = smem_u32(gsm_raw);
     const uint32_t sbase = (raw_u + 1023u) & ~1023u;
     uint8_t *sm = gsm_raw + (sbase - raw_u);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kGmBar);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + Cfg::kBar);
     uint64_t *full = bars, *ready = bars + 3, *sfree = bars + 6, *estage = bars + 9;
     uint64_t *mdone = bars + 12, *edone = bars + 20, *drain = bars + 28;
-    uint32_t *tmem_at = reinterpret_cast<uint32_t *>(sm + kGmMisc);
-    volatile int *abort_f = reinterpret_cast<volatile int *>(sm + kGmMisc + 4);
+    uint32_t *tmem_at = reinterpret_cast<uint32_t *>(sm + Cfg::kMisc);
+    volatile int *abort_f = reinterpret_cast<volatile int *>(sm + Cfg::kMisc + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = g.n, nsb = g.W.nsb;
-    const int ntn = (n + kGmN - 1) / kGmN, ntiles = g.W.mtiles * ntn;
+    const int ntn = (n + N - 1) / N, ntiles = g.W.mtiles * ntn;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kGmStages; i++) {
@@ -228,7 +249,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
         *abort_f = 0;
         fence_mbar_init();
     }
-    if (warp == kGmMma) tm_alloc(tmem_at, kGmTmemCols);
+    if (warp == kGmMma) tm_alloc(tmem_at, Cfg::kTmemCols);
     tm_fence_before();
     __syncthreads();
     tm_fence_after();
@@ -240,7 +261,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
         int gs = 0;   // stages issued by this CTA
         bool ok = true;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-            const int mt = tile / ntn, n0 = (tile % ntn) * kGmN;
+            const int mt = tile / ntn, n0 = (tile % ntn) * N;
             const uint8_t *wt = g.W.t + (size_t)mt * nsb * kGmTileBytes;
             for (int s = 0; s < nsb; s++, gs++) {
                 const int slot = gs % kGmStages;
@@ -251,13 +272,13 @@ __global__ void __launch_bounds__(kGmThreads, 1)
                     break;
                 }
                 if (lane == 0) {
-                    uint8_t *st = sm + slot * kGmStageBytes;
-                    mbar_arrive_expect(&full[slot], kGmTileBytes + kGmBStage + 2 * kGmQStage);
+                    uint8_t *st = sm + slot * Cfg::kStageBytes;
+                    mbar_arrive_expect(&full[slot], kGmTileBytes + Cfg::kBStage + 2 * Cfg::kQStage);
                     bulk_g2s(st, wt + (size_t)s * kGmTileBytes, kGmTileBytes, &full[slot]);
-                    tma_load_2d(st + kGmOffB, &tq, s * 256, n0, &full[slot]);
-                    tma_load_2d(st + kGmOffB + kGmN * 128, &tq, s * 256 + 128, n0, &full[slot]);
-                    tma_load_2d(st + kGmOffDq, &td, s * 8, n0, &full[slot]);
-                    tma_load_2d(st + kGmOffFq, &tf, s * 8, n0, &full[slot]);
+                    tma_load_2d(st + Cfg::kOffB, &tq, s * 256, n0, &full[slot]);
+                    tma_load_2d(st + Cfg::kOffB + N * 128, &tq, s * 256 + 128, n0, &full[slot]);
+                    tma_load_2d(st + Cfg::kOffDq, &td, s * 8, n0, &full[slot]);
+                    tma_load_2d(st + Cfg::kOffFq, &tf, s * 8, n0, &full[slot]);
                 }
                 __syncwarp();
             }
@@ -278,13 +299,13 @@ __global__ void __launch_bounds__(kGmThreads, 1)
                     ok = false;
                     break;
                 }
-                uint8_t *st = sm + slot * kGmStageBytes;
+                uint8_t *st = sm + slot * Cfg::kStageBytes;
                 // (d_t, d_t+1, fsum_t, fsum_t+1) per block and activation-row pair for the chains
-                const float *dq = reinterpret_cast<const float *>(st + kGmOffDq);
-                const float *fq = reinterpret_cast<const float *>(st + kGmOffFq);
-                float4 *df = reinterpret_cast<float4 *>(st + kGmOffDf);
-                for (int idx = lane; idx < 8 * kGmN / 2; idx += 32) {
-                    const int k = idx / (kGmN / 2), t = (idx % (kGmN / 2)) * 2;
+                const float *dq = reinterpret_cast<const float *>(st + Cfg::kOffDq);
+                const float *fq = reinterpret_cast<const float *>(st + Cfg::kOffFq);
+                float4 *df = reinterpret_cast<float4 *>(st + Cfg::kOffDf);
+                for (int idx = lane; idx < 8 * N / 2; idx += 32) {
+                    const int k = idx / (N / 2), t = (idx % (N / 2)) * 2;
                     df[idx] = make_float4(dq[t * 8 + k], dq[(t + 1) * 8 + k], fq[t * 8 + k], fq[(t + 1) * 8 + k]);
                 }
                 mbar_arrive(&ready[slot]);
@@ -296,9 +317,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
                     }
                     tm_fence_after();
                     if (lane == 0) {
-                        const uint32_t a = sbase + slot * kGmStageBytes + (k >> 2) * (kGmM * 128) + (k & 3) * 32;
-                        const uint32_t b = sbase + slot * kGmStageBytes + kGmOffB + (k >> 2) * (kGmN * 128) + (k & 3) * 32;
-                        tm_mma_i8(tmem + k * kGmN, sw128_desc(a), sw128_desc(b), kGmIdesc, 0u);
+                        const uint32_t a = sbase + slot * Cfg::kStageBytes + (k >> 2) * (kGmM * 128) + (k & 3) * 32;
+                        const uint32_t b = sbase + slot * Cfg::kStageBytes + Cfg::kOffB + (k >> 2) * (N * 128) + (k & 3) * 32;
+                        tm_mma_i8(tmem + k * N, sw128_desc(a), sw128_desc(b), Cfg::kIdesc, 0u);
                         tm_commit(&mdone[k]);
                         if (k == 7) tm_commit(&sfree[slot]);
                     }
@@ -313,15 +334,15 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     } else {
         const int q = warp & 3, wg = warp >> 2;
         const float2 magic = make_float2(-12582912.0f, -12582912.0f);
-        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(wg * kGmTpt);
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(wg * Cfg::kTpt);
         int gs = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-            const int mt = tile / ntn, n0 = (tile % ntn) * kGmN;
+            const int mt = tile / ntn, n0 = (tile % ntn) * N;
             // two activation rows per packed f32x2 chain: acc[j] = rows (2 j, 2 j + 1) of this thread
-            float2 acc[kGmTpt / 2];
+            float2 acc[Cfg::kTpt / 2];
 #pragma unroll
-            for (int j = 0; j < kGmTpt / 2; j++) acc[j] = make_float2(0.0f, 0.0f);
+            for (int j = 0; j < Cfg::kTpt / 2; j++) acc[j] = make_float2(0.0f, 0.0f);
             for (int s = 0; s < nsb; s++, gs++) {
                 const int slot = gs % kGmStages;
                 if (__any_sync(0xffffffffu, *abort_f) || !wait_all(&ready[slot], (uint32_t)(gs / kGmStages) & 1u)) {
@@ -329,13 +350,13 @@ __global__ void __launch_bounds__(kGmThreads, 1)
                     ok = false;
                     break;
                 }
-                const uint8_t *st = sm + slot * kGmStageBytes;
+                const uint8_t *st = sm + slot * Cfg::kStageBytes;
                 const uint4 sc = lds128(st + kGmACodes + q * 512 + lane * 16);
                 const unsigned long long A = (unsigned long long)sc.x | ((unsigned long long)sc.y << 32);
                 const unsigned long long B = (unsigned long long)sc.z | ((unsigned long long)sc.w << 32);
                 const float D = half_bits_to_float((uint32_t)(A >> 48));
                 const float M = half_bits_to_float((uint32_t)(B >> 48));
-                const float4 *dfw = reinterpret_cast<const float4 *>(st + kGmOffDf) + wg * (kGmTpt / 2);
+                const float4 *dfw = reinterpret_cast<const float4 *>(st + Cfg::kOffDf) + wg * (Cfg::kTpt / 2);
 #pragma unroll 1
                 for (int k = 0; k < 8; k++) {
                     const float ds = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
@@ -346,17 +367,17 @@ __global__ void __launch_bounds__(kGmThreads, 1)
                         break;
                     }
                     tm_fence_after();
-                    uint32_t is[kGmTpt];
-                    tm_ld(trow + (uint32_t)(k * kGmN), is);
+                    uint32_t is[Cfg::kTpt];
+                    tm_ld(trow + (uint32_t)(k * N), is);
                     tm_wait_ld();
                     tm_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&edone[k]);
-                    const float4 *dk = dfw + k * (kGmN / 2);
+                    const float4 *dk = dfw + k * (N / 2);
                     // per row: acc = fmaf((float)isum, ds * d, acc); acc = fmaf(-os, fsum, acc),
                     // two rows per packed instruction (each lane of f32x2 rounds as the scalar op)
 #pragma unroll
-                    for (int j = 0; j < kGmTpt / 2; j++) {
+                    for (int j = 0; j < Cfg::kTpt / 2; j++) {
                         const float4 p = dk[j];   // d_2j, d_2j+1, fsum_2j, fsum_2j+1
                         const float2 f = __fadd2_rn(make_float2(int_bits_plus_magic(is[2 * j]),
                                                                 int_bits_plus_magic(is[2 * j + 1])), magic);
@@ -373,10 +394,10 @@ __global__ void __launch_bounds__(kGmThreads, 1)
             }
             if (!ok) break;
             // the tile's outputs (stores of consecutive weight rows by consecutive lanes)
-            const int vb = n0 + wg * kGmTpt, row = mt * kGmM + q * 32 + lane;
+            const int vb = n0 + wg * Cfg::kTpt, row = mt * kGmM + q * 32 + lane;
             const bool valid = row < g.W.rows;
 #pragma unroll
-            for (int i = 0; i < kGmTpt; i++) {
+            for (int i = 0; i < Cfg::kTpt; i++) {
                 const int v = vb + i;
                 const float a = (i & 1) ? acc[i >> 1].y : acc[i >> 1].x;
                 if (v < n) {
@@ -400,7 +421,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     __syncthreads();
     if (warp == kGmMma) {
         tm_fence_after();
-        tm_dealloc(tmem, kGmTmemCols);
+        tm_dealloc(tmem, Cfg::kTmemCols);
     }
     if (threadIdx.x == 0 && *abort_f && g.status) *g.status = -91;   // a device wait timed out
 }
@@ -430,11 +451,22 @@ int sm_count() {
     return n;
 }
 
+template <int EPI, int N>
+void gemm_n(const GemmMaps &maps, const GemmArgs &g, cudaStream_t s) {
+    const int ntiles = g.W.mtiles * ((g.n + N - 1) / N);
+    const int grid = ntiles < sm_count() ? ntiles : sm_count();
+    const int i = gm_index(N);
+    launch_k(k_gemm<EPI, N>, dim3((unsigned)grid), dim3(kGmThreads), (size_t)GmCfg<N>::kSmem, s, maps.q[i], maps.d[i],
+             maps.fs[i], g);
+}
+
+// The tallest activation tile that still gives at least half the SMs a tile, else 16 rows.
 template <int EPI>
 void gemm_t(const GemmMaps &maps, const GemmArgs &g, cudaStream_t s) {
-    const int ntiles = g.W.mtiles * ((g.n + kGmN - 1) / kGmN);
-    const int grid = ntiles < sm_count() ? ntiles : sm_count();
-    launch_k(k_gemm<EPI>, dim3((unsigned)grid), dim3(kGmThreads), (size_t)kGmSmem, s, maps.q, maps.d, maps.fs, g);
+    const int half = sm_count() / 2;
+    if (g.W.mtiles * ((g.n + 63) / 64) >= half) gemm_n<EPI, 64>(maps, g, s);
+    else if (g.W.mtiles * ((g.n + 31) / 32) >= half) gemm_n<EPI, 32>(maps, g, s);
+    else gemm_n<EPI, 16>(maps, g, s);
 }
 
 }  // namespace
@@ -452,39 +484,43 @@ int gemm_maps(const Act &a, int nrows, GemmMaps *m) {
     const int nb = a.cols / 32;
     cuuint64_t qdim[2] = {(cuuint64_t)a.cols, (cuuint64_t)nrows};
     cuuint64_t qstr[1] = {(cuuint64_t)a.cols};
-    cuuint32_t qbox[2] = {128, (cuuint32_t)kGmN};
     cuuint64_t ddim[2] = {(cuuint64_t)nb, (cuuint64_t)nrows};
     cuuint64_t dstr[1] = {(cuuint64_t)nb * 4};
-    cuuint32_t dbox[2] = {8, (cuuint32_t)kGmN};
     cuuint32_t one[2] = {1, 1};
-    CUresult r0 = enc(&m->q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.q, qdim, qstr, qbox, one,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    CUresult r1 = enc(&m->d, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.d, ddim, dstr, dbox, one,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    CUresult r2 = enc(&m->fs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.fs, ddim, dstr, dbox, one,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r0 != CUDA_SUCCESS || r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) {
-        char b[160];
-        snprintf(b, sizeof b, "cuTensorMapEncodeTiled failed (%d %d %d)", (int)r0, (int)r1, (int)r2);
-        set_last_error(b);
-        return -1;
+    for (int i = 0; i < 3; i++) {   // activation tile heights 16, 32, 64
+        const cuuint32_t h = 16u << i;
+        cuuint32_t qbox[2] = {128, h};
+        cuuint32_t dbox[2] = {8, h};
+        CUresult r0 = enc(&m->q[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.q, qdim, qstr, qbox, one,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        CUresult r1 = enc(&m->d[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.d, ddim, dstr, dbox, one,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        CUresult r2 = enc(&m->fs[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.fs, ddim, dstr, dbox, one,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r0 != CUDA_SUCCESS || r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) {
+            char b[160];
+            snprintf(b, sizeof b, "cuTensorMapEncodeTiled failed (%d %d %d)", (int)r0, (int)r1, (int)r2);
+            set_last_error(b);
+            return -1;
+        }
     }
     m->rows = nrows;
     m->cols = a.cols;
     return 0;
 }
 
-int gemm_init() {
-    const int s = (int)kGmSmem;
-    if (cudaFuncSetAttribute(k_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) != cudaSuccess ||
-        cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) != cudaSuccess ||
-        cudaFuncSetAttribute(k_gemm<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) != cudaSuccess)
-        return -1;
-    return 0;
+template <int N>
+bool gemm_init_n() {
+    const int s = (int)GmCfg<N>::kSmem;
+    return cudaFuncSetAttribute(k_gemm<0, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) == cudaSuccess &&
+           cudaFuncSetAttribute(k_gemm<1, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) == cudaSuccess &&
+           cudaFuncSetAttribute(k_gemm<4, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, s) == cudaSuccess;
 }
+
+int gemm_init() { return gemm_init_n<16>() && gemm_init_n<32>() && gemm_init_n<64>() ? 0 : -1; }
 
 size_t gemm_tiled_bytes(int rows, int cols) {
     const int npanels = (rows + kPanelRows - 1) / kPanelRows;

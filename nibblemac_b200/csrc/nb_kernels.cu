@@ -3269,90 +3269,83 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
 }
 
 // Gated DeltaNet layer of a prefill chunk: rows 0..n-1 of y (any n), with no deferred commit to
-// replay and nothing logged (the caller flushes a pending commit first). The layout and the
-// arithmetic are k_deltanet3's (4-CTA cluster per key head, state columns per CTA, state rows
-// per warp, the ordered kv / o chains handed warp to warp); the state stays in registers over
-// the whole chunk, which arrives in blocks of kDnBlk rows: a block's conv inputs, z columns and
-// gate inputs are loaded, convolved and normalised, its tokens run through the recurrence, its
-// outputs are normed and quantised, and a cluster barrier frees the block buffers (peers write
-// this CTA's output rows) before the next block. The decay of a block's first token is applied
-// in its own first sweep instead of inside the previous token's sweep: per element the same
-// operations in the same order (kern_lin.c: S *= decay, kv = S.k, delta, S += k delta, o = S.q).
+// replay and nothing logged (the caller flushes a pending commit first). The per-element
+// arithmetic is k_deltanet2's (same citations); the schedule suits long passes: one CTA per key
+// head, thread j owns state column j with all of its kDK rows in registers for the whole chunk,
+// so a token's update, its output dot product and the next token's kv dot product are one sweep
+// over the rows with the two ordered add chains (rows 0..kDK-1 in order, kern_lin.c) interleaved
+// and no partial sum crossing threads; the delta of the next token is the thread's own. The
+// elementwise products take two rows per packed f32x2 instruction (each lane rounds as the
+// scalar operation), except the k * delta products: ptxas contracts a packed multiply that
+// feeds a packed add into one fused multiply-add (one rounding instead of two; measured on
+// B200 with CUDA 12.9, --fmad=false and explicit .rn alike), so those stay scalar __fmul_rn.
+// Rows arrive in blocks of kDnBlk: the block's conv inputs, z rows and gates are loaded,
+// convolved and normalised, its tokens swept, its outputs normed and quantised. The decay of a
+// block's first token is applied in a sweep of its own instead of inside the previous token's:
+// per element the same operations in the same order.
 constexpr int kDnBlk = 16;
 
-template <int KC>
-__global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1)
-    k_deltanet_rows(LinLayer L, LinDims d, const float *y, int n, Act out) {
-    constexpr int S = KC - 1;
-    constexpr int NR = kDnBlk;
-    constexpr int NT = (NR + kDnParts - 1) / kDnParts;   // output rows per warp per block
-    const int h = blockIdx.x / kDnCl, c = (int)cluster_rank();
-    const int j = threadIdx.x, w = j >> 5, lane = j & 31;
-    const int col = c * kDnCols + lane;
-    const int i0 = w * kDnPart;
+__global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d, const float *y, int n, Act out) {
+    constexpr int KC = 4, S = KC - 1, NR = kDnBlk, NP = kDK / 2;
+    const int h = blockIdx.x, j = threadIdx.x, w = j >> 5, lane = j & 31;
     const int C = d.C;
-    // conv taps and states, the state elements: written only by this layer's DeltaNet, which
-    // ran before this kernel's predecessor, so requested before pdl_wait
+    // conv taps and states, the state column: written only by this layer's DeltaNet, which ran
+    // before this kernel's predecessor, so requested before pdl_wait
     ConvCh<KC> cq, ck, cv;
     conv_load(cq, L, C, h * kDK + j);
     conv_load(ck, L, C, d.kd + h * kDK + j);
-    if (w == 0) conv_load(cv, L, C, 2 * d.kd + h * kDV + col);
-    float *rec = L.rec + (size_t)h * kDK * kDV + col;
-    float Sr[kDnPart];
+    conv_load(cv, L, C, 2 * d.kd + h * kDV + j);
+    float *rec = L.rec + (size_t)h * kDK * kDV + j;
+    float2 Sc[NP];   // rows (2 m, 2 m + 1) of column j
 #pragma unroll
-    for (int r = 0; r < kDnPart; r++) Sr[r] = ld_early(rec + (size_t)(i0 + r) * kDV);
-    const float nw = L.norm_w[col];
+    for (int m = 0; m < NP; m++)
+        Sc[m] = make_float2(ld_early(rec + (size_t)(2 * m) * kDV), ld_early(rec + (size_t)(2 * m + 1) * kDV));
+    const float nw = L.norm_w[j];
     pdl_wait();
     pdl_trigger();
     __shared__ __align__(16) float sq[NR][kDK], sk[NR][kDK];
-    __shared__ __align__(16) float sv[NR][kDnCols];
-    __shared__ __align__(16) float so[NR][kDV];
+    __shared__ __align__(16) float sv[NR][kDV];   // v rows; token t's output replaces its v row
+    __shared__ __align__(16) float sz[NR][kDV];
     __shared__ float sbeta[NR], sdec[NR], srn[NR];
-    __shared__ float sdelta[kDnCols], xo[kDnParts][kDnCols], xk_[kDnParts][kDnCols];
-    const bool own_qk = w == c;
-    const int tg = j - (kDK - NR);   // this thread's gate row within a block
-    const int nbo = out.cols >> 5, gcol = h * kDV + col;
+    const int nbo = out.cols >> 5, col = h * kDV + j;
     for (int b0 = 0; b0 < n; b0 += NR) {
         const int nb = n - b0 < NR ? n - b0 : NR;
         const float *yb = y + (size_t)b0 * d.ldy;
-        float xq[NR], xk[NR], xv[NR], zt[NT];
+        float xq[NR], xk[NR], xv[NR], xz[NR];
 #pragma unroll
         for (int t = 0; t < NR; t++) {
-            xq[t] = xk[t] = xv[t] = 0.0f;
+            xq[t] = xk[t] = xv[t] = xz[t] = 0.0f;
             if (t < nb) {
                 const float *yr = yb + (size_t)t * d.ldy;
                 xq[t] = ld_early(yr + h * kDK + j);
                 xk[t] = ld_early(yr + d.kd + h * kDK + j);
-                if (w == 0) xv[t] = ld_early(yr + 2 * d.kd + h * kDV + col);
+                xv[t] = ld_early(yr + 2 * d.kd + h * kDV + j);
+                xz[t] = ld_early(yr + C + h * kDV + j);
             }
         }
-#pragma unroll
-        for (int q = 0; q < NT; q++) {
-            const int t = w + q * kDnParts;
-            zt[q] = t < nb ? ld_early(yb + (size_t)t * d.ldy + C + h * kDV + col) : 0.0f;
-        }
-        if (tg >= 0 && tg < nb) {   // gates of row tg
-            const float *yr = yb + (size_t)tg * d.ldy;
+        if (j < nb) {   // gates of row j
+            const float *yr = yb + (size_t)j * d.ldy;
             const float gb = yr[C + d.vd + h], ga = yr[C + d.vd + d.nv + h];
-            sbeta[tg] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-gb)));
+            sbeta[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-gb)));
             const float xs = __fadd_rn(ga, L.dt_bias[h]);
             const float sp = xs > 20.0f ? xs : glibc_log1pf(glibc_expf(xs));
-            sdec[tg] = glibc_expf(__fmul_rn(L.A[h], sp));
+            sdec[j] = glibc_expf(__fmul_rn(L.A[h], sp));
         }
-        // ---- conv + SiLU (q / k channel j; v channel col on warp 0)
+        // ---- conv + SiLU of this thread's three channels
 #pragma unroll
         for (int t = 0; t < NR; t++) {
             if (t < nb) {
                 sq[t][j] = conv_step(cq, xq[t]);
                 sk[t][j] = conv_step(ck, xk[t]);
-                if (w == 0) sv[t][lane] = conv_step(cv, xv[t]);
+                sv[t][j] = conv_step(cv, xv[t]);
+                sz[t][j] = xz[t];
             }
         }
         __syncthreads();
         // ---- L2 norm of q and k: 4 lanes per (token, vector)
         {
             const float qscale = inv_sqrt_ref((float)kDK);
-            for (int u0 = w * 8; u0 < 2 * nb; u0 += kDnParts * 8) {
+            for (int u0 = w * 8; u0 < 2 * nb; u0 += (kDV / 32) * 8) {
                 const int u = u0 + (lane >> 2), l = lane & 3;
                 const bool act = u < 2 * nb;
                 float *vec = act ? ((u & 1) ? sk[u >> 1] : sq[u >> 1]) : sq[0];
@@ -3374,83 +3367,68 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
             }
         }
         __syncthreads();
-        // ---- recurrence (named barriers as in k_deltanet3): the block's first decay and kv
-        float pk[kDnPart];
+        // ---- the block's first decay and kv (rows in order)
+        float kv = 0.0f;
         {
-            const float dec = sdec[0];
-            const float *k0 = sk[0] + i0;
+            const float2 dec2 = make_float2(sdec[0], sdec[0]);
+            const float4 *k4 = reinterpret_cast<const float4 *>(sk[0]);
 #pragma unroll
-            for (int r = 0; r < kDnPart; r++) {
-                Sr[r] = __fmul_rn(Sr[r], dec);
-                pk[r] = __fmul_rn(Sr[r], k0[r]);
-            }
-            float kv = 0.0f;
-            if (w > 0) {
-                bar_sync_n(1 + w, 64);
-                kv = xk_[w][lane];
-            }
-#pragma unroll
-            for (int r = 0; r < kDnPart; r++) kv = __fadd_rn(kv, pk[r]);
-            if (w < kDnParts - 1) {
-                xk_[w + 1][lane] = kv;
-                bar_arrive_n(2 + w, 64);
-            } else {
-                sdelta[lane] = __fmul_rn(__fadd_rn(sv[0][lane], -kv), sbeta[0]);
+            for (int m = 0; m < NP; m += 2) {
+                const float4 kk = k4[m / 2];
+                Sc[m] = __fmul2_rn(Sc[m], dec2);
+                Sc[m + 1] = __fmul2_rn(Sc[m + 1], dec2);
+                const float2 p0 = __fmul2_rn(Sc[m], make_float2(kk.x, kk.y));
+                const float2 p1 = __fmul2_rn(Sc[m + 1], make_float2(kk.z, kk.w));
+                kv = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(kv, p0.x), p0.y), p1.x), p1.y);
             }
         }
-        const bool last_block = b0 + nb == n;
+        // ---- tokens: S += k delta, o = S.q; then S *= decay of the next token, its kv = S.k
         for (int t = 0; t < nb; t++) {
-            bar_sync_n(1, kDnParts * 32);   // delta of token t
-            const float delta = sdelta[lane];
-            const bool next = t + 1 < nb;
-            const float decn = next ? sdec[t + 1] : 0.0f;
-            const float *kt = sk[t] + i0, *qt = sq[t] + i0, *kn = sk[next ? t + 1 : t] + i0;
-            const bool store_rec = !next && last_block;
-            float po[kDnPart];
-#pragma unroll
-            for (int r = 0; r < kDnPart; r++) {
-                float sv_ = __fadd_rn(Sr[r], __fmul_rn(kt[r], delta));
-                po[r] = __fmul_rn(sv_, qt[r]);
-                if (store_rec) rec[(size_t)(i0 + r) * kDV] = sv_;
-                if (next) {
-                    sv_ = __fmul_rn(sv_, decn);
-                    pk[r] = __fmul_rn(sv_, kn[r]);
-                }
-                Sr[r] = sv_;
-            }
+            const float delta = __fmul_rn(__fadd_rn(sv[t][j], -kv), sbeta[t]);
+            const float4 *k4 = reinterpret_cast<const float4 *>(sk[t]);
+            const float4 *q4 = reinterpret_cast<const float4 *>(sq[t]);
             float o = 0.0f, kvn = 0.0f;
-            if (w > 0) {
-                bar_sync_n(1 + w, 64);
-                o = xo[w][lane];
-                kvn = xk_[w][lane];
-            }
-            if (next) {
+            if (t + 1 < nb) {
+                const float2 dn2 = make_float2(sdec[t + 1], sdec[t + 1]);
+                const float4 *n4 = reinterpret_cast<const float4 *>(sk[t + 1]);
 #pragma unroll
-                for (int r = 0; r < kDnPart; r++) {
-                    o = __fadd_rn(o, po[r]);
-                    kvn = __fadd_rn(kvn, pk[r]);
+                for (int m = 0; m < NP; m += 2) {
+                    const float4 kk = k4[m / 2], qq = q4[m / 2], nn = n4[m / 2];
+                    float2 s0 = __fadd2_rn(Sc[m], make_float2(__fmul_rn(kk.x, delta), __fmul_rn(kk.y, delta)));
+                    float2 s1 = __fadd2_rn(Sc[m + 1], make_float2(__fmul_rn(kk.z, delta), __fmul_rn(kk.w, delta)));
+                    const float2 p0 = __fmul2_rn(s0, make_float2(qq.x, qq.y));
+                    const float2 p1 = __fmul2_rn(s1, make_float2(qq.z, qq.w));
+                    s0 = __fmul2_rn(s0, dn2);
+                    s1 = __fmul2_rn(s1, dn2);
+                    const float2 r0 = __fmul2_rn(s0, make_float2(nn.x, nn.y));
+                    const float2 r1 = __fmul2_rn(s1, make_float2(nn.z, nn.w));
+                    o = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(o, p0.x), p0.y), p1.x), p1.y);
+                    kvn = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(kvn, r0.x), r0.y), r1.x), r1.y);
+                    Sc[m] = s0;
+                    Sc[m + 1] = s1;
                 }
             } else {
 #pragma unroll
-                for (int r = 0; r < kDnPart; r++) o = __fadd_rn(o, po[r]);
+                for (int m = 0; m < NP; m += 2) {
+                    const float4 kk = k4[m / 2], qq = q4[m / 2];
+                    const float2 s0 = __fadd2_rn(Sc[m], make_float2(__fmul_rn(kk.x, delta), __fmul_rn(kk.y, delta)));
+                    const float2 s1 = __fadd2_rn(Sc[m + 1], make_float2(__fmul_rn(kk.z, delta), __fmul_rn(kk.w, delta)));
+                    const float2 p0 = __fmul2_rn(s0, make_float2(qq.x, qq.y));
+                    const float2 p1 = __fmul2_rn(s1, make_float2(qq.z, qq.w));
+                    o = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(o, p0.x), p0.y), p1.x), p1.y);
+                    Sc[m] = s0;
+                    Sc[m + 1] = s1;
+                }
             }
-            if (w < kDnParts - 1) {
-                xo[w + 1][lane] = o;
-                xk_[w + 1][lane] = kvn;
-                bar_arrive_n(2 + w, 64);
-            } else {
-                if (next) sdelta[lane] = __fmul_rn(__fadd_rn(sv[t + 1][lane], -kvn), sbeta[t + 1]);
-#pragma unroll
-                for (int r = 0; r < kDnCl; r++) st_dsmem(&so[t][col], (uint32_t)r, o);   // to every CTA
-            }
+            sv[t][j] = o;   // thread j alone reads and writes column j of the v / output rows
+            kv = kvn;
         }
-        cluster_arrive();   // every CTA's output columns of the block in every CTA
-        cluster_wait();
-        // ---- gated RMSNorm over the 128 outputs, then A8 of this CTA's 32-column block
-        for (int u0 = w * 8; u0 < nb; u0 += kDnParts * 8) {
+        __syncthreads();
+        // ---- gated RMSNorm over the head's 128 outputs, then A8 of each warp's 32-column block
+        for (int u0 = w * 8; u0 < nb; u0 += (kDV / 32) * 8) {
             const int u = u0 + (lane >> 2), l = lane & 3;
             const bool act = u < nb;
-            const float *vec = so[act ? u : 0];
+            const float *vec = sv[act ? u : 0];
             float cs = 0.0f;
             if (act) {
 #pragma unroll 32
@@ -3463,27 +3441,24 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
             if (act && l == 0) srn[u] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)kDV), d.eps));
         }
         __syncthreads();
-#pragma unroll
-        for (int q = 0; q < NT; q++) {
-            const int t = w + q * kDnParts;
-            if (t < nb) {
-                float v = __fmul_rn(__fmul_rn(so[t][col], srn[t]), nw);
-                v = __fmul_rn(v, pf_silu(zt[q]));
-                const size_t row = (size_t)(b0 + t);
-                quant_block_warp(v, lane, out.q + row * out.cols + (gcol & ~31), out.d + row * nbo + (gcol >> 5),
-                                 out.fs + row * nbo + (gcol >> 5));
-            }
+        for (int t = 0; t < nb; t++) {
+            float v = __fmul_rn(__fmul_rn(sv[t][j], srn[t]), nw);
+            v = __fmul_rn(v, pf_silu(sz[t][j]));
+            const size_t row = (size_t)(b0 + t);
+            quant_block_warp(v, lane, out.q + row * out.cols + (col & ~31), out.d + row * nbo + (col >> 5),
+                             out.fs + row * nbo + (col >> 5));
         }
-        // the block's buffers (this CTA's, and the output rows its peers write) are free again
-        cluster_arrive();
-        cluster_wait();
+        __syncthreads();   // the block's buffers are free again
     }
-    const float none[S > 0 ? S : 1] = {};
-    if (own_qk) {
-        conv_store(cq, L, C, none, 0);
-        conv_store(ck, L, C, none, 0);
+#pragma unroll
+    for (int m = 0; m < NP; m++) {
+        rec[(size_t)(2 * m) * kDV] = Sc[m].x;
+        rec[(size_t)(2 * m + 1) * kDV] = Sc[m].y;
     }
-    if (w == 0) conv_store(cv, L, C, none, 0);
+    const float none[S] = {};
+    conv_store(cq, L, C, none, 0);
+    conv_store(ck, L, C, none, 0);
+    conv_store(cv, L, C, none, 0);
 }
 
 
@@ -4185,7 +4160,7 @@ void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
     launch_k(k_deltanet, d.nk, kDV, sm, s, L, d, y, st, out);
 }
 void launch_deltanet_rows(const LinLayer &L, const LinDims &d, const float *y, int n, Act out, cudaStream_t s) {
-    launch_k(k_deltanet_rows<4>, dim3(d.nk * kDnCl, 1), kDnParts * 32, 0, s, L, d, y, n, out);
+    launch_k(k_deltanet_rows, dim3(d.nk), kDV, 0, s, L, d, y, n, out);
 }
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
                       const Step *st, cudaStream_t s, int nseq) {
@@ -4311,7 +4286,7 @@ int kernels_init(int max_ctx, int hd, int rep) {
     max_carveout(k_norm_quant);
     max_carveout(k_deltanet3<4, 4, PINFER_SPEC_MAX_K>);
     max_carveout(k_deltanet3<4, kMaxRows, PINFER_SPEC_MAX_K>);
-    max_carveout(k_deltanet_rows<4>);
+    max_carveout(k_deltanet_rows);
     // raise the dynamic shared memory limits once, outside any stream capture
     raise_smem(k_matvec<1, 0>, mv_smem<1>());
     raise_smem(k_matvec<1, 1>, mv_smem<1>());
