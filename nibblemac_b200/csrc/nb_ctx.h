@@ -69,6 +69,7 @@ struct PrefillScratch {
     Act act_h, act_mid;
     GemmMaps maps_h, maps_ol, maps_oa, maps_f;
     Step *steps = nullptr;                    // [kPrefillSub]
+    float *dn_recs = nullptr, *dn_o = nullptr;   // DeltaNet records and raw outputs of a chunk
     SeqPass *d_pass = nullptr;                // [chunks of max_ctx][kPrefillSub]
     float *logits = nullptr;                  // [kPrefillRows][vocab] (forward_all), on first use
     unsigned long long *partial = nullptr;

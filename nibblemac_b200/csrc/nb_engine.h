@@ -195,9 +195,12 @@ void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
                      Step *st, Act out, cudaStream_t s, int nseq = 1, int rps = kMaxRows,
                      int keep_max = PINFER_SPEC_MAX_K);
 bool deltanet_batch_ok(const LinDims &d);
-// a prefill chunk's rows 0..n-1 of y in one launch (no deferred commit, nothing logged; the
-// shape deltanet_batch_ok accepts)
-void launch_deltanet_rows(const LinLayer &L, const LinDims &d, const float *y, int n, Act out, cudaStream_t s);
+// a prefill chunk's rows 0..n-1 of y (no deferred commit, nothing logged; the shape
+// deltanet_batch_ok accepts): prep, recurrence and post kernels through two scratch buffers,
+// recs (deltanet_rec_floats) and o_rows ([n][vd])
+size_t deltanet_rec_floats(const LinDims &d, int rows);
+void launch_deltanet_rows(const LinLayer &L, const LinDims &d, const float *y, int n, float *recs, float *o_rows,
+                          Act out, int *status, cudaStream_t s);
 // attention grids cover d.rps rows of each of nseq sequences; nseq > 1 needs the cluster kernel
 // (attn_batch_ok)
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,

@@ -3268,110 +3268,146 @@ __global__ void __cluster_dims__(kDnCl, 1, 1) __launch_bounds__(kDnParts * 32, 1
     }
 }
 
-// Gated DeltaNet layer of a prefill chunk: rows 0..n-1 of y (any n), with no deferred commit to
-// replay and nothing logged (the caller flushes a pending commit first). The per-element
-// arithmetic is k_deltanet2's (same citations); the schedule suits long passes: one CTA per key
-// head, thread j owns state column j with all of its kDK rows in registers for the whole chunk,
-// so a token's update, its output dot product and the next token's kv dot product are one sweep
-// over the rows with the two ordered add chains (rows 0..kDK-1 in order, kern_lin.c) interleaved
-// and no partial sum crossing threads; the delta of the next token is the thread's own. The
-// elementwise products take two rows per packed f32x2 instruction (each lane rounds as the
+// Gated DeltaNet layer of a prefill chunk, rows 0..n-1 of y (any n), in three kernels, with no
+// deferred commit to replay and nothing logged (the caller flushes a pending commit first). The
+// per-element arithmetic is k_deltanet2's (same citations); the work is split by its shape:
+//   k_deltanet_prep  conv + SiLU of every q / k / v channel, the L2 norms and the gates: the conv
+//                    is a filter over the inputs (rows b - 3 .. b), so every 16-row block of every
+//                    head is independent (grid heads x blocks); one record per (row, head).
+//   k_deltanet_rows  the recurrence, sequential over the rows: one CTA per key head, thread j owns
+//                    state column j with all of its kDK rows in registers for the whole chunk, so
+//                    a token's update, its output dot product and the next token's kv dot product
+//                    are one sweep over the rows with the two ordered add chains (rows 0..kDK-1 in
+//                    order, kern_lin.c) interleaved and no partial sum crossing threads; the
+//                    records stream in by bulk copies, two 16-row blocks in flight.
+//   k_deltanet_post  the gated RMSNorm over a row's 128 outputs and the A8 of the result (grid
+//                    rows x heads).
+// The elementwise products take two rows per packed f32x2 instruction (each lane rounds as the
 // scalar operation), except the k * delta products: ptxas contracts a packed multiply that
 // feeds a packed add into one fused multiply-add (one rounding instead of two; measured on
 // B200 with CUDA 12.9, --fmad=false and explicit .rn alike), so those stay scalar __fmul_rn.
-// Rows arrive in blocks of kDnBlk: the block's conv inputs, z rows and gates are loaded,
-// convolved and normalised, its tokens swept, its outputs normed and quantised. The decay of a
-// block's first token is applied in a sweep of its own instead of inside the previous token's:
-// per element the same operations in the same order.
+// The decay of a block's first token is applied in a sweep of its own instead of inside the
+// previous token's: per element the same operations in the same order.
 constexpr int kDnBlk = 16;
+constexpr int kDnCh = kDK + kDK + kDV;          // channels of one head: q ++ k ++ v
+constexpr int kDnRec = kDnCh + 4;               // record: q, k (L2-normed), v (conv), beta, decay, 2 pad
 
-__global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d, const float *y, int n, Act out) {
-    constexpr int KC = 4, S = KC - 1, NR = kDnBlk, NP = kDK / 2;
-    const int h = blockIdx.x, j = threadIdx.x, w = j >> 5, lane = j & 31;
+template <int KC>
+__global__ void __launch_bounds__(kDnCh) k_deltanet_prep(LinLayer L, LinDims d, const float *y, int n, float *recs) {
+    constexpr int S = KC - 1;
+    const int h = blockIdx.x, b0 = blockIdx.y * kDnBlk, c = threadIdx.x, w = c >> 5, lane = c & 31;
+    const int nb = n - b0 < kDnBlk ? n - b0 : kDnBlk;
     const int C = d.C;
-    // conv taps and states, the state column: written only by this layer's DeltaNet, which ran
-    // before this kernel's predecessor, so requested before pdl_wait
-    ConvCh<KC> cq, ck, cv;
-    conv_load(cq, L, C, h * kDK + j);
-    conv_load(ck, L, C, d.kd + h * kDK + j);
-    conv_load(cv, L, C, 2 * d.kd + h * kDV + j);
+    const int ch = c < kDK ? h * kDK + c : c < 2 * kDK ? d.kd + h * kDK + (c - kDK) : 2 * d.kd + h * kDV + (c - 2 * kDK);
+    // taps, and for the chunk's first block the conv state (written by this layer's previous
+    // chunk, before this kernel's predecessor): requested before pdl_wait
+    ConvCh<KC> cv;
+    cv.c = ch;
+#pragma unroll
+    for (int r = 0; r < KC; r++) cv.w[r] = ld_early(L.conv_w + (size_t)ch * KC + r);
+#pragma unroll
+    for (int r = 0; r < S; r++) cv.st[r] = b0 == 0 ? ld_early(L.conv_state + (size_t)r * C + ch) : 0.0f;
+    pdl_wait();
+    pdl_trigger();
+    if (b0 > 0) {   // a later block: the state is the chunk's own three inputs before it
+#pragma unroll
+        for (int r = 0; r < S; r++) cv.st[r] = y[(size_t)(b0 - S + r) * d.ldy + ch];
+    }
+    __shared__ __align__(16) float sx[kDnBlk][kDnCh + 4];
+    __shared__ float sg[kDnBlk][2];
+    float xin[kDnBlk];
+#pragma unroll
+    for (int t = 0; t < kDnBlk; t++) xin[t] = t < nb ? ld_early(y + (size_t)(b0 + t) * d.ldy + ch) : 0.0f;
+#pragma unroll
+    for (int t = 0; t < kDnBlk; t++)
+        if (t < nb) sx[t][c] = conv_step(cv, xin[t]);
+    if (c < nb) {   // gates of row b0 + c
+        const float *yr = y + (size_t)(b0 + c) * d.ldy;
+        const float gb = yr[C + d.vd + h], ga = yr[C + d.vd + d.nv + h];
+        sg[c][0] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-gb)));
+        const float xs = __fadd_rn(ga, L.dt_bias[h]);
+        const float sp = xs > 20.0f ? xs : glibc_log1pf(glibc_expf(xs));
+        sg[c][1] = glibc_expf(__fmul_rn(L.A[h], sp));
+    }
+    __syncthreads();
+    // L2 norm of q and k: 4 lanes per (row, vector)
+    if (w < 4) {
+        const float qscale = inv_sqrt_ref((float)kDK);
+        const int u = w * 8 + (lane >> 2), l = lane & 3;
+        const bool act = u < 2 * nb;
+        float *vec = act ? &sx[u >> 1][(u & 1) * kDK] : &sx[0][0];
+        float cs = 0.0f;
+        if (act) {
+#pragma unroll 32
+            for (int i = l; i < kDK; i += 4) cs = madd(cs, vec[i], vec[i]);
+        }
+        const int base = lane & ~3;
+        const float c0 = __shfl_sync(0xffffffffu, cs, base), c1 = __shfl_sync(0xffffffffu, cs, base + 1);
+        const float c2 = __shfl_sync(0xffffffffu, cs, base + 2), c3 = __shfl_sync(0xffffffffu, cs, base + 3);
+        const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+        const float r = inv_sqrt_ref(__fadd_rn(ss, 1e-6f));
+        __syncwarp();
+        if (act) {
+            const float sc = (u & 1) ? 1.0f : qscale;
+            for (int i = l; i < kDK; i += 4) vec[i] = __fmul_rn(__fmul_rn(vec[i], r), sc);
+        }
+    }
+    static_assert(2 * kDnBlk <= 4 * 8, "one pass of four warps covers the block's vectors");
+    __syncthreads();
+    for (int t = 0; t < nb; t++) {
+        float *rec = recs + ((size_t)(b0 + t) * d.nk + h) * kDnRec;
+        rec[c] = sx[t][c];
+        if (c < 2) rec[kDnCh + c] = sg[t][c];
+    }
+}
+
+__global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d, const float *y, int n,
+                                                          const float *recs, float *o_rows, int *status) {
+    constexpr int KC = 4, S = KC - 1, NP = kDK / 2;
+    const int h = blockIdx.x, j = threadIdx.x;
+    const int C = d.C;
+    // the state column: written only by this layer's recurrence in an earlier chunk
     float *rec = L.rec + (size_t)h * kDK * kDV + j;
     float2 Sc[NP];   // rows (2 m, 2 m + 1) of column j
 #pragma unroll
     for (int m = 0; m < NP; m++)
         Sc[m] = make_float2(ld_early(rec + (size_t)(2 * m) * kDV), ld_early(rec + (size_t)(2 * m + 1) * kDV));
-    const float nw = L.norm_w[j];
+    extern __shared__ __align__(16) float dnb[];   // [2][kDnBlk][kDnRec]: two blocks of records
+    __shared__ __align__(8) uint64_t bar[2];
+    if (j == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
     pdl_wait();
     pdl_trigger();
-    __shared__ __align__(16) float sq[NR][kDK], sk[NR][kDK];
-    __shared__ __align__(16) float sv[NR][kDV];   // v rows; token t's output replaces its v row
-    __shared__ __align__(16) float sz[NR][kDV];
-    __shared__ float sbeta[NR], sdec[NR], srn[NR];
-    const int nbo = out.cols >> 5, col = h * kDV + j;
-    for (int b0 = 0; b0 < n; b0 += NR) {
-        const int nb = n - b0 < NR ? n - b0 : NR;
-        const float *yb = y + (size_t)b0 * d.ldy;
-        float xq[NR], xk[NR], xv[NR], xz[NR];
-#pragma unroll
-        for (int t = 0; t < NR; t++) {
-            xq[t] = xk[t] = xv[t] = xz[t] = 0.0f;
-            if (t < nb) {
-                const float *yr = yb + (size_t)t * d.ldy;
-                xq[t] = ld_early(yr + h * kDK + j);
-                xk[t] = ld_early(yr + d.kd + h * kDK + j);
-                xv[t] = ld_early(yr + 2 * d.kd + h * kDV + j);
-                xz[t] = ld_early(yr + C + h * kDV + j);
-            }
+    const int nblk = (n + kDnBlk - 1) / kDnBlk;
+    auto issue = [&](int b) {   // thread 0: block b's records into buffer b % 2
+        const int b0 = b * kDnBlk, nb = n - b0 < kDnBlk ? n - b0 : kDnBlk;
+        float *dst = dnb + (size_t)(b & 1) * kDnBlk * kDnRec;
+        mbar_arrive_expect(&bar[b & 1], (uint32_t)(nb * kDnRec * 4));
+        for (int t = 0; t < nb; t++)
+            bulk_g2s(dst + (size_t)t * kDnRec, recs + ((size_t)(b0 + t) * d.nk + h) * kDnRec, kDnRec * 4, &bar[b & 1]);
+    };
+    if (j == 0) {
+        issue(0);
+        if (nblk > 1) issue(1);
+    }
+    bool ok = true;
+    for (int b = 0; b < nblk; b++) {
+        const int b0 = b * kDnBlk, nb = n - b0 < kDnBlk ? n - b0 : kDnBlk;
+        if (!mbar_wait(&bar[b & 1], (uint32_t)(b >> 1) & 1u)) {   // timed out: reported, no hang
+            ok = false;
+            break;
         }
-        if (j < nb) {   // gates of row j
-            const float *yr = yb + (size_t)j * d.ldy;
-            const float gb = yr[C + d.vd + h], ga = yr[C + d.vd + d.nv + h];
-            sbeta[j] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-gb)));
-            const float xs = __fadd_rn(ga, L.dt_bias[h]);
-            const float sp = xs > 20.0f ? xs : glibc_log1pf(glibc_expf(xs));
-            sdec[j] = glibc_expf(__fmul_rn(L.A[h], sp));
-        }
-        // ---- conv + SiLU of this thread's three channels
-#pragma unroll
-        for (int t = 0; t < NR; t++) {
-            if (t < nb) {
-                sq[t][j] = conv_step(cq, xq[t]);
-                sk[t][j] = conv_step(ck, xk[t]);
-                sv[t][j] = conv_step(cv, xv[t]);
-                sz[t][j] = xz[t];
-            }
-        }
-        __syncthreads();
-        // ---- L2 norm of q and k: 4 lanes per (token, vector)
-        {
-            const float qscale = inv_sqrt_ref((float)kDK);
-            for (int u0 = w * 8; u0 < 2 * nb; u0 += (kDV / 32) * 8) {
-                const int u = u0 + (lane >> 2), l = lane & 3;
-                const bool act = u < 2 * nb;
-                float *vec = act ? ((u & 1) ? sk[u >> 1] : sq[u >> 1]) : sq[0];
-                float cs = 0.0f;
-                if (act) {
-#pragma unroll 32
-                    for (int i = l; i < kDK; i += 4) cs = madd(cs, vec[i], vec[i]);
-                }
-                const int base = lane & ~3;
-                const float c0 = __shfl_sync(0xffffffffu, cs, base), c1 = __shfl_sync(0xffffffffu, cs, base + 1);
-                const float c2 = __shfl_sync(0xffffffffu, cs, base + 2), c3 = __shfl_sync(0xffffffffu, cs, base + 3);
-                const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
-                const float r = inv_sqrt_ref(__fadd_rn(ss, 1e-6f));
-                __syncwarp();
-                if (act) {
-                    const float sc = (u & 1) ? 1.0f : qscale;
-                    for (int i = l; i < kDK; i += 4) vec[i] = __fmul_rn(__fmul_rn(vec[i], r), sc);
-                }
-            }
-        }
-        __syncthreads();
-        // ---- the block's first decay and kv (rows in order)
+        const float *blk = dnb + (size_t)(b & 1) * kDnBlk * kDnRec;
+        // the block's first decay and kv (rows in order)
         float kv = 0.0f;
         {
-            const float2 dec2 = make_float2(sdec[0], sdec[0]);
-            const float4 *k4 = reinterpret_cast<const float4 *>(sk[0]);
+            const float dec = blk[kDnCh + 1];
+            const float2 dec2 = make_float2(dec, dec);
+            const float4 *k4 = reinterpret_cast<const float4 *>(blk + kDK);
 #pragma unroll
             for (int m = 0; m < NP; m += 2) {
                 const float4 kk = k4[m / 2];
@@ -3382,15 +3418,18 @@ __global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d,
                 kv = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(kv, p0.x), p0.y), p1.x), p1.y);
             }
         }
-        // ---- tokens: S += k delta, o = S.q; then S *= decay of the next token, its kv = S.k
+        // tokens: S += k delta, o = S.q; then S *= decay of the next token, its kv = S.k
         for (int t = 0; t < nb; t++) {
-            const float delta = __fmul_rn(__fadd_rn(sv[t][j], -kv), sbeta[t]);
-            const float4 *k4 = reinterpret_cast<const float4 *>(sk[t]);
-            const float4 *q4 = reinterpret_cast<const float4 *>(sq[t]);
+            const float *r = blk + (size_t)t * kDnRec;
+            const float delta = __fmul_rn(__fadd_rn(r[2 * kDK + j], -kv), r[kDnCh]);
+            const float4 *q4 = reinterpret_cast<const float4 *>(r);
+            const float4 *k4 = reinterpret_cast<const float4 *>(r + kDK);
             float o = 0.0f, kvn = 0.0f;
             if (t + 1 < nb) {
-                const float2 dn2 = make_float2(sdec[t + 1], sdec[t + 1]);
-                const float4 *n4 = reinterpret_cast<const float4 *>(sk[t + 1]);
+                const float *rn = r + kDnRec;
+                const float dn = rn[kDnCh + 1];
+                const float2 dn2 = make_float2(dn, dn);
+                const float4 *n4 = reinterpret_cast<const float4 *>(rn + kDK);
 #pragma unroll
                 for (int m = 0; m < NP; m += 2) {
                     const float4 kk = k4[m / 2], qq = q4[m / 2], nn = n4[m / 2];
@@ -3420,45 +3459,69 @@ __global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d,
                     Sc[m + 1] = s1;
                 }
             }
-            sv[t][j] = o;   // thread j alone reads and writes column j of the v / output rows
+            o_rows[(size_t)(b0 + t) * d.vd + h * kDV + j] = o;
             kv = kvn;
         }
-        __syncthreads();
-        // ---- gated RMSNorm over the head's 128 outputs, then A8 of each warp's 32-column block
-        for (int u0 = w * 8; u0 < nb; u0 += (kDV / 32) * 8) {
-            const int u = u0 + (lane >> 2), l = lane & 3;
-            const bool act = u < nb;
-            const float *vec = sv[act ? u : 0];
-            float cs = 0.0f;
-            if (act) {
-#pragma unroll 32
-                for (int i = l; i < kDV; i += 4) cs = madd(cs, vec[i], vec[i]);
-            }
-            const int base = lane & ~3;
-            const float c0 = __shfl_sync(0xffffffffu, cs, base), c1 = __shfl_sync(0xffffffffu, cs, base + 1);
-            const float c2 = __shfl_sync(0xffffffffu, cs, base + 2), c3 = __shfl_sync(0xffffffffu, cs, base + 3);
-            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
-            if (act && l == 0) srn[u] = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)kDV), d.eps));
-        }
-        __syncthreads();
-        for (int t = 0; t < nb; t++) {
-            float v = __fmul_rn(__fmul_rn(sv[t][j], srn[t]), nw);
-            v = __fmul_rn(v, pf_silu(sz[t][j]));
-            const size_t row = (size_t)(b0 + t);
-            quant_block_warp(v, lane, out.q + row * out.cols + (col & ~31), out.d + row * nbo + (col >> 5),
-                             out.fs + row * nbo + (col >> 5));
-        }
-        __syncthreads();   // the block's buffers are free again
+        __syncthreads();   // every thread is done with buffer b % 2 before it is refilled
+        if (j == 0 && b + 2 < nblk) issue(b + 2);
+    }
+    if (!ok) {   // let the copies in flight land (a second bounded wait) before shared memory goes
+        if (j == 0 && status) *status = -90;
+        mbar_wait(&bar[0], 0);
+        mbar_wait(&bar[1], 0);
+        return;
     }
 #pragma unroll
     for (int m = 0; m < NP; m++) {
         rec[(size_t)(2 * m) * kDV] = Sc[m].x;
         rec[(size_t)(2 * m + 1) * kDV] = Sc[m].y;
     }
-    const float none[S] = {};
-    conv_store(cq, L, C, none, 0);
-    conv_store(ck, L, C, none, 0);
-    conv_store(cv, L, C, none, 0);
+    // conv states: the last three inputs of [old state, rows 0..n-1] for this thread's channels
+    const int chs[3] = {h * kDK + j, d.kd + h * kDK + j, 2 * d.kd + h * kDV + j};
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+        float v[S];
+#pragma unroll
+        for (int r = 0; r < S; r++) {
+            const int i = n + r;   // index into [old 0..S-1, row 0, row 1, ...]
+            v[r] = i < S ? L.conv_state[(size_t)i * C + chs[q]] : y[(size_t)(i - S) * d.ldy + chs[q]];
+        }
+#pragma unroll
+        for (int r = 0; r < S; r++) L.conv_state[(size_t)r * C + chs[q]] = v[r];
+    }
+}
+
+// The gated RMSNorm of one row's 128 outputs of one head, then A8 (grid rows x heads).
+__global__ void __launch_bounds__(kDV) k_deltanet_post(LinLayer L, LinDims d, const float *y, const float *o_rows,
+                                                       Act out) {
+    const int v = blockIdx.x, h = blockIdx.y, j = threadIdx.x, lane = j & 31;
+    const float nw = L.norm_w[j];
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float so[kDV];
+    __shared__ float srn;
+    const int col = h * kDV + j;
+    so[j] = o_rows[(size_t)v * d.vd + col];
+    const float z = y[(size_t)v * d.ldy + d.C + col];
+    __syncthreads();
+    if (j < 32) {
+        const int l = lane & 3;
+        float cs = 0.0f;
+        if (lane < 4) {
+#pragma unroll 32
+            for (int i = l; i < kDV; i += 4) cs = madd(cs, so[i], so[i]);
+        }
+        const float c0 = __shfl_sync(0xffffffffu, cs, 0), c1 = __shfl_sync(0xffffffffu, cs, 1);
+        const float c2 = __shfl_sync(0xffffffffu, cs, 2), c3 = __shfl_sync(0xffffffffu, cs, 3);
+        const float ss = __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), 0.0f);
+        if (lane == 0) srn = inv_sqrt_ref(__fadd_rn(__fdiv_rn(ss, (float)kDV), d.eps));
+    }
+    __syncthreads();
+    float x = __fmul_rn(__fmul_rn(so[j], srn), nw);
+    x = __fmul_rn(x, pf_silu(z));
+    const int nbo = out.cols >> 5;
+    quant_block_warp(x, lane, out.q + (size_t)v * out.cols + (col & ~31), out.d + (size_t)v * nbo + (col >> 5),
+                     out.fs + (size_t)v * nbo + (col >> 5));
 }
 
 
@@ -4159,8 +4222,13 @@ void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
     const size_t sm = deltanet_smem(d.rep);
     launch_k(k_deltanet, d.nk, kDV, sm, s, L, d, y, st, out);
 }
-void launch_deltanet_rows(const LinLayer &L, const LinDims &d, const float *y, int n, Act out, cudaStream_t s) {
-    launch_k(k_deltanet_rows, dim3(d.nk), kDV, 0, s, L, d, y, n, out);
+size_t deltanet_rec_floats(const LinDims &d, int rows) { return (size_t)rows * d.nk * kDnRec; }
+void launch_deltanet_rows(const LinLayer &L, const LinDims &d, const float *y, int n, float *recs, float *o_rows,
+                          Act out, int *status, cudaStream_t s) {
+    launch_k(k_deltanet_prep<4>, dim3(d.nk, (n + kDnBlk - 1) / kDnBlk), kDnCh, 0, s, L, d, y, n, recs);
+    launch_k(k_deltanet_rows, dim3(d.nk), kDV, sizeof(float) * 2 * kDnBlk * kDnRec, s, L, d, y, n,
+             (const float *)recs, o_rows, status);
+    launch_k(k_deltanet_post, dim3(n, d.nk), kDV, 0, s, L, d, y, (const float *)o_rows, out);
 }
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
                       const Step *st, cudaStream_t s, int nseq) {
@@ -4286,7 +4354,9 @@ int kernels_init(int max_ctx, int hd, int rep) {
     max_carveout(k_norm_quant);
     max_carveout(k_deltanet3<4, 4, PINFER_SPEC_MAX_K>);
     max_carveout(k_deltanet3<4, kMaxRows, PINFER_SPEC_MAX_K>);
-    max_carveout(k_deltanet_rows);
+    max_carveout(k_deltanet_prep<4>);
+    max_carveout(k_deltanet_post);
+    raise_smem(k_deltanet_rows, sizeof(float) * 2 * kDnBlk * kDnRec);
     // raise the dynamic shared memory limits once, outside any stream capture
     raise_smem(k_matvec<1, 0>, mv_smem<1>());
     raise_smem(k_matvec<1, 1>, mv_smem<1>());

@@ -6,12 +6,14 @@
 // A chunk of R rows is one pass: the embedding and every RMSNorm + A8 over the R rows, each
 // projection one tcgen05 GEMM over them (the weights' tile image read once per chunk), the
 // SwiGLU + A8 between gate / up and down. A Gated DeltaNet layer runs the chunk's rows in order
-// in one launch (k_deltanet_rows: the recurrence is sequential, its state stays in registers).
+// (k_deltanet_prep / _rows / _post: the conv, norms and gates of all rows in parallel,
+// the sequential recurrence with its state in registers, the gated norms in parallel).
 // An attention layer sees the chunk as consecutive 16-row sub-passes, Step blocks with
 // row0 = 16 i and pos0 = n_past + 16 i over the context's one KV cache (no per-sequence
 // stride): k_attn_prep writes the K / V rows of the whole chunk, then every row attends to the
-// positions up to its own. Every row's arithmetic is the 16-row CUDA-core path's, so logits,
-// states and later tokens are bit-identical to it, and to the reference.
+// positions up to its own (k_attn5: one CTA per KV group and 4 rows). Every row's
+// arithmetic is the 16-row CUDA-core path's, so logits, states and later tokens are
+// bit-identical to it, and to the reference.
 #include <algorithm>
 #include <vector>
 
@@ -51,6 +53,8 @@ int prefill_alloc(pinfer_ctx *c, bool logits) {
             (rc = c->dalloc(&p.act_mid.q, R * mid)) || (rc = c->dalloc(&p.act_mid.d, sizeof(float) * R * (mid / 32))) ||
             (rc = c->dalloc(&p.act_mid.fs, sizeof(float) * R * (mid / 32))) ||
             (rc = c->dalloc(&p.steps, sizeof(Step) * kPrefillSub)) ||
+            (rc = c->dalloc(&p.dn_recs, sizeof(float) * deltanet_rec_floats(c->lind, (int)R))) ||
+            (rc = c->dalloc(&p.dn_o, sizeof(float) * R * c->vd)) ||
             (rc = c->dalloc(&p.d_pass, sizeof(SeqPass) * kPrefillSub * chunks)))
             return rc;
         p.act_h.cols = c->H;
@@ -106,7 +110,7 @@ void enqueue_chunk(pinfer_ctx *c, int R, bool logits) {
         } else {
             pf_gemm(c, 0, p.maps_h, T.win, R, p.y, c->lind.ldy);
             const Act o = with_cols(p.act_mid, c->vd);
-            launch_deltanet_rows(c->lin[D.lin], c->lind, p.y, R, o, s);
+            launch_deltanet_rows(c->lin[D.lin], c->lind, p.y, R, p.dn_recs, p.dn_o, o, &c->step->status, s);
             pf_gemm(c, 1, p.maps_ol, T.out, R, p.x, c->H);
         }
         launch_norm_quant(p.x, D.post_norm, c->H, c->eps, p.steps, p.act_h, s, nsub, kMaxRows);
