@@ -208,6 +208,10 @@ void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, flo
 void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf,
                  const Step *st, Act out, cudaStream_t s, int nseq = 1);
 bool attn_batch_ok(const AttnDims &d);
+// the sub-passes of one context's prefill chunk (nseq Step blocks over one KV cache): one CTA per
+// (row, KV group) with the group's query heads, else as launch_attn
+void launch_attn_rows(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf, const Step *st,
+                      Act out, cudaStream_t s, int nseq);
 // greedy / out: sequence i's at greedy + i * n_max, out + i * n_max
 void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s, int nseq = 1);
 void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s, int nseq = 1);

@@ -2390,9 +2390,12 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
 // division, scaling), P.V in position order from zero, sigmoid gate, A8. The probabilities are
 // kept position-major (att[p][q]), so the P.V loop reads a position's 16 values with four
 // 16-byte loads; thread j owns output column j of all the group's queries (16 independent
-// chains), with V read 8 positions ahead.
+// chains), with V read 8 positions ahead. QS = G (one row of the group per CTA) is the prefill
+// form: a chunk's rows over a long context get many CTAs and a probability table that fits
+// shared memory at 4096 positions.
+template <int QS = kAttnQ>
 size_t attn5_smem(int max_ctx) {
-    return sizeof(float) * ((size_t)kAttnQ * kAttnHd + (((size_t)max_ctx + 3) & ~(size_t)3) * kAttnQ);
+    return sizeof(float) * ((size_t)QS * kAttnHd + (((size_t)max_ctx + 3) & ~(size_t)3) * QS);
 }
 
 // sum4_ref over a[i * stride], i < n (the same 4-lane order and final combination)
@@ -2411,12 +2414,14 @@ __device__ float sum4_strided(const float *a, int stride, int n) {
     return __fadd_rn(__fadd_rn(__fadd_rn(c0, c1), __fadd_rn(c2, c3)), t);
 }
 
+template <int QS = kAttnQ>
 __global__ void __launch_bounds__(kAttnHd)
     k_attn5(AttnLayer L, AttnDims d, const float *y, const float *qbuf, const Step *st, Act out) {
     pdl_wait();
     pdl_trigger();
-    constexpr int HD = kAttnHd, QS = kAttnQ;   // att row stride: 16 queries
-    const int G = d.nq / d.nkv, QR = kAttnQ / G;
+    constexpr int HD = kAttnHd;   // att row stride: QS queries
+    static_assert(QS % 4 == 0, "att rows are read as float4");
+    const int G = d.nq / d.nkv, QR = QS / G;
     const int nch = (d.rps + QR - 1) / QR;
     const int g = blockIdx.x / nch, rc = blockIdx.x % nch, seq = blockIdx.y, tid = threadIdx.x;
     st += seq;
@@ -4241,7 +4246,7 @@ bool attn4_ok(const AttnDims &d) {
            attn4_smem(d.max_ctx) <= (size_t)attn4_lim;
 }
 bool attn5_ok(const AttnDims &d) {
-    static const int attn5_lim = dyn_smem_limit(k_attn5);
+    static const int attn5_lim = dyn_smem_limit(k_attn5<>);
     const int G = d.nkv > 0 ? d.nq / d.nkv : 0;
     return d.hd == kAttnHd && G > 0 && d.nq % d.nkv == 0 && G <= kAttnQ && kAttnQ % G == 0 &&
            attn5_smem(d.max_ctx) <= (size_t)attn5_lim;
@@ -4254,7 +4259,7 @@ void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const fl
                  const Step *st, Act out, cudaStream_t s, int nseq) {
     if (nseq > 1 && attn5_ok(d)) {   // one CTA per (sequence, KV group, rows): many in flight
         const int QR = kAttnQ / (d.nq / d.nkv), nch = (d.rps + QR - 1) / QR;
-        launch_k(k_attn5, dim3(d.nkv * nch, nseq), kAttnHd, attn5_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
+        launch_k(k_attn5<>, dim3(d.nkv * nch, nseq), kAttnHd, attn5_smem(d.max_ctx), s, L, d, y, qbuf, st, out);
         return;
     }
     if (nseq > 1 && attn4_ok(d)) {   // grouped queries share the K / V reads (one context: the
@@ -4275,6 +4280,20 @@ void launch_attn(const AttnLayer &L, const AttnDims &d, const float *y, const fl
     }
     const size_t sm = ((size_t)d.hd + d.max_ctx) * sizeof(float);
     launch_k(k_attn, dim3(kMaxRows, d.nq), d.hd, sm, s, L, d, y, qbuf, st, out);
+}
+void launch_attn_rows(const AttnLayer &L, const AttnDims &d, const float *y, const float *qbuf, const Step *st,
+                      Act out, cudaStream_t s, int nseq) {
+    static const int lim4 = dyn_smem_limit(k_attn5<4>), lim8 = dyn_smem_limit(k_attn5<8>);
+    const int G = d.nkv > 0 && d.nq % d.nkv == 0 ? d.nq / d.nkv : 0;
+    if (d.hd == kAttnHd && G == 4 && attn5_smem<4>(d.max_ctx) <= (size_t)lim4) {
+        launch_k(k_attn5<4>, dim3(d.nkv * d.rps, nseq), kAttnHd, attn5_smem<4>(d.max_ctx), s, L, d, y, qbuf, st, out);
+        return;
+    }
+    if (d.hd == kAttnHd && G == 8 && attn5_smem<8>(d.max_ctx) <= (size_t)lim8) {
+        launch_k(k_attn5<8>, dim3(d.nkv * d.rps, nseq), kAttnHd, attn5_smem<8>(d.max_ctx), s, L, d, y, qbuf, st, out);
+        return;
+    }
+    launch_attn(L, d, y, qbuf, st, out, s, nseq);
 }
 void launch_gen_start(Step *st, const int *greedy, int *out, cudaStream_t s, int nseq) {
     launch_k(k_gen_start, nseq, 32, 0, s, st, greedy, out);
@@ -4406,7 +4425,9 @@ int kernels_init(int max_ctx, int hd, int rep) {
         raise_smem(k_attn2, attn2_smem(max_ctx));
         raise_smem(k_attn3, attn3_smem(max_ctx));
         raise_smem(k_attn4, attn4_smem(max_ctx));
-        raise_smem(k_attn5, attn5_smem(max_ctx));
+        raise_smem(k_attn5<>, attn5_smem(max_ctx));
+        raise_smem(k_attn5<4>, attn5_smem<4>(max_ctx));
+        raise_smem(k_attn5<8>, attn5_smem<8>(max_ctx));
     }
     if (gemm_init() != 0) return -1;
     return cudaGetLastError() == cudaSuccess ? 0 : -1;

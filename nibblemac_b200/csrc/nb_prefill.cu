@@ -11,9 +11,9 @@
 // An attention layer sees the chunk as consecutive 16-row sub-passes, Step blocks with
 // row0 = 16 i and pos0 = n_past + 16 i over the context's one KV cache (no per-sequence
 // stride): k_attn_prep writes the K / V rows of the whole chunk, then every row attends to the
-// positions up to its own (k_attn5: one CTA per KV group and 4 rows). Every row's
-// arithmetic is the 16-row CUDA-core path's, so logits, states and later tokens are
-// bit-identical to it, and to the reference.
+// positions up to its own (k_attn5 with one row per CTA: the group's query heads share each
+// K / V row). Every row's arithmetic is the 16-row CUDA-core path's, so logits, states and
+// later tokens are bit-identical to it, and to the reference.
 #include <algorithm>
 #include <vector>
 
@@ -105,7 +105,7 @@ void enqueue_chunk(pinfer_ctx *c, int R, bool logits) {
             pf_gemm(c, 0, p.maps_h, T.win, R, p.y, c->attd.ldy);
             const Act o = with_cols(p.act_mid, c->nq * c->hd);
             launch_attn_prep(c->att[l], ad, p.y, p.qbuf, p.steps, s, nsub);
-            launch_attn(c->att[l], ad, p.y, p.qbuf, p.steps, o, s, nsub);
+            launch_attn_rows(c->att[l], ad, p.y, p.qbuf, p.steps, o, s, nsub);
             pf_gemm(c, 1, p.maps_oa, T.out, R, p.x, c->H);
         } else {
             pf_gemm(c, 0, p.maps_h, T.win, R, p.y, c->lind.ldy);
