@@ -2390,7 +2390,7 @@ __global__ void __cluster_dims__(kAttnCL, 1, 1) __launch_bounds__(kAttnHd)
 // division, scaling), P.V in position order from zero, sigmoid gate, A8. The probabilities are
 // kept position-major (att[p][q]), so the P.V loop reads a position's 16 values with four
 // 16-byte loads; thread j owns output column j of all the group's queries (16 independent
-// chains), with V read 8 positions ahead. QS = G (one row of the group per CTA) is the prefill
+// chains), with V read 8 positions ahead (32 for QS <= 8). QS = G (one row per CTA) is the prefill
 // form: a chunk's rows over a long context get many CTAs and a probability table that fits
 // shared memory at 4096 positions.
 template <int QS = kAttnQ>
@@ -2448,17 +2448,38 @@ __global__ void __launch_bounds__(kAttnHd)
     }
     __syncthreads();
 
-    // 1. scores: 64 positions per pass, 4 threads per position, all queries per K fragment
+    // 1. scores: 64 positions per pass, 4 threads per position, all queries per K fragment. With
+    // few queries per fragment (QS <= 8) the next pass's fragment is requested before this pass's
+    // products, so the L2 latency is not paid per pass; with 16 the registers go to occupancy.
     const float scale = inv_sqrt_ref((float)HD);
     const float *K = L.kc + (size_t)g * d.max_ctx * HD;
     const int k4 = tid & 3;
+    constexpr bool PIPE = QS <= 8;
+    float4 kn[PIPE ? HD / 16 : 1];
+    if constexpr (PIPE) {
+        const int pp = tid >> 2;
+        const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)(pp < np_max ? pp : 0) * HD) + k4;
+#pragma unroll
+        for (int i = 0; i < HD / 16; i++) kn[i] = __ldg(kr + 4 * i);
+    }
     for (int base = 0; base < np_max; base += HD / 4) {
         const int pp = base + (tid >> 2);
         const bool act = pp < np_max;
-        const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)(act ? pp : 0) * HD) + k4;
         float4 kf[HD / 16];
+        if constexpr (PIPE) {
 #pragma unroll
-        for (int i = 0; i < HD / 16; i++) kf[i] = __ldg(kr + 4 * i);
+            for (int i = 0; i < HD / 16; i++) kf[i] = kn[i];
+            if (base + HD / 4 < np_max) {
+                const int pn = pp + HD / 4;
+                const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)(pn < np_max ? pn : 0) * HD) + k4;
+#pragma unroll
+                for (int i = 0; i < HD / 16; i++) kn[i] = __ldg(kr + 4 * i);
+            }
+        } else {
+            const float4 *kr = reinterpret_cast<const float4 *>(K + (size_t)(act ? pp : 0) * HD) + k4;
+#pragma unroll
+            for (int i = 0; i < HD / 16; i++) kf[i] = __ldg(kr + 4 * i);
+        }
         for (int q = 0; q < Q; q++) {
             const float4 *q4 = reinterpret_cast<const float4 *>(qv + (size_t)q * HD);
             float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f, c3 = 0.0f;
@@ -2498,7 +2519,7 @@ __global__ void __launch_bounds__(kAttnHd)
     float acc[QS];
 #pragma unroll
     for (int q = 0; q < QS; q++) acc[q] = 0.0f;
-    constexpr int PF = 8;
+    constexpr int PF = QS <= 8 ? 32 : 8;   // V rows in flight: a few queries' chains are short
     float vn[PF];
 #pragma unroll
     for (int i = 0; i < PF; i++) vn[i] = i < np_min ? __ldg(V + (size_t)i * HD) : 0.0f;
