@@ -51,6 +51,8 @@ struct WeightStore {
         GemmW win, out, gu, down;   // gu: gate ++ up
     } tiles[kMaxLayers];
     GemmW head_tile;                // the whole LM head (logits of every prefill row)
+    TileLayer mtp_tiles;            // the MTP head's decoder block (its gu: gate ++ up)
+    GemmW mtp_fc_tile;              // the MTP head's input projection fc [e | h]
     ~WeightStore() {
         for (void *p : ptrs) cudaFree(p);
     }
@@ -70,6 +72,11 @@ struct PrefillScratch {
     GemmMaps maps_h, maps_ol, maps_oa, maps_f;
     Step *steps = nullptr;                    // [kPrefillSub]
     float *dn_recs = nullptr, *dn_o = nullptr;   // DeltaNet records and raw outputs of a chunk
+    // MTP prompts: the chunk's final-normed rows, the MTP sub-passes (next tokens), [e | h] A8
+    float *hn = nullptr;
+    Step *msteps = nullptr;
+    Act act_cat;
+    GemmMaps maps_cat;
     SeqPass *d_pass = nullptr;                // [chunks of max_ctx][kPrefillSub]
     float *logits = nullptr;                  // [kPrefillRows][vocab] (forward_all), on first use
     unsigned long long *partial = nullptr;
@@ -176,6 +183,7 @@ struct pinfer_ctx {
 int ensure_gemm_tiles(pinfer_ctx *c, bool head);   // the shared tile images (head: the LM head's too)
 bool prefill_gemm_ok(const pinfer_ctx *c);          // the model shape has the prefill kernels
 // n rows (> kMaxRows worth it) at positions n_past.. in chunks of up to kPrefillRows rows;
-// logits_all (host, [n][vocab], unsharded heads only) receives every row's logits. Advances
-// n_past; asynchronous on the context's stream unless logits are copied out.
-int prefill_gemm(pinfer_ctx *c, const int32_t *tokens, int n, float *logits_all);
+// logits_all (host, [n][vocab], unsharded heads only) receives every row's logits; next (the
+// tokens following rows 0..n-1) runs the MTP head's pass over each chunk too, filling its KV
+// rows. Advances n_past; asynchronous on the context's stream unless logits are copied out.
+int prefill_gemm(pinfer_ctx *c, const int32_t *tokens, int n, float *logits_all, const int32_t *next = nullptr);

@@ -632,10 +632,19 @@ int zero_mtp_rows(pinfer_ctx *c, int from, int to) {
 
 // The prompt with the MTP head (pf_spec_prefill, spec.c:172-195): chunk by chunk the main pass
 // with its normed rows, then the MTP pass over the same rows (row i with token i + 1; the last
-// row with the first generated token), which fills the MTP KV rows and drafts d1.
+// row with the first generated token), which fills the MTP KV rows and drafts d1. The rows
+// before the last pass go through the GEMM chunks (nb_prefill.cu), the last pass as 16 rows.
 int forward_tokens_mtp(pinfer_ctx *c, const int32_t *tokens, int n) {
     int rc;
     if ((rc = zero_mtp_rows(c, c->mtp_rows, c->n_past))) return rc;
+    // the rows before the last pass: GEMM chunks with the MTP pass over each (every such row's
+    // next token is in the prompt)
+    const int tail = (n - 1) % kMaxRows + 1;
+    if (n - tail > kMaxRows && prefill_gemm_ok(c)) {
+        if ((rc = prefill_gemm(c, tokens, n - tail, nullptr, tokens + 1))) return rc;
+        tokens += n - tail;
+        n = tail;
+    }
     int next[kMaxRows];
     for (int t0 = 0; t0 < n; t0 += kMaxRows) {
         const int nb = std::min(kMaxRows, n - t0);

@@ -218,9 +218,9 @@ void launch_accept(Step *st, const int *greedy, int *out, cudaStream_t s, int ns
 void launch_pass_end(Step *st, cudaStream_t s, int nseq = 1);
 // MTP draft head (see the kernels' comments)
 void launch_norm_rows(const float *x, const float *w, int H, float eps, const Step *st, float *out,
-                      cudaStream_t s);
+                      cudaStream_t s, int nseq = 1);
 void launch_mtp_input(const Mat &E, const float *h, const Step *ms, const float *w_emb, const float *w_hid,
-                      int H, float eps, Act out, cudaStream_t s);
+                      int H, float eps, Act out, cudaStream_t s, int nseq = 1);
 void launch_mtp_chain_set(Step *st, Step *ms, int step, cudaStream_t s);
 void launch_mtp_chain_take(Step *st, const Step *ms, int step, const float *mrows, float *mcur, int H,
                            cudaStream_t s);

@@ -3579,8 +3579,9 @@ __device__ __forceinline__ float embed_val(const Mat &E, int tok, int c) {
 __global__ void k_norm_rows(const float *x, const float *w, int H, float eps, const Step *st, float *out) {
     pdl_wait();
     pdl_trigger();
-    const int v = blockIdx.x;
-    if (v >= st->n) return;
+    st += blockIdx.y;   // the sub-pass of a multi-pass chunk (row r = its row0 + v)
+    if ((int)blockIdx.x >= st->n) return;
+    const int v = st->row0 + blockIdx.x;
     extern __shared__ float xr[];   // [H]
     __shared__ float rr;
     for (int i = threadIdx.x; i < H; i += blockDim.x) xr[i] = x[(size_t)v * H + i];
@@ -3599,11 +3600,12 @@ __global__ void k_mtp_input(Mat E, const float *h, const Step *ms, const float *
                             int H, float eps, Act out) {
     pdl_wait();
     pdl_trigger();
-    const int v = blockIdx.x;
-    if (v >= ms->n) return;
+    ms += blockIdx.y;   // the sub-pass of a multi-pass chunk (row r = its row0 + blockIdx.x)
+    if ((int)blockIdx.x >= ms->n) return;
+    const int v = ms->row0 + blockIdx.x;
     extern __shared__ float cat[];   // [2H]: embedding row, hidden row
     __shared__ float r2[2];
-    int tok = ms->tokens[v];
+    int tok = ms->tokens[blockIdx.x];
     if (tok < 0 || tok >= E.rows) tok = 0;   // ids come from the argmax of this head
     for (int c = threadIdx.x; c < H; c += blockDim.x) {
         cat[c] = embed_val(E, tok, c);
@@ -4336,12 +4338,13 @@ void launch_keys_argmax(const unsigned long long *keys, Step *st, cudaStream_t s
     launch_k(k_keys_argmax, nseq, rps, 0, s, keys, st, kstride);
 }
 void launch_norm_rows(const float *x, const float *w, int H, float eps, const Step *st, float *out,
-                      cudaStream_t s) {
-    launch_k(k_norm_rows, kMaxRows, 256, (size_t)H * sizeof(float), s, x, w, H, eps, st, out);
+                      cudaStream_t s, int nseq) {
+    launch_k(k_norm_rows, dim3(kMaxRows, nseq), 256, (size_t)H * sizeof(float), s, x, w, H, eps, st, out);
 }
 void launch_mtp_input(const Mat &E, const float *h, const Step *ms, const float *w_emb, const float *w_hid,
-                      int H, float eps, Act out, cudaStream_t s) {
-    launch_k(k_mtp_input, kMaxRows, 256, 2 * (size_t)H * sizeof(float), s, E, h, ms, w_emb, w_hid, H, eps, out);
+                      int H, float eps, Act out, cudaStream_t s, int nseq) {
+    launch_k(k_mtp_input, dim3(kMaxRows, nseq), 256, 2 * (size_t)H * sizeof(float), s, E, h, ms, w_emb, w_hid, H, eps,
+             out);
 }
 void launch_mtp_chain_set(Step *st, Step *ms, int step, cudaStream_t s) {
     launch_k(k_mtp_chain_set, 1, 32, 0, s, st, ms, step);

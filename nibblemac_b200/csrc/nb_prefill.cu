@@ -55,9 +55,19 @@ int prefill_alloc(pinfer_ctx *c, bool logits) {
             (rc = c->dalloc(&p.steps, sizeof(Step) * kPrefillSub)) ||
             (rc = c->dalloc(&p.dn_recs, sizeof(float) * deltanet_rec_floats(c->lind, (int)R))) ||
             (rc = c->dalloc(&p.dn_o, sizeof(float) * R * c->vd)) ||
-            (rc = c->dalloc(&p.d_pass, sizeof(SeqPass) * kPrefillSub * chunks)))
+            (rc = c->dalloc(&p.d_pass, sizeof(SeqPass) * kPrefillSub * chunks * 2)))
             return rc;
         p.act_h.cols = c->H;
+        if (c->mtp_ok) {
+            if ((rc = c->dalloc(&p.hn, sizeof(float) * R * c->H)) ||
+                (rc = c->dalloc(&p.msteps, sizeof(Step) * kPrefillSub)) ||
+                (rc = c->dalloc(&p.act_cat.q, R * 2 * c->H)) ||
+                (rc = c->dalloc(&p.act_cat.d, sizeof(float) * R * (2 * c->H / 32))) ||
+                (rc = c->dalloc(&p.act_cat.fs, sizeof(float) * R * (2 * c->H / 32))))
+                return rc;
+            p.act_cat.cols = 2 * c->H;
+            if (gemm_maps(p.act_cat, (int)R, &p.maps_cat)) return PINFER_E_NOMEM;
+        }
         if (gemm_maps(p.act_h, (int)R, &p.maps_h) || gemm_maps(with_cols(p.act_mid, c->vd), (int)R, &p.maps_ol) ||
             gemm_maps(with_cols(p.act_mid, c->nq * c->hd), (int)R, &p.maps_oa) ||
             gemm_maps(with_cols(p.act_mid, c->ffn), (int)R, &p.maps_f))
@@ -87,36 +97,60 @@ void pf_gemm(pinfer_ctx *c, int epi, const GemmMaps &maps, const GemmW &W, int R
     launch_gemm(epi, maps, g, c->stream);
 }
 
-// One chunk of R rows whose sub-pass shapes are in p.steps (set by the caller).
-void enqueue_chunk(pinfer_ctx *c, int R, bool logits) {
+// A full-attention decoder block over the chunk's R rows (sub-passes st), its KV cache in A.
+void attention_block(pinfer_ctx *c, const pinfer_ctx::Layer &D, const WeightStore::TileLayer &T,
+                     const AttnLayer &A, const Step *st, int R) {
     PrefillScratch &p = c->pf;
-    const WeightStore &ws = *c->weights;
     cudaStream_t s = c->stream;
     const int nsub = (R + kMaxRows - 1) / kMaxRows;
     AttnDims ad = c->attd;
     ad.rps = kMaxRows;
     ad.ss_kv = 0;   // every sub-pass reads and writes the one cache
+    launch_norm_quant(p.x, D.in_norm, c->H, c->eps, st, p.act_h, s, nsub, kMaxRows);
+    pf_gemm(c, 0, p.maps_h, T.win, R, p.y, c->attd.ldy);
+    const Act o = with_cols(p.act_mid, c->nq * c->hd);
+    launch_attn_prep(A, ad, p.y, p.qbuf, st, s, nsub);
+    launch_attn_rows(A, ad, p.y, p.qbuf, st, o, s, nsub);
+    pf_gemm(c, 1, p.maps_oa, T.out, R, p.x, c->H);
+    launch_norm_quant(p.x, D.post_norm, c->H, c->eps, st, p.act_h, s, nsub, kMaxRows);
+    pf_gemm(c, 0, p.maps_h, T.gu, R, p.y, 2 * c->ffn);
+    launch_swiglu_quant(p.y, 2 * c->ffn, c->ffn, R, with_cols(p.act_mid, c->ffn), s);
+    pf_gemm(c, 1, p.maps_f, T.down, R, p.x, c->H);
+}
+
+// One chunk of R rows whose sub-pass shapes are in p.steps (set by the caller); with mtp, the
+// MTP head's pass over the same rows follows (its sub-passes in p.msteps: the next tokens):
+// u = fc [rmsnorm(embed(next)) | rmsnorm(final-normed row)], then its decoder block, which
+// writes the MTP KV rows (pf_spec_prefill, spec.c:172-195; pf_mtp_forward, mtp.c:62-100).
+void enqueue_chunk(pinfer_ctx *c, int R, bool logits, bool mtp) {
+    PrefillScratch &p = c->pf;
+    const WeightStore &ws = *c->weights;
+    cudaStream_t s = c->stream;
+    const int nsub = (R + kMaxRows - 1) / kMaxRows;
     launch_embed(c->embed, p.steps, p.x, c->H, s, nsub, kMaxRows);
     for (int l = 0; l < c->n_layers; l++) {
         const auto &D = c->layers[l];
         const auto &T = ws.tiles[l];
-        launch_norm_quant(p.x, D.in_norm, c->H, c->eps, p.steps, p.act_h, s, nsub, kMaxRows);
         if (D.is_full) {
-            pf_gemm(c, 0, p.maps_h, T.win, R, p.y, c->attd.ldy);
-            const Act o = with_cols(p.act_mid, c->nq * c->hd);
-            launch_attn_prep(c->att[l], ad, p.y, p.qbuf, p.steps, s, nsub);
-            launch_attn_rows(c->att[l], ad, p.y, p.qbuf, p.steps, o, s, nsub);
-            pf_gemm(c, 1, p.maps_oa, T.out, R, p.x, c->H);
-        } else {
-            pf_gemm(c, 0, p.maps_h, T.win, R, p.y, c->lind.ldy);
-            const Act o = with_cols(p.act_mid, c->vd);
-            launch_deltanet_rows(c->lin[D.lin], c->lind, p.y, R, p.dn_recs, p.dn_o, o, &c->step->status, s);
-            pf_gemm(c, 1, p.maps_ol, T.out, R, p.x, c->H);
+            attention_block(c, D, T, c->att[l], p.steps, R);
+            continue;
         }
+        launch_norm_quant(p.x, D.in_norm, c->H, c->eps, p.steps, p.act_h, s, nsub, kMaxRows);
+        pf_gemm(c, 0, p.maps_h, T.win, R, p.y, c->lind.ldy);
+        const Act o = with_cols(p.act_mid, c->vd);
+        launch_deltanet_rows(c->lin[D.lin], c->lind, p.y, R, p.dn_recs, p.dn_o, o, &c->step->status, s);
+        pf_gemm(c, 1, p.maps_ol, T.out, R, p.x, c->H);
         launch_norm_quant(p.x, D.post_norm, c->H, c->eps, p.steps, p.act_h, s, nsub, kMaxRows);
         pf_gemm(c, 0, p.maps_h, T.gu, R, p.y, 2 * c->ffn);
         launch_swiglu_quant(p.y, 2 * c->ffn, c->ffn, R, with_cols(p.act_mid, c->ffn), s);
         pf_gemm(c, 1, p.maps_f, T.down, R, p.x, c->H);
+    }
+    if (mtp) {
+        launch_norm_rows(p.x, c->norm, c->H, c->eps, p.steps, p.hn, s, nsub);
+        launch_mtp_input(c->embed, p.hn, p.msteps, c->mtp_norm_emb, c->mtp_norm_hid, c->H, c->eps, p.act_cat, s,
+                         nsub);
+        pf_gemm(c, 0, p.maps_cat, ws.mtp_fc_tile, R, p.x, c->H);
+        attention_block(c, c->mtp_layer, ws.mtp_tiles, c->mtp_att, p.msteps, R);
     }
     if (logits) {
         launch_norm_quant(p.x, c->norm, c->H, c->eps, p.steps, p.act_h, s, nsub, kMaxRows);
@@ -139,6 +173,14 @@ int ensure_gemm_tiles(pinfer_ctx *c, bool head) {
                 (rc = tile_into(c, D.gate, D.up, &T.gu)) || (rc = tile_into(c, D.down, none, &T.down)))
                 return rc;
         }
+        if (c->mtp_ok) {
+            const auto &D = c->mtp_layer;
+            auto &T = ws.mtp_tiles;
+            if ((rc = tile_into(c, D.win, none, &T.win)) || (rc = tile_into(c, D.out, none, &T.out)) ||
+                (rc = tile_into(c, D.gate, D.up, &T.gu)) || (rc = tile_into(c, D.down, none, &T.down)) ||
+                (rc = tile_into(c, c->mtp_fc, none, &ws.mtp_fc_tile)))
+                return rc;
+        }
         NB_CUDA_OK(cudaStreamSynchronize(c->stream));   // other contexts' streams use them next
         ws.tiles_ok = true;
     }
@@ -154,18 +196,21 @@ bool prefill_gemm_ok(const pinfer_ctx *c) {
     return deltanet_batch_ok(c->lind) && attn_batch_ok(c->attd);
 }
 
-int prefill_gemm(pinfer_ctx *c, const int32_t *tokens, int n, float *logits_all) {
-    const bool logits = logits_all != nullptr;
+int prefill_gemm(pinfer_ctx *c, const int32_t *tokens, int n, float *logits_all, const int32_t *next) {
+    const bool logits = logits_all != nullptr, mtp = next != nullptr;
     int rc;
     if (logits && c->shard_world > 1) return PINFER_E_ARG;   // the sharded head has no whole tile
+    if ((mtp && !c->mtp_ok) || (mtp && logits)) return PINFER_E_ARG;   // the MTP pass reuses the rows
     if ((rc = ensure_gemm_tiles(c, logits)) || (rc = prefill_alloc(c, logits))) return rc;
     PrefillScratch &p = c->pf;
     cudaStream_t s = c->stream;
     // a deferred commit of the last generation is applied first: k_deltanet_rows replays none
     launch_flush(c->lin, c->n_lin, c->lind, c->step, s);
     // every chunk's sub-pass shapes in one copy (a pageable source: staged before the call returns)
+    // (the MTP sub-passes, with the next tokens, after the main ones)
     const int nchunks = (n + kPrefillRows - 1) / kPrefillRows;
-    std::vector<SeqPass> hp((size_t)nchunks * kPrefillSub);
+    const size_t nmain = (size_t)nchunks * kPrefillSub;
+    std::vector<SeqPass> hp(nmain * (mtp ? 2 : 1));
     for (int j = 0; j < nchunks; j++)
         for (int i = 0; i < kPrefillSub; i++) {
             const int t0 = j * kPrefillRows + i * kMaxRows;
@@ -175,12 +220,19 @@ int prefill_gemm(pinfer_ctx *c, const int32_t *tokens, int n, float *logits_all)
             q.row0 = i * kMaxRows;
             q.logged = 0;
             for (int t = 0; t < q.n; t++) q.tokens[t] = tokens[t0 + t];
+            if (mtp) {
+                SeqPass &m = hp[nmain + (size_t)j * kPrefillSub + i];
+                m = q;
+                for (int t = 0; t < q.n; t++) m.tokens[t] = next[t0 + t];
+            }
         }
     NB_CUDA_OK(cudaMemcpyAsync(p.d_pass, hp.data(), sizeof(SeqPass) * hp.size(), cudaMemcpyHostToDevice, s));
     for (int j = 0; j < nchunks; j++) {
         const int R = std::min(kPrefillRows, n - j * kPrefillRows);
-        launch_set_pass_seqs(p.steps, p.d_pass + (size_t)j * kPrefillSub, (R + kMaxRows - 1) / kMaxRows, s);
-        enqueue_chunk(c, R, logits);
+        const int nsub = (R + kMaxRows - 1) / kMaxRows;
+        launch_set_pass_seqs(p.steps, p.d_pass + (size_t)j * kPrefillSub, nsub, s);
+        if (mtp) launch_set_pass_seqs(p.msteps, p.d_pass + nmain + (size_t)j * kPrefillSub, nsub, s);
+        enqueue_chunk(c, R, logits, mtp);
         if (logits)
             NB_CUDA_OK(cudaMemcpyAsync(logits_all + (size_t)j * kPrefillRows * c->vocab, p.logits,
                                        sizeof(float) * (size_t)R * c->vocab, cudaMemcpyDeviceToHost, s));

@@ -252,6 +252,30 @@ def test_mtp_speculation_matches_reference(pair, k, nv):
     assert toks2 == rtoks2 and [st2.rounds, st2.drafted, st2.accepted] == rst2
 
 
+@pytest.mark.parametrize("k", [1, 3])
+def test_mtp_long_prompts_match_reference(pair, k):
+    """Prompts long enough for the tensor-core prefill chunks with the MTP head's pass over each
+    chunk (150 rows: chunks of 64, 64 and 16, then a 6-row pass; a 70-row continuation: one
+    64-row chunk after the first call's rows): tokens and statistics as the reference's, and the
+    state, MTP KV rows included, byte for byte."""
+    from nibblemac_b200._lib import SpecStats
+    name, dev, ref = pair
+    p = prompt(dev.n_vocab, 150, 70 + k)
+    dev.reset()
+    st = SpecStats()
+    toks, status = dev.generate(p, 32, k=k, stats=st)
+    rtoks, rst, rstatus = ref.generate_mtp(p, 32, k, 0)
+    assert status == rstatus == 0 and toks == rtoks
+    assert [st.rounds, st.drafted, st.accepted] == rst
+    assert dev.save_state() == ref.save_state(), f"{name} k={k}: state after a 150-token prompt"
+    q = prompt(dev.n_vocab, 70, 80 + k)
+    st2 = SpecStats()
+    toks2, _ = dev.generate(q, 24, k=k, stats=st2, append=True)
+    rtoks2, rst2, _ = ref.generate_mtp(q, 24, k, 0, append=True)
+    assert toks2 == rtoks2 and [st2.rounds, st2.drafted, st2.accepted] == rst2
+    assert dev.save_state() == ref.save_state(), f"{name} k={k}: state after the continuation"
+
+
 @pytest.fixture(scope="module")
 def looping_pair(looping_model):
     from nibblemac_b200.model import Model
