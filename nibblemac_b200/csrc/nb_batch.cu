@@ -57,6 +57,7 @@ struct pinfer_b200_batch {
     bool sharded = false;
     int row_base = 0;
     int *status = nullptr;
+    float *dn_recs = nullptr, *dn_o = nullptr;   // prefill passes' DeltaNet records and raw outputs
     Step *steps = nullptr, *h_steps = nullptr;
     SeqPass *d_pass = nullptr, *h_pass = nullptr;
     int pass_slots = 0;
@@ -122,7 +123,9 @@ Act with_cols(Act a, int cols) {
 }
 
 // One pass over R rows of nseq sequences (at most rps rows each), the shapes in the Step blocks.
-void enqueue_forward(pinfer_b200_batch *b, int R, int nseq, int rps, bool head) {
+// prefill: an unlogged pass with no deferred commit (the prompts' passes), whose DeltaNet layers
+// run as conv / norms in parallel, the recurrence with its state in registers, the gated norms.
+void enqueue_forward(pinfer_b200_batch *b, int R, int nseq, int rps, bool head, bool prefill = false) {
     const pinfer_ctx *c = b->src;
     cudaStream_t s = b->stream;
     launch_embed(c->embed, b->steps, b->x, c->H, s, nseq, rps);
@@ -141,7 +144,10 @@ void enqueue_forward(pinfer_b200_batch *b, int R, int nseq, int rps, bool head) 
         } else {
             gemm(b, 0, b->maps_h, T.win, R, b->y, c->lind.ldy);
             const Act o = with_cols(b->act_mid, c->vd);
-            launch_deltanet(b->lin[D.lin], b->lind, b->y, b->steps, o, s, nseq, rps, b->kmax);
+            if (prefill)
+                launch_deltanet_rows_seqs(b->lin[D.lin], b->lind, b->y, R, b->steps, nseq, b->dn_recs, b->dn_o, o, s);
+            else
+                launch_deltanet(b->lin[D.lin], b->lind, b->y, b->steps, o, s, nseq, rps, b->kmax);
             gemm(b, 1, b->maps_ol, T.out, R, b->x, c->H);
         }
         launch_norm_quant(b->x, D.post_norm, c->H, c->eps, b->steps, b->act_h, s, nseq, rps);
@@ -231,6 +237,8 @@ int batch_alloc(pinfer_b200_batch *b) {
         (rc = b->dalloc(&b->act_mid.fs, sizeof(float) * R * (mid / 32))) ||
         (rc = b->dalloc(&b->partial, sizeof(unsigned long long) * R * b->head.npanels)) ||
         (rc = b->dalloc(&b->nan0, sizeof(int) * R)) || (rc = b->dalloc(&b->status, sizeof(int))) ||
+        (rc = b->dalloc(&b->dn_recs, sizeof(float) * deltanet_rec_floats(b->lind, (int)R))) ||
+        (rc = b->dalloc(&b->dn_o, sizeof(float) * R * c->vd)) ||
         (rc = b->dalloc(&b->keys, sizeof(unsigned long long) * 2 * R)) ||
         (rc = b->dalloc(&b->steps, sizeof(Step) * S)) || (rc = b->dalloc(&b->d_seeds, sizeof(unsigned long long) * S)) ||
         (rc = b->dalloc(&b->d_ndone, sizeof(int))))
@@ -417,7 +425,7 @@ int pinfer_b200_batch_generate_synthetic(pinfer_b200_batch *b, int n_seq, const 
         }
         if (R == 0) break;
         if ((rc = set_passes(R))) return rc;
-        enqueue_forward(b, R, n_seq, rps, false);
+        enqueue_forward(b, R, n_seq, rps, false, true);
     }
     // the last prompt token of every sequence, with the LM head: the first generated token
     {

@@ -201,6 +201,10 @@ bool deltanet_batch_ok(const LinDims &d);
 size_t deltanet_rec_floats(const LinDims &d, int rows);
 void launch_deltanet_rows(const LinLayer &L, const LinDims &d, const float *y, int n, float *recs, float *o_rows,
                           Act out, int *status, cudaStream_t s);
+// the same for an unlogged pass of up to 16 rows per sequence of a batch (R rows in all;
+// sequence i's rows at st[i].row0, its states at d's per-sequence strides)
+void launch_deltanet_rows_seqs(const LinLayer &L, const LinDims &d, const float *y, int R, Step *st, int nseq,
+                               float *recs, float *o_rows, Act out, cudaStream_t s);
 // attention grids cover d.rps rows of each of nseq sequences; nseq > 1 needs the cluster kernel
 // (attn_batch_ok)
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,

@@ -3318,15 +3318,27 @@ constexpr int kDnBlk = 16;
 constexpr int kDnCh = kDK + kDK + kDV;          // channels of one head: q ++ k ++ v
 constexpr int kDnRec = kDnCh + 4;               // record: q, k (L2-normed), v (conv), beta, decay, 2 pad
 
+// st == nullptr: one chunk of n rows (grid heads x 16-row blocks); else one pass of up to 16 rows
+// per sequence of a batch (grid heads x sequences; sequence i's rows at st[i].row0, its states
+// at the batch's per-sequence strides).
 template <int KC>
-__global__ void __launch_bounds__(kDnCh) k_deltanet_prep(LinLayer L, LinDims d, const float *y, int n, float *recs) {
+__global__ void __launch_bounds__(kDnCh) k_deltanet_prep(LinLayer L, LinDims d, const float *y, int n, float *recs,
+                                                         const Step *st) {
     constexpr int S = KC - 1;
-    const int h = blockIdx.x, b0 = blockIdx.y * kDnBlk, c = threadIdx.x, w = c >> 5, lane = c & 31;
-    const int nb = n - b0 < kDnBlk ? n - b0 : kDnBlk;
+    const int h = blockIdx.x, c = threadIdx.x, w = c >> 5, lane = c & 31;
+    int b0 = blockIdx.y * kDnBlk, base = b0, nb = n - b0 < kDnBlk ? n - b0 : kDnBlk;
+    if (st) {   // written between passes only, so read before pdl_wait
+        st += blockIdx.y;
+        L.conv_state += blockIdx.y * d.ss_conv;
+        b0 = 0;
+        base = ld_early_s32(&st->row0);
+        nb = ld_early_s32(&st->n);
+        nb = nb < kDnBlk ? nb : kDnBlk;
+    }
     const int C = d.C;
     const int ch = c < kDK ? h * kDK + c : c < 2 * kDK ? d.kd + h * kDK + (c - kDK) : 2 * d.kd + h * kDV + (c - 2 * kDK);
-    // taps, and for the chunk's first block the conv state (written by this layer's previous
-    // chunk, before this kernel's predecessor): requested before pdl_wait
+    // taps, and for the chunk's first block the conv state (written by this layer's DeltaNet of
+    // an earlier pass, before this kernel's predecessor): requested before pdl_wait
     ConvCh<KC> cv;
     cv.c = ch;
 #pragma unroll
@@ -3335,20 +3347,21 @@ __global__ void __launch_bounds__(kDnCh) k_deltanet_prep(LinLayer L, LinDims d, 
     for (int r = 0; r < S; r++) cv.st[r] = b0 == 0 ? ld_early(L.conv_state + (size_t)r * C + ch) : 0.0f;
     pdl_wait();
     pdl_trigger();
+    if (nb <= 0) return;
     if (b0 > 0) {   // a later block: the state is the chunk's own three inputs before it
 #pragma unroll
-        for (int r = 0; r < S; r++) cv.st[r] = y[(size_t)(b0 - S + r) * d.ldy + ch];
+        for (int r = 0; r < S; r++) cv.st[r] = y[(size_t)(base - S + r) * d.ldy + ch];
     }
     __shared__ __align__(16) float sx[kDnBlk][kDnCh + 4];
     __shared__ float sg[kDnBlk][2];
     float xin[kDnBlk];
 #pragma unroll
-    for (int t = 0; t < kDnBlk; t++) xin[t] = t < nb ? ld_early(y + (size_t)(b0 + t) * d.ldy + ch) : 0.0f;
+    for (int t = 0; t < kDnBlk; t++) xin[t] = t < nb ? ld_early(y + (size_t)(base + t) * d.ldy + ch) : 0.0f;
 #pragma unroll
     for (int t = 0; t < kDnBlk; t++)
         if (t < nb) sx[t][c] = conv_step(cv, xin[t]);
-    if (c < nb) {   // gates of row b0 + c
-        const float *yr = y + (size_t)(b0 + c) * d.ldy;
+    if (c < nb) {   // gates of row base + c
+        const float *yr = y + (size_t)(base + c) * d.ldy;
         const float gb = yr[C + d.vd + h], ga = yr[C + d.vd + d.nv + h];
         sg[c][0] = __fdiv_rn(1.0f, __fadd_rn(1.0f, glibc_expf(-gb)));
         const float xs = __fadd_rn(ga, L.dt_bias[h]);
@@ -3381,23 +3394,45 @@ __global__ void __launch_bounds__(kDnCh) k_deltanet_prep(LinLayer L, LinDims d, 
     static_assert(2 * kDnBlk <= 4 * 8, "one pass of four warps covers the block's vectors");
     __syncthreads();
     for (int t = 0; t < nb; t++) {
-        float *rec = recs + ((size_t)(b0 + t) * d.nk + h) * kDnRec;
+        float *rec = recs + ((size_t)(base + t) * d.nk + h) * kDnRec;
         rec[c] = sx[t][c];
         if (c < 2) rec[kDnCh + c] = sg[t][c];
     }
 }
 
 __global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d, const float *y, int n,
-                                                          const float *recs, float *o_rows, int *status) {
+                                                          const float *recs, float *o_rows, int *status,
+                                                          Step *st) {
     constexpr int KC = 4, S = KC - 1, NP = kDK / 2;
     const int h = blockIdx.x, j = threadIdx.x;
     const int C = d.C;
-    // the state column: written only by this layer's recurrence in an earlier chunk
+    int base = 0;
+    if (st) {   // one sequence of a batch pass: its rows, states and status word
+        st += blockIdx.y;
+        L.conv_state += blockIdx.y * d.ss_conv;
+        L.rec += blockIdx.y * d.ss_rec;
+        n = ld_early_s32(&st->n);
+        base = ld_early_s32(&st->row0);
+        status = &st->status;
+        if (ld_early_s32(&st->logged) || ld_early_s32(&st->pend_keep) > 0 || ld_early_s32(&st->pend_conv) > 0) {
+            // a verify pass or a deferred commit: not this kernel's (the engine never sends one)
+            pdl_wait();
+            pdl_trigger();
+            if (j == 0) st->status = -92;
+            return;
+        }
+    }
+    // the state column: written only by this layer's recurrence in an earlier chunk (a sequence
+    // with no rows in this pass leaves it alone)
     float *rec = L.rec + (size_t)h * kDK * kDV + j;
     float2 Sc[NP];   // rows (2 m, 2 m + 1) of column j
 #pragma unroll
-    for (int m = 0; m < NP; m++)
-        Sc[m] = make_float2(ld_early(rec + (size_t)(2 * m) * kDV), ld_early(rec + (size_t)(2 * m + 1) * kDV));
+    for (int m = 0; m < NP; m++) Sc[m] = make_float2(0.0f, 0.0f);
+    if (n > 0) {
+#pragma unroll
+        for (int m = 0; m < NP; m++)
+            Sc[m] = make_float2(ld_early(rec + (size_t)(2 * m) * kDV), ld_early(rec + (size_t)(2 * m + 1) * kDV));
+    }
     extern __shared__ __align__(16) float dnb[];   // [2][kDnBlk][kDnRec]: two blocks of records
     __shared__ __align__(8) uint64_t bar[2];
     if (j == 0) {
@@ -3408,13 +3443,15 @@ __global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d,
     __syncthreads();
     pdl_wait();
     pdl_trigger();
+    if (n <= 0) return;
     const int nblk = (n + kDnBlk - 1) / kDnBlk;
     auto issue = [&](int b) {   // thread 0: block b's records into buffer b % 2
         const int b0 = b * kDnBlk, nb = n - b0 < kDnBlk ? n - b0 : kDnBlk;
         float *dst = dnb + (size_t)(b & 1) * kDnBlk * kDnRec;
         mbar_arrive_expect(&bar[b & 1], (uint32_t)(nb * kDnRec * 4));
         for (int t = 0; t < nb; t++)
-            bulk_g2s(dst + (size_t)t * kDnRec, recs + ((size_t)(b0 + t) * d.nk + h) * kDnRec, kDnRec * 4, &bar[b & 1]);
+            bulk_g2s(dst + (size_t)t * kDnRec, recs + ((size_t)(base + b0 + t) * d.nk + h) * kDnRec, kDnRec * 4,
+                     &bar[b & 1]);
     };
     if (j == 0) {
         issue(0);
@@ -3485,7 +3522,7 @@ __global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d,
                     Sc[m + 1] = s1;
                 }
             }
-            o_rows[(size_t)(b0 + t) * d.vd + h * kDV + j] = o;
+            o_rows[(size_t)(base + b0 + t) * d.vd + h * kDV + j] = o;
             kv = kvn;
         }
         __syncthreads();   // every thread is done with buffer b % 2 before it is refilled
@@ -3510,7 +3547,7 @@ __global__ void __launch_bounds__(kDV, 1) k_deltanet_rows(LinLayer L, LinDims d,
 #pragma unroll
         for (int r = 0; r < S; r++) {
             const int i = n + r;   // index into [old 0..S-1, row 0, row 1, ...]
-            v[r] = i < S ? L.conv_state[(size_t)i * C + chs[q]] : y[(size_t)(i - S) * d.ldy + chs[q]];
+            v[r] = i < S ? L.conv_state[(size_t)i * C + chs[q]] : y[(size_t)(base + i - S) * d.ldy + chs[q]];
         }
 #pragma unroll
         for (int r = 0; r < S; r++) L.conv_state[(size_t)r * C + chs[q]] = v[r];
@@ -4253,10 +4290,18 @@ void launch_deltanet(const LinLayer &L, const LinDims &d, const float *y,
 size_t deltanet_rec_floats(const LinDims &d, int rows) { return (size_t)rows * d.nk * kDnRec; }
 void launch_deltanet_rows(const LinLayer &L, const LinDims &d, const float *y, int n, float *recs, float *o_rows,
                           Act out, int *status, cudaStream_t s) {
-    launch_k(k_deltanet_prep<4>, dim3(d.nk, (n + kDnBlk - 1) / kDnBlk), kDnCh, 0, s, L, d, y, n, recs);
+    launch_k(k_deltanet_prep<4>, dim3(d.nk, (n + kDnBlk - 1) / kDnBlk), kDnCh, 0, s, L, d, y, n, recs,
+             (const Step *)nullptr);
     launch_k(k_deltanet_rows, dim3(d.nk), kDV, sizeof(float) * 2 * kDnBlk * kDnRec, s, L, d, y, n,
-             (const float *)recs, o_rows, status);
+             (const float *)recs, o_rows, status, (Step *)nullptr);
     launch_k(k_deltanet_post, dim3(n, d.nk), kDV, 0, s, L, d, y, (const float *)o_rows, out);
+}
+void launch_deltanet_rows_seqs(const LinLayer &L, const LinDims &d, const float *y, int R, Step *st, int nseq,
+                               float *recs, float *o_rows, Act out, cudaStream_t s) {
+    launch_k(k_deltanet_prep<4>, dim3(d.nk, nseq), kDnCh, 0, s, L, d, y, 0, recs, (const Step *)st);
+    launch_k(k_deltanet_rows, dim3(d.nk, nseq), kDV, sizeof(float) * 2 * kDnBlk * kDnRec, s, L, d, y, 0,
+             (const float *)recs, o_rows, (int *)nullptr, st);
+    launch_k(k_deltanet_post, dim3(R, d.nk), kDV, 0, s, L, d, y, (const float *)o_rows, out);
 }
 void launch_attn_prep(const AttnLayer &L, const AttnDims &d, const float *y, float *qbuf,
                       const Step *st, cudaStream_t s, int nseq) {
