@@ -357,32 +357,43 @@ __global__ void __launch_bounds__(kGmThreads, 1)
                 const float D = half_bits_to_float((uint32_t)(A >> 48));
                 const float M = half_bits_to_float((uint32_t)(B >> 48));
                 const float4 *dfw = reinterpret_cast<const float4 *>(st + Cfg::kOffDf) + wg * (Cfg::kTpt / 2);
+                // blocks in pairs: the commit after block k + 1's MMA also covers block k's
+                // (tcgen05.commit tracks every earlier MMA of the issuing thread), so one wait,
+                // one TMEM-load wait and one fence pair serve both
 #pragma unroll 1
-                for (int k = 0; k < 8; k++) {
-                    const float ds = __fmul_rn(D, (float)(uint32_t)((A >> (6 * k)) & 63u));
-                    const float os = __fmul_rn(M, (float)(uint32_t)((B >> (6 * k)) & 63u));
-                    const float2 ds2 = make_float2(ds, ds), nos2 = make_float2(-os, -os);
-                    if (!wait_all(&mdone[k], (uint32_t)gs & 1u)) {
+                for (int k = 0; k < 8; k += 2) {
+                    if (!wait_all(&mdone[k + 1], (uint32_t)gs & 1u)) {
                         ok = false;
                         break;
                     }
                     tm_fence_after();
-                    uint32_t is[Cfg::kTpt];
-                    tm_ld(trow + (uint32_t)(k * N), is);
+                    uint32_t is[2][Cfg::kTpt];
+                    tm_ld(trow + (uint32_t)(k * N), is[0]);
+                    tm_ld(trow + (uint32_t)((k + 1) * N), is[1]);
                     tm_wait_ld();
                     tm_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&edone[k]);
-                    const float4 *dk = dfw + k * (N / 2);
-                    // per row: acc = fmaf((float)isum, ds * d, acc); acc = fmaf(-os, fsum, acc),
-                    // two rows per packed instruction (each lane of f32x2 rounds as the scalar op)
+                    if (lane == 0) {
+                        mbar_arrive(&edone[k]);
+                        mbar_arrive(&edone[k + 1]);
+                    }
 #pragma unroll
-                    for (int j = 0; j < Cfg::kTpt / 2; j++) {
-                        const float4 p = dk[j];   // d_2j, d_2j+1, fsum_2j, fsum_2j+1
-                        const float2 f = __fadd2_rn(make_float2(int_bits_plus_magic(is[2 * j]),
-                                                                int_bits_plus_magic(is[2 * j + 1])), magic);
-                        acc[j] = __ffma2_rn(f, __fmul2_rn(ds2, make_float2(p.x, p.y)), acc[j]);
-                        acc[j] = __ffma2_rn(nos2, make_float2(p.z, p.w), acc[j]);
+                    for (int kk = 0; kk < 2; kk++) {
+                        const int kb = k + kk;
+                        const float ds = __fmul_rn(D, (float)(uint32_t)((A >> (6 * kb)) & 63u));
+                        const float os = __fmul_rn(M, (float)(uint32_t)((B >> (6 * kb)) & 63u));
+                        const float2 ds2 = make_float2(ds, ds), nos2 = make_float2(-os, -os);
+                        const float4 *dk = dfw + kb * (N / 2);
+                        // per row: acc = fmaf((float)isum, ds * d, acc); acc = fmaf(-os, fsum, acc),
+                        // two rows per packed instruction (each lane of f32x2 rounds as the scalar op)
+#pragma unroll
+                        for (int j = 0; j < Cfg::kTpt / 2; j++) {
+                            const float4 p = dk[j];   // d_2j, d_2j+1, fsum_2j, fsum_2j+1
+                            const float2 f = __fadd2_rn(make_float2(int_bits_plus_magic(is[kk][2 * j]),
+                                                                    int_bits_plus_magic(is[kk][2 * j + 1])), magic);
+                            acc[j] = __ffma2_rn(f, __fmul2_rn(ds2, make_float2(p.x, p.y)), acc[j]);
+                            acc[j] = __ffma2_rn(nos2, make_float2(p.z, p.w), acc[j]);
+                        }
                     }
                 }
                 if (!ok) {
