@@ -212,6 +212,7 @@ int batch_alloc(pinfer_b200_batch *b) {
         if (D.is_full) {
             AttnLayer &A = b->att[l];
             A = c->att[l];
+            A.ks = A.vs = nullptr;   // int8 row scales serve the context's state blob only
             const size_t kv = sizeof(float) * S * b->attd.ss_kv;
             if ((rc = b->dalloc(&A.kc, kv)) || (rc = b->dalloc(&A.vc, kv))) return rc;
         } else {

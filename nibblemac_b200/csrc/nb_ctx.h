@@ -88,6 +88,7 @@ struct pinfer_ctx {
     int H = 0, ffn = 0, n_layers = 0, vocab = 0, nq = 0, nkv = 0, hd = 0, rot = 0;
     int nk = 0, nv = 0, dk = 0, dv = 0, K = 0, kd = 0, vd = 0, C = 0;
     int max_ctx = 0, n_past = 0;
+    int kv_dtype = 0;   // PINFER_KV_*: K / V rows rounded to this precision (held widened)
     float eps = 0;
     int eos = 0;
     int has_mtp = 0;

@@ -210,6 +210,7 @@ int alloc_and_upload(pinfer_ctx *c) {
                       c->C + c->vd + 2 * c->nv, c->eps};
     c->attd = AttnDims{c->nq, c->nkv, c->hd, c->rot, c->max_ctx, 2 * c->nq * c->hd + 2 * c->nkv * c->hd,
                        c->eps, dcos, dsin};
+    c->attd.kv_dtype = c->kv_dtype;
     for (int l = 0; l < c->n_layers; l++) {
         const PqLayer &L = f.layers[l];
         auto &D = c->layers[l];
@@ -272,6 +273,16 @@ int alloc_and_upload(pinfer_ctx *c) {
 
 // This context's own buffers: recurrent and conv states, logs, KV caches, activations, the step
 // block (everything but the model's parameters).
+// int8 KV storage: the row scales beside a cache (the state blob carries them)
+int alloc_kv_scales(pinfer_ctx *c, AttnLayer *A) {
+    A->ks = A->vs = nullptr;
+    if (c->kv_dtype != PINFER_KV_I8) return PINFER_OK;
+    const size_t b = (size_t)c->nkv * c->max_ctx * sizeof(float);
+    int rc;
+    if ((rc = c->dalloc(&A->ks, b)) || (rc = c->dalloc(&A->vs, b))) return rc;
+    return PINFER_OK;
+}
+
 int alloc_state(pinfer_ctx *c) {
     int rc;
     const int cap = PINFER_SPEC_MAX_K + 1;
@@ -281,6 +292,7 @@ int alloc_state(pinfer_ctx *c) {
             AttnLayer &A = c->att[l];
             const size_t kv = (size_t)c->nkv * c->max_ctx * c->hd * sizeof(float);
             if ((rc = c->dalloc(&A.kc, kv)) || (rc = c->dalloc(&A.vc, kv))) return rc;
+            if ((rc = alloc_kv_scales(c, &A))) return rc;
         } else {
             LinLayer &N = c->lin[D.lin];
             if ((rc = c->dalloc(&N.conv_state, sizeof(float) * (size_t)std::max(c->K - 1, 1) * c->C)) ||
@@ -292,6 +304,7 @@ int alloc_state(pinfer_ctx *c) {
     }
     if (c->mtp_ok) {
         const size_t kv = (size_t)c->nkv * c->max_ctx * c->hd * sizeof(float);
+        if ((rc = alloc_kv_scales(c, &c->mtp_att))) return rc;
         if ((rc = c->dalloc(&c->mtp_att.kc, kv)) || (rc = c->dalloc(&c->mtp_att.vc, kv)) ||
             (rc = c->dalloc(&c->hn, sizeof(float) * kMaxRows * c->H)) ||
             (rc = c->dalloc(&c->mrows, sizeof(float) * kMaxRows * c->H)) ||
@@ -626,6 +639,11 @@ int zero_mtp_rows(pinfer_ctx *c, int from, int to) {
     for (int g = 0; g < c->nkv; g++) {
         CUDA_OK(cudaMemsetAsync(c->mtp_att.kc + g * gstride + (size_t)from * c->hd, 0, (size_t)(to - from) * row, c->stream));
         CUDA_OK(cudaMemsetAsync(c->mtp_att.vc + g * gstride + (size_t)from * c->hd, 0, (size_t)(to - from) * row, c->stream));
+        if (c->mtp_att.ks) {   // int8 storage: the rows' scales too (forward_kv.c:127-137)
+            const size_t sc = (size_t)g * c->max_ctx + from, n = (size_t)(to - from) * sizeof(float);
+            CUDA_OK(cudaMemsetAsync(c->mtp_att.ks + sc, 0, n, c->stream));
+            CUDA_OK(cudaMemsetAsync(c->mtp_att.vs + sc, 0, n, c->stream));
+        }
     }
     return PINFER_OK;
 }
@@ -834,9 +852,8 @@ pinfer_ctx *pinfer_load(const char *path, const pinfer_params *params, int *err)
     else if (!std::isfinite(p.gpu_split) || p.gpu_split < 0.0f || p.gpu_split > 1.0f) {
         set_err("gpu_split must be finite and in [0,1]");
         rc = PINFER_E_ARG;
-    } else if (p.kv_dtype != PINFER_KV_F32) {
-        set_err(p.kv_dtype < PINFER_KV_F32 || p.kv_dtype > PINFER_KV_I8 ? "unknown kv_dtype"
-                                                                         : "this build stores fp32 KV rows only");
+    } else if (p.kv_dtype < PINFER_KV_F32 || p.kv_dtype > PINFER_KV_I8) {
+        set_err("unknown kv_dtype");
         rc = PINFER_E_ARG;
     } else if (p.max_ctx > 1 << 20) {
         set_err("max_ctx too large");
@@ -849,6 +866,7 @@ pinfer_ctx *pinfer_load(const char *path, const pinfer_params *params, int *err)
         // the file is validated first (model.c order), then the device is required
         rc = c->file.open_file(path);
         if (rc == PINFER_OK) {
+            c->kv_dtype = p.kv_dtype;
             set_dims(c);
             c->max_ctx = p.max_ctx;
             c->fp = c->file.fingerprint();
@@ -1004,7 +1022,8 @@ int pinfer_generate_greedy(pinfer_ctx *c, const int32_t *prompt, int n_prompt, i
 //   72-byte header: "PINFERS", version 2, n_past, kv_dtype, MTP rows, model dims, full-attention
 //                   mask, pf_model_fingerprint of the file
 //   per linear-attention layer (layer order): conv state [(K-1)][C], recurrent state [nv][dk][dv]
-//   per full-attention layer: K rows [n_kv][n_past][hd], then V rows (fp32 storage)
+//   per full-attention layer: K rows [n_kv][n_past][hd], then V rows, at the storage precision
+//                   (fp32, fp16, or int8 with each group's row scales after its rows)
 //   MTP rows (mtp_rows of them): the MTP head's K and V rows, as the reference writes them
 // Every generation ends with its deferred DeltaNet commit flushed, so the device state is
 // complete whenever the API returns.
@@ -1019,6 +1038,40 @@ struct StateHdr {
 static_assert(sizeof(StateHdr) == 72, "state header layout of engine/src/state.c:24-30");
 constexpr uint32_t kStateVersion = 2;
 
+// bytes of one K or V row in the blob: hd elements at the storage precision, plus the int8
+// scale (state.c:40-44, forward_kv.c:66-77)
+size_t kv_row_bytes(const pinfer_ctx *c) {
+    return c->kv_dtype == PINFER_KV_F16 ? (size_t)c->hd * 2
+                                        : c->kv_dtype == PINFER_KV_I8 ? (size_t)c->hd + 4 : (size_t)c->hd * 4;
+}
+
+// IEEE binary16 bits of a float that binary16 represents exactly (the device rounded it when it
+// stored the row), and back: sign, exponent rebias, subnormals, infinities, NaN (quiet, the top
+// payload bits kept, as the reference's conversion writes them).
+uint16_t f16_bits_exact(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    const uint32_t sign = (u >> 16) & 0x8000u, e = (u >> 23) & 0xffu, man = u & 0x7fffffu;
+    if (e == 0xffu) return (uint16_t)(sign | 0x7c00u | (man ? 0x200u | (man >> 13) : 0u));
+    if (e == 0 && man == 0) return (uint16_t)sign;
+    const int ex = (int)e - 127;
+    if (ex >= -14) return (uint16_t)(sign | ((uint32_t)(ex + 15) << 10) | (man >> 13));
+    // binary16 subnormal: value = m * 2^-24 with m < 1024
+    const uint32_t full = man | 0x800000u;   // 1.man * 2^ex = full * 2^(ex - 23)
+    return (uint16_t)(sign | (full >> (uint32_t)(-1 - ex)));
+}
+float f16_value(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1fu, man = h & 0x3ffu;
+    float v;
+    if (e == 0x1fu) {
+        const uint32_t u = sign | 0x7f800000u | (man << 13);
+        memcpy(&v, &u, 4);
+        return v;
+    }
+    v = e == 0 ? std::ldexp((float)man, -24) : std::ldexp((float)(man | 0x400u), (int)e - 25);
+    return sign ? -v : v;
+}
+
 size_t lin_state_floats(const pinfer_ctx *c) {
     return (size_t)std::max(c->K - 1, 1) * c->C + (size_t)c->nv * c->dk * c->dv;
 }
@@ -1026,7 +1079,7 @@ size_t state_bytes(const pinfer_ctx *c, int n_past, int n_mtp = 0) {
     int n_full = 0;
     for (int l = 0; l < c->n_layers; l++) n_full += c->layers[l].is_full;
     return sizeof(StateHdr) + (size_t)c->n_lin * lin_state_floats(c) * 4 +
-           (size_t)(n_full * (size_t)n_past + n_mtp) * 2 * c->nkv * c->hd * 4;
+           (size_t)(n_full * (size_t)n_past + n_mtp) * 2 * c->nkv * kv_row_bytes(c);
 }
 int mtp_rows_saved(const pinfer_ctx *c) {   // state.c:51-53
     return c->mtp_ok && c->mtp_rows > 0 ? std::min(c->mtp_rows, c->n_past) : 0;
@@ -1037,7 +1090,7 @@ StateHdr state_header(const pinfer_ctx *c) {
     memcpy(s.magic, "PINFERS", 8);
     s.version = kStateVersion;
     s.n_past = (uint32_t)c->n_past;
-    s.kv_dtype = PINFER_KV_F32;
+    s.kv_dtype = (uint32_t)c->kv_dtype;
     s.mtp_rows = (uint32_t)mtp_rows_saved(c);
     s.n_layers = h->n_layers;
     s.hidden = h->hidden;
@@ -1066,17 +1119,71 @@ int state_copy(pinfer_ctx *c, char *cur, int n_past, int dir, int n_mtp = 0) {
     const size_t conv = (size_t)std::max(c->K - 1, 1) * c->C * 4, rec = (size_t)c->nv * c->dk * c->dv * 4;
     for (int i = 0; i < c->n_lin; i++)
         if ((rc = mv(c->lin[i].conv_state, conv)) || (rc = mv(c->lin[i].rec, rec))) return rc;
-    const size_t rows = (size_t)n_past * c->hd * 4, gstride = (size_t)c->max_ctx * c->hd;
+    const size_t gstride = (size_t)c->max_ctx * c->hd;
+    // n rows of group g of one cache: fp32 as they are; fp16 / int8 (the device holds the widened
+    // values) converted to the stored form, int8 scales after the group's rows (state.c:64-83)
+    std::vector<float> tmp;
+    auto rows_of = [&](float *cache, float *scales, int g, int n) -> int {
+        if (n <= 0) return PINFER_OK;
+        float *dev = cache + g * gstride;
+        const size_t cnt = (size_t)n * c->hd;
+        if (c->kv_dtype == PINFER_KV_F32) return mv(dev, cnt * 4);
+        tmp.resize(cnt);
+        float *sc = scales ? scales + (size_t)g * c->max_ctx : nullptr;
+        std::vector<float> s(c->kv_dtype == PINFER_KV_I8 ? (size_t)n : 0);
+        if (dir == 0) {
+            CUDA_OK(cudaMemcpyAsync(tmp.data(), dev, cnt * 4, cudaMemcpyDeviceToHost, c->stream));
+            if (sc) CUDA_OK(cudaMemcpyAsync(s.data(), sc, (size_t)n * 4, cudaMemcpyDeviceToHost, c->stream));
+            CUDA_OK(cudaStreamSynchronize(c->stream));
+        }
+        if (c->kv_dtype == PINFER_KV_F16) {
+            uint16_t *h = reinterpret_cast<uint16_t *>(cur);
+            for (size_t i = 0; i < cnt; i++) {
+                if (dir == 0) {
+                    const uint16_t b = f16_bits_exact(tmp[i]);
+                    memcpy(h + i, &b, 2);
+                } else {
+                    uint16_t b;
+                    memcpy(&b, h + i, 2);
+                    tmp[i] = f16_value(b);
+                }
+            }
+            cur += cnt * 2;
+        } else {   // int8: q = value / scale (exact: |q| <= 127), NaN from a row with an infinity: 0
+            int8_t *q = reinterpret_cast<int8_t *>(cur);
+            float *bs = reinterpret_cast<float *>(cur + cnt);
+            if (dir == 1) memcpy(s.data(), bs, (size_t)n * 4);
+            for (int r = 0; r < n; r++)
+                for (int i = 0; i < c->hd; i++) {
+                    const size_t k = (size_t)r * c->hd + i;
+                    if (dir == 0) {
+                        const float y = s[r] != 0.0f ? std::rint(tmp[k] / s[r]) : 0.0f;
+                        q[k] = (int8_t)(y > 127.0f ? 127 : y < -127.0f ? -127 : y == y ? (int)y : 0);
+                    } else {
+                        tmp[k] = (float)q[k] * s[r];
+                    }
+                }
+            if (dir == 0) memcpy(bs, s.data(), (size_t)n * 4);
+            cur += cnt + (size_t)n * 4;
+        }
+        if (dir == 1) {
+            CUDA_OK(cudaMemcpyAsync(dev, tmp.data(), cnt * 4, cudaMemcpyHostToDevice, c->stream));
+            if (sc) CUDA_OK(cudaMemcpyAsync(sc, s.data(), (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+            CUDA_OK(cudaStreamSynchronize(c->stream));   // tmp and s are reused
+        }
+        return PINFER_OK;
+    };
     for (int l = 0; l < c->n_layers; l++) {
         if (!c->layers[l].is_full) continue;
         for (int kv = 0; kv < 2; kv++)
             for (int g = 0; g < c->nkv; g++)
-                if ((rc = mv((kv ? c->att[l].vc : c->att[l].kc) + g * gstride, rows))) return rc;
+                if ((rc = rows_of(kv ? c->att[l].vc : c->att[l].kc, kv ? c->att[l].vs : c->att[l].ks, g, n_past)))
+                    return rc;
     }
-    const size_t mrows_b = (size_t)n_mtp * c->hd * 4;   // the MTP head's K then V rows
-    for (int kv = 0; kv < 2 && n_mtp > 0; kv++)
+    for (int kv = 0; kv < 2 && n_mtp > 0; kv++)   // the MTP head's K then V rows
         for (int g = 0; g < c->nkv; g++)
-            if ((rc = mv((kv ? c->mtp_att.vc : c->mtp_att.kc) + g * gstride, mrows_b))) return rc;
+            if ((rc = rows_of(kv ? c->mtp_att.vc : c->mtp_att.kc, kv ? c->mtp_att.vs : c->mtp_att.ks, g, n_mtp)))
+                return rc;
     CUDA_OK(cudaStreamSynchronize(c->stream));
     return PINFER_OK;
 }
@@ -1287,6 +1394,7 @@ pinfer_ctx *pinfer_b200_clone(const pinfer_ctx *src, int max_ctx, int *err) {
     c->mtp_att.q_norm = src->mtp_att.q_norm;
     c->mtp_att.k_norm = src->mtp_att.k_norm;
     c->lind = src->lind;
+    c->kv_dtype = src->kv_dtype;
     c->attd = src->attd;
     c->attd.max_ctx = c->max_ctx;   // the RoPE tables cover the source's (larger) context
     c->weights = src->weights;

@@ -116,8 +116,9 @@ struct LinDims {
 };
 
 struct AttnLayer {
-    float *kc, *vc;        // [nkv][max_ctx][hd]
+    float *kc, *vc;        // [nkv][max_ctx][hd], fp32 (with fp16 / int8 storage: the widened values)
     const float *q_norm, *k_norm;
+    float *ks = nullptr, *vs = nullptr;   // int8 storage: row scales [nkv][max_ctx] (for the state blob)
 };
 
 struct AttnDims {
@@ -125,6 +126,7 @@ struct AttnDims {
     float eps;
     const float *rope_cos, *rope_sin;   // [max_ctx][rot / 2]
     int rps = kMaxRows;                 // rows per sequence in the launch grid
+    int kv_dtype = 0;                   // PINFER_KV_*: the precision K / V rows are stored at
     size_t ss_kv = 0;                   // per-sequence stride (floats) of a batch's KV caches
 };
 

@@ -7,6 +7,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cfloat>
 #include <utility>
 #include <cstdio>
 
@@ -1780,6 +1781,35 @@ __global__ void k_set_gen(Step *st, GenArgs g, const unsigned long long *seeds) 
 // KV head (RMSNorm with k_norm, RoPE, stored at position pos0 + t), its V row, and every query
 // head (RMSNorm with q_norm, RoPE). RoPE tables come from the host, computed with glibc
 // exactly as pf_rope_tables does (forward.c:19-32). grid (rows, nq + nkv), hd threads.
+// A K or V row at the storage precision of pf_kv_store (forward_kv.c:83-123), widened back to
+// fp32 as pf_kv_widen reads it (forward_kv.c:139-166), one element per thread of the block:
+// fp16 rounds to nearest even (widening is exact); int8 scales by the row's absolute maximum
+// (exact in any order), q = rint(x * (127 / amax)) clamped to [-127, 127] (NaN: 0), value
+// q * (amax / 127). The attention kernels then read fp32 rows equal to the reference's widened
+// rows. Every thread of the block calls it (block-wide maximum).
+__device__ float kv_store_round(float x, int dtype, float *scale_out, float *red) {
+    if (dtype == PINFER_KV_F16) return __half2float(__float2half_rn(x));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float a = fabsf(x);
+    for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (lane == 0) red[warp] = a;
+    __syncthreads();
+    if (warp == 0) {
+        a = lane < nw ? red[lane] : 0.0f;
+        for (int o = 16; o; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) red[32] = a;
+    }
+    __syncthreads();
+    const float amax = red[32];
+    __syncthreads();   // red is free again
+    const float inv = amax > __fdiv_rn(127.0f, FLT_MAX) ? __fdiv_rn(127.0f, amax) : 0.0f;
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float yq = rintf(__fmul_rn(x, inv));
+    const int q = yq > 127.0f ? 127 : yq < -127.0f ? -127 : (yq == yq ? (int)yq : 0);
+    *scale_out = sc;
+    return __fmul_rn((float)q, sc);
+}
+
 __global__ void k_attn_prep(AttnLayer L, AttnDims d, const float *y, float *qbuf,
                             const Step *st) {
     pdl_wait();
@@ -1825,9 +1855,20 @@ __global__ void k_attn_prep(AttnLayer L, AttnDims d, const float *y, float *qbuf
         qbuf[((size_t)row * d.nq + idx) * hd + tid] = v;
     } else {
         const int g = idx - d.nq;
-        L.kc[((size_t)g * d.max_ctx + pos) * hd + tid] = v;
-        L.vc[((size_t)g * d.max_ctx + pos) * hd + tid] =
-            y[(size_t)row * d.ldy + (size_t)2 * hd * d.nq + (size_t)d.nkv * hd + (size_t)g * hd + tid];
+        const size_t r = (size_t)g * d.max_ctx + pos;
+        float vv = y[(size_t)row * d.ldy + (size_t)2 * hd * d.nq + (size_t)d.nkv * hd + (size_t)g * hd + tid];
+        if (d.kv_dtype != PINFER_KV_F32) {   // uniform over the block
+            __shared__ float red[33];
+            float sk = 0.0f, sv = 0.0f;
+            v = kv_store_round(v, d.kv_dtype, &sk, red);
+            vv = kv_store_round(vv, d.kv_dtype, &sv, red);
+            if (d.kv_dtype == PINFER_KV_I8 && tid == 0 && L.ks) {
+                L.ks[r] = sk;
+                L.vs[r] = sv;
+            }
+        }
+        L.kc[r * hd + tid] = v;
+        L.vc[r * hd + tid] = vv;
     }
 }
 

@@ -24,10 +24,12 @@ def _i32(a) -> np.ndarray:
 class Model:
     """A context on the B200: ``Model(path).generate(prompt, 128)``."""
 
-    def __init__(self, path: str | os.PathLike, max_ctx: int = 4096, lib: Lib | None = None) -> None:
+    def __init__(self, path: str | os.PathLike, max_ctx: int = 4096, lib: Lib | None = None,
+                 kv_dtype: int = 0) -> None:
         self.lib = lib or load_library()
         p = self.lib.pinfer_default_params()
         p.max_ctx = max_ctx
+        p.kv_dtype = kv_dtype   # PINFER_KV_F32 / F16 / I8
         err = ctypes.c_int(0)
         self.ctx = self.lib.pinfer_load(os.fspath(path).encode(), ctypes.byref(p), ctypes.byref(err))
         if not self.ctx:

@@ -92,7 +92,8 @@ class _SpecStats(ctypes.Structure):
 class RefEngine:
     """The reference engine (scalar build + Q4K restatement) on one model file."""
 
-    def __init__(self, model_path, max_ctx: int = 4096, lib_path: Path | None = None) -> None:
+    def __init__(self, model_path, max_ctx: int = 4096, lib_path: Path | None = None,
+                 kv_dtype: int = 0) -> None:
         path = lib_path or HERE / "_ref" / "libpinfer_ref.so"
         if not Path(path).exists():
             raise FileNotFoundError(f"{path} missing: build it with `make -C oracle ref`")
@@ -124,6 +125,7 @@ class RefEngine:
         p = L.pinfer_default_params()
         p.max_ctx = max_ctx
         p.n_threads = 1
+        p.kv_dtype = kv_dtype
         err = ctypes.c_int(0)
         self.ctx = L.pinfer_load(str(model_path).encode(), ctypes.byref(p), ctypes.byref(err))
         if not self.ctx:

@@ -341,3 +341,39 @@ def test_adaptive_speculation_keeps_tokens(pair, k, ngram):
     rtoks, _, _ = ref.generate_mtp(p, 40, k, ngram=ngram)
     assert rtoks == plain
     assert st.rounds > 0 and st.drafted < k * st.rounds, (st.rounds, st.drafted)
+
+
+@pytest.mark.parametrize("kv_dtype", [1, 2])
+def test_narrow_kv_storage_matches_reference(small_model, kv_dtype):
+    """pinfer_params.kv_dtype fp16 (1) and int8 (2): K / V rows rounded as pf_kv_store stores
+    them (forward_kv.c:83-123) and read widened (pf_kv_widen): the logits of a 130-row prompt
+    (prefill chunks, then a 16-row pass) and of its continuation, the state blob (rows at the
+    storage precision, int8 scales after each group's rows) byte for byte, MTP speculation
+    tokens and counts, and a blob loaded into a fresh context continuing exactly."""
+    from nibblemac_b200._lib import SpecStats
+    from nibblemac_b200.model import Model
+    from oracle import RefEngine
+    dev = Model(small_model, max_ctx=512, kv_dtype=kv_dtype)
+    ref = RefEngine(small_model, max_ctx=512, kv_dtype=kv_dtype)
+    try:
+        a, b = prompt(dev.n_vocab, 130, 90 + kv_dtype), prompt(dev.n_vocab, 7, 95)
+        assert np.array_equal(bits(dev.eval(a)), bits(ref.eval(a)))
+        assert np.array_equal(bits(dev.eval(b)), bits(ref.eval(b)))
+        blob = dev.save_state()
+        assert blob == ref.save_state()
+        st = SpecStats()
+        toks, status = dev.generate(prompt(dev.n_vocab, 40, 97), 24, k=3, stats=st, append=True)
+        rtoks, rst, _ = ref.generate_mtp(prompt(dev.n_vocab, 40, 97), 24, 3, 0, append=True)
+        assert status == 0 and toks == rtoks and [st.rounds, st.drafted, st.accepted] == rst
+        assert dev.save_state() == ref.save_state()
+        fresh = Model(small_model, max_ctx=512, kv_dtype=kv_dtype)
+        try:
+            fresh.load_state(blob)
+            dev.load_state(blob)
+            nxt = prompt(dev.n_vocab, 5, 99)
+            assert np.array_equal(bits(fresh.eval(nxt)), bits(dev.eval(nxt)))
+        finally:
+            fresh.close()
+    finally:
+        dev.close()
+        ref.close()

@@ -72,7 +72,9 @@ def test_missing_file(lib, tmp_path):
 def test_bad_params(lib, tiny_model):
     assert load(lib, tiny_model, gpu_split=2.0)[1] == PINFER_E_ARG
     assert load(lib, tiny_model, kv_dtype=7)[1] == PINFER_E_ARG
-    assert load(lib, tiny_model, kv_dtype=1)[1] == PINFER_E_ARG   # fp32 KV only in this build
+    assert load(lib, tiny_model, kv_dtype=-1)[1] == PINFER_E_ARG
+    for dt in (1, 2):   # fp16 / int8 KV storage are accepted (this host then lacks the device)
+        assert load(lib, tiny_model, kv_dtype=dt)[1] != PINFER_E_ARG
 
 
 HEADER_PATCHES = {
