@@ -16,6 +16,8 @@ context (restored with pinfer_rewind before every step, outside the timed region
          and greedy stream copied in, 1-token prefill, decode, tokens copied out)
   prefill  pinfer_eval of the 511 context tokens from an empty state (tensor-core chunks of up
          to 64 rows), and at N=1 of configs[4]'s 4095 tokens on the 2B shape: device and wall ms
+  config4 / config5  configs[3] (256 requests per GPU, one batch) and, at N=1, configs[4] on one
+         GPU (batch of 8 contexts of 4096 tokens, head unsharded; --config5 shards it over ranks)
 Multi-GPU: one independent replica per GPU (replicas only, no collective on the data path),
 weak scaling; value = all tokens / max over ranks of the device time.
 --impl reference: the reference engine's own CPU path (oracle/_ref, scalar C) on the host
@@ -149,14 +151,41 @@ def measure_prefill(m, torch, tokens: np.ndarray, reps: int = 3) -> dict:
             "tok_s": round(len(tokens) / (d / 1000.0), 1)}
 
 
-def measure_prefill5(torch, rank: int) -> dict:
-    """configs[4]'s context on one GPU: the 2B-shaped model, 4095 tokens prefilled."""
+def measure_config5(torch, rank: int, local: int) -> tuple[dict, dict]:
+    """configs[4] on one GPU (the head unsharded): the 2B-shaped model's 4095-token context
+    prefilled on one context (pinfer_eval), then one step of the configured batch of 8 such
+    contexts at k = 3, p = 0.8 (as `--config5`: tokens / device time of the verify rounds, the
+    prompts' prefill outside). Returns (prefill record, decode record)."""
     from nibblemac_b200.model import Model
     path = model_path(rank, None, "2b")
-    m = Model(path, max_ctx=CTX5 + 16)
+    max_ctx = CTX5 + N_GEN + 16
+    m = Model(path, max_ctx=max_ctx)
     try:
-        ctx = np.random.default_rng(4321).integers(0, m.n_vocab, CTX5).astype(np.int32)
-        return {"model": "2b", **measure_prefill(m, torch, ctx[:-1], reps=2)}
+        rng = np.random.default_rng(4321)
+        ctx = rng.integers(0, m.n_vocab, CTX5).astype(np.int32)
+        prefill = {"model": "2b", **measure_prefill(m, torch, ctx[:-1], reps=2)}
+        nseq = 8
+        b = m.batch(nseq, max_ctx, max_k=K_DRAFT)
+        try:
+            prompts = [ctx] + [rng.integers(0, m.n_vocab, CTX5).astype(np.int32) for _ in range(nseq - 1)]
+            greedy, _, status, _ = b.generate_synthetic(prompts, N_GEN)
+            assert status == [0] * nseq
+            pad = [g + [0] * (N_GEN - len(g)) for g in greedy]
+            seeds = [600 + j for j in range(nseq)]
+            b.generate_synthetic(prompts, N_GEN, K_DRAFT, pad, seeds, P_MAIN)   # warm-up
+            with Clocks(local) as clk:
+                toks, st, status, ms = b.generate_synthetic(prompts, N_GEN, K_DRAFT, pad, seeds, P_MAIN)
+            assert status == [0] * nseq and toks == greedy, "speculative output differs from plain greedy"
+            tokens = sum(len(g) - 1 for g in greedy)
+            decode = {"metric": "greedy spec-decode tok/s (k=3), 2B shape", "value": round(tokens / (ms / 1000.0), 1),
+                      "unit": UNIT, "n_gpus": 1, "ms": round(ms, 1), "verify_rounds": b.rounds(),
+                      "workload": f"configs[4] on one GPU: Qwen3.5-2B-shaped Q4K, k=3, p={P_MAIN}, "
+                                  f"{CTX5}-token contexts, {N_GEN} generated each, batch {nseq}; the LM "
+                                  "head unsharded (one GPU); verify rounds timed, prefill outside",
+                      "clocks": clk.summary()}
+        finally:
+            b.close()
+        return prefill, decode
     finally:
         m.close()
 
@@ -734,7 +763,8 @@ def main() -> None:
     ap.add_argument("--no-config4", action="store_true",
                     help="leave the configs[3] multi-stream record out of the default line")
     ap.add_argument("--no-prefill5", action="store_true",
-                    help="leave the configs[4] (2B, 4095-token) prefill time out of the default line")
+                    help="leave the configs[4] (2B, 4095-token contexts) prefill time and one-GPU batch "
+                         "record out of the default line")
     ap.add_argument("--config4", action="store_true",
                     help="configs[3]: 256 requests per GPU in one multi-sequence batch "
                          "(one JSON line)")
@@ -900,8 +930,9 @@ def main() -> None:
                                   "per round"}}
         extra["matvec"] = {k: v for k, v in mv.items() if not k.startswith("_")}
     m.close()
+    config5 = None
     if rank == 0 and world == 1 and not args.no_prefill5:
-        prefill["config5"] = measure_prefill5(torch, rank)
+        prefill["config5"], config5 = measure_config5(torch, rank, local)
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup,
@@ -915,7 +946,7 @@ def main() -> None:
                 "gpu_launches": int(rounds * kernels_per_round * world),
                 "kernels_per_round": kernels_per_round, "rounds": rounds,
                 "sweep": sweep, "config2_plain": config2, "roofline": roof, "clocks": clk.summary(),
-                "config4": config4, "prefill": prefill}
+                "config4": config4, "config5": config5, "prefill": prefill}
         line.update(extra)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(path, dev_blob, greedy)
