@@ -168,6 +168,14 @@ int nb_libm_eval_device(int fn, const float *x, float *y, long long n, void *str
  * and returns; *status_out receives that word. 0, -4 (arguments), -3 (CUDA error). */
 int nb_test_bounded_wait(unsigned spin_limit, int *status_out);
 
+/* Host test hooks of the state blob's narrow K / V rows (pinfer_params.kv_dtype; the reference's
+ * format, engine/src/state.c:64-83 with forward_kv.c:83-123): nb_test_kv_f16 dir 0 writes the
+ * binary16 bits of n floats that binary16 represents exactly (NaN: quiet, top payload bits),
+ * dir 1 the floats of n binary16 bit patterns; nb_test_kv_i8 the int8 codes of rows of widened
+ * values q * scale (one scale per row of hd). 0, or -4 (arguments). No device needed. */
+int nb_test_kv_f16(int dir, const void *in, void *out, long long n);
+int nb_test_kv_i8(const float *v, const float *scales, int rows, int hd, int8_t *q);
+
 /* Allocation-free Q4K x A8 matmul. No counterpart in the reference (its CPU pf_matmul takes
  * caller buffers and needs no scratch).
  * Y [n][rows] = W (device panel layout) x A8(X [n][cols]), the same kernels and the same

@@ -1072,6 +1072,13 @@ float f16_value(uint16_t h) {
     return sign ? -v : v;
 }
 
+// the int8 code of a widened value v = q * s (q recovered exactly: |q| <= 127); a row whose
+// scale is 0 (all zeros) or infinite (an infinity in the row: every value NaN) has codes 0
+int8_t i8_code(float v, float s) {
+    const float y = s != 0.0f ? std::rint(v / s) : 0.0f;
+    return (int8_t)(y > 127.0f ? 127 : y < -127.0f ? -127 : y == y ? (int)y : 0);
+}
+
 size_t lin_state_floats(const pinfer_ctx *c) {
     return (size_t)std::max(c->K - 1, 1) * c->C + (size_t)c->nv * c->dk * c->dv;
 }
@@ -1157,8 +1164,7 @@ int state_copy(pinfer_ctx *c, char *cur, int n_past, int dir, int n_mtp = 0) {
                 for (int i = 0; i < c->hd; i++) {
                     const size_t k = (size_t)r * c->hd + i;
                     if (dir == 0) {
-                        const float y = s[r] != 0.0f ? std::rint(tmp[k] / s[r]) : 0.0f;
-                        q[k] = (int8_t)(y > 127.0f ? 127 : y < -127.0f ? -127 : y == y ? (int)y : 0);
+                        q[k] = i8_code(tmp[k], s[r]);
                     } else {
                         tmp[k] = (float)q[k] * s[r];
                     }
@@ -1356,6 +1362,22 @@ int pinfer_b200_forward_all(pinfer_ctx *c, const int32_t *tokens, int n, float *
 }
 
 void *pinfer_b200_stream(pinfer_ctx *c) { return c ? (void *)c->stream : nullptr; }
+
+int nb_test_kv_f16(int dir, const void *in, void *out, long long n) {
+    if ((dir != 0 && dir != 1) || !in || !out || n < 0) return PINFER_E_ARG;
+    for (long long i = 0; i < n; i++) {
+        if (dir == 0) static_cast<uint16_t *>(out)[i] = f16_bits_exact(static_cast<const float *>(in)[i]);
+        else static_cast<float *>(out)[i] = f16_value(static_cast<const uint16_t *>(in)[i]);
+    }
+    return PINFER_OK;
+}
+
+int nb_test_kv_i8(const float *v, const float *scales, int rows, int hd, int8_t *q) {
+    if (!v || !scales || !q || rows < 0 || hd < 0) return PINFER_E_ARG;
+    for (int r = 0; r < rows; r++)
+        for (int i = 0; i < hd; i++) q[(size_t)r * hd + i] = i8_code(v[(size_t)r * hd + i], scales[r]);
+    return PINFER_OK;
+}
 
 pinfer_ctx *pinfer_b200_clone(const pinfer_ctx *src, int max_ctx, int *err) {
     int dummy;
